@@ -1,0 +1,295 @@
+#!/usr/bin/env python3
+"""Benchmark: Qwen2 decode tokens/s on the B200 path.
+
+Workload: the 24-layer Qwen2.5-0.5B-shaped LM (hidden 896, 14/2 heads, hd 64,
+ffn 4864 SwiGLU, vocab 151936, tied Q8_0 lm_head), random N(0, 0.02) Q8_0
+weights (synthetic, seeded), batch 2 (CFG cond + uncond rows), greedy decode
+from an f16 KV cache of --kv positions (default 1024, filled from N(0,1)).
+One step = embed -> 24 layers -> output_norm -> lm_head -> argmax for both
+rows; tokens/s counts both rows.  The 550 MB of weights per step exceed the
+126 MB L2, so every step streams them from HBM (no flush needed).
+
+  value : device-resident loop (token ids stay in HBM), CUDA events on the
+          launching stream, max over ranks
+  e2e   : the same steps through the C ABI with HOST token buffers
+          (vvq2_decode_step: H2D ids, D2H argmax ids every step)
+  roofline : the dominant kernel (the fused dequant GEMV), algorithmic bytes
+          per launch / mean launch time from CUDA events, vs measured HBM peak
+  cpu_baseline : the CPU oracle (port of the reference's ggml CPU numerics)
+          on this host's cores, bounded sample of decode steps
+
+--impl reference times that CPU implementation alone (the reference cannot be
+built here: its ggml submodule is absent).  Multi-GPU: C2 does not shard,
+so N GPUs run N independent replicas (weak scaling, no collectives)."""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "vibevoice.cpp_b200"))
+
+C2 = dict(hidden=896, n_heads=14, n_kv_heads=2, head_dim=64, ffn=4864, n_layers=24, vocab=151936,
+          rope_theta=1.0e6, rms_eps=1.0e-6)
+SEED = 20261201
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def cpu_decode_rate(model, hp, kv_len, budget_s=15.0, flags=None):
+    """CPU oracle (test infrastructure) decode steps/s on this host, bounded sample."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import vvq2_oracle as O
+    flags = O.GGML_CPU if flags is None else flags
+    rng = np.random.default_rng(SEED + 1)
+    max_steps = 64
+    ora = O.Model(hp, 2, kv_len + max_steps + 2, flags)
+    for li, t in enumerate(model["layers"]):
+        ora.set_layer(li, t)
+    ora.set_output(model["output_norm"], model["lm_head"], model["tok_embd"])
+    w = hp["n_kv_heads"] * hp["head_dim"]
+    for li in range(hp["n_layers"]):
+        for s in range(2):
+            ora.kv_load(s, li, rng.standard_normal((kv_len, w), dtype=np.float32),
+                        rng.standard_normal((kv_len, w), dtype=np.float32))
+    for s in range(2):
+        ora.set_past_len(s, kv_len)
+    tok = rng.integers(0, hp["vocab"], size=2).astype(np.int32)
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_steps:
+        pos = [ora.past_len(0), ora.past_len(1)]
+        h = ora.forward([0, 1], ora.embed(tok)[:, None, :], pos, output_norm=True)
+        tok = ora.lm_head(h[:, 0]).astype(np.int32)
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return 2 * n / dt, n, cores
+
+
+class ClockSampler:
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.out = ROOT / "gpurun_out" / f"clocks_rank{index}.csv"
+
+    def __enter__(self):
+        try:
+            self.out.parent.mkdir(exist_ok=True)
+            self.f = open(self.out, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+            self.f.close()
+
+    def summary(self):
+        if not self.proc or not self.out.exists():
+            return None
+        rows = [r.split(", ") for r in self.out.read_text().strip().splitlines() if r.strip()]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and r[5 + i].strip() == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    import synth
+    model = synth.model_q8_0(SEED, C2)
+    rate, n, cores = cpu_decode_rate(model, C2, args.kv, budget_s=max(5.0, 4.0 * args.steps / 10))
+    line = {
+        "impl": "reference", "metric": "qwen2_decode_tokens_per_s", "value": round(rate, 3), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": n, "warmup": 0, "ms_per_step": round(2000.0 / rate, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->f32 (ggml q8_0 dot)",
+        "data": "synthetic", "config": workload_config(args),
+        "cpu_baseline": {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} greedy decode steps x 2 rows of the full C2 stack (ggml CPU numerics)"},
+        "e2e": {"value": round(rate, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's ggml CPU backend cannot be built here (ggml submodule absent); "
+                "this is the CPU restatement of its numerics (oracle/), all host threads",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args):
+    return {"workload": "C2: Qwen2.5-0.5B-shaped 24-layer LM, Q8_0 (tied lm_head), batch 2 CFG greedy decode",
+            "model": "qwen2.5-0.5b-shaped (random init)", "global_batch": 2 * args.gpus, "kv_len": args.kv,
+            "seq_len": args.kv, "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single",
+            "l2": "weights 550 MB/step > 126 MB L2: streamed from HBM each step, no flush"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--kv", type=int, default=1024)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank, local, world = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    import synth
+    import vvq2
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    hp = C2
+    model = synth.model_q8_0(SEED, hp)
+    eng = vvq2.Engine(hp, device=local)
+    for li, t in enumerate(model["layers"]):
+        eng.set_layer(li, t)
+    eng.set_output(model["output_norm"], model["lm_head"], model["tok_embd"])
+    prof_steps = 20
+    total = args.warmup + args.steps * 2 + prof_steps + 8
+    kv = eng.kv(2, args.kv + total)
+    w = hp["n_kv_heads"] * hp["head_dim"]
+    g = torch.Generator(device="cuda").manual_seed(SEED + rank)
+    for li in range(hp["n_layers"]):
+        for s in range(2):
+            k = torch.randn((args.kv, w), generator=g, device="cuda", dtype=torch.float32)
+            v = torch.randn((args.kv, w), generator=g, device="cuda", dtype=torch.float32)
+            kv.load_prefix(s, li, k, v)
+    for s in range(2):
+        kv.set_past_len(s, args.kv)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    tok = torch.randint(0, hp["vocab"], (2,), dtype=torch.int32, device="cuda")
+
+    def steps(n):
+        for _ in range(n):
+            eng.decode_step(kv, [0, 1], tok, tok, stream=sh)
+
+    steps(args.warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0 = vvq2.launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        steps(args.steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = vvq2.launches() - l0
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = 2 * world * args.steps / (ms / 1000.0)
+
+    # e2e: host token buffers through the C ABI (H2D ids + D2H argmax ids per step)
+    host_tok = tok.cpu().numpy().astype(np.int32)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(args.steps):
+        host_tok = eng.decode_step(kv, [0, 1], host_tok, stream=sh)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e2.elapsed_time(e3)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e = 2 * world * args.steps / (ms_e2e / 1000.0)
+
+    # roofline of the dominant kernel (fused dequant GEMV): events per launch
+    eng.profile(True)
+    tok.copy_(torch.from_numpy(host_tok).cuda())
+    for _ in range(prof_steps):
+        eng.decode_step(kv, [0, 1], tok, tok, stream=sh)
+    g_ms, g_bytes, g_n = eng.profile_read(0)
+    a_ms, a_bytes, a_n = eng.profile_read(1)
+    eng.profile(False)
+    peak, peak_kind = measured_peaks()
+    achieved = (g_bytes / g_n) / (g_ms / g_n / 1000.0) / 1e9 if g_n else None
+    traffic = None
+    tf = ROOT / "profiles" / "gemv_q8_0_c2_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+
+    line = {
+        "metric": "qwen2_decode_tokens_per_s", "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8xint8->f32 (q8_0 weights x q8_0 activations), f16 KV",
+        "data": "synthetic (seeded random-init weights of the architecture)",
+        "config": workload_config(argparse.Namespace(**{**vars(args), "gpus": world})),
+        "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1) if achieved else None, "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
+                     "traffic": traffic, "kernel": "k_gemv (fused RMSNorm/quant + Q8_0 dp4a GEMV + epilogue)",
+                     "peak_source": peak_kind,
+                     "algorithmic_bytes_per_launch": round(g_bytes / g_n) if g_n else None,
+                     "mean_launch_us": round(1000.0 * g_ms / g_n, 3) if g_n else None,
+                     "attn_decode": {"achieved_gbs": round(a_bytes / (a_ms / 1000.0) / 1e9, 1) if a_n else None,
+                                     "mean_launch_us": round(1000.0 * a_ms / a_n, 3) if a_n else None},
+                     "step_hbm_gbs": round(synth.weight_bytes(model) * 1.0 / (ms / args.steps / 1000.0) / 1e9, 1)},
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rate, n, cores = cpu_decode_rate(model, hp, args.kv)
+        line["cpu_baseline"] = {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                                "sample": f"{n} greedy decode steps x 2 rows of the full C2 stack, ggml CPU "
+                                          f"numerics (oracle/, OpenMP over {cores} threads)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

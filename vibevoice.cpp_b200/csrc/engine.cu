@@ -1,0 +1,995 @@
+// engine.cu -- host side of the B200 Qwen2 path and the exported C ABI.
+//
+// Mirrors the reference's layer interface (src/qwen2.hpp: Qwen2Hparams,
+// Qwen2LayerWeights, ResidentKV) and the stack drivers that call it
+// (run_qwen2_stack, src/vibevoice_tts.cpp:363-464; the ASR prefill/decode
+// loops, src/vibevoice_asr.cpp:554-652,665-801), but keeps everything on the
+// device: weights are uploaded once and repacked, the KV cache is an f16 paged
+// pool, positions and the causal mask are computed by the kernels, and a step
+// is a fixed sequence of launches on one stream.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cctype>
+#include <cstdarg>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/vvq2_capi.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace vvq2;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CU(expr)                                                                        \
+    do {                                                                                \
+        cudaError_t e_ = (expr);                                                        \
+        if (e_ != cudaSuccess)                                                          \
+            return fail(VVQ2_ERR_CUDA, "%s:%d %s: %s", __FILE__, __LINE__, #expr,      \
+                        cudaGetErrorString(e_));                                        \
+    } while (0)
+
+bool type_ok(int t) {
+    return t == W_F32 || t == W_F16 || t == W_Q8_0 || t == W_Q5_K || t == W_Q6_K;
+}
+
+int block_elems(int t) { return t == W_Q8_0 ? 32 : (t == W_Q5_K || t == W_Q6_K) ? 256 : 1; }
+int block_bytes(int t) {
+    switch (t) {
+        case W_F32: return 4;
+        case W_F16: return 2;
+        case W_Q8_0: return 34;
+        case W_Q5_K: return 176;
+        case W_Q6_K: return 210;
+        default: return 0;
+    }
+}
+
+bool is_device_ptr(const void* p) {
+    if (!p) return false;
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+struct Owned {
+    DevW w;
+    std::vector<void*> allocs;
+};
+
+}  // namespace
+
+struct vvq2_ctx {
+    vvq2_hparams hp{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    float rope_ts = 0.f;
+    struct Layer {
+        bool set = false;
+        DevW qkv, o, gate, up, down;
+        float* attn_norm = nullptr;
+        float* ffn_norm = nullptr;
+        float* qkv_bias = nullptr;
+    };
+    std::vector<Layer> layers;
+    float* out_norm = nullptr;
+    DevW lm_head, tok_embd;
+    std::vector<void*> allocs;
+    // scratch for up to GEMV_MAX_M activation rows
+    float *X = nullptr, *Q = nullptr, *ATT = nullptr, *FA = nullptr, *LOGITS = nullptr;
+    float *part = nullptr, *part_ml = nullptr;
+    int* counters = nullptr;
+    RowMeta* meta = nullptr;
+    RowMeta* meta_host = nullptr;   // pinned
+    unsigned long long* amax = nullptr;
+    int32_t* tok = nullptr;
+    int max_splits_cap = 64;
+
+    // measurement: per-launch CUDA events (captured into decode graphs when on)
+    struct Rec { int kind; int e0, e1; double bytes; };
+    bool prof_on = false;
+    std::vector<cudaEvent_t> events;
+    double prof_ms[3] = {0, 0, 0}, prof_bytes[3] = {0, 0, 0};
+    int64_t prof_n[3] = {0, 0, 0};
+
+    // decode-step CUDA graphs, keyed by (kv, sequence set, length bucket, profiling)
+    struct Graph {
+        vvq2_kv* kv;
+        std::vector<int> seqs;
+        int bucket;
+        bool prof;
+        cudaGraphExec_t exec;
+        int kernels;
+        std::vector<Rec> recs;
+    };
+    std::vector<Graph> graphs;
+    // c->meta currently holds the next decode step of (meta_kv, meta_seqs)
+    vvq2_kv* meta_kv = nullptr;
+    std::vector<int> meta_seqs;
+
+    template <class T>
+    int alloc(T** p, size_t n) {
+        void* q = nullptr;
+        cudaError_t e = cudaMalloc(&q, n * sizeof(T) > 0 ? n * sizeof(T) : 16);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(VVQ2_ERR_OUT_OF_MEMORY, "cudaMalloc(%zu): %s", n * sizeof(T), cudaGetErrorString(e));
+        }
+        allocs.push_back(q);
+        *p = static_cast<T*>(q);
+        return 0;
+    }
+};
+
+struct vvq2_kv {
+    vvq2_ctx* ctx = nullptr;
+    int n_seqs = 0, max_seq = 0, max_pages = 0;
+    size_t layer_elems = 0;      // halves per layer per pool
+    __half* k = nullptr;
+    __half* v = nullptr;
+    int* block_table = nullptr;
+    std::vector<int> past;
+
+    KvLayer layer(int li) const {
+        KvLayer L;
+        L.k = k + (size_t)li * layer_elems;
+        L.v = v + (size_t)li * layer_elems;
+        L.block_table = block_table;
+        L.max_pages = max_pages;
+        L.n_kv = ctx->hp.n_kv_heads;
+        L.hd = ctx->hp.head_dim;
+        return L;
+    }
+};
+
+namespace {
+
+// Host repack of one GGUF tensor into the device layout (DevW).
+int upload_tensor(vvq2_ctx* c, const vvq2_tensor& t, DevW* out, int expect_ne0, int expect_ne1,
+                  const char* name) {
+    if (!t.data) return fail(VVQ2_ERR_INVALID_ARG, "%s: missing tensor", name);
+    if (!type_ok(t.type)) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "%s: ggml type %d not supported", name, t.type);
+    if ((expect_ne0 > 0 && t.ne0 != expect_ne0) || (expect_ne1 > 0 && t.ne1 != expect_ne1))
+        return fail(VVQ2_ERR_INVALID_ARG, "%s: shape [%lld, %lld], expected [%d, %d]", name,
+                    (long long)t.ne0, (long long)t.ne1, expect_ne0, expect_ne1);
+    const int be = block_elems(t.type), bb = block_bytes(t.type);
+    if (t.ne0 % be) return fail(VVQ2_ERR_INVALID_ARG, "%s: ne0 %lld not a multiple of %d", name, (long long)t.ne0, be);
+    const int64_t rows = t.ne1, cols = t.ne0, nb = cols / be;
+    const uint8_t* src = static_cast<const uint8_t*>(t.data);
+    DevW w;
+    w.type = t.type;
+    w.rows = (int)rows;
+    w.cols = (int)cols;
+    std::vector<uint8_t> q;
+    std::vector<uint16_t> d;
+    switch (t.type) {
+        case W_Q8_0:
+            w.row_stride = cols;
+            q.resize((size_t)rows * cols);
+            d.resize((size_t)rows * nb);
+            for (int64_t r = 0; r < rows; ++r)
+                for (int64_t b = 0; b < nb; ++b) {
+                    const uint8_t* blk = src + ((size_t)r * nb + b) * 34;
+                    memcpy(&d[(size_t)r * nb + b], blk, 2);
+                    memcpy(&q[(size_t)r * cols + b * 32], blk + 2, 32);
+                }
+            break;
+        case W_Q6_K:
+            w.row_stride = nb * Q6K_PACKED;
+            q.resize((size_t)rows * w.row_stride);
+            d.resize((size_t)rows * nb);
+            for (int64_t r = 0; r < rows; ++r)
+                for (int64_t b = 0; b < nb; ++b) {
+                    const uint8_t* blk = src + ((size_t)r * nb + b) * 210;
+                    memcpy(&q[(size_t)r * w.row_stride + b * Q6K_PACKED], blk, Q6K_PACKED);
+                    memcpy(&d[(size_t)r * nb + b], blk + 208, 2);
+                }
+            break;
+        default:   // Q5_K blocks (176 B, 16-aligned), F32, F16: as-is
+            w.row_stride = nb * bb;
+            q.assign(src, src + (size_t)rows * w.row_stride);
+            break;
+    }
+    uint8_t* dq = nullptr;
+    if (int rc = c->alloc(&dq, q.size())) return rc;
+    CU(cudaMemcpy(dq, q.data(), q.size(), cudaMemcpyHostToDevice));
+    w.q = dq;
+    if (!d.empty()) {
+        __half* dd = nullptr;
+        if (int rc = c->alloc(&dd, d.size())) return rc;
+        CU(cudaMemcpy(dd, d.data(), d.size() * 2, cudaMemcpyHostToDevice));
+        w.d = dd;
+    }
+    *out = w;
+    return 0;
+}
+
+// 1-D f32 vector (norm weights, biases) from any float type
+int upload_vec(vvq2_ctx* c, const vvq2_tensor& t, int n, float** out, const char* name) {
+    if (!t.data) return fail(VVQ2_ERR_INVALID_ARG, "%s: missing tensor", name);
+    if (t.ne0 * std::max<int64_t>(t.ne1, 1) != n)
+        return fail(VVQ2_ERR_INVALID_ARG, "%s: %lld elements, expected %d", name, (long long)(t.ne0 * t.ne1), n);
+    std::vector<float> h(n);
+    if (t.type == W_F32) memcpy(h.data(), t.data, (size_t)n * 4);
+    else if (t.type == W_F16) {
+        const __half* s = static_cast<const __half*>(t.data);
+        for (int i = 0; i < n; ++i) h[i] = __half2float(s[i]);
+    } else {
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "%s: vector type %d", name, t.type);
+    }
+    if (int rc = c->alloc(out, (size_t)n)) return rc;
+    CU(cudaMemcpy(*out, h.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+int check_ctx(vvq2_ctx* c) {
+    if (!c) return fail(VVQ2_ERR_INVALID_ARG, "null context");
+    CU(cudaSetDevice(c->device));
+    return 0;
+}
+
+cudaStream_t pick_stream(vvq2_ctx* c, void* s) { return s ? static_cast<cudaStream_t>(s) : c->stream; }
+
+// Attention split: ~2 CTAs per SM overall, at most max_splits_cap splits per row.
+void choose_split(const vvq2_ctx* c, int M, int max_lim, int* split, int* nsplit) {
+    const int target = 296;
+    const int per_row = std::max(1, target / std::max(1, M * c->hp.n_kv_heads));
+    int s = (max_lim + per_row - 1) / per_row;
+    s = std::max(s, 64);
+    s = (s + 31) / 32 * 32;
+    while ((max_lim + s - 1) / s > c->max_splits_cap) s += 32;
+    s = std::min(s, 512);
+    *split = s;
+    *nsplit = (max_lim + s - 1) / s;
+}
+
+size_t weight_bytes(const DevW& w) {
+    if (w.type < 0) return 0;
+    size_t b = (size_t)w.rows * w.row_stride;
+    if (w.d) b += (size_t)w.rows * (w.cols / (w.type == W_Q8_0 ? 32 : 256)) * 2;
+    return b;
+}
+
+// Records CUDA events around launches when profiling (kind 0 GEMV, 1 attention).
+struct Recorder {
+    vvq2_ctx* c;
+    cudaStream_t st;
+    std::vector<vvq2_ctx::Rec>* recs;
+    int e0 = -1;
+    cudaError_t begin() {
+        if (!recs) return cudaSuccess;
+        const int need = (int)recs->size() * 2 + 2;
+        while ((int)c->events.size() < need) {
+            cudaEvent_t e;
+            cudaError_t err = cudaEventCreate(&e);
+            if (err != cudaSuccess) return err;
+            c->events.push_back(e);
+        }
+        e0 = (int)recs->size() * 2;
+        return cudaEventRecord(c->events[e0], st);
+    }
+    cudaError_t end(int kind, double bytes) {
+        if (!recs) return cudaSuccess;
+        cudaError_t err = cudaEventRecord(c->events[e0 + 1], st);
+        recs->push_back({kind, e0, e0 + 1, bytes});
+        return err;
+    }
+};
+
+// One pass over layers for M <= GEMV_MAX_M rows already in c->X with metadata
+// in c->meta (device); attention uses `split` keys per CTA on an nsplit grid.
+int run_layers_decode(vvq2_ctx* c, vvq2_kv* kv, int M, int split, int nsplit, int first, int n_layers,
+                      cudaStream_t st, std::vector<vvq2_ctx::Rec>* recs, double attn_bytes_per_layer) {
+    const vvq2_hparams& hp = c->hp;
+    const int H = hp.hidden_size, nq = hp.n_heads, nkv = hp.n_kv_heads, hd = hp.head_dim;
+    const int F = hp.intermediate_size;
+    Recorder R{c, st, recs};
+    auto gemv = [&](const GemvArgs& g, double out_bytes) -> int {
+        CU(R.begin());
+        CU(gemv_launch(g, st));
+        const double b = (double)weight_bytes(g.w0) + (g.epi == EPI_SWIGLU ? (double)weight_bytes(g.w1) : 0.0) +
+                         4.0 * M * g.K + out_bytes;
+        CU(R.end(0, b));
+        return 0;
+    };
+    for (int li = first; li < first + n_layers; ++li) {
+        const vvq2_ctx::Layer& L = c->layers[li];
+        const KvLayer kvl = kv->layer(li);
+        GemvArgs g;
+        g.M = M;
+        g.meta = c->meta;
+        g.kv = kvl;
+        g.n_q_heads = nq;
+        g.n_kv_heads = nkv;
+        g.hd = hd;
+        g.rope_ts = c->rope_ts;
+        g.eps = hp.rms_norm_eps;
+        // 1. RMSNorm + QKV + bias + RoPE + KV append
+        g.w0 = L.qkv;
+        g.K = H;
+        g.x = c->X;
+        g.x_stride = H;
+        g.norm_w = L.attn_norm;
+        g.bias = L.qkv_bias;
+        g.y = c->Q;
+        g.y_stride = nq * hd;
+        g.epi = EPI_QKV;
+        if (int rc = gemv(g, 4.0 * M * nq * hd + 2.0 * M * 2 * nkv * hd)) return rc;
+        // 2. attention
+        AttnDecodeArgs ad;
+        ad.q = c->Q;
+        ad.out = c->ATT;
+        ad.meta = c->meta;
+        ad.kv = kvl;
+        ad.M = M;
+        ad.nq = nq;
+        ad.nkv = nkv;
+        ad.hd = hd;
+        ad.split = split;
+        ad.max_splits = nsplit;
+        ad.scale = 1.0f / sqrtf((float)hd);
+        ad.part = c->part;
+        ad.part_ml = c->part_ml;
+        ad.counters = c->counters;
+        CU(R.begin());
+        CU(attn_decode_launch(ad, st));
+        CU(R.end(1, attn_bytes_per_layer));
+        // 3. O-proj + residual
+        GemvArgs o = g;
+        o.w0 = L.o;
+        o.K = nq * hd;
+        o.x = c->ATT;
+        o.x_stride = nq * hd;
+        o.norm_w = nullptr;
+        o.bias = nullptr;
+        o.y = c->X;
+        o.y_stride = H;
+        o.epi = EPI_RESID;
+        if (int rc = gemv(o, 8.0 * M * H)) return rc;
+        // 4. RMSNorm + gate/up + SwiGLU
+        GemvArgs f = g;
+        f.w0 = L.gate;
+        f.w1 = L.up;
+        f.K = H;
+        f.x = c->X;
+        f.x_stride = H;
+        f.norm_w = L.ffn_norm;
+        f.bias = nullptr;
+        f.y = c->FA;
+        f.y_stride = F;
+        f.epi = EPI_SWIGLU;
+        if (int rc = gemv(f, 4.0 * M * F)) return rc;
+        // 5. down + residual
+        GemvArgs d = g;
+        d.w0 = L.down;
+        d.K = F;
+        d.x = c->FA;
+        d.x_stride = F;
+        d.norm_w = nullptr;
+        d.bias = nullptr;
+        d.y = c->X;
+        d.y_stride = H;
+        d.epi = EPI_RESID;
+        if (int rc = gemv(d, 8.0 * M * H)) return rc;
+    }
+    return 0;
+}
+
+// Whole decode step on the stream: embed(c->tok) -> layers -> output_norm ->
+// lm_head -> argmax -> c->tok, then every row's metadata moves one position on.
+int enqueue_decode(vvq2_ctx* c, vvq2_kv* kv, int M, int split, int nsplit, cudaStream_t st,
+                   std::vector<vvq2_ctx::Rec>* recs, double attn_bytes) {
+    const int H = c->hp.hidden_size;
+    CU(embed_launch(c->tok_embd, c->tok, M, c->X, st));
+    if (int rc = run_layers_decode(c, kv, M, split, nsplit, 0, c->hp.n_layers, st, recs, attn_bytes)) return rc;
+    GemvArgs g;
+    g.w0 = c->lm_head;
+    g.M = M;
+    g.K = H;
+    g.x = c->X;
+    g.x_stride = H;
+    g.norm_w = c->out_norm;
+    g.eps = c->hp.rms_norm_eps;
+    g.y = nullptr;
+    g.argmax = c->amax;
+    g.epi = EPI_ARGMAX;
+    CU(argmax_init_launch(c->amax, M, st));
+    Recorder R{c, st, recs};
+    CU(R.begin());
+    CU(gemv_launch(g, st));
+    CU(R.end(0, (double)weight_bytes(c->lm_head) + 4.0 * M * H));
+    CU(argmax_final_launch(c->amax, M, c->tok, st));
+    CU(advance_meta_launch(c->meta, M, st));
+    return 0;
+}
+
+}  // namespace
+
+// ======================================================================= C ABI
+
+extern "C" {
+
+int vvq2_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    int ok = 0;
+    for (int i = 0; i < n; ++i) {
+        cudaDeviceProp p{};
+        if (cudaGetDeviceProperties(&p, i) == cudaSuccess && p.major == 10) ++ok;
+    }
+    return ok;
+}
+
+int vvq2_backend_selected(void) {
+    const char* env = std::getenv("VIBEVOICE_BACKEND");
+    if (!env) return 0;
+    std::string s(env);
+    for (auto& ch : s) ch = (char)std::tolower((unsigned char)ch);
+    if (s != "b200" && s != "vvq2") return 0;
+    return vvq2_device_count() > 0 ? 1 : 0;
+}
+
+const char* vvq2_version(void) { return "vvq2 0.1 (sm_100a)"; }
+const char* vvq2_last_error(void) { return g_err.c_str(); }
+int64_t vvq2_kernel_launches(void) { return (int64_t)launch_count(); }
+
+int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
+    if (!hp || !out) return fail(VVQ2_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    if (hp->hidden_size <= 0 || hp->n_heads <= 0 || hp->n_kv_heads <= 0 || hp->head_dim <= 0 ||
+        hp->n_layers <= 0 || hp->n_heads % hp->n_kv_heads)
+        return fail(VVQ2_ERR_INVALID_ARG, "bad hparams");
+    if (hp->head_dim != 64 && hp->head_dim != 128)
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "head_dim %d (64 and 128 supported)", hp->head_dim);
+    if (hp->n_heads / hp->n_kv_heads > 8)
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "GQA group %d > 8", hp->n_heads / hp->n_kv_heads);
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+        cudaGetLastError();
+        return fail(VVQ2_ERR_NO_DEVICE, "no CUDA device %d", device);
+    }
+    cudaDeviceProp p{};
+    CU(cudaGetDeviceProperties(&p, device));
+    if (p.major != 10) return fail(VVQ2_ERR_NO_DEVICE, "device %d is sm_%d%d, need sm_100", device, p.major, p.minor);
+    CU(cudaSetDevice(device));
+    CU(gemv_prepare());
+    vvq2_ctx* c = new vvq2_ctx();
+    c->hp = *hp;
+    c->device = device;
+    c->layers.resize(hp->n_layers);
+    c->rope_ts = powf(hp->rope_theta, -2.0f / (float)hp->head_dim);
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete c;
+        return fail(VVQ2_ERR_CUDA, "stream create failed");
+    }
+    const int M = GEMV_MAX_M;
+    const int qw = hp->n_heads * hp->head_dim;
+    const int F = std::max(hp->intermediate_size, 1);
+    int rc = 0;
+    rc = rc ? rc : c->alloc(&c->X, (size_t)M * hp->hidden_size);
+    rc = rc ? rc : c->alloc(&c->Q, (size_t)M * qw);
+    rc = rc ? rc : c->alloc(&c->ATT, (size_t)M * qw);
+    rc = rc ? rc : c->alloc(&c->FA, (size_t)M * F);
+    rc = rc ? rc : c->alloc(&c->part, (size_t)M * c->max_splits_cap * qw);
+    rc = rc ? rc : c->alloc(&c->part_ml, (size_t)M * c->max_splits_cap * hp->n_heads * 2);
+    rc = rc ? rc : c->alloc(&c->counters, (size_t)M * hp->n_kv_heads);
+    rc = rc ? rc : c->alloc(&c->meta, (size_t)M);
+    rc = rc ? rc : c->alloc(&c->amax, (size_t)M);
+    rc = rc ? rc : c->alloc(&c->tok, (size_t)M);
+    if (!rc && hp->vocab_size > 0) rc = c->alloc(&c->LOGITS, (size_t)M * hp->vocab_size);
+    if (!rc && cudaMallocHost(&c->meta_host, sizeof(RowMeta) * M) != cudaSuccess)
+        rc = fail(VVQ2_ERR_OUT_OF_MEMORY, "pinned alloc failed");
+    if (!rc && cudaMemset(c->counters, 0, sizeof(int) * M * hp->n_kv_heads) != cudaSuccess)
+        rc = fail(VVQ2_ERR_CUDA, "memset failed");
+    if (rc) {
+        vvq2_free(c);
+        return rc;
+    }
+    *out = c;
+    return 0;
+}
+
+void vvq2_free(vvq2_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (auto& g : c->graphs) cudaGraphExecDestroy(g.exec);
+    for (cudaEvent_t e : c->events) cudaEventDestroy(e);
+    for (void* p : c->allocs) cudaFree(p);
+    if (c->meta_host) cudaFreeHost(c->meta_host);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+int vvq2_set_layer(vvq2_ctx* c, int li, const vvq2_layer_weights* w) {
+    if (int rc = check_ctx(c)) return rc;
+    if (!w || li < 0 || li >= c->hp.n_layers) return fail(VVQ2_ERR_INVALID_ARG, "bad layer %d", li);
+    const vvq2_hparams& hp = c->hp;
+    const int H = hp.hidden_size, qw = hp.n_heads * hp.head_dim, kvw = hp.n_kv_heads * hp.head_dim;
+    const int F = hp.intermediate_size;
+    vvq2_ctx::Layer L;
+    if (w->attn_q.type != w->attn_k.type || w->attn_q.type != w->attn_v.type)
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "attn_q/k/v types differ");
+    // concatenated QKV rows [q; k; v] so one GEMV streams them
+    {
+        const int t = w->attn_q.type;
+        if (!type_ok(t)) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "attn_q type %d", t);
+        const size_t rb = (size_t)(H / block_elems(t)) * block_bytes(t);
+        if (H % block_elems(t)) return fail(VVQ2_ERR_INVALID_ARG, "hidden %d vs block %d", H, block_elems(t));
+        for (const vvq2_tensor* tt : {&w->attn_q, &w->attn_k, &w->attn_v})
+            if (!tt->data || tt->ne0 != H) return fail(VVQ2_ERR_INVALID_ARG, "attn q/k/v shape");
+        if (w->attn_q.ne1 != qw || w->attn_k.ne1 != kvw || w->attn_v.ne1 != kvw)
+            return fail(VVQ2_ERR_INVALID_ARG, "attn q/k/v rows");
+        std::vector<uint8_t> cat(rb * (qw + 2 * kvw));
+        memcpy(cat.data(), w->attn_q.data, rb * qw);
+        memcpy(cat.data() + rb * qw, w->attn_k.data, rb * kvw);
+        memcpy(cat.data() + rb * (qw + kvw), w->attn_v.data, rb * kvw);
+        vvq2_tensor tc{cat.data(), t, H, qw + 2 * kvw};
+        if (int rc = upload_tensor(c, tc, &L.qkv, H, qw + 2 * kvw, "attn_qkv")) return rc;
+        std::vector<float> bias(qw + 2 * kvw, 0.0f);
+        bool any = false;
+        const vvq2_tensor* bs[3] = {&w->attn_q_bias, &w->attn_k_bias, &w->attn_v_bias};
+        const int off[3] = {0, qw, qw + kvw}, n[3] = {qw, kvw, kvw};
+        for (int i = 0; i < 3; ++i) {
+            if (!bs[i]->data) continue;
+            any = true;
+            if (bs[i]->ne0 * std::max<int64_t>(bs[i]->ne1, 1) != n[i]) return fail(VVQ2_ERR_INVALID_ARG, "bias size");
+            if (bs[i]->type == W_F32) memcpy(&bias[off[i]], bs[i]->data, (size_t)n[i] * 4);
+            else if (bs[i]->type == W_F16)
+                for (int j = 0; j < n[i]; ++j) bias[off[i] + j] = __half2float(static_cast<const __half*>(bs[i]->data)[j]);
+            else return fail(VVQ2_ERR_NOT_IMPLEMENTED, "bias type");
+        }
+        if (any) {
+            if (int rc = c->alloc(&L.qkv_bias, bias.size())) return rc;
+            CU(cudaMemcpy(L.qkv_bias, bias.data(), bias.size() * 4, cudaMemcpyHostToDevice));
+        }
+    }
+    if (int rc = upload_tensor(c, w->attn_o, &L.o, qw, H, "attn_o")) return rc;
+    if (int rc = upload_tensor(c, w->ffn_gate, &L.gate, H, F, "ffn_gate")) return rc;
+    if (int rc = upload_tensor(c, w->ffn_up, &L.up, H, F, "ffn_up")) return rc;
+    if (L.gate.type != L.up.type) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "ffn_gate/up types differ");
+    if (int rc = upload_tensor(c, w->ffn_down, &L.down, F, H, "ffn_down")) return rc;
+    if (int rc = upload_vec(c, w->attn_norm, H, &L.attn_norm, "attn_norm")) return rc;
+    if (int rc = upload_vec(c, w->ffn_norm, H, &L.ffn_norm, "ffn_norm")) return rc;
+    L.set = true;
+    c->layers[li] = L;
+    return 0;
+}
+
+int vvq2_set_output(vvq2_ctx* c, const vvq2_tensor* on, const vvq2_tensor* lm, const vvq2_tensor* te) {
+    if (int rc = check_ctx(c)) return rc;
+    const int H = c->hp.hidden_size;
+    if (on && on->data)
+        if (int rc = upload_vec(c, *on, H, &c->out_norm, "output_norm")) return rc;
+    if (lm && lm->data) {
+        if (c->hp.vocab_size <= 0 || lm->ne1 != c->hp.vocab_size)
+            return fail(VVQ2_ERR_INVALID_ARG, "lm_head rows %lld vs vocab %d", (long long)lm->ne1, c->hp.vocab_size);
+        if (int rc = upload_tensor(c, *lm, &c->lm_head, H, (int)lm->ne1, "lm_head")) return rc;
+    }
+    if (te && te->data) {
+        if (lm && te->data == lm->data && te->type == lm->type) c->tok_embd = c->lm_head;   // tied
+        else if (int rc = upload_tensor(c, *te, &c->tok_embd, H, (int)te->ne1, "tok_embd")) return rc;
+    }
+    return 0;
+}
+
+int vvq2_kv_init(vvq2_ctx* c, int n_seqs, int max_seq, vvq2_kv** out) {
+    if (int rc = check_ctx(c)) return rc;
+    if (!out || n_seqs <= 0 || max_seq <= 0) return fail(VVQ2_ERR_INVALID_ARG, "bad kv size");
+    *out = nullptr;
+    vvq2_kv* kv = new vvq2_kv();
+    kv->ctx = c;
+    kv->n_seqs = n_seqs;
+    kv->max_seq = max_seq;
+    kv->max_pages = (max_seq + KV_PAGE - 1) / KV_PAGE;
+    const size_t pages = (size_t)n_seqs * kv->max_pages;
+    kv->layer_elems = pages * c->hp.n_kv_heads * KV_PAGE * c->hp.head_dim;
+    const size_t bytes = kv->layer_elems * c->hp.n_layers * sizeof(__half);
+    if (cudaMalloc(&kv->k, bytes) != cudaSuccess || cudaMalloc(&kv->v, bytes) != cudaSuccess ||
+        cudaMalloc(&kv->block_table, pages * sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        vvq2_kv_free(kv);
+        return fail(VVQ2_ERR_OUT_OF_MEMORY, "kv cache of %zu bytes", 2 * bytes);
+    }
+    // pages of sequence s are [s*max_pages, (s+1)*max_pages): the block table keeps
+    // the indirection so pages can later be shared or reassigned
+    std::vector<int> bt(pages);
+    for (size_t i = 0; i < pages; ++i) bt[i] = (int)i;
+    cudaMemcpy(kv->block_table, bt.data(), pages * sizeof(int), cudaMemcpyHostToDevice);
+    cudaMemset(kv->k, 0, bytes);
+    cudaMemset(kv->v, 0, bytes);
+    if (cudaGetLastError() != cudaSuccess) {
+        vvq2_kv_free(kv);
+        return fail(VVQ2_ERR_CUDA, "kv init copy failed");
+    }
+    kv->past.assign(n_seqs, 0);
+    *out = kv;
+    return 0;
+}
+
+void vvq2_kv_free(vvq2_kv* kv) {
+    if (!kv) return;
+    if (kv->ctx) {
+        vvq2_ctx* c = kv->ctx;
+        cudaSetDevice(c->device);
+        cudaStreamSynchronize(c->stream);
+        for (auto& g : c->graphs)
+            if (g.kv == kv) cudaGraphExecDestroy(g.exec);
+        c->graphs.erase(std::remove_if(c->graphs.begin(), c->graphs.end(),
+                                       [kv](const vvq2_ctx::Graph& g) { return g.kv == kv; }),
+                        c->graphs.end());
+        if (c->meta_kv == kv) c->meta_kv = nullptr;
+    }
+    if (kv->k) cudaFree(kv->k);
+    if (kv->v) cudaFree(kv->v);
+    if (kv->block_table) cudaFree(kv->block_table);
+    delete kv;
+}
+
+int vvq2_kv_set_past_len(vvq2_kv* kv, int seq, int past) {
+    if (!kv || seq < 0 || seq >= kv->n_seqs || past < 0 || past > kv->max_seq)
+        return fail(VVQ2_ERR_INVALID_ARG, "bad seq/past_len");
+    kv->past[seq] = past;
+    if (kv->ctx && kv->ctx->meta_kv == kv) kv->ctx->meta_kv = nullptr;
+    return 0;
+}
+
+int vvq2_kv_past_len(const vvq2_kv* kv, int seq) {
+    if (!kv || seq < 0 || seq >= kv->n_seqs) return fail(VVQ2_ERR_INVALID_ARG, "bad seq");
+    return kv->past[seq];
+}
+
+static int kv_xfer(vvq2_kv* kv, int seq, int layer, float* k, float* v, const float* kc, const float* vc,
+                   int n_pos, bool upload) {
+    if (!kv) return fail(VVQ2_ERR_INVALID_ARG, "null kv");
+    vvq2_ctx* c = kv->ctx;
+    if (int rc = check_ctx(c)) return rc;
+    if (seq < 0 || seq >= kv->n_seqs || layer < 0 || layer >= c->hp.n_layers || n_pos < 0 || n_pos > kv->max_seq)
+        return fail(VVQ2_ERR_INVALID_ARG, "bad kv transfer");
+    if (n_pos == 0) return 0;
+    const size_t n = (size_t)n_pos * c->hp.n_kv_heads * c->hp.head_dim;
+    float *dk = nullptr, *dv = nullptr;
+    CU(cudaMalloc(&dk, n * 4));
+    if (cudaMalloc(&dv, n * 4) != cudaSuccess) {
+        cudaFree(dk);
+        return fail(VVQ2_ERR_OUT_OF_MEMORY, "kv staging");
+    }
+    cudaError_t e = cudaSuccess;
+    if (upload) {
+        e = cudaMemcpy(dk, kc, n * 4, cudaMemcpyDefault);
+        if (e == cudaSuccess) e = cudaMemcpy(dv, vc, n * 4, cudaMemcpyDefault);
+        if (e == cudaSuccess) e = kv_upload_launch(kv->layer(layer), seq, dk, dv, n_pos, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    } else {
+        e = kv_download_launch(kv->layer(layer), seq, dk, dv, n_pos, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        if (e == cudaSuccess) e = cudaMemcpy(k, dk, n * 4, cudaMemcpyDefault);
+        if (e == cudaSuccess) e = cudaMemcpy(v, dv, n * 4, cudaMemcpyDefault);
+    }
+    cudaFree(dk);
+    cudaFree(dv);
+    if (e != cudaSuccess) return fail(VVQ2_ERR_CUDA, "kv transfer: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+int vvq2_kv_load_prefix(vvq2_kv* kv, int seq, int layer, const float* k, const float* v, int n_pos) {
+    if (!k || !v) return fail(VVQ2_ERR_INVALID_ARG, "null k/v");
+    return kv_xfer(kv, seq, layer, nullptr, nullptr, k, v, n_pos, true);
+}
+
+int vvq2_kv_read(vvq2_kv* kv, int seq, int layer, float* k, float* v, int n_pos) {
+    if (!k || !v) return fail(VVQ2_ERR_INVALID_ARG, "null k/v");
+    return kv_xfer(kv, seq, layer, k, v, nullptr, nullptr, n_pos, false);
+}
+
+int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_tok, const float* x,
+                 const int* pos_start, int first_layer, int n_layers, int flags, float* y, void* stream) {
+    if (int rc = check_ctx(c)) return rc;
+    if (!kv || kv->ctx != c || !seqs || !x || !pos_start || !y || n_seqs <= 0 || n_tok <= 0)
+        return fail(VVQ2_ERR_INVALID_ARG, "bad forward arguments");
+    if (first_layer < 0 || n_layers < 0 || first_layer + n_layers > c->hp.n_layers)
+        return fail(VVQ2_ERR_INVALID_ARG, "layer range [%d, %d)", first_layer, first_layer + n_layers);
+    for (int li = first_layer; li < first_layer + n_layers; ++li)
+        if (!c->layers[li].set) return fail(VVQ2_ERR_INVALID_ARG, "layer %d has no weights", li);
+    if ((flags & VVQ2_OUTPUT_NORM) && !c->out_norm) return fail(VVQ2_ERR_INVALID_ARG, "no output_norm set");
+    std::vector<char> seen(kv->n_seqs, 0);
+    for (int s = 0; s < n_seqs; ++s) {
+        if (seqs[s] < 0 || seqs[s] >= kv->n_seqs || seen[seqs[s]])
+            return fail(VVQ2_ERR_INVALID_ARG, "bad or repeated sequence id %d", seqs[s]);
+        seen[seqs[s]] = 1;
+        if (kv->past[seqs[s]] + n_tok > kv->max_seq)
+            return fail(VVQ2_ERR_INVALID_ARG, "KV overflow: seq %d past %d + %d > max_seq %d", seqs[s],
+                        kv->past[seqs[s]], n_tok, kv->max_seq);
+        if (pos_start[s] < 0) return fail(VVQ2_ERR_INVALID_ARG, "negative position");
+    }
+    cudaStream_t st = pick_stream(c, stream);
+    const int H = c->hp.hidden_size;
+    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
+    const bool last_only = (flags & VVQ2_LAST_ONLY) != 0;
+    // Token chunks of at most GEMV_MAX_M rows over all sequences; each chunk
+    // runs through every layer before the next (resident chunked prefill,
+    // the ordering tests/test_qwen2_resident.cpp checks).
+    const int tok_per_chunk = std::max(1, GEMV_MAX_M / n_seqs);
+    if (n_seqs > GEMV_MAX_M) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "more than %d sequences per call", GEMV_MAX_M);
+    for (int t0 = 0; t0 < n_tok; t0 += tok_per_chunk) {
+        const int nt = std::min(tok_per_chunk, n_tok - t0);
+        const int M = n_seqs * nt;
+        int max_lim = 1;
+        for (int s = 0; s < n_seqs; ++s)
+            for (int t = 0; t < nt; ++t) {
+                RowMeta& r = c->meta_host[s * nt + t];
+                r.seq = seqs[s];
+                r.pos = pos_start[s] + t0 + t;
+                r.cidx = kv->past[seqs[s]] + t0 + t;
+                r.kvlen = kv->past[seqs[s]] + t0 + nt;
+                max_lim = std::max(max_lim, std::min(r.pos + 1, r.kvlen));
+            }
+        CU(cudaMemcpyAsync(c->meta, c->meta_host, sizeof(RowMeta) * M, cudaMemcpyHostToDevice, st));
+        for (int s = 0; s < n_seqs; ++s)
+            CU(cudaMemcpyAsync(c->X + (size_t)s * nt * H, x + ((size_t)s * n_tok + t0) * H,
+                               sizeof(float) * nt * H, x_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+        c->meta_kv = nullptr;   // c->meta no longer describes a decode step
+        int split = 0, nsplit = 0;
+        choose_split(c, M, max_lim, &split, &nsplit);
+        if (int rc = run_layers_decode(c, kv, M, split, nsplit, first_layer, n_layers, st, nullptr, 0.0)) return rc;
+        if (flags & VVQ2_OUTPUT_NORM) CU(rmsnorm_launch(c->X, c->out_norm, M, H, c->hp.rms_norm_eps, c->X, st));
+        const cudaMemcpyKind k = y_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+        for (int s = 0; s < n_seqs; ++s) {
+            if (last_only) {
+                if (t0 + nt == n_tok)
+                    CU(cudaMemcpyAsync(y + (size_t)s * H, c->X + ((size_t)s * nt + nt - 1) * H, sizeof(float) * H, k, st));
+            } else {
+                CU(cudaMemcpyAsync(y + ((size_t)s * n_tok + t0) * H, c->X + (size_t)s * nt * H,
+                                   sizeof(float) * nt * H, k, st));
+            }
+        }
+        // the meta staging buffer is reused by the next chunk
+        CU(cudaStreamSynchronize(st));
+    }
+    if (flags & VVQ2_ADVANCE)
+        for (int s = 0; s < n_seqs; ++s) kv->past[seqs[s]] += n_tok;
+    return 0;
+}
+
+int vvq2_lm_head(vvq2_ctx* c, int n, const float* h, float* logits, int32_t* argmax, void* stream) {
+    if (int rc = check_ctx(c)) return rc;
+    if (c->lm_head.type < 0) return fail(VVQ2_ERR_INVALID_ARG, "no lm_head set");
+    if (n <= 0 || !h) return fail(VVQ2_ERR_INVALID_ARG, "bad lm_head arguments");
+    cudaStream_t st = pick_stream(c, stream);
+    const int H = c->hp.hidden_size, V = c->lm_head.rows;
+    const bool h_dev = is_device_ptr(h);
+    for (int i0 = 0; i0 < n; i0 += GEMV_MAX_M) {
+        const int M = std::min(GEMV_MAX_M, n - i0);
+        CU(cudaMemcpyAsync(c->X, h + (size_t)i0 * H, sizeof(float) * M * H,
+                           h_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+        CU(argmax_init_launch(c->amax, M, st));
+        GemvArgs g;
+        g.w0 = c->lm_head;
+        g.M = M;
+        g.K = H;
+        g.x = c->X;
+        g.x_stride = H;
+        g.y = logits ? c->LOGITS : nullptr;
+        g.y_stride = V;
+        g.argmax = c->amax;
+        g.epi = EPI_ARGMAX;
+        CU(gemv_launch(g, st));
+        CU(argmax_final_launch(c->amax, M, c->tok, st));
+        if (argmax)
+            CU(cudaMemcpyAsync(argmax + i0, c->tok, sizeof(int32_t) * M,
+                               is_device_ptr(argmax) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+        if (logits)
+            CU(cudaMemcpyAsync(logits + (size_t)i0 * V, c->LOGITS, sizeof(float) * M * V,
+                               is_device_ptr(logits) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+        CU(cudaStreamSynchronize(st));
+    }
+    return 0;
+}
+
+int vvq2_embed(vvq2_ctx* c, int n, const int32_t* tokens, float* out, void* stream) {
+    if (int rc = check_ctx(c)) return rc;
+    if (c->tok_embd.type < 0) return fail(VVQ2_ERR_INVALID_ARG, "no tok_embd set");
+    if (n <= 0 || !tokens || !out) return fail(VVQ2_ERR_INVALID_ARG, "bad embed arguments");
+    for (int i = 0; i < n && !is_device_ptr(tokens); ++i)
+        if (tokens[i] < 0 || tokens[i] >= c->tok_embd.rows) return fail(VVQ2_ERR_INVALID_ARG, "token id %d", tokens[i]);
+    cudaStream_t st = pick_stream(c, stream);
+    const int H = c->hp.hidden_size;
+    int32_t* dt = nullptr;
+    float* dout = nullptr;
+    CU(cudaMalloc(&dt, sizeof(int32_t) * n));
+    CU(cudaMalloc(&dout, sizeof(float) * n * H));
+    cudaError_t e = cudaMemcpyAsync(dt, tokens, sizeof(int32_t) * n, cudaMemcpyDefault, st);
+    if (e == cudaSuccess) e = embed_launch(c->tok_embd, dt, n, dout, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, dout, sizeof(float) * n * H, cudaMemcpyDefault, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFree(dt);
+    cudaFree(dout);
+    if (e != cudaSuccess) return fail(VVQ2_ERR_CUDA, "embed: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, const int32_t* tokens_in,
+                     int32_t* tokens_out, void* stream) {
+    if (int rc = check_ctx(c)) return rc;
+    if (!kv || kv->ctx != c || !seqs || !tokens_in || !tokens_out || n_seqs <= 0 || n_seqs > GEMV_MAX_M)
+        return fail(VVQ2_ERR_INVALID_ARG, "bad decode_step arguments");
+    if (c->tok_embd.type < 0 || c->lm_head.type < 0 || !c->out_norm)
+        return fail(VVQ2_ERR_INVALID_ARG, "decode_step needs output_norm, lm_head and tok_embd");
+    for (int li = 0; li < c->hp.n_layers; ++li)
+        if (!c->layers[li].set) return fail(VVQ2_ERR_INVALID_ARG, "layer %d has no weights", li);
+    std::vector<char> seen(kv->n_seqs, 0);
+    for (int s = 0; s < n_seqs; ++s) {
+        if (seqs[s] < 0 || seqs[s] >= kv->n_seqs || seen[seqs[s]])
+            return fail(VVQ2_ERR_INVALID_ARG, "bad or repeated sequence id");
+        seen[seqs[s]] = 1;
+        if (kv->past[seqs[s]] + 1 > kv->max_seq) return fail(VVQ2_ERR_INVALID_ARG, "KV overflow");
+    }
+    cudaStream_t st = pick_stream(c, stream);
+    const int M = n_seqs;
+    std::vector<int> sv(seqs, seqs + n_seqs);
+    int max_lim = 1;
+    double attn_bytes = 0.0;
+    for (int s = 0; s < n_seqs; ++s) {
+        max_lim = std::max(max_lim, kv->past[seqs[s]] + 1);
+        attn_bytes += 4.0 * (kv->past[seqs[s]] + 1) * c->hp.n_kv_heads * c->hp.head_dim;   // f16 K and V
+    }
+    attn_bytes += 8.0 * M * c->hp.n_heads * c->hp.head_dim;
+    // graphs are specialised per 512-position bucket of the longest row: the
+    // attention grid covers the bucket and CTAs past a row's length exit
+    const int bucket = (max_lim + 511) / 512 * 512;
+    if (c->meta_kv != kv || c->meta_seqs != sv) {
+        for (int s = 0; s < n_seqs; ++s) {
+            RowMeta& r = c->meta_host[s];
+            r.seq = seqs[s];
+            r.pos = kv->past[seqs[s]];
+            r.cidx = kv->past[seqs[s]];
+            r.kvlen = kv->past[seqs[s]] + 1;
+        }
+        CU(cudaMemcpyAsync(c->meta, c->meta_host, sizeof(RowMeta) * M, cudaMemcpyHostToDevice, st));
+        c->meta_kv = kv;
+        c->meta_seqs = sv;
+    }
+    vvq2_ctx::Graph* gr = nullptr;
+    for (auto& g : c->graphs)
+        if (g.kv == kv && g.seqs == sv && g.bucket == bucket && g.prof == c->prof_on) gr = &g;
+    if (!gr) {
+        int split = 0, nsplit = 0;
+        choose_split(c, M, bucket, &split, &nsplit);
+        vvq2_ctx::Graph g{kv, sv, bucket, c->prof_on, nullptr, 0, {}};
+        const long long k0 = launch_count();
+        cudaGraph_t graph = nullptr;
+        CU(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        int rc = enqueue_decode(c, kv, M, split, nsplit, st, c->prof_on ? &g.recs : nullptr, attn_bytes);
+        cudaError_t e = cudaStreamEndCapture(st, &graph);
+        if (rc) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        CU(e);
+        e = cudaGraphInstantiate(&g.exec, graph, 0);
+        cudaGraphDestroy(graph);
+        CU(e);
+        g.kernels = (int)(launch_count() - k0);
+        c->graphs.push_back(std::move(g));
+        gr = &c->graphs.back();
+    }
+    CU(cudaMemcpyAsync(c->tok, tokens_in, sizeof(int32_t) * M, cudaMemcpyDefault, st));
+    CU(cudaGraphLaunch(gr->exec, st));
+    note_launch(gr->kernels);
+    CU(cudaMemcpyAsync(tokens_out, c->tok, sizeof(int32_t) * M, cudaMemcpyDefault, st));
+    if (c->prof_on) {
+        CU(cudaStreamSynchronize(st));
+        for (const auto& r : gr->recs) {
+            float ms = 0.f;
+            CU(cudaEventElapsedTime(&ms, c->events[r.e0], c->events[r.e1]));
+            c->prof_ms[r.kind] += ms;
+            c->prof_bytes[r.kind] += r.bytes;
+            c->prof_n[r.kind] += 1;
+        }
+    } else if (!is_device_ptr(tokens_out)) {
+        CU(cudaStreamSynchronize(st));
+    }
+    for (int s = 0; s < n_seqs; ++s) kv->past[seqs[s]] += 1;
+    return 0;
+}
+
+int vvq2_profile(vvq2_ctx* c, int enable) {
+    if (int rc = check_ctx(c)) return rc;
+    c->prof_on = enable != 0;
+    for (int k = 0; k < 3; ++k) c->prof_ms[k] = c->prof_bytes[k] = 0.0, c->prof_n[k] = 0;
+    return 0;
+}
+
+int vvq2_profile_read(vvq2_ctx* c, int kind, double* ms, double* bytes, int64_t* launches) {
+    if (int rc = check_ctx(c)) return rc;
+    if (kind < 0 || kind > 2) return fail(VVQ2_ERR_INVALID_ARG, "bad profile kind");
+    if (ms) *ms = c->prof_ms[kind];
+    if (bytes) *bytes = c->prof_bytes[kind];
+    if (launches) *launches = c->prof_n[kind];
+    return 0;
+}
+
+int vvq2_dequantize(int type, const void* src, int64_t n, float* dst) {
+    if (!src || !dst || n <= 0 || !type_ok(type) || n % block_elems(type))
+        return fail(VVQ2_ERR_INVALID_ARG, "bad dequantize arguments");
+    if (vvq2_device_count() == 0) return fail(VVQ2_ERR_NO_DEVICE, "no sm_100 device");
+    // treat as one row of n elements; reuse the weight upload (repack) path
+    vvq2_ctx tmp;
+    vvq2_tensor t{src, type, n, 1};
+    DevW w;
+    int rc = upload_tensor(&tmp, t, &w, 0, 0, "dequantize");
+    float* d = nullptr;
+    if (!rc) rc = tmp.alloc(&d, (size_t)n);
+    cudaError_t e = cudaSuccess;
+    if (!rc) e = dequant_rows_launch(w, d, 0);
+    if (!rc && e == cudaSuccess) e = cudaMemcpy(dst, d, sizeof(float) * n, cudaMemcpyDefault);
+    for (void* p : tmp.allocs) cudaFree(p);
+    if (rc) return rc;
+    if (e != cudaSuccess) return fail(VVQ2_ERR_CUDA, "dequantize: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+int vvq2_rope_neox(const float* x, int n_tok, int n_heads, int hd, const int32_t* pos, float theta, float* y) {
+    if (!x || !pos || !y || n_tok <= 0 || n_heads <= 0 || hd <= 0 || hd % 2)
+        return fail(VVQ2_ERR_INVALID_ARG, "bad rope arguments");
+    if (vvq2_device_count() == 0) return fail(VVQ2_ERR_NO_DEVICE, "no sm_100 device");
+    const size_t n = (size_t)n_tok * n_heads * hd;
+    float *dx = nullptr, *dy = nullptr;
+    int32_t* dp = nullptr;
+    CU(cudaMalloc(&dx, n * 4));
+    CU(cudaMalloc(&dy, n * 4));
+    CU(cudaMalloc(&dp, (size_t)n_tok * 4));
+    cudaError_t e = cudaMemcpy(dx, x, n * 4, cudaMemcpyDefault);
+    if (e == cudaSuccess) e = cudaMemcpy(dp, pos, (size_t)n_tok * 4, cudaMemcpyDefault);
+    if (e == cudaSuccess) e = rope_launch(dx, n_tok, n_heads, hd, dp, powf(theta, -2.0f / (float)hd), dy, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(y, dy, n * 4, cudaMemcpyDefault);
+    cudaFree(dx);
+    cudaFree(dy);
+    cudaFree(dp);
+    if (e != cudaSuccess) return fail(VVQ2_ERR_CUDA, "rope: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+int vvq2_rms_norm(const float* x, const float* w, int rows, int n, float eps, float* y) {
+    if (!x || !w || !y || rows <= 0 || n <= 0) return fail(VVQ2_ERR_INVALID_ARG, "bad rms_norm arguments");
+    if (vvq2_device_count() == 0) return fail(VVQ2_ERR_NO_DEVICE, "no sm_100 device");
+    const size_t nx = (size_t)rows * n;
+    float *dx = nullptr, *dw = nullptr;
+    CU(cudaMalloc(&dx, nx * 4));
+    CU(cudaMalloc(&dw, (size_t)n * 4));
+    cudaError_t e = cudaMemcpy(dx, x, nx * 4, cudaMemcpyDefault);
+    if (e == cudaSuccess) e = cudaMemcpy(dw, w, (size_t)n * 4, cudaMemcpyDefault);
+    if (e == cudaSuccess) e = rmsnorm_launch(dx, dw, rows, n, eps, dx, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(y, dx, nx * 4, cudaMemcpyDefault);
+    cudaFree(dx);
+    cudaFree(dw);
+    if (e != cudaSuccess) return fail(VVQ2_ERR_CUDA, "rms_norm: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,81 @@
+// kernels.h -- launch interfaces of the sm_100a kernels (host side).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace vvq2 {
+
+void note_launch(int n = 1);   // counts this library's kernel launches
+
+// ---------------------------------------------------------------- GEMV
+enum GemvEpi : int {
+    EPI_QKV = 0,     // +bias, RoPE Q/K, Q -> y[m][nq*hd], K/V -> paged cache
+    EPI_RESID = 1,   // y[m][r] += W.x  (residual add, in place)
+    EPI_SWIGLU = 2,  // y[m][i] = silu(W0.x)[i] * (W1.x)[i]
+    EPI_STORE = 3,   // y[m][r] = W.x (+bias)
+    EPI_ARGMAX = 4   // logits to y (optional) + first-max argmax key to argmax[m]
+};
+
+struct GemvArgs {
+    DevW w0, w1;
+    int M = 0, K = 0, n_units = 0;
+    const float* x = nullptr;      // [M][x_stride] f32 activations
+    int x_stride = 0;
+    const float* norm_w = nullptr; // RMSNorm weight (f32 [K]) or null
+    float eps = 0.f;
+    int epi = 0;
+    const float* bias = nullptr;
+    float* y = nullptr;
+    int y_stride = 0;
+    const RowMeta* meta = nullptr;
+    KvLayer kv;
+    int n_q_heads = 0, n_kv_heads = 0, hd = 0;
+    float rope_ts = 0.f;
+    unsigned long long* argmax = nullptr;
+};
+
+cudaError_t gemv_launch(GemvArgs a, cudaStream_t st);
+size_t gemv_smem_bytes(int wt, int M, int K);
+cudaError_t gemv_prepare();
+
+// ------------------------------------------------------ decode attention
+struct AttnDecodeArgs {
+    const float* q = nullptr;      // [M][nq*hd] (roped)
+    float* out = nullptr;          // [M][nq*hd]
+    const RowMeta* meta = nullptr;
+    KvLayer kv;
+    int M = 0, nq = 0, nkv = 0, hd = 0;
+    int split = 0;                 // keys per CTA
+    int max_splits = 0;            // grid.x
+    float scale = 0.f;
+    float* part = nullptr;         // [M][max_splits][nq][hd] unnormalized partial O
+    float* part_ml = nullptr;      // [M][max_splits][nq][2] (running max, sum)
+    int* counters = nullptr;       // [M][nkv], zero between launches
+};
+cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st);
+
+// ------------------------------------------------------------- misc
+long long launch_count();
+// dequantize a repacked device weight matrix to f32 [rows][cols]
+cudaError_t dequant_rows_launch(const DevW& w, float* dst, cudaStream_t st);
+cudaError_t rope_launch(const float* x, int n_tok, int n_heads, int hd, const int32_t* pos,
+                        float ts, float* y, cudaStream_t st);
+cudaError_t rmsnorm_launch(const float* x, const float* w, int rows, int n, float eps, float* y,
+                           cudaStream_t st);
+// rows of a tok_embd table (any weight type) -> f32 [n][cols]
+cudaError_t embed_launch(const DevW& t, const int32_t* tok, int n, float* out, cudaStream_t st);
+// f32 [n_pos][n_kv][hd] -> f16 paged cache of one sequence / layer
+cudaError_t kv_upload_launch(const KvLayer& kv, int seq, const float* k, const float* v,
+                             int n_pos, cudaStream_t st);
+cudaError_t kv_download_launch(const KvLayer& kv, int seq, float* k, float* v, int n_pos,
+                               cudaStream_t st);
+cudaError_t argmax_init_launch(unsigned long long* keys, int n, cudaStream_t st);
+cudaError_t advance_meta_launch(RowMeta* meta, int n, cudaStream_t st);
+cudaError_t argmax_final_launch(const unsigned long long* keys, int n, int32_t* out,
+                                cudaStream_t st);
+
+}  // namespace vvq2

@@ -1,0 +1,186 @@
+// misc.cu -- small kernels around the hot path: dequantization (tests),
+// standalone RoPE / RMSNorm (rope.hpp / rms_norm.hpp equivalents), token
+// embedding rows, KV prefix upload/readback and argmax finalisation.
+#include <atomic>
+
+#include "common.cuh"
+#include "dequant.cuh"
+#include "kernels.h"
+
+namespace vvq2 {
+
+namespace {
+std::atomic<long long> g_launches{0};
+}
+
+void note_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+namespace {
+
+__global__ void k_dequant(DevW w, int64_t n, float* out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = deq_elem(w, (int)(i / w.cols), (int)(i % w.cols));
+}
+
+// ggml_rope_ext NEOX on [n_tok][n_heads][hd]; one thread per rotation pair
+__global__ void k_rope(const float* x, int n_tok, int n_heads, int hd, const int32_t* pos, float ts,
+                       float* y) {
+    const int half = hd / 2;
+    const int64_t n = (int64_t)n_tok * n_heads * half;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        const int i = (int)(t % half);
+        const int64_t th = t / half;          // token * n_heads + head
+        const int tok = (int)(th / n_heads);
+        float x0 = x[th * hd + i], x1 = x[th * hd + i + half];
+        rope_pair(x0, x1, pos[tok], i, ts);
+        y[th * hd + i] = x0;
+        y[th * hd + i + half] = x1;
+    }
+}
+
+// ggml_rms_norm + ggml_mul: one CTA per row
+__global__ void k_rmsnorm(const float* x, const float* w, int n, float eps, float* y) {
+    __shared__ float red[32];
+    __shared__ float scale_s;
+    const float* xr = x + (size_t)blockIdx.x * n;
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(xr[k], xr[k]));
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t = __fadd_rn(t, red[i]);
+        const float mean = __fdiv_rn(t, (float)n);
+        scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    }
+    __syncthreads();
+    const float sc = scale_s;
+    for (int k = threadIdx.x; k < n; k += blockDim.x)
+        y[(size_t)blockIdx.x * n + k] = __fmul_rn(__fmul_rn(xr[k], sc), w[k]);
+}
+
+__global__ void k_embed(DevW t, const int32_t* tok, int n, float* out) {
+    const int i = blockIdx.x;
+    const int r = tok[i];
+    if (r < 0 || r >= t.rows) {
+        for (int k = threadIdx.x; k < t.cols; k += blockDim.x) out[(size_t)i * t.cols + k] = 0.f;
+        return;
+    }
+    for (int k = threadIdx.x; k < t.cols; k += blockDim.x) out[(size_t)i * t.cols + k] = deq_elem(t, r, k);
+}
+
+__global__ void k_kv_upload(KvLayer kv, int seq, const float* k, const float* v, int n_pos) {
+    const int w = kv.n_kv * kv.hd;
+    const int64_t n = (int64_t)n_pos * w;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        const int p = (int)(t / w), r = (int)(t % w), h = r / kv.hd, d = r % kv.hd;
+        const size_t off = kv_offset(kv, seq, p, h) + d;
+        kv.k[off] = __float2half_rn(k[t]);
+        kv.v[off] = __float2half_rn(v[t]);
+    }
+}
+
+__global__ void k_kv_download(KvLayer kv, int seq, float* k, float* v, int n_pos) {
+    const int w = kv.n_kv * kv.hd;
+    const int64_t n = (int64_t)n_pos * w;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        const int p = (int)(t / w), r = (int)(t % w), h = r / kv.hd, d = r % kv.hd;
+        const size_t off = kv_offset(kv, seq, p, h) + d;
+        k[t] = __half2float(kv.k[off]);
+        v[t] = __half2float(kv.v[off]);
+    }
+}
+
+// decode graphs end by moving every row one position forward
+__global__ void k_advance_meta(RowMeta* meta, int n) {
+    if (threadIdx.x < n) {
+        RowMeta r = meta[threadIdx.x];
+        r.pos += 1;
+        r.cidx += 1;
+        r.kvlen += 1;
+        meta[threadIdx.x] = r;
+    }
+}
+
+__global__ void k_argmax_init(unsigned long long* keys, int n) {
+    if (threadIdx.x < n) keys[threadIdx.x] = 0ull;
+}
+
+__global__ void k_argmax_final(const unsigned long long* keys, int n, int32_t* out) {
+    if (threadIdx.x < n) out[threadIdx.x] = argmax_key_index(keys[threadIdx.x]);
+}
+
+int grid_for(int64_t n, int threads) {
+    const int64_t g = (n + threads - 1) / threads;
+    return (int)(g < 148 * 16 ? (g < 1 ? 1 : g) : 148 * 16);
+}
+
+}  // namespace
+
+cudaError_t dequant_rows_launch(const DevW& w, float* dst, cudaStream_t st) {
+    const int64_t n = (int64_t)w.rows * w.cols;
+    k_dequant<<<grid_for(n, 256), 256, 0, st>>>(w, n, dst);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t rope_launch(const float* x, int n_tok, int n_heads, int hd, const int32_t* pos, float ts,
+                        float* y, cudaStream_t st) {
+    const int64_t n = (int64_t)n_tok * n_heads * (hd / 2);
+    k_rope<<<grid_for(n, 256), 256, 0, st>>>(x, n_tok, n_heads, hd, pos, ts, y);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_launch(const float* x, const float* w, int rows, int n, float eps, float* y,
+                           cudaStream_t st) {
+    k_rmsnorm<<<rows, 256, 0, st>>>(x, w, n, eps, y);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t embed_launch(const DevW& t, const int32_t* tok, int n, float* out, cudaStream_t st) {
+    k_embed<<<n, 256, 0, st>>>(t, tok, n, out);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t kv_upload_launch(const KvLayer& kv, int seq, const float* k, const float* v, int n_pos,
+                             cudaStream_t st) {
+    const int64_t n = (int64_t)n_pos * kv.n_kv * kv.hd;
+    if (n == 0) return cudaSuccess;
+    k_kv_upload<<<grid_for(n, 256), 256, 0, st>>>(kv, seq, k, v, n_pos);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t kv_download_launch(const KvLayer& kv, int seq, float* k, float* v, int n_pos,
+                               cudaStream_t st) {
+    const int64_t n = (int64_t)n_pos * kv.n_kv * kv.hd;
+    if (n == 0) return cudaSuccess;
+    k_kv_download<<<grid_for(n, 256), 256, 0, st>>>(kv, seq, k, v, n_pos);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t advance_meta_launch(RowMeta* meta, int n, cudaStream_t st) {
+    k_advance_meta<<<1, 32, 0, st>>>(meta, n);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t argmax_init_launch(unsigned long long* keys, int n, cudaStream_t st) {
+    k_argmax_init<<<1, 32, 0, st>>>(keys, n);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t argmax_final_launch(const unsigned long long* keys, int n, int32_t* out, cudaStream_t st) {
+    k_argmax_final<<<1, 32, 0, st>>>(keys, n, out);
+    note_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace vvq2

@@ -1,0 +1,85 @@
+"""Seeded synthetic Qwen2 weights in GGUF block formats (numpy only).
+
+The benchmark configurations use random-initialised weights of the real
+architecture (there are no checkpoints offline): weights N(0, 0.02) f32,
+q/k/v biases N(0, 0.02), RMSNorm weights 1 + N(0, 0.02), quantized to Q8_0
+with the ggml reference rounding (d = amax/127 stored f16, q = roundf(x/d)),
+which is bit-exact with gguf-py's Q8_0.quantize_blocks."""
+from __future__ import annotations
+
+import numpy as np
+
+F32, F16, Q8_0 = 0, 1, 8
+
+
+def _roundf(v: np.ndarray) -> np.ndarray:
+    """C roundf (half away from zero), exact for |v| < 2^23."""
+    a = np.abs(v)
+    f = np.floor(a)
+    return np.sign(v) * (f + np.floor(2.0 * (a - f)))
+
+
+def q8_0(w: np.ndarray) -> np.ndarray:
+    """f32 [rows, cols] -> raw Q8_0 bytes [rows, cols/32*34] (quantize_row_q8_0_ref)."""
+    w = np.ascontiguousarray(w, np.float32)
+    rows, cols = w.shape
+    b = w.reshape(-1, 32)
+    d = (np.abs(b).max(axis=1, keepdims=True) / np.float32(127)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        idv = np.where(d == 0, np.float32(0), np.float32(1) / d).astype(np.float32)
+    q = _roundf((b * idv).astype(np.float32)).astype(np.int8)
+    out = np.empty((b.shape[0], 34), np.uint8)
+    out[:, :2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = q.view(np.uint8)
+    return out.reshape(rows, -1)
+
+
+def f32_tensor(a: np.ndarray):
+    a = np.ascontiguousarray(a, np.float32)
+    return (a.view(np.uint8).reshape(-1), F32, a.shape[-1], 1 if a.ndim == 1 else a.shape[0])
+
+
+def q8_0_tensor(rng, rows: int, cols: int, std: float = 0.02, chunk: int = 8192):
+    out = np.empty((rows, cols // 32 * 34), np.uint8)
+    for r0 in range(0, rows, chunk):
+        r1 = min(rows, r0 + chunk)
+        out[r0:r1] = q8_0((rng.standard_normal((r1 - r0, cols), dtype=np.float32) * std))
+    return (out.reshape(-1), Q8_0, cols, rows)
+
+
+def layer_q8_0(rng, hp: dict, bias: bool = True) -> dict:
+    H, nq, nkv, hd, F = hp["hidden"], hp["n_heads"], hp["n_kv_heads"], hp["head_dim"], hp["ffn"]
+    g = lambda *s: (rng.standard_normal(s, dtype=np.float32) * 0.02)
+    return {
+        "attn_norm": f32_tensor(1.0 + g(H)),
+        "attn_q": q8_0_tensor(rng, nq * hd, H),
+        "attn_k": q8_0_tensor(rng, nkv * hd, H),
+        "attn_v": q8_0_tensor(rng, nkv * hd, H),
+        "attn_o": q8_0_tensor(rng, H, nq * hd),
+        "attn_q_bias": f32_tensor(g(nq * hd)) if bias else None,
+        "attn_k_bias": f32_tensor(g(nkv * hd)) if bias else None,
+        "attn_v_bias": f32_tensor(g(nkv * hd)) if bias else None,
+        "ffn_norm": f32_tensor(1.0 + g(H)),
+        "ffn_gate": q8_0_tensor(rng, F, H),
+        "ffn_up": q8_0_tensor(rng, F, H),
+        "ffn_down": q8_0_tensor(rng, H, F),
+    }
+
+
+def model_q8_0(seed: int, hp: dict, n_layers: int | None = None) -> dict:
+    """Full LM: layers, output_norm, tied Q8_0 lm_head / token embedding."""
+    rng = np.random.default_rng(seed)
+    n = hp["n_layers"] if n_layers is None else n_layers
+    layers = [layer_q8_0(rng, hp) for _ in range(n)]
+    head = q8_0_tensor(rng, hp["vocab"], hp["hidden"])
+    norm = f32_tensor(1.0 + rng.standard_normal(hp["hidden"], dtype=np.float32) * 0.02)
+    return {"layers": layers, "output_norm": norm, "lm_head": head, "tok_embd": head}
+
+
+def tensor_bytes(spec) -> int:
+    return 0 if spec is None else int(spec[0].nbytes)
+
+
+def weight_bytes(model: dict) -> int:
+    n = sum(tensor_bytes(t) for L in model["layers"] for t in L.values())
+    return n + tensor_bytes(model["output_norm"]) + tensor_bytes(model["lm_head"])
