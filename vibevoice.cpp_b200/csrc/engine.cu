@@ -281,12 +281,7 @@ struct Recorder {
     cudaError_t begin() {
         if (!recs) return cudaSuccess;
         const int need = (int)recs->size() * 2 + 2;
-        while ((int)c->events.size() < need) {
-            cudaEvent_t e;
-            cudaError_t err = cudaEventCreate(&e);
-            if (err != cudaSuccess) return err;
-            c->events.push_back(e);
-        }
+        if ((int)c->events.size() < need) return cudaErrorInvalidValue;   // vvq2_profile pre-creates
         e0 = (int)recs->size() * 2;
         return cudaEventRecord(c->events[e0], st);
     }
@@ -305,6 +300,9 @@ int run_layers_decode(vvq2_ctx* c, vvq2_kv* kv, int M, int split, int nsplit, in
     const vvq2_hparams& hp = c->hp;
     const int H = hp.hidden_size, nq = hp.n_heads, nkv = hp.n_kv_heads, hd = hp.head_dim;
     const int F = hp.intermediate_size;
+    if (nsplit > c->max_splits_cap)
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "context of %d keys needs %d attention splits (max %d)",
+                    nsplit * split, nsplit, c->max_splits_cap);
     Recorder R{c, st, recs};
     auto gemv = [&](const GemvArgs& g, double out_bytes) -> int {
         CU(R.begin());
@@ -922,6 +920,13 @@ int vvq2_profile(vvq2_ctx* c, int enable) {
     if (int rc = check_ctx(c)) return rc;
     c->prof_on = enable != 0;
     for (int k = 0; k < 3; ++k) c->prof_ms[k] = c->prof_bytes[k] = 0.0, c->prof_n[k] = 0;
+    // events are created here, never during stream capture
+    const size_t need = 2 * (6 * (size_t)c->hp.n_layers + 8);
+    while (c->prof_on && c->events.size() < need) {
+        cudaEvent_t e;
+        CU(cudaEventCreate(&e));
+        c->events.push_back(e);
+    }
     return 0;
 }
 
