@@ -196,8 +196,12 @@ def main():
             kv.load_prefix(s, li, k, v)
     for s in range(2):
         kv.set_past_len(s, args.kv)
-    stream = torch.cuda.current_stream()
+    # a real stream object: handle 0 would mean "the library's own stream" and the
+    # events below would not see the work
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     sh = stream.cuda_stream
+    assert sh != 0
     tok = torch.randint(0, hp["vocab"], (2,), dtype=torch.int32, device="cuda")
 
     def steps(n):

@@ -16,6 +16,14 @@ def pytest_configure(config):
 
 
 @pytest.fixture(scope="session")
+def vv():
+    """The product binding, on a machine with an sm_100 device (gpu tests)."""
+    import vvq2
+    assert vvq2.lib().vvq2_device_count() > 0, "no sm_100 device visible"
+    return vvq2
+
+
+@pytest.fixture(scope="session")
 def golden():
     import numpy as np
 

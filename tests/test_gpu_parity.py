@@ -4,8 +4,13 @@ tests/test_qwen2_block.cpp and tests/test_qwen2_resident.cpp, and adds the
 quantized / batch-2 / f16-KV cases no reference test covers.
 
 Tolerance (the north star's): max |gpu - oracle| / max |oracle| <= 2e-3 on
-layer outputs, fp32 accumulation.  The decode GEMV reproduces ggml's integer
-dot products, so it is compared with the oracle in ggml activation mode."""
+layer outputs, fp32 accumulation.  The GPU path multiplies exactly dequantized
+weights by f32 activations, so it is compared with the oracle's exact mode
+(same f16 K/V and Q rounding, same ggml CPU RoPE recurrence); the reference
+CPU backend's int8-activation numerics are checked separately, loosely."""
+
+# what the GPU path computes: exact dequant x f32 activations, f16 K/V and Q,
+# ggml CPU rope cache, f32 flash-attention accumulation
 import numpy as np
 import pytest
 
@@ -13,18 +18,8 @@ import vvq2_oracle as O
 from fixtures_util import C1, cos_sim, golden_layer, random_layer, rel_err
 
 pytestmark = pytest.mark.gpu
-
-# what the decode path computes: ggml int8-activation dots, f16 K/V and Q,
-# ggml CPU rope cache, f32 flash-attention accumulation
-GPU_MODE = O.ACT_GGML | O.KV_F16 | O.Q_F16 | O.ROPE_GGML
+GPU_MODE = O.KV_F16 | O.Q_F16 | O.ROPE_GGML
 TOL = 2e-3
-
-
-@pytest.fixture(scope="module")
-def vv():
-    import vvq2
-    assert vvq2.lib().vvq2_device_count() > 0, "no sm_100 device visible"
-    return vvq2
 
 
 @pytest.mark.parametrize("name,qt", [("q8_0", O.Q8_0), ("q5_K", O.Q5_K), ("q6_K", O.Q6_K)])
@@ -69,7 +64,7 @@ def test_qwen2_layer_f32_vs_hf_golden(vv, golden):
     resident chunks).  K/V are stored f16, so the bound is the reference's
     flash-attention tolerance; against the oracle in the same numerics it is tight."""
     hp, t, x, y, pos = golden_layer(golden("qwen2_layer0.npz"))
-    eng, kv, ora = _pair(vv, hp, [t], 1, 80, O.KV_F16 | O.Q_F16 | O.ROPE_GGML | O.ACT_GGML)
+    eng, kv, ora = _pair(vv, hp, [t], 1, 80, GPU_MODE)
     got = eng.forward(kv, [0], x, [0])
     ref = ora.forward([0], x, [0])
     assert rel_err(got, ref) < 1e-4

@@ -15,7 +15,7 @@ from fixtures_util import C2, rel_err
 
 pytestmark = pytest.mark.gpu
 
-GPU_MODE = O.ACT_GGML | O.KV_F16 | O.Q_F16 | O.ROPE_GGML
+GPU_MODE = O.KV_F16 | O.Q_F16 | O.ROPE_GGML
 
 
 def build(seed, hp, n_layers):

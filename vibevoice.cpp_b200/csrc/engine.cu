@@ -106,6 +106,9 @@ struct vvq2_ctx {
     unsigned long long* amax = nullptr;
     int32_t* tok = nullptr;
     int max_splits_cap = 64;
+    int max_rows = GEMV_MAX_M;     // activation rows per GEMV launch (shared-memory bound)
+    int* err = nullptr;            // device error word written by bounded waits
+    std::vector<vvq2_kv*> kvs;   // caches created on this context (released with it)
 
     // measurement: per-launch CUDA events (captured into decode graphs when on)
     struct Rec { int kind; int e0, e1; double bytes; };
@@ -252,15 +255,24 @@ int check_ctx(vvq2_ctx* c) {
 
 cudaStream_t pick_stream(vvq2_ctx* c, void* s) { return s ? static_cast<cudaStream_t>(s) : c->stream; }
 
+// A kernel whose bounded wait gave up leaves a nonzero word; report and clear it.
+int check_device_error(vvq2_ctx* c) {
+    int e = 0;
+    CU(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+        cudaMemset(c->err, 0, sizeof(int));
+        return fail(VVQ2_ERR_CUDA, "a device-side wait timed out (code %d)", e);
+    }
+    return 0;
+}
+
 // Attention split: ~2 CTAs per SM overall, at most max_splits_cap splits per row.
 void choose_split(const vvq2_ctx* c, int M, int max_lim, int* split, int* nsplit) {
     const int target = 296;
     const int per_row = std::max(1, target / std::max(1, M * c->hp.n_kv_heads));
     int s = (max_lim + per_row - 1) / per_row;
-    s = std::max(s, 64);
-    s = (s + 31) / 32 * 32;
-    while ((max_lim + s - 1) / s > c->max_splits_cap) s += 32;
-    s = std::min(s, 512);
+    s = (std::max(s, KV_PAGE) + KV_PAGE - 1) / KV_PAGE * KV_PAGE;   // whole pages per split
+    while ((max_lim + s - 1) / s > c->max_splits_cap) s += KV_PAGE;
     *split = s;
     *nsplit = (max_lim + s - 1) / s;
 }
@@ -283,11 +295,11 @@ struct Recorder {
         const int need = (int)recs->size() * 2 + 2;
         if ((int)c->events.size() < need) return cudaErrorInvalidValue;   // vvq2_profile pre-creates
         e0 = (int)recs->size() * 2;
-        return cudaEventRecord(c->events[e0], st);
+        return cudaEventRecordWithFlags(c->events[e0], st, cudaEventRecordExternal);
     }
     cudaError_t end(int kind, double bytes) {
         if (!recs) return cudaSuccess;
-        cudaError_t err = cudaEventRecord(c->events[e0 + 1], st);
+        cudaError_t err = cudaEventRecordWithFlags(c->events[e0 + 1], st, cudaEventRecordExternal);
         recs->push_back({kind, e0, e0 + 1, bytes});
         return err;
     }
@@ -351,6 +363,7 @@ int run_layers_decode(vvq2_ctx* c, vvq2_kv* kv, int M, int split, int nsplit, in
         ad.part = c->part;
         ad.part_ml = c->part_ml;
         ad.counters = c->counters;
+        ad.err = c->err;
         CU(R.begin());
         CU(attn_decode_launch(ad, st));
         CU(R.end(1, attn_bytes_per_layer));
@@ -462,8 +475,8 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     if (hp->hidden_size <= 0 || hp->n_heads <= 0 || hp->n_kv_heads <= 0 || hp->head_dim <= 0 ||
         hp->n_layers <= 0 || hp->n_heads % hp->n_kv_heads)
         return fail(VVQ2_ERR_INVALID_ARG, "bad hparams");
-    if (hp->head_dim != 64 && hp->head_dim != 128)
-        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "head_dim %d (64 and 128 supported)", hp->head_dim);
+    if (hp->head_dim != 32 && hp->head_dim != 64 && hp->head_dim != 128)
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "head_dim %d (32, 64 and 128 supported)", hp->head_dim);
     if (hp->n_heads / hp->n_kv_heads > 8)
         return fail(VVQ2_ERR_NOT_IMPLEMENTED, "GQA group %d > 8", hp->n_heads / hp->n_kv_heads);
     int ndev = 0;
@@ -476,6 +489,7 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     if (p.major != 10) return fail(VVQ2_ERR_NO_DEVICE, "device %d is sm_%d%d, need sm_100", device, p.major, p.minor);
     CU(cudaSetDevice(device));
     CU(gemv_prepare());
+    CU(attn_decode_prepare());
     vvq2_ctx* c = new vvq2_ctx();
     c->hp = *hp;
     c->device = device;
@@ -499,10 +513,13 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     rc = rc ? rc : c->alloc(&c->meta, (size_t)M);
     rc = rc ? rc : c->alloc(&c->amax, (size_t)M);
     rc = rc ? rc : c->alloc(&c->tok, (size_t)M);
+    rc = rc ? rc : c->alloc(&c->err, (size_t)1);
+    c->max_rows = std::min(GEMV_MAX_M, gemv_max_rows(std::max({hp->hidden_size, qw, F})));
     if (!rc && hp->vocab_size > 0) rc = c->alloc(&c->LOGITS, (size_t)M * hp->vocab_size);
     if (!rc && cudaMallocHost(&c->meta_host, sizeof(RowMeta) * M) != cudaSuccess)
         rc = fail(VVQ2_ERR_OUT_OF_MEMORY, "pinned alloc failed");
-    if (!rc && cudaMemset(c->counters, 0, sizeof(int) * M * hp->n_kv_heads) != cudaSuccess)
+    if (!rc && (cudaMemset(c->counters, 0, sizeof(int) * M * hp->n_kv_heads) != cudaSuccess ||
+                cudaMemset(c->err, 0, sizeof(int)) != cudaSuccess))
         rc = fail(VVQ2_ERR_CUDA, "memset failed");
     if (rc) {
         vvq2_free(c);
@@ -519,6 +536,16 @@ void vvq2_free(vvq2_ctx* c) {
     for (auto& g : c->graphs) cudaGraphExecDestroy(g.exec);
     for (cudaEvent_t e : c->events) cudaEventDestroy(e);
     for (void* p : c->allocs) cudaFree(p);
+    // caches outlive nothing: their device memory goes with the context and the
+    // handles stay valid only for vvq2_kv_free
+    for (vvq2_kv* kv : c->kvs) {
+        if (kv->k) cudaFree(kv->k);
+        if (kv->v) cudaFree(kv->v);
+        if (kv->block_table) cudaFree(kv->block_table);
+        kv->k = kv->v = nullptr;
+        kv->block_table = nullptr;
+        kv->ctx = nullptr;
+    }
     if (c->meta_host) cudaFreeHost(c->meta_host);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -626,6 +653,7 @@ int vvq2_kv_init(vvq2_ctx* c, int n_seqs, int max_seq, vvq2_kv** out) {
         return fail(VVQ2_ERR_CUDA, "kv init copy failed");
     }
     kv->past.assign(n_seqs, 0);
+    c->kvs.push_back(kv);
     *out = kv;
     return 0;
 }
@@ -642,6 +670,7 @@ void vvq2_kv_free(vvq2_kv* kv) {
                                        [kv](const vvq2_ctx::Graph& g) { return g.kv == kv; }),
                         c->graphs.end());
         if (c->meta_kv == kv) c->meta_kv = nullptr;
+        c->kvs.erase(std::remove(c->kvs.begin(), c->kvs.end(), kv), c->kvs.end());
     }
     if (kv->k) cudaFree(kv->k);
     if (kv->v) cudaFree(kv->v);
@@ -650,7 +679,7 @@ void vvq2_kv_free(vvq2_kv* kv) {
 }
 
 int vvq2_kv_set_past_len(vvq2_kv* kv, int seq, int past) {
-    if (!kv || seq < 0 || seq >= kv->n_seqs || past < 0 || past > kv->max_seq)
+    if (!kv || !kv->ctx || seq < 0 || seq >= kv->n_seqs || past < 0 || past > kv->max_seq)
         return fail(VVQ2_ERR_INVALID_ARG, "bad seq/past_len");
     kv->past[seq] = past;
     if (kv->ctx && kv->ctx->meta_kv == kv) kv->ctx->meta_kv = nullptr;
@@ -664,7 +693,7 @@ int vvq2_kv_past_len(const vvq2_kv* kv, int seq) {
 
 static int kv_xfer(vvq2_kv* kv, int seq, int layer, float* k, float* v, const float* kc, const float* vc,
                    int n_pos, bool upload) {
-    if (!kv) return fail(VVQ2_ERR_INVALID_ARG, "null kv");
+    if (!kv || !kv->ctx) return fail(VVQ2_ERR_INVALID_ARG, "null or released kv");
     vvq2_ctx* c = kv->ctx;
     if (int rc = check_ctx(c)) return rc;
     if (seq < 0 || seq >= kv->n_seqs || layer < 0 || layer >= c->hp.n_layers || n_pos < 0 || n_pos > kv->max_seq)
@@ -732,8 +761,9 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
     // Token chunks of at most GEMV_MAX_M rows over all sequences; each chunk
     // runs through every layer before the next (resident chunked prefill,
     // the ordering tests/test_qwen2_resident.cpp checks).
-    const int tok_per_chunk = std::max(1, GEMV_MAX_M / n_seqs);
-    if (n_seqs > GEMV_MAX_M) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "more than %d sequences per call", GEMV_MAX_M);
+    const int tok_per_chunk = std::max(1, c->max_rows / n_seqs);
+    if (n_seqs > c->max_rows)
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "more than %d sequences per call", c->max_rows);
     for (int t0 = 0; t0 < n_tok; t0 += tok_per_chunk) {
         const int nt = std::min(tok_per_chunk, n_tok - t0);
         const int M = n_seqs * nt;
@@ -768,6 +798,7 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
         }
         // the meta staging buffer is reused by the next chunk
         CU(cudaStreamSynchronize(st));
+        if (int rc = check_device_error(c)) return rc;
     }
     if (flags & VVQ2_ADVANCE)
         for (int s = 0; s < n_seqs; ++s) kv->past[seqs[s]] += n_tok;
@@ -781,8 +812,9 @@ int vvq2_lm_head(vvq2_ctx* c, int n, const float* h, float* logits, int32_t* arg
     cudaStream_t st = pick_stream(c, stream);
     const int H = c->hp.hidden_size, V = c->lm_head.rows;
     const bool h_dev = is_device_ptr(h);
-    for (int i0 = 0; i0 < n; i0 += GEMV_MAX_M) {
-        const int M = std::min(GEMV_MAX_M, n - i0);
+    const int rows_per = gemv_max_rows(H);
+    for (int i0 = 0; i0 < n; i0 += rows_per) {
+        const int M = std::min(rows_per, n - i0);
         CU(cudaMemcpyAsync(c->X, h + (size_t)i0 * H, sizeof(float) * M * H,
                            h_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
         CU(argmax_init_launch(c->amax, M, st));
@@ -834,7 +866,7 @@ int vvq2_embed(vvq2_ctx* c, int n, const int32_t* tokens, float* out, void* stre
 int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, const int32_t* tokens_in,
                      int32_t* tokens_out, void* stream) {
     if (int rc = check_ctx(c)) return rc;
-    if (!kv || kv->ctx != c || !seqs || !tokens_in || !tokens_out || n_seqs <= 0 || n_seqs > GEMV_MAX_M)
+    if (!kv || kv->ctx != c || !seqs || !tokens_in || !tokens_out || n_seqs <= 0 || n_seqs > c->max_rows)
         return fail(VVQ2_ERR_INVALID_ARG, "bad decode_step arguments");
     if (c->tok_embd.type < 0 || c->lm_head.type < 0 || !c->out_norm)
         return fail(VVQ2_ERR_INVALID_ARG, "decode_step needs output_norm, lm_head and tok_embd");
@@ -911,6 +943,7 @@ int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, cons
         }
     } else if (!is_device_ptr(tokens_out)) {
         CU(cudaStreamSynchronize(st));
+        if (int rc = check_device_error(c)) return rc;
     }
     for (int s = 0; s < n_seqs; ++s) kv->past[seqs[s]] += 1;
     return 0;

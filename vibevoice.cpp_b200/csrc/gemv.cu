@@ -1,23 +1,27 @@
 // gemv.cu -- decode-time (<= 8 activation rows) fused dequant GEMV on sm_100a.
 //
 // One kernel family covers every linear of the Qwen2 layer at decode time
-// (src/qwen2.cpp:19-26,274-276,349 and the FFN at :33-40), the lm_head
+// (src/qwen2.cpp:19-26,274-276,349 and the SwiGLU FFN at :33-40), the lm_head
 // (src/vibevoice_asr.cpp:285-311) and its greedy argmax (:702-706).
 //
-// Prologue (per CTA, from L2): optional RMSNorm (src/rms_norm.hpp:11-17) of
-// the f32 activation rows, then quantization to the weight's ggml vec_dot
-// type -- Q8_0 (per 32, f16 scale) for Q8_0 weights, Q8_K (per 256, f32 scale,
-// int16 bsums) for Q5_K/Q6_K, f16 for F16 and f32 for F32 -- into shared
-// memory.  This reproduces the integer dot products ggml's CPU backend runs
-// (ggml_vec_dot_*_q8_*), so results differ from the reference only in float
-// summation order.
+// Numerics: weights are dequantized exactly as ggml's dequantize_row_* does
+// (bit-identical f32 values), activations stay f32, products accumulate in f32
+// (Blackwell packed FFMA2).  This is the
+// "exact" restatement of ggml_mul_mat; ggml's CPU backend additionally rounds
+// the activations to int8 blocks (its vec_dot_type), a step whose rounding
+// flips cascade through RMSNorm, so it is reproduced only by the CPU oracle.
 //
-// Main loop: each warp owns NR weight rows; lanes stride over 32-element
-// blocks, reading 16-byte vectors of the repacked weights once from HBM and
-// doing dp4a against the shared-memory activations for all M rows.
-//
-// Epilogues: QKV (+bias, NEOX RoPE on Q/K, Q to a buffer, K/V appended to the
-// f16 paged cache), residual add, SwiGLU, plain store, and argmax.
+// Structure: a persistent grid (one wave of resident CTAs).  Each CTA first stages the
+// M activation rows in shared memory -- applying the RMSNorm
+// (src/rms_norm.hpp:11-17) when the linear follows one -- then its warps walk
+// 4-row units of the weight matrix.  Lanes take 16-element chunks (one 16-byte
+// load per Q8_0 row, two for F16, ...), so every weight byte is read from HBM
+// once; the activation chunk is read from shared memory once per lane and
+// reused for the 4 rows.  Epilogues: QKV (+bias, NEOX RoPE on Q/K, Q to a
+// buffer, K/V appended to the f16 paged cache), residual add, SwiGLU, store,
+// and argmax.  Kernels are launched with programmatic dependent launch: each
+// warp starts pulling its first unit's weights into L2 before
+// griddepcontrol.wait, overlapping the previous kernel's tail.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -27,61 +31,165 @@ namespace {
 
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+constexpr int NR = 4;                        // weight rows per warp unit
 constexpr size_t GEMV_SMEM_MAX = 200 * 1024;
 
-// activation-quantization kind derived from the weight type
-__host__ __device__ constexpr int act_kind(int wt) {
-    return wt == W_Q8_0 ? 0 : (wt == W_Q5_K || wt == W_Q6_K) ? 1 : 2;  // 0 q8_0, 1 q8_K, 2 float
-}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
 
-// shared-memory carve-up for M rows of K activations
-struct ActSmem {
-    int8_t* q;      // [M][K]
-    float* d;       // [M][K/32] (q8_0) or [M][K/256] (q8_K)
-    int16_t* bs;    // [M][K/16] (q8_K)
-    float* f;       // [M][K] (float kind)
+// One 16-element chunk of one weight row, as loaded (raw bits + block scales).
+struct Chunk {
+    uint4 r0, r1, r2, r3;   // raw: Q8_0 q in r0; Q5_K qs/qh in r0/r1; Q6_K ql/qh in r0/r1;
+                            // F16 in r0/r1; F32 in r0..r3
+    float scale;            // Q8_0 d; Q5_K d*sc; Q6_K d*sc
+    float mscale;           // Q5_K dmin*m
+    int shift;              // Q5_K sub-block j; Q6_K quarter k
 };
 
-__host__ __device__ inline size_t act_smem_bytes(int wt, int M, int K) {
-    const int kind = act_kind(wt);
-    if (kind == 0) return (size_t)M * K + (size_t)M * (K / 32) * 4 + 64;
-    if (kind == 1) return (size_t)M * K + (size_t)M * (K / 256) * 4 + (size_t)M * (K / 16) * 2 + 64;
-    return (size_t)M * K * 4 + 64;
-}
-
-__device__ inline ActSmem carve(uint8_t* base, int wt, int M, int K) {
-    ActSmem s{};
-    const int kind = act_kind(wt);
-    if (kind == 2) {
-        s.f = reinterpret_cast<float*>(base);
-        return s;
-    }
-    s.q = reinterpret_cast<int8_t*>(base);
-    uint8_t* p = base + (size_t)M * K;
-    s.d = reinterpret_cast<float*>(p);
-    p += (size_t)M * (K / (kind == 0 ? 32 : 256)) * 4;
-    s.bs = reinterpret_cast<int16_t*>(p);
-    return s;
-}
-
-// Prologue: optional RMSNorm then quantization of M activation rows into smem.
 template <int WT>
-__device__ void load_activations(const GemvArgs& a, ActSmem s, float* red) {
+__device__ __forceinline__ void load_chunk(const DevW& W, int row, int c, Chunk& ch) {
+    const uint8_t* rp = W.q + (size_t)row * W.row_stride;
+    if constexpr (WT == W_Q8_0) {
+        ch.r0 = __ldg(reinterpret_cast<const uint4*>(rp) + c);
+        ch.scale = __half2float(W.d[(size_t)row * (W.cols / 32) + c / 2]);
+    } else if constexpr (WT == W_Q5_K) {
+        const int sb = c >> 4, e0 = (c & 15) * 16, j = e0 / 32, l0 = e0 & 31;
+        const uint8_t* b = rp + (size_t)sb * Q5K_BYTES;
+        const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(b));
+        ch.r0 = __ldg(reinterpret_cast<const uint4*>(b + 48 + 32 * (j >> 1) + l0));
+        ch.r1 = __ldg(reinterpret_cast<const uint4*>(b + 16 + l0));
+        const uint8_t* scb = reinterpret_cast<const uint8_t*>(&hdr) + 4;
+        int sc, m;
+        if (j < 4) {
+            sc = scb[j] & 63;
+            m = scb[j + 4] & 63;
+        } else {
+            sc = (scb[j + 4] & 0xF) | ((scb[j - 4] >> 6) << 4);
+            m = (scb[j + 4] >> 4) | ((scb[j] >> 6) << 4);
+        }
+        const __half2 dh = *reinterpret_cast<const __half2*>(&hdr.x);
+        ch.scale = __fmul_rn(__low2float(dh), (float)sc);    // d1 = d*sc   (dequantize_row_q5_K)
+        ch.mscale = __fmul_rn(__high2float(dh), (float)m);   // m1 = dmin*m
+        ch.shift = j;
+    } else if constexpr (WT == W_Q6_K) {
+        const int sb = c >> 4, e0 = (c & 15) * 16;
+        const int hf = e0 >> 7, r = e0 & 127, k = r >> 5, l0 = r & 31;
+        const uint8_t* b = rp + (size_t)sb * Q6K_PACKED;
+        ch.r0 = __ldg(reinterpret_cast<const uint4*>(b + hf * 64 + (k & 1) * 32 + l0));
+        ch.r1 = __ldg(reinterpret_cast<const uint4*>(b + 128 + hf * 32 + l0));
+        const int8_t sc = reinterpret_cast<const int8_t*>(b + 192)[hf * 8 + (l0 >> 4) + 2 * k];
+        ch.scale = __fmul_rn(__half2float(W.d[(size_t)row * (W.cols / 256) + sb]), (float)sc);  // d*sc
+        ch.shift = k;
+    } else if constexpr (WT == W_F16) {
+        const uint4* p = reinterpret_cast<const uint4*>(rp) + 2 * c;
+        ch.r0 = __ldg(p);
+        ch.r1 = __ldg(p + 1);
+    } else {
+        const uint4* p = reinterpret_cast<const uint4*>(rp) + 4 * c;
+        ch.r0 = __ldg(p);
+        ch.r1 = __ldg(p + 1);
+        ch.r2 = __ldg(p + 2);
+        ch.r3 = __ldg(p + 3);
+    }
+}
+
+__device__ __forceinline__ uint32_t word(const uint4& v, int t) {
+    return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w;
+}
+
+// Dequantized weights g*4 .. g*4+3 of the chunk, bit-exact with ggml's
+// dequantize_row_*: Q8_0 q*d; Q5_K d1*q - m1; Q6_K (d*sc)*(q-32); F16/F32 as is.
+template <int WT>
+__device__ __forceinline__ void expand4(const Chunk& ch, int g, float* w) {
+    if constexpr (WT == W_Q8_0) {
+        const uint32_t q = word(ch.r0, g);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = __fmul_rn((float)(int8_t)((q >> (8 * e)) & 0xff), ch.scale);
+    } else if constexpr (WT == W_Q5_K) {
+        const int j = ch.shift;
+        const uint32_t q = ((word(ch.r0, g) >> (4 * (j & 1))) & 0x0F0F0F0Fu) |
+                           (((word(ch.r1, g) >> j) & 0x01010101u) << 4);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            w[e] = __fsub_rn(__fmul_rn(ch.scale, (float)((q >> (8 * e)) & 0xff)), ch.mscale);
+    } else if constexpr (WT == W_Q6_K) {
+        const int k = ch.shift;
+        const uint32_t q = ((word(ch.r0, g) >> (4 * (k >> 1))) & 0x0F0F0F0Fu) |
+                           (((word(ch.r1, g) >> (2 * k)) & 0x03030303u) << 4);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = __fmul_rn(ch.scale, (float)((int)((q >> (8 * e)) & 0xff) - 32));
+    } else if constexpr (WT == W_F16) {
+        const uint4& v = g < 2 ? ch.r0 : ch.r1;
+        const uint32_t a = word(v, (g & 1) * 2), b = word(v, (g & 1) * 2 + 1);
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&a));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&b));
+        w[0] = f0.x; w[1] = f0.y; w[2] = f1.x; w[3] = f1.y;
+    } else {
+        const uint4& v = g == 0 ? ch.r0 : g == 1 ? ch.r1 : g == 2 ? ch.r2 : ch.r3;
+        w[0] = __uint_as_float(v.x); w[1] = __uint_as_float(v.y);
+        w[2] = __uint_as_float(v.z); w[3] = __uint_as_float(v.w);
+    }
+}
+
+// L2 prefetch of the chunks a lane will read for one weight row
+template <int WT>
+__device__ __forceinline__ void prefetch_row(const DevW& W, int row, int lane, int nchunk) {
+    const uint8_t* rp = W.q + (size_t)row * W.row_stride;
+    const int bytes_per_chunk = (int)(W.row_stride / nchunk);
+    for (int c = lane; c < nchunk; c += 32)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + (size_t)c * bytes_per_chunk));
+}
+
+// Row r of unit u: (tensor, row).  QKV: two NEOX pairs (i0, i0+1) of one head;
+// SwiGLU: gate rows i0, i0+1 then up rows i0, i0+1; else 4 consecutive rows.
+template <int EPI>
+__device__ __forceinline__ void unit_rows(const GemvArgs& a, int u, int* row, int* which) {
+    if constexpr (EPI == EPI_QKV) {
+        const int half = a.hd / 2, per_head = half / 2;
+        const int h = u / per_head, i0 = 2 * (u % per_head);
+        row[0] = h * a.hd + i0;
+        row[1] = row[0] + 1;
+        row[2] = row[0] + half;
+        row[3] = row[1] + half;
+        which[0] = which[1] = which[2] = which[3] = 0;
+    } else if constexpr (EPI == EPI_SWIGLU) {
+        row[0] = row[2] = 2 * u;
+        row[1] = row[3] = 2 * u + 1;
+        which[0] = which[1] = 0;
+        which[2] = which[3] = 1;
+    } else {
+#pragma unroll
+        for (int j = 0; j < NR; ++j) {
+            row[j] = u * NR + j;
+            which[j] = 0;
+        }
+    }
+}
+
+// Stage M activation rows (optionally RMSNorm'd) as f32 in shared memory.
+__device__ void stage_activations(const GemvArgs& a, float* act) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int M = a.M, K = a.K;
+    __shared__ float red[GEMV_MAX_M * GEMV_WARPS];
     __shared__ float row_scale[GEMV_MAX_M];
+    const int K4 = K / 4;
     if (a.norm_w) {
-        // ggml_compute_forward_rms_norm_f32: mean of squares, scale = 1/sqrtf(mean + eps)
+        // ggml_compute_forward_rms_norm_f32: scale = 1/sqrtf(mean(x^2) + eps)
         float ss[GEMV_MAX_M];
 #pragma unroll
-        for (int m = 0; m < GEMV_MAX_M; ++m) ss[m] = 0.0f;
-        for (int k = tid; k < K; k += GEMV_THREADS) {
+        for (int m = 0; m < GEMV_MAX_M; ++m) ss[m] = 0.f;
+        for (int k = tid; k < K4; k += GEMV_THREADS) {
 #pragma unroll
-            for (int m = 0; m < GEMV_MAX_M; ++m)
+            for (int m = 0; m < GEMV_MAX_M; ++m) {
                 if (m < M) {
-                    const float v = a.x[(size_t)m * a.x_stride + k];
-                    ss[m] = __fadd_rn(ss[m], __fmul_rn(v, v));
+                    const float4 v = reinterpret_cast<const float4*>(a.x + (size_t)m * a.x_stride)[k];
+                    reinterpret_cast<float4*>(act + (size_t)m * K)[k] = v;
+                    ss[m] = fmaf(v.x, v.x, ss[m]);
+                    ss[m] = fmaf(v.y, v.y, ss[m]);
+                    ss[m] = fmaf(v.z, v.z, ss[m]);
+                    ss[m] = fmaf(v.w, v.w, ss[m]);
                 }
+            }
         }
 #pragma unroll
         for (int m = 0; m < GEMV_MAX_M; ++m) {
@@ -92,462 +200,311 @@ __device__ void load_activations(const GemvArgs& a, ActSmem s, float* red) {
         }
         __syncthreads();
         if (tid < M) {
-            float t = 0.0f;
-            for (int w = 0; w < GEMV_WARPS; ++w) t = __fadd_rn(t, red[tid * GEMV_WARPS + w]);
+            float t = 0.f;
+            for (int w = 0; w < GEMV_WARPS; ++w) t += red[tid * GEMV_WARPS + w];
             const float mean = __fdiv_rn(t, (float)K);
             row_scale[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
         }
         __syncthreads();
-    }
-    auto act = [&](int m, int k) -> float {
-        const float v = a.x[(size_t)m * a.x_stride + k];
-        if (!a.norm_w) return v;
-        return __fmul_rn(__fmul_rn(v, row_scale[m]), a.norm_w[k]);   // (x*scale)*w
-    };
-    constexpr int kind = act_kind(WT);
-    if constexpr (kind == 0) {
-        // quantize_row_q8_0_ref: 8 lanes per 32-block, 4 elements each
-        const int nb = K / 32;
-        // warp-uniform trip count: every lane reaches the shuffles
-        for (int t0 = warp * 4; t0 < M * nb; t0 += GEMV_WARPS * 4) {
-            const int t = t0 + (lane >> 3);
-            const bool on = t < M * nb;
-            const int m = on ? t / nb : 0, b = on ? t % nb : 0, sub = lane & 7;
-            float v[4], amax = 0.0f;
+        for (int k = tid; k < K4; k += GEMV_THREADS) {
+            const float4 w = reinterpret_cast<const float4*>(a.norm_w)[k];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                v[e] = on ? act(m, b * 32 + sub * 4 + e) : 0.0f;
-                amax = fmaxf(amax, fabsf(v[e]));
+            for (int m = 0; m < GEMV_MAX_M; ++m) {
+                if (m < M) {
+                    float4* p = reinterpret_cast<float4*>(act + (size_t)m * K) + k;
+                    float4 v = *p;
+                    const float s = row_scale[m];
+                    v.x = __fmul_rn(__fmul_rn(v.x, s), w.x);   // (x*scale)*w
+                    v.y = __fmul_rn(__fmul_rn(v.y, s), w.y);
+                    v.z = __fmul_rn(__fmul_rn(v.z, s), w.z);
+                    v.w = __fmul_rn(__fmul_rn(v.w, s), w.w);
+                    *p = v;
+                }
             }
-#pragma unroll
-            for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o, 8));
-            if (!on) continue;
-            const float d = __fdiv_rn(amax, 127.0f);
-            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-            char4 q;
-            q.x = (signed char)roundf(__fmul_rn(v[0], id));
-            q.y = (signed char)roundf(__fmul_rn(v[1], id));
-            q.z = (signed char)roundf(__fmul_rn(v[2], id));
-            q.w = (signed char)roundf(__fmul_rn(v[3], id));
-            *reinterpret_cast<char4*>(s.q + (size_t)m * K + b * 32 + sub * 4) = q;
-            if (sub == 0) s.d[m * nb + b] = __half2float(__float2half_rn(d));
-        }
-    } else if constexpr (kind == 1) {
-        // quantize_row_q8_K_ref: one warp per 256-block, 8 elements per lane
-        const int nb = K / 256;
-        for (int t = warp; t < M * nb; t += GEMV_WARPS) {
-            const int m = t / nb, b = t % nb;
-            float v[8];
-            float ax = 0.0f, mx = 0.0f;
-            int ai = 0x7fffffff;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int k = b * 256 + lane * 8 + e;
-                v[e] = act(m, k);
-                const float av = fabsf(v[e]);
-                if (av > ax) { ax = av; mx = v[e]; ai = k; }
-            }
-            // first index of the largest magnitude (strict > in ggml)
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ax2 = __shfl_xor_sync(0xffffffffu, ax, o);
-                const float mx2 = __shfl_xor_sync(0xffffffffu, mx, o);
-                const int ai2 = __shfl_xor_sync(0xffffffffu, ai, o);
-                if (ax2 > ax || (ax2 == ax && ai2 < ai)) { ax = ax2; mx = mx2; ai = ai2; }
-            }
-            int8_t* qd = s.q + (size_t)m * K + b * 256 + lane * 8;
-            if (ax == 0.0f) {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) qd[e] = 0;
-                if (lane < 16) s.bs[m * (K / 16) + b * 16 + lane] = 0;
-                if (lane == 0) s.d[m * nb + b] = 0.0f;
-                continue;
-            }
-            const float iscale = __fdiv_rn(-127.0f, mx);
-            int sum = 0;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                int q = __float2int_rn(__fmul_rn(iscale, v[e]));
-                q = q < 127 ? q : 127;
-                qd[e] = (int8_t)q;
-                sum += q;
-            }
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            if ((lane & 1) == 0) s.bs[m * (K / 16) + b * 16 + lane / 2] = (int16_t)sum;
-            if (lane == 0) s.d[m * nb + b] = __fdiv_rn(1.0f, iscale);
         }
     } else {
-        for (int t = tid; t < M * K; t += GEMV_THREADS) {
-            const int m = t / K, k = t % K;
-            const float v = act(m, k);
-            s.f[t] = (WT == W_F16) ? __half2float(__float2half_rn(v)) : v;
+        for (int k = tid; k < K4; k += GEMV_THREADS) {
+#pragma unroll
+            for (int m = 0; m < GEMV_MAX_M; ++m)
+                if (m < M)
+                    reinterpret_cast<float4*>(act + (size_t)m * K)[k] =
+                        reinterpret_cast<const float4*>(a.x + (size_t)m * a.x_stride)[k];
         }
     }
     __syncthreads();
 }
 
-__device__ __forceinline__ int dot8(const uint4& w0, const uint4& w1, const uint4& a0, const uint4& a1) {
-    int s = 0;
-    s = __dp4a((int)w0.x, (int)a0.x, s);
-    s = __dp4a((int)w0.y, (int)a0.y, s);
-    s = __dp4a((int)w0.z, (int)a0.z, s);
-    s = __dp4a((int)w0.w, (int)a0.w, s);
-    s = __dp4a((int)w1.x, (int)a1.x, s);
-    s = __dp4a((int)w1.y, (int)a1.y, s);
-    s = __dp4a((int)w1.z, (int)a1.z, s);
-    s = __dp4a((int)w1.w, (int)a1.w, s);
-    return s;
+// zero only the fields the type uses, so unused ones stay dead in registers
+template <int WT>
+__device__ __forceinline__ void clear_chunk(Chunk& ch) {
+    ch.r0 = make_uint4(0, 0, 0, 0);
+    if constexpr (WT != W_Q8_0) ch.r1 = make_uint4(0, 0, 0, 0);
+    if constexpr (WT == W_F32) ch.r2 = ch.r3 = make_uint4(0, 0, 0, 0);
+    if constexpr (WT == W_Q8_0 || WT == W_Q5_K || WT == W_Q6_K) ch.scale = 0.f;
+    if constexpr (WT == W_Q5_K) ch.mscale = 0.f;
+    if constexpr (WT == W_Q5_K || WT == W_Q6_K) ch.shift = 0;
 }
 
-// Row r of a unit: which tensor and which row.
-template <int EPI, int NR>
-__device__ __forceinline__ void unit_rows(const GemvArgs& a, int u, int* row, int* which) {
-    if constexpr (EPI == EPI_QKV) {
-        const int half = a.hd / 2;
-        const int h = u / half, i = u % half;
-        row[0] = h * a.hd + i;
-        row[1] = row[0] + half;
-        which[0] = which[1] = 0;
-    } else if constexpr (EPI == EPI_SWIGLU) {
-        row[0] = u;
-        row[1] = u;
-        which[0] = 0;
-        which[1] = 1;
-    } else {
+// Work decomposition.  A unit is NR weight rows; a unit is split across `wpu`
+// warps (each takes every wpu-th 512-element "item" of the row: one 16-element
+// chunk per lane), so 8 / wpu units form a CTA group.  CTAs loop over groups
+// (persistent when there are more groups than resident CTAs).  Partial sums
+// meet in shared memory; the unit's first warp runs the epilogue.
+struct Work {
+    int nchunk, niter, wpu, upc, sub, slot, n_it, n_groups;
+};
+
+__device__ __forceinline__ Work make_work(const GemvArgs& a, int warp) {
+    Work w;
+    w.nchunk = a.K / 16;
+    w.niter = (w.nchunk + 31) / 32;
+    w.wpu = a.wpu;
+    w.upc = GEMV_WARPS / a.wpu;
+    w.sub = warp % a.wpu;
+    w.slot = warp / a.wpu;
+    w.n_it = (w.niter - w.sub + w.wpu - 1) / w.wpu;   // >= 1 because wpu <= niter
+    w.n_groups = (a.n_units + w.upc - 1) / w.upc;
+    return w;
+}
+
+template <int WT, int EPI>
+__device__ __forceinline__ void load_item(const GemvArgs& a, const Work& w, int group, int l, int lane,
+                                          Chunk* dst) {
+    const int u = group * w.upc + w.slot;
+    const int c = (w.sub + l * w.wpu) * 32 + lane;
+    int r[NR], wh[NR];
+    unit_rows<EPI>(a, u < a.n_units ? u : 0, r, wh);
 #pragma unroll
-        for (int j = 0; j < NR; ++j) {
-            row[j] = u * NR + j;
-            which[j] = 0;
-        }
+    for (int j = 0; j < NR; ++j) {
+        const DevW& W = wh[j] ? a.w1 : a.w0;
+        if (u < a.n_units && c < w.nchunk && r[j] < W.rows) load_chunk<WT>(W, r[j], c, dst[j]);
+        else clear_chunk<WT>(dst[j]);
     }
 }
 
-template <int WT, int NR, int EPI>
-__global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const GemvArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ float red[GEMV_MAX_M * GEMV_WARPS];
-    __shared__ unsigned long long best[GEMV_MAX_M];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int M = a.M, K = a.K;
-    ActSmem s = carve(smem, WT, M, K);
-    if (EPI == EPI_ARGMAX && threadIdx.x < GEMV_MAX_M) best[threadIdx.x] = 0ull;
-    load_activations<WT>(a, s, red);
-
-    const int u = blockIdx.x * GEMV_WARPS + warp;
-    float acc[NR][GEMV_MAX_M];
+template <int WT, int MB>
+__device__ __forceinline__ void compute_item(const Chunk* ch, const float* act, int K, int M, int c,
+                                             float2 (&acc2)[NR][MB]) {
+    const int rot = (c >> 1) & 3;   // conflict-free float4 order within 8-lane phases
 #pragma unroll
-    for (int j = 0; j < NR; ++j)
+    for (int t = 0; t < 4; ++t) {
+        const int g = (t + rot) & 3;
+        float w[NR][4];
 #pragma unroll
-        for (int m = 0; m < GEMV_MAX_M; ++m) acc[j][m] = 0.0f;
-
-    int row[NR], which[NR];
-    bool valid = u < a.n_units;
-    if (valid) {
-        unit_rows<EPI, NR>(a, u, row, which);
+        for (int j = 0; j < NR; ++j) expand4<WT>(ch[j], g, w[j]);
 #pragma unroll
-        for (int j = 0; j < NR; ++j)
-            if (row[j] >= (which[j] ? a.w1.rows : a.w0.rows)) row[j] = -1;
-    }
-    if (valid) {
-        if constexpr (WT == W_Q8_0) {
-            const int nb = K / 32;
-#pragma unroll 2
-            for (int b = lane; b < nb; b += 32) {
-                uint4 wq0[NR], wq1[NR];
-                float wd[NR];
-#pragma unroll
-                for (int j = 0; j < NR; ++j) {
-                    if (row[j] < 0) { wq0[j] = wq1[j] = make_uint4(0, 0, 0, 0); wd[j] = 0.0f; continue; }
-                    const DevW& W = which[j] ? a.w1 : a.w0;
-                    const uint4* p = reinterpret_cast<const uint4*>(W.q + (size_t)row[j] * W.row_stride + b * 32);
-                    wq0[j] = __ldg(p);
-                    wq1[j] = __ldg(p + 1);
-                    wd[j] = __half2float(W.d[(size_t)row[j] * nb + b]);
-                }
-#pragma unroll
-                for (int m = 0; m < GEMV_MAX_M; ++m) {
-                    if (m >= M) break;
-                    const uint4* ap = reinterpret_cast<const uint4*>(s.q + (size_t)m * K + b * 32);
-                    const uint4 a0 = ap[0], a1 = ap[1];
-                    const float da = s.d[m * nb + b];
-#pragma unroll
-                    for (int j = 0; j < NR; ++j) {
-                        const int si = dot8(wq0[j], wq1[j], a0, a1);
-                        acc[j][m] = __fadd_rn(acc[j][m], __fmul_rn((float)si, __fmul_rn(wd[j], da)));
-                    }
-                }
-            }
-        } else if constexpr (WT == W_Q5_K) {
-            const int nsb = K / 256;
-            // warp-uniform trip count; 8-lane groups are all-on or all-off
-            for (int t0 = 0; t0 < nsb * 8; t0 += 32) {
-                const int t = t0 + lane;
-                const bool on = t < nsb * 8;
-                const int sb = on ? t >> 3 : 0, sub = t & 7;
-                uint32_t qw[NR][8];
-                int sc[NR], mn[NR];
-                float dd[NR], dm[NR];
-#pragma unroll
-                for (int j = 0; j < NR; ++j) {
-                    const DevW& W = which[j] ? a.w1 : a.w0;
-                    if (row[j] < 0 || !on) {
-#pragma unroll
-                        for (int w = 0; w < 8; ++w) qw[j][w] = 0;
-                        sc[j] = mn[j] = 0; dd[j] = dm[j] = 0.0f;
-                        continue;
-                    }
-                    const uint8_t* blk = W.q + (size_t)row[j] * W.row_stride + (size_t)sb * Q5K_BYTES;
-                    const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));        // d, dmin, scales[12]
-                    const uint4* qh4 = reinterpret_cast<const uint4*>(blk + 16);
-                    const uint4* qs4 = reinterpret_cast<const uint4*>(blk + 48 + 32 * (sub >> 1));
-                    const uint4 h0 = __ldg(qh4), h1 = __ldg(qh4 + 1), s0 = __ldg(qs4), s1 = __ldg(qs4 + 1);
-                    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-                    const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-                    const int shift = 4 * (sub & 1);
-#pragma unroll
-                    for (int w = 0; w < 8; ++w)
-                        qw[j][w] = ((sw[w] >> shift) & 0x0F0F0F0Fu) | (((hw[w] >> sub) & 0x01010101u) << 4);
-                    const uint8_t* scb = reinterpret_cast<const uint8_t*>(&hdr) + 4;
-                    if (sub < 4) {
-                        sc[j] = scb[sub] & 63;
-                        mn[j] = scb[sub + 4] & 63;
-                    } else {
-                        sc[j] = (scb[sub + 4] & 0xF) | ((scb[sub - 4] >> 6) << 4);
-                        mn[j] = (scb[sub + 4] >> 4) | ((scb[sub] >> 6) << 4);
-                    }
-                    const __half2 dh = *reinterpret_cast<const __half2*>(&hdr.x);
-                    dd[j] = __low2float(dh);
-                    dm[j] = __high2float(dh);
-                }
-#pragma unroll
-                for (int m = 0; m < GEMV_MAX_M; ++m) {
-                    if (m >= M) break;
-                    const uint4* ap = reinterpret_cast<const uint4*>(s.q + (size_t)m * K + sb * 256 + sub * 32);
-                    const uint4 a0 = ap[0], a1 = ap[1];   // sb = 0 when off: in bounds, result discarded
-                    const float da = on ? s.d[m * nsb + sb] : 0.0f;
-                    const int bsum = (int)s.bs[m * (K / 16) + sb * 16 + 2 * sub] +
-                                     (int)s.bs[m * (K / 16) + sb * 16 + 2 * sub + 1];
-#pragma unroll
-                    for (int j = 0; j < NR; ++j) {
-                        const uint4 w0 = make_uint4(qw[j][0], qw[j][1], qw[j][2], qw[j][3]);
-                        const uint4 w1 = make_uint4(qw[j][4], qw[j][5], qw[j][6], qw[j][7]);
-                        int is = sc[j] * dot8(w0, w1, a0, a1);
-                        int ms = mn[j] * bsum;
-                        // exact integer sums over the 8 sub-blocks of the super-block
-#pragma unroll
-                        for (int o = 1; o < 8; o <<= 1) {
-                            is += __shfl_xor_sync(0xffffffffu, is, o, 8);
-                            ms += __shfl_xor_sync(0xffffffffu, ms, o, 8);
-                        }
-                        if (sub == 0) {
-                            const float d = __fmul_rn(dd[j], da), dmin = __fmul_rn(dm[j], da);
-                            acc[j][m] = __fadd_rn(acc[j][m], __fmul_rn(d, (float)is));
-                            acc[j][m] = __fsub_rn(acc[j][m], __fmul_rn(dmin, (float)ms));
-                        }
-                    }
-                }
-            }
-        } else if constexpr (WT == W_Q6_K) {
-            const int nsb = K / 256;
-            for (int t0 = 0; t0 < nsb * 8; t0 += 32) {
-                const int t = t0 + lane;
-                const bool on = t < nsb * 8;
-                const int sb = on ? t >> 3 : 0, L = t & 7, hf = L >> 2, kq = L & 3;
-                uint32_t qw[NR][8];
-                int sc0[NR], sc1[NR];
-                float dd[NR];
-#pragma unroll
-                for (int j = 0; j < NR; ++j) {
-                    const DevW& W = which[j] ? a.w1 : a.w0;
-                    if (row[j] < 0 || !on) {
-#pragma unroll
-                        for (int w = 0; w < 8; ++w) qw[j][w] = 0x20202020u;
-                        sc0[j] = sc1[j] = 0; dd[j] = 0.0f;
-                        continue;
-                    }
-                    const uint8_t* blk = W.q + (size_t)row[j] * W.row_stride + (size_t)sb * Q6K_PACKED;
-                    const uint4* ql4 = reinterpret_cast<const uint4*>(blk + hf * 64 + (kq & 1) * 32);
-                    const uint4* qh4 = reinterpret_cast<const uint4*>(blk + 128 + hf * 32);
-                    const uint4 l0 = __ldg(ql4), l1 = __ldg(ql4 + 1), h0 = __ldg(qh4), h1 = __ldg(qh4 + 1);
-                    const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-                    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-                    const int ns = (kq >> 1) * 4;
-#pragma unroll
-                    for (int w = 0; w < 8; ++w)
-                        qw[j][w] = ((lw[w] >> ns) & 0x0F0F0F0Fu) | (((hw[w] >> (2 * kq)) & 0x03030303u) << 4);
-                    const int8_t* scl = reinterpret_cast<const int8_t*>(blk + 192);
-                    sc0[j] = scl[2 * L];
-                    sc1[j] = scl[2 * L + 1];
-                    dd[j] = __half2float(W.d[(size_t)row[j] * nsb + sb]);
-                }
-#pragma unroll
-                for (int m = 0; m < GEMV_MAX_M; ++m) {
-                    if (m >= M) break;
-                    const uint4* ap = reinterpret_cast<const uint4*>(s.q + (size_t)m * K + sb * 256 + L * 32);
-                    const uint4 a0 = ap[0], a1 = ap[1];   // sb = 0 when off: in bounds, result discarded
-                    const float da = on ? s.d[m * nsb + sb] : 0.0f;
-#pragma unroll
-                    for (int j = 0; j < NR; ++j) {
-                        int d1 = 0, d2 = 0;
-                        d1 = __dp4a((int)__vsub4(qw[j][0], 0x20202020u), (int)a0.x, d1);
-                        d1 = __dp4a((int)__vsub4(qw[j][1], 0x20202020u), (int)a0.y, d1);
-                        d1 = __dp4a((int)__vsub4(qw[j][2], 0x20202020u), (int)a0.z, d1);
-                        d1 = __dp4a((int)__vsub4(qw[j][3], 0x20202020u), (int)a0.w, d1);
-                        d2 = __dp4a((int)__vsub4(qw[j][4], 0x20202020u), (int)a1.x, d2);
-                        d2 = __dp4a((int)__vsub4(qw[j][5], 0x20202020u), (int)a1.y, d2);
-                        d2 = __dp4a((int)__vsub4(qw[j][6], 0x20202020u), (int)a1.z, d2);
-                        d2 = __dp4a((int)__vsub4(qw[j][7], 0x20202020u), (int)a1.w, d2);
-                        int is = sc0[j] * d1 + sc1[j] * d2;
-#pragma unroll
-                        for (int o = 1; o < 8; o <<= 1) is += __shfl_xor_sync(0xffffffffu, is, o, 8);
-                        if (L == 0) acc[j][m] = __fadd_rn(acc[j][m], __fmul_rn(__fmul_rn(dd[j], da), (float)is));
-                    }
-                }
-            }
-        } else {
-            // F32 / F16 weights: f32 (or f16-rounded) activations, f32 FMA
-            for (int k = lane * 4; k < K; k += 128) {
-                float wv[NR][4];
-#pragma unroll
-                for (int j = 0; j < NR; ++j) {
-                    const DevW& W = which[j] ? a.w1 : a.w0;
-                    if (row[j] < 0) { wv[j][0] = wv[j][1] = wv[j][2] = wv[j][3] = 0.0f; continue; }
-                    if constexpr (WT == W_F32) {
-                        const float4 f = __ldg(reinterpret_cast<const float4*>(W.q + (size_t)row[j] * W.row_stride) + k / 4);
-                        wv[j][0] = f.x; wv[j][1] = f.y; wv[j][2] = f.z; wv[j][3] = f.w;
-                    } else {
-                        const uint2 h = __ldg(reinterpret_cast<const uint2*>(W.q + (size_t)row[j] * W.row_stride + k * 2));
-                        const __half2 h0 = *reinterpret_cast<const __half2*>(&h.x);
-                        const __half2 h1 = *reinterpret_cast<const __half2*>(&h.y);
-                        wv[j][0] = __low2float(h0); wv[j][1] = __high2float(h0);
-                        wv[j][2] = __low2float(h1); wv[j][3] = __high2float(h1);
-                    }
-                }
-#pragma unroll
-                for (int m = 0; m < GEMV_MAX_M; ++m) {
-                    if (m >= M) break;
-                    const float4 av = *reinterpret_cast<const float4*>(s.f + (size_t)m * K + k);
-#pragma unroll
-                    for (int j = 0; j < NR; ++j) {
-                        acc[j][m] = fmaf(wv[j][0], av.x, acc[j][m]);
-                        acc[j][m] = fmaf(wv[j][1], av.y, acc[j][m]);
-                        acc[j][m] = fmaf(wv[j][2], av.z, acc[j][m]);
-                        acc[j][m] = fmaf(wv[j][3], av.w, acc[j][m]);
-                    }
-                }
-            }
-        }
-    }
-    // lane reduction: every lane ends with every sum
-#pragma unroll
-    for (int j = 0; j < NR; ++j)
-#pragma unroll
-        for (int m = 0; m < GEMV_MAX_M; ++m)
-            if (m < M) acc[j][m] = warp_sum(acc[j][m]);
-
-    // ---------------------------------------------------------- epilogues
-    if constexpr (EPI == EPI_QKV) {
-        if (valid && lane < M) {
-            const int m = lane;
-            float v0 = 0.f, v1 = 0.f;
-#pragma unroll
-            for (int mm = 0; mm < GEMV_MAX_M; ++mm)
-                if (mm == m) { v0 = acc[0][mm]; v1 = acc[1][mm]; }
-            if (a.bias) {
-                v0 = __fadd_rn(v0, a.bias[row[0]]);
-                v1 = __fadd_rn(v1, a.bias[row[1]]);
-            }
-            const int h = row[0] / a.hd, i = row[0] % a.hd;
-            const RowMeta rm = a.meta[m];
-            if (h < a.n_q_heads + a.n_kv_heads) rope_pair(v0, v1, rm.pos, i, a.rope_ts);
-            if (h < a.n_q_heads) {
-                float* q = a.y + (size_t)m * a.y_stride + h * a.hd;
-                q[i] = v0;
-                q[i + a.hd / 2] = v1;
-            } else {
-                const bool is_k = h < a.n_q_heads + a.n_kv_heads;
-                const int kvh = is_k ? h - a.n_q_heads : h - a.n_q_heads - a.n_kv_heads;
-                __half* dst = (is_k ? a.kv.k : a.kv.v) + kv_offset(a.kv, rm.seq, rm.cidx, kvh);
-                dst[i] = __float2half_rn(v0);
-                dst[i + a.hd / 2] = __float2half_rn(v1);
-            }
-        }
-    } else if constexpr (EPI == EPI_SWIGLU) {
-        if (valid && lane < M) {
-            float g = 0.f, up = 0.f;
-#pragma unroll
-            for (int mm = 0; mm < GEMV_MAX_M; ++mm)
-                if (mm == lane) { g = acc[0][mm]; up = acc[1][mm]; }
-            a.y[(size_t)lane * a.y_stride + row[0]] = __fmul_rn(silu_ref(g), up);
-        }
-    } else if constexpr (EPI == EPI_RESID || EPI == EPI_STORE) {
-        if (valid && lane < NR * M) {
-            const int j = lane / M, m = lane % M;
-            float v = 0.f;
-            int r = -1;
-#pragma unroll
-            for (int jj = 0; jj < NR; ++jj)
-#pragma unroll
-                for (int mm = 0; mm < GEMV_MAX_M; ++mm)
-                    if (jj == j && mm == m) { v = acc[jj][mm]; r = row[jj]; }
-            if (r >= 0) {
-                if (a.bias) v = __fadd_rn(v, a.bias[r]);
-                float* dst = a.y + (size_t)m * a.y_stride + r;
-                if (EPI == EPI_RESID) *dst = __fadd_rn(*dst, v);   // ggml_add(x, o)
-                else *dst = v;
-            }
-        }
-    } else if constexpr (EPI == EPI_ARGMAX) {
-        if (valid && lane < M) {
-            const int m = lane;
-            unsigned long long k = 0ull;
+        for (int m = 0; m < MB; ++m) {
+            if (m >= M) break;
+            const float4 av = reinterpret_cast<const float4*>(act + (size_t)m * K + c * 16)[g];
+            const float2 a01 = make_float2(av.x, av.y), a23 = make_float2(av.z, av.w);
 #pragma unroll
             for (int j = 0; j < NR; ++j) {
-                float v = 0.f;
-#pragma unroll
-                for (int mm = 0; mm < GEMV_MAX_M; ++mm)
-                    if (mm == m) v = acc[j][mm];
-                if (row[j] >= 0) {
-                    if (a.y) a.y[(size_t)m * a.y_stride + row[j]] = v;
-                    const unsigned long long kk = argmax_key(v, row[j]);
-                    k = kk > k ? kk : k;
-                }
+                acc2[j][m] = __ffma2_rn(make_float2(w[j][0], w[j][1]), a01, acc2[j][m]);
+                acc2[j][m] = __ffma2_rn(make_float2(w[j][2], w[j][3]), a23, acc2[j][m]);
             }
-            atomicMax(&best[m], k);
         }
-        __syncthreads();
-        if (threadIdx.x < M) atomicMax(a.argmax + threadIdx.x, best[threadIdx.x]);
     }
 }
 
-template <int WT, int NR, int EPI>
-cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
-    const size_t smem = act_smem_bytes(WT, a.M, a.K);
-    if (smem > GEMV_SMEM_MAX) return cudaErrorInvalidValue;   // gemv_prepare() opted in up to this
-    auto kern = k_gemv<WT, NR, EPI>;
-    const int grid = (a.n_units + GEMV_WARPS - 1) / GEMV_WARPS;
-    kern<<<grid, GEMV_THREADS, smem, st>>>(a);
-    note_launch();
-    return cudaGetLastError();
+template <int WT, int EPI, int MB>
+__global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
+    extern __shared__ __align__(16) float act[];
+    __shared__ unsigned long long best[GEMV_MAX_M];
+    __shared__ float part[GEMV_WARPS][NR * GEMV_MAX_M];
+    __shared__ float rope_c[EPI == EPI_QKV ? GEMV_MAX_M : 1][EPI == EPI_QKV ? 64 : 1];
+    __shared__ float rope_s[EPI == EPI_QKV ? GEMV_MAX_M : 1][EPI == EPI_QKV ? 64 : 1];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int M = a.M, K = a.K;
+    const Work w = make_work(a, warp);
+    const int my_groups = blockIdx.x < w.n_groups ? (w.n_groups - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const int n_items = my_groups * w.n_it;
+
+    // weights do not depend on the previous kernel: issue the first item's
+    // loads, then wait for the producer of the activations
+    Chunk A[NR], B[NR];
+    if (n_items > 0) load_item<WT, EPI>(a, w, blockIdx.x, 0, lane, A);
+    pdl_launch();
+    pdl_wait();
+    if (EPI == EPI_ARGMAX && threadIdx.x < GEMV_MAX_M) best[threadIdx.x] = 0ull;
+    if constexpr (EPI == EPI_QKV) {
+        // NEOX cos/sin per (row, pair) with ggml's CPU theta recurrence, once per CTA
+        const int half = a.hd / 2;
+        for (int t = threadIdx.x; t < M * half; t += GEMV_THREADS) {
+            const int m = t / half, i = t % half;
+            float th = (float)a.meta[m].pos;
+            for (int k = 0; k < i; ++k) th = __fmul_rn(th, a.rope_ts);
+            rope_c[m][i] = cosf(th);
+            rope_s[m][i] = sinf(th);
+        }
+    }
+    stage_activations(a, act);   // ends with __syncthreads
+
+    float2 acc2[NR][MB];
+#pragma unroll
+    for (int j = 0; j < NR; ++j)
+#pragma unroll
+        for (int m = 0; m < MB; ++m) acc2[j][m] = make_float2(0.f, 0.f);
+
+    int row[NR], which[NR];
+    // one flattened item sequence per warp, ping-ponged between register sets
+    // A and B so the next item's loads are in flight while one is computed
+    auto finish = [&](int i) {
+        // called after item i; if it closed a group: reduce, epilogue, reset
+        if ((i % w.n_it) != w.n_it - 1) return;
+        const int group = blockIdx.x + (i / w.n_it) * gridDim.x;
+        const int u = group * w.upc + w.slot;
+#pragma unroll
+        for (int j = 0; j < NR; ++j)
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                const float v = (m < M) ? warp_sum(acc2[j][m].x + acc2[j][m].y) : 0.f;
+                acc2[j][m] = make_float2(0.f, 0.f);
+                if (lane == j * M + m && m < M) part[warp][lane] = v;
+            }
+        __syncthreads();
+        if (w.sub == 0 && u < a.n_units) {
+            unit_rows<EPI>(a, u, row, which);
+            float v = 0.f;
+            int jj = 0, mm = 0;
+            if (lane < NR * M) {
+                jj = lane / M;
+                mm = lane % M;
+                for (int s2 = 0; s2 < w.wpu; ++s2) v += part[warp + s2][lane];
+            }
+            if constexpr (EPI == EPI_QKV) {
+                // lanes (j, m): NEOX partners j and j+2 sit in lanes L and L + 2M
+                if (a.bias && lane < NR * M) v = __fadd_rn(v, a.bias[row[jj]]);
+                const float partner = __shfl_down_sync(0xffffffffu, v, 2 * M);
+                if (lane < 2 * M) {
+                    const int r0 = row[jj];
+                    const int h = r0 / a.hd, i2 = r0 % a.hd;
+                    const RowMeta rm = a.meta[mm];
+                    float x0 = v, x1 = partner;
+                    if (h < a.n_q_heads + a.n_kv_heads) {
+                        const float c = rope_c[mm][i2], s = rope_s[mm][i2];
+                        const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+                        const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+                        x0 = y0;
+                        x1 = y1;
+                    }
+                    if (h < a.n_q_heads) {
+                        float* q = a.y + (size_t)mm * a.y_stride + h * a.hd;
+                        q[i2] = x0;
+                        q[i2 + a.hd / 2] = x1;
+                    } else {
+                        const bool is_k = h < a.n_q_heads + a.n_kv_heads;
+                        const int kvh = is_k ? h - a.n_q_heads : h - a.n_q_heads - a.n_kv_heads;
+                        __half* dst = (is_k ? a.kv.k : a.kv.v) + kv_offset(a.kv, rm.seq, rm.cidx, kvh);
+                        dst[i2] = __float2half_rn(x0);
+                        dst[i2 + a.hd / 2] = __float2half_rn(x1);
+                    }
+                }
+            } else if constexpr (EPI == EPI_SWIGLU) {
+                const float up = __shfl_down_sync(0xffffffffu, v, 2 * M);
+                if (lane < 2 * M) a.y[(size_t)mm * a.y_stride + row[jj]] = __fmul_rn(silu_ref(v), up);
+            } else if constexpr (EPI == EPI_RESID || EPI == EPI_STORE) {
+                if (lane < NR * M && row[jj] < a.w0.rows) {
+                    if (a.bias) v = __fadd_rn(v, a.bias[row[jj]]);
+                    float* dst = a.y + (size_t)mm * a.y_stride + row[jj];
+                    if (EPI == EPI_RESID) *dst = __fadd_rn(*dst, v);   // ggml_add(x, o)
+                    else *dst = v;
+                }
+            } else if constexpr (EPI == EPI_ARGMAX) {
+                unsigned long long k = 0ull;
+                if (lane < NR * M && row[jj] < a.w0.rows) {
+                    if (a.y) a.y[(size_t)mm * a.y_stride + row[jj]] = v;
+                    k = argmax_key(v, row[jj]);
+                }
+                // max over the NR rows of each m (lanes m, m+M, m+2M, m+3M)
+                for (int o = M; o < NR * M; o <<= 1) {
+                    const unsigned long long k2 = __shfl_down_sync(0xffffffffu, k, o);
+                    k = k2 > k ? k2 : k;
+                }
+                if (lane < M) atomicMax(&best[lane], k);
+            }
+        }
+        __syncthreads();   // part[] is reused by the next group
+    };
+    auto item_chunk = [&](int i) { return (w.sub + (i % w.n_it) * w.wpu) * 32 + lane; };
+    auto item_group = [&](int i) { return blockIdx.x + (i / w.n_it) * gridDim.x; };
+    for (int i = 0; i < n_items; i += 2) {
+        if (i + 1 < n_items) load_item<WT, EPI>(a, w, item_group(i + 1), (i + 1) % w.n_it, lane, B);
+        {
+            const int c = item_chunk(i);
+            if (c < w.nchunk) compute_item<WT, MB>(A, act, K, M, c, acc2);
+        }
+        finish(i);
+        if (i + 1 < n_items) {
+            if (i + 2 < n_items) load_item<WT, EPI>(a, w, item_group(i + 2), (i + 2) % w.n_it, lane, A);
+            const int c = item_chunk(i + 1);
+            if (c < w.nchunk) compute_item<WT, MB>(B, act, K, M, c, acc2);
+            finish(i + 1);
+        }
+    }
+    if constexpr (EPI == EPI_ARGMAX) {
+        __syncthreads();
+        if (threadIdx.x < M && best[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, best[threadIdx.x]);
+    }
 }
 
-template <int EPI, int NR>
+template <int WT, int EPI>
+cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
+    const size_t smem = (size_t)a.M * a.K * sizeof(float);
+    if (smem > GEMV_SMEM_MAX) return cudaErrorInvalidValue;
+    // persistent grid: one wave of resident CTAs at most
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    GemvArgs b = a;
+    const int niter = (a.K / 16 + 31) / 32;
+    b.wpu = 1;
+    while (b.wpu * 2 <= GEMV_WARPS && b.wpu * 2 <= niter) b.wpu *= 2;   // warps per unit <= items per row
+    const int upc = GEMV_WARPS / b.wpu;
+    const int n_groups = (a.n_units + upc - 1) / upc;
+    int per_sm = 1;
+    if (a.M <= 2) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemv<WT, EPI, 2>, GEMV_THREADS, smem);
+    else cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_gemv<WT, EPI, GEMV_MAX_M>, GEMV_THREADS, smem);
+    const int cap = sms * (per_sm > 0 ? per_sm : 1);
+    const int grid = n_groups < cap ? n_groups : cap;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = a.M <= 2 ? cudaLaunchKernelEx(&cfg, k_gemv<WT, EPI, 2>, b)
+                             : cudaLaunchKernelEx(&cfg, k_gemv<WT, EPI, GEMV_MAX_M>, b);
+    note_launch();
+    return e;
+}
+
+template <int EPI>
 cudaError_t launch_wt(const GemvArgs& a, cudaStream_t st) {
     switch (a.w0.type) {
-        case W_Q8_0: return launch_t<W_Q8_0, NR, EPI>(a, st);
-        case W_Q5_K: return launch_t<W_Q5_K, NR, EPI>(a, st);
-        case W_Q6_K: return launch_t<W_Q6_K, NR, EPI>(a, st);
-        case W_F32: return launch_t<W_F32, NR, EPI>(a, st);
-        case W_F16: return launch_t<W_F16, NR, EPI>(a, st);
+        case W_Q8_0: return launch_t<W_Q8_0, EPI>(a, st);
+        case W_Q5_K: return launch_t<W_Q5_K, EPI>(a, st);
+        case W_Q6_K: return launch_t<W_Q6_K, EPI>(a, st);
+        case W_F32: return launch_t<W_F32, EPI>(a, st);
+        case W_F16: return launch_t<W_F16, EPI>(a, st);
         default: return cudaErrorInvalidValue;
     }
 }
 
-template <int EPI, int NR>
+template <int EPI>
 cudaError_t prepare_wt() {
-    const void* fns[] = {(const void*)k_gemv<W_Q8_0, NR, EPI>, (const void*)k_gemv<W_Q5_K, NR, EPI>,
-                         (const void*)k_gemv<W_Q6_K, NR, EPI>, (const void*)k_gemv<W_F32, NR, EPI>,
-                         (const void*)k_gemv<W_F16, NR, EPI>};
+    const void* fns[] = {(const void*)k_gemv<W_Q8_0, EPI, 2>, (const void*)k_gemv<W_Q5_K, EPI, 2>,
+                         (const void*)k_gemv<W_Q6_K, EPI, 2>, (const void*)k_gemv<W_F32, EPI, 2>,
+                         (const void*)k_gemv<W_F16, EPI, 2>,
+                         (const void*)k_gemv<W_Q8_0, EPI, GEMV_MAX_M>, (const void*)k_gemv<W_Q5_K, EPI, GEMV_MAX_M>,
+                         (const void*)k_gemv<W_Q6_K, EPI, GEMV_MAX_M>, (const void*)k_gemv<W_F32, EPI, GEMV_MAX_M>,
+                         (const void*)k_gemv<W_F16, EPI, GEMV_MAX_M>};
     for (const void* f : fns) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_SMEM_MAX);
         if (e != cudaSuccess) return e;
@@ -557,40 +514,49 @@ cudaError_t prepare_wt() {
 
 }  // namespace
 
-size_t gemv_smem_bytes(int wt, int M, int K) { return act_smem_bytes(wt, M, K); }
+size_t gemv_smem_bytes(int wt, int M, int K) {
+    (void)wt;
+    return (size_t)M * K * sizeof(float);
+}
+
+int gemv_max_rows(int K) {
+    const int m = (int)(GEMV_SMEM_MAX / ((size_t)K * sizeof(float)));
+    return m < GEMV_MAX_M ? m : GEMV_MAX_M;
+}
 
 // Opt every instantiation in to large dynamic shared memory once per device,
 // before any launch or stream capture.
 cudaError_t gemv_prepare() {
     cudaError_t e;
-    if ((e = prepare_wt<EPI_QKV, 2>()) != cudaSuccess) return e;
-    if ((e = prepare_wt<EPI_SWIGLU, 2>()) != cudaSuccess) return e;
-    if ((e = prepare_wt<EPI_RESID, 2>()) != cudaSuccess) return e;
-    if ((e = prepare_wt<EPI_STORE, 4>()) != cudaSuccess) return e;
-    return prepare_wt<EPI_ARGMAX, 4>();
+    if ((e = prepare_wt<EPI_QKV>()) != cudaSuccess) return e;
+    if ((e = prepare_wt<EPI_SWIGLU>()) != cudaSuccess) return e;
+    if ((e = prepare_wt<EPI_RESID>()) != cudaSuccess) return e;
+    if ((e = prepare_wt<EPI_STORE>()) != cudaSuccess) return e;
+    return prepare_wt<EPI_ARGMAX>();
 }
 
 cudaError_t gemv_launch(GemvArgs a, cudaStream_t st) {
-    if (a.M < 1 || a.M > GEMV_MAX_M) return cudaErrorInvalidValue;
+    if (a.M < 1 || a.M > GEMV_MAX_M || a.K % 16) return cudaErrorInvalidValue;
     if (a.w0.type == W_Q8_0 && a.K % 32) return cudaErrorInvalidValue;
     if ((a.w0.type == W_Q5_K || a.w0.type == W_Q6_K) && a.K % 256) return cudaErrorInvalidValue;
-    if ((a.w0.type == W_F32 || a.w0.type == W_F16) && a.K % 4) return cudaErrorInvalidValue;
     switch (a.epi) {
         case EPI_QKV:
-            a.n_units = a.w0.rows / 2;
-            return launch_wt<EPI_QKV, 2>(a, st);
+            if (a.hd % 4) return cudaErrorInvalidValue;
+            a.n_units = a.w0.rows / 4;
+            return launch_wt<EPI_QKV>(a, st);
         case EPI_SWIGLU:
-            a.n_units = a.w0.rows;
-            return launch_wt<EPI_SWIGLU, 2>(a, st);
+            if (a.w0.rows % 2) return cudaErrorInvalidValue;
+            a.n_units = a.w0.rows / 2;
+            return launch_wt<EPI_SWIGLU>(a, st);
         case EPI_RESID:
-            a.n_units = (a.w0.rows + 1) / 2;
-            return launch_wt<EPI_RESID, 2>(a, st);
+            a.n_units = (a.w0.rows + NR - 1) / NR;
+            return launch_wt<EPI_RESID>(a, st);
         case EPI_STORE:
-            a.n_units = (a.w0.rows + 3) / 4;
-            return launch_wt<EPI_STORE, 4>(a, st);
+            a.n_units = (a.w0.rows + NR - 1) / NR;
+            return launch_wt<EPI_STORE>(a, st);
         case EPI_ARGMAX:
-            a.n_units = (a.w0.rows + 3) / 4;
-            return launch_wt<EPI_ARGMAX, 4>(a, st);
+            a.n_units = (a.w0.rows + NR - 1) / NR;
+            return launch_wt<EPI_ARGMAX>(a, st);
         default:
             return cudaErrorInvalidValue;
     }

@@ -36,11 +36,13 @@ struct GemvArgs {
     int n_q_heads = 0, n_kv_heads = 0, hd = 0;
     float rope_ts = 0.f;
     unsigned long long* argmax = nullptr;
+    int wpu = 1;                   // warps per unit (set by gemv_launch)
 };
 
 cudaError_t gemv_launch(GemvArgs a, cudaStream_t st);
 size_t gemv_smem_bytes(int wt, int M, int K);
 cudaError_t gemv_prepare();
+int gemv_max_rows(int K);   // activation rows that fit the GEMV's shared memory
 
 // ------------------------------------------------------ decode attention
 struct AttnDecodeArgs {
@@ -55,8 +57,10 @@ struct AttnDecodeArgs {
     float* part = nullptr;         // [M][max_splits][nq][hd] unnormalized partial O
     float* part_ml = nullptr;      // [M][max_splits][nq][2] (running max, sum)
     int* counters = nullptr;       // [M][nkv], zero between launches
+    int* err = nullptr;            // set to nonzero if a bounded wait gave up
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st);
+cudaError_t attn_decode_prepare();
 
 // ------------------------------------------------------------- misc
 long long launch_count();

@@ -225,9 +225,11 @@ class KV:
     def __del__(self):
         self.close()
 
-    def load_prefix(self, seq: int, layer: int, k: np.ndarray, v: np.ndarray) -> None:
-        k = np.ascontiguousarray(k, np.float32)
-        v = np.ascontiguousarray(v, np.float32)
+    def load_prefix(self, seq: int, layer: int, k, v) -> None:
+        """k, v: f32 [n_pos][n_kv*hd], numpy (host) or torch (host or device)."""
+        if not hasattr(k, "data_ptr"):
+            k = np.ascontiguousarray(k, np.float32)
+            v = np.ascontiguousarray(v, np.float32)
         _chk(lib().vvq2_kv_load_prefix(self.kv, seq, layer, _p(k), _p(v), k.shape[0]))
 
     def read(self, seq: int, layer: int, n_pos: int):
