@@ -192,6 +192,12 @@ const char* vvq2_last_error(void);
 /* Number of this library's kernels launched so far in this process (bench). */
 int64_t vvq2_kernel_launches(void);
 
+/* ---- test hook (no counterpart in the reference) ----------------------
+ * y f32 [t][n] = x [t][k] . W[n][k]^T through the tensor-core (tcgen05) GEMM
+ * used for prefill: x rounded to f16, W (host GGUF blocks of `type`)
+ * dequantized exactly and rounded to f16, f32 accumulation.  k % 64 == 0. */
+int  vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int t, float* y);
+
 /* ---- measurement (no counterpart in the reference, which has no profiler
  * hooks; used by bench.py for the roofline figure) -------------------------
  * While enabled, vvq2_decode_step brackets every GEMV (kind 0) and attention

@@ -248,8 +248,11 @@ __global__ void __launch_bounds__(AD_THREADS) k_attn_decode(const AttnDecodeArgs
             const int h = hs + k * HSUB;
             if (h < G) {
                 const float inv = 1.0f / run_sum[h];
-                float2* dst = reinterpret_cast<float2*>(a.out + (size_t)m * a.nq * HD + (size_t)(g * G + h) * HD) + dp;
-                *dst = make_float2(o[k].x * inv, o[k].y * inv);
+                const size_t off = (size_t)m * a.nq * HD + (size_t)(g * G + h) * HD;
+                if (a.out_h)
+                    reinterpret_cast<__half2*>(a.out_h + off)[dp] = __floats2half2_rn(o[k].x * inv, o[k].y * inv);
+                else
+                    reinterpret_cast<float2*>(a.out + off)[dp] = make_float2(o[k].x * inv, o[k].y * inv);
             }
         }
         return;
@@ -315,8 +318,11 @@ __global__ void __launch_bounds__(AD_THREADS) k_attn_decode(const AttnDecodeArgs
             num.x = fmaf(wts[h][ss], p.x, num.x);
             num.y = fmaf(wts[h][ss], p.y, num.y);
         }
-        reinterpret_cast<float2*>(a.out + (size_t)m * a.nq * HD + (size_t)qh * HD)[d2] =
-            make_float2(num.x * inv_den[h], num.y * inv_den[h]);
+        const size_t off = (size_t)m * a.nq * HD + (size_t)qh * HD;
+        if (a.out_h)
+            reinterpret_cast<__half2*>(a.out_h + off)[d2] = __floats2half2_rn(num.x * inv_den[h], num.y * inv_den[h]);
+        else
+            reinterpret_cast<float2*>(a.out + off)[d2] = make_float2(num.x * inv_den[h], num.y * inv_den[h]);
     }
     if (tid == 0) a.counters[m * a.nkv + g] = 0;   // ready for the next launch
 }

@@ -27,6 +27,39 @@ using namespace vvq2;
 
 namespace {
 
+constexpr int PREFILL_ROWS = 512;   // token rows per tensor-core chunk
+
+// cuTensorMapEncodeTiled from the driver, fetched through the runtime (no -lcuda)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D f16 activation matrix [rows][cols] (row-major) as a TMA map with a
+// 64 x 128 box and the 128-byte swizzle the UMMA descriptors assume
+bool make_act_map(CUtensorMap* m, const __half* base, int rows, int cols) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || cols % 64 || ((uintptr_t)base & 15)) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 thread_local std::string g_err;
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
@@ -99,6 +132,9 @@ struct vvq2_ctx {
     std::vector<void*> allocs;
     // scratch for up to GEMV_MAX_M activation rows
     float *X = nullptr, *Q = nullptr, *ATT = nullptr, *FA = nullptr, *LOGITS = nullptr;
+    // prefill (tensor-core) scratch for up to PREFILL_ROWS token rows
+    __half *Xh = nullptr, *ATTh = nullptr, *Ah = nullptr;
+    float2* rope_cs = nullptr;
     float *part = nullptr, *part_ml = nullptr;
     int* counters = nullptr;
     RowMeta* meta = nullptr;
@@ -408,6 +444,91 @@ int run_layers_decode(vvq2_ctx* c, vvq2_kv* kv, int M, int split, int nsplit, in
     return 0;
 }
 
+// One pass over layers for M (<= PREFILL_ROWS) rows in c->X with metadata in
+// c->meta, on the tensor-core path: RMSNorm->f16, tcgen05 GEMMs with fused
+// epilogues, and flash attention over each row's causal prefix.
+int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, int first, int n_layers, cudaStream_t st) {
+    const vvq2_hparams& hp = c->hp;
+    const int H = hp.hidden_size, nq = hp.n_heads, nkv = hp.n_kv_heads, hd = hp.head_dim;
+    const int F = hp.intermediate_size, qw = nq * hd;
+    CU(rope_table_launch(c->meta, M, hd, c->rope_ts, c->rope_cs, st));
+    CUtensorMap mapX, mapA, mapF;
+    if (!make_act_map(&mapX, c->Xh, M, H) || !make_act_map(&mapA, c->ATTh, M, qw) || !make_act_map(&mapF, c->Ah, M, F))
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "activation tensor map (dims %d/%d/%d must be multiples of 64)", H, qw, F);
+    for (int li = first; li < first + n_layers; ++li) {
+        const vvq2_ctx::Layer& L = c->layers[li];
+        const KvLayer kvl = kv->layer(li);
+        GemmArgs g;
+        g.T = M;
+        g.meta = c->meta;
+        g.kv = kvl;
+        g.nq = nq;
+        g.nkv = nkv;
+        g.hd = hd;
+        g.rope_cs = c->rope_cs;
+        g.err = c->err;
+        // 1. RMSNorm -> f16, QKV GEMM (+bias, RoPE, K/V append; Q f32)
+        CU(rmsnorm_f16_launch(c->X, L.attn_norm, M, H, hp.rms_norm_eps, c->Xh, st));
+        GemmArgs q = g;
+        q.w0 = L.qkv;
+        q.N = L.qkv.rows;
+        q.K = H;
+        q.epi = EPI_QKV;
+        q.bias = L.qkv_bias;
+        q.y = c->Q;
+        q.y_stride = qw;
+        CU(gemm_tc_launch(q, mapX, st));
+        // 2. causal attention, one CTA per (row, kv head), f16 output
+        AttnDecodeArgs ad;
+        ad.q = c->Q;
+        ad.out_h = c->ATTh;
+        ad.meta = c->meta;
+        ad.kv = kvl;
+        ad.M = M;
+        ad.nq = nq;
+        ad.nkv = nkv;
+        ad.hd = hd;
+        ad.split = (max_lim + KV_PAGE - 1) / KV_PAGE * KV_PAGE;
+        ad.max_splits = 1;
+        ad.scale = 1.0f / sqrtf((float)hd);
+        ad.part = c->part;
+        ad.part_ml = c->part_ml;
+        ad.counters = c->counters;
+        ad.err = c->err;
+        CU(attn_decode_launch(ad, st));
+        // 3. O-proj + residual
+        GemmArgs o = g;
+        o.w0 = L.o;
+        o.N = H;
+        o.K = qw;
+        o.epi = EPI_RESID;
+        o.y = c->X;
+        o.y_stride = H;
+        CU(gemm_tc_launch(o, mapA, st));
+        // 4. RMSNorm -> f16, gate/up GEMM with SwiGLU epilogue (f16 out)
+        CU(rmsnorm_f16_launch(c->X, L.ffn_norm, M, H, hp.rms_norm_eps, c->Xh, st));
+        GemmArgs f = g;
+        f.w0 = L.gate;
+        f.w1 = L.up;
+        f.N = F;
+        f.K = H;
+        f.epi = EPI_SWIGLU;
+        f.yh = c->Ah;
+        f.yh_stride = F;
+        CU(gemm_tc_launch(f, mapX, st));
+        // 5. down + residual
+        GemmArgs d = g;
+        d.w0 = L.down;
+        d.N = H;
+        d.K = F;
+        d.epi = EPI_RESID;
+        d.y = c->X;
+        d.y_stride = H;
+        CU(gemm_tc_launch(d, mapF, st));
+    }
+    return 0;
+}
+
 // Whole decode step on the stream: embed(c->tok) -> layers -> output_norm ->
 // lm_head -> argmax -> c->tok, then every row's metadata moves one position on.
 int enqueue_decode(vvq2_ctx* c, vvq2_kv* kv, int M, int split, int nsplit, cudaStream_t st,
@@ -500,23 +621,30 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
         return fail(VVQ2_ERR_CUDA, "stream create failed");
     }
     const int M = GEMV_MAX_M;
+    const int P = PREFILL_ROWS;
     const int qw = hp->n_heads * hp->head_dim;
     const int F = std::max(hp->intermediate_size, 1);
     int rc = 0;
-    rc = rc ? rc : c->alloc(&c->X, (size_t)M * hp->hidden_size);
-    rc = rc ? rc : c->alloc(&c->Q, (size_t)M * qw);
+    if (cudaSuccess != gemm_tc_prepare()) rc = fail(VVQ2_ERR_CUDA, "gemm prepare failed");
+    if (!encode_fn()) rc = rc ? rc : fail(VVQ2_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    rc = rc ? rc : c->alloc(&c->X, (size_t)P * hp->hidden_size);
+    rc = rc ? rc : c->alloc(&c->Q, (size_t)P * qw);
+    rc = rc ? rc : c->alloc(&c->Xh, (size_t)P * std::max(hp->hidden_size, qw));
+    rc = rc ? rc : c->alloc(&c->ATTh, (size_t)P * qw);
+    rc = rc ? rc : c->alloc(&c->Ah, (size_t)P * F);
+    rc = rc ? rc : c->alloc(&c->rope_cs, (size_t)P * hp->head_dim / 2);
     rc = rc ? rc : c->alloc(&c->ATT, (size_t)M * qw);
     rc = rc ? rc : c->alloc(&c->FA, (size_t)M * F);
     rc = rc ? rc : c->alloc(&c->part, (size_t)M * c->max_splits_cap * qw);
     rc = rc ? rc : c->alloc(&c->part_ml, (size_t)M * c->max_splits_cap * hp->n_heads * 2);
     rc = rc ? rc : c->alloc(&c->counters, (size_t)M * hp->n_kv_heads);
-    rc = rc ? rc : c->alloc(&c->meta, (size_t)M);
+    rc = rc ? rc : c->alloc(&c->meta, (size_t)P);
     rc = rc ? rc : c->alloc(&c->amax, (size_t)M);
     rc = rc ? rc : c->alloc(&c->tok, (size_t)M);
     rc = rc ? rc : c->alloc(&c->err, (size_t)1);
     c->max_rows = std::min(GEMV_MAX_M, gemv_max_rows(std::max({hp->hidden_size, qw, F})));
     if (!rc && hp->vocab_size > 0) rc = c->alloc(&c->LOGITS, (size_t)M * hp->vocab_size);
-    if (!rc && cudaMallocHost(&c->meta_host, sizeof(RowMeta) * M) != cudaSuccess)
+    if (!rc && cudaMallocHost(&c->meta_host, sizeof(RowMeta) * P) != cudaSuccess)
         rc = fail(VVQ2_ERR_OUT_OF_MEMORY, "pinned alloc failed");
     if (!rc && (cudaMemset(c->counters, 0, sizeof(int) * M * hp->n_kv_heads) != cudaSuccess ||
                 cudaMemset(c->err, 0, sizeof(int)) != cudaSuccess))
@@ -761,9 +889,12 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
     // Token chunks of at most GEMV_MAX_M rows over all sequences; each chunk
     // runs through every layer before the next (resident chunked prefill,
     // the ordering tests/test_qwen2_resident.cpp checks).
-    const int tok_per_chunk = std::max(1, c->max_rows / n_seqs);
-    if (n_seqs > c->max_rows)
-        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "more than %d sequences per call", c->max_rows);
+    // Few rows: decode GEMV path.  Otherwise tensor-core chunks of up to
+    // PREFILL_ROWS rows.
+    const bool tc_path = n_seqs * n_tok > c->max_rows;
+    if (n_seqs > PREFILL_ROWS)
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "more than %d sequences per call", PREFILL_ROWS);
+    const int tok_per_chunk = std::max(1, (tc_path ? PREFILL_ROWS : c->max_rows) / n_seqs);
     for (int t0 = 0; t0 < n_tok; t0 += tok_per_chunk) {
         const int nt = std::min(tok_per_chunk, n_tok - t0);
         const int M = n_seqs * nt;
@@ -782,9 +913,13 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
             CU(cudaMemcpyAsync(c->X + (size_t)s * nt * H, x + ((size_t)s * n_tok + t0) * H,
                                sizeof(float) * nt * H, x_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
         c->meta_kv = nullptr;   // c->meta no longer describes a decode step
-        int split = 0, nsplit = 0;
-        choose_split(c, M, max_lim, &split, &nsplit);
-        if (int rc = run_layers_decode(c, kv, M, split, nsplit, first_layer, n_layers, st, nullptr, 0.0)) return rc;
+        if (tc_path && M > c->max_rows) {
+            if (int rc = run_layers_prefill(c, kv, M, max_lim, first_layer, n_layers, st)) return rc;
+        } else {
+            int split = 0, nsplit = 0;
+            choose_split(c, M, max_lim, &split, &nsplit);
+            if (int rc = run_layers_decode(c, kv, M, split, nsplit, first_layer, n_layers, st, nullptr, 0.0)) return rc;
+        }
         if (flags & VVQ2_OUTPUT_NORM) CU(rmsnorm_launch(c->X, c->out_norm, M, H, c->hp.rms_norm_eps, c->X, st));
         const cudaMemcpyKind k = y_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
         for (int s = 0; s < n_seqs; ++s) {
@@ -1027,6 +1162,52 @@ int vvq2_rms_norm(const float* x, const float* w, int rows, int n, float eps, fl
     cudaFree(dx);
     cudaFree(dw);
     if (e != cudaSuccess) return fail(VVQ2_ERR_CUDA, "rms_norm: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+int vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int t, float* y) {
+    if (!w || !x || !y || n <= 0 || k <= 0 || t <= 0 || k % 64) return fail(VVQ2_ERR_INVALID_ARG, "bad gemm args");
+    if (vvq2_device_count() == 0) return fail(VVQ2_ERR_NO_DEVICE, "no sm_100 device");
+    if (gemm_tc_prepare() != cudaSuccess) return fail(VVQ2_ERR_CUDA, "gemm prepare failed");
+    vvq2_ctx tmp;
+    vvq2_tensor tw{w, type, k, n};
+    DevW dw;
+    int rc = upload_tensor(&tmp, tw, &dw, 0, 0, "debug_gemm");
+    float *dx = nullptr, *dy = nullptr;
+    __half* dxh = nullptr;
+    int* derr = nullptr;
+    if (!rc) rc = tmp.alloc(&dx, (size_t)t * k);
+    if (!rc) rc = tmp.alloc(&dxh, (size_t)t * k);
+    if (!rc) rc = tmp.alloc(&dy, (size_t)t * n);
+    if (!rc) rc = tmp.alloc(&derr, (size_t)1);
+    cudaError_t e = cudaSuccess;
+    if (!rc) {
+        e = cudaMemcpy(dx, x, sizeof(float) * t * k, cudaMemcpyDefault);
+        if (e == cudaSuccess) e = cudaMemset(derr, 0, sizeof(int));
+        if (e == cudaSuccess) e = to_f16_launch(dx, (int64_t)t * k, dxh, 0);
+        CUtensorMap map;
+        if (e == cudaSuccess && !make_act_map(&map, dxh, t, k)) rc = fail(VVQ2_ERR_CUDA, "tensor map");
+        if (!rc && e == cudaSuccess) {
+            GemmArgs g;
+            g.w0 = dw;
+            g.T = t;
+            g.N = n;
+            g.K = k;
+            g.epi = EPI_STORE;
+            g.y = dy;
+            g.y_stride = n;
+            g.err = derr;
+            e = gemm_tc_launch(g, map, 0);
+        }
+        if (!rc && e == cudaSuccess) e = cudaDeviceSynchronize();
+        int herr = 0;
+        if (!rc && e == cudaSuccess) e = cudaMemcpy(&herr, derr, sizeof(int), cudaMemcpyDeviceToHost);
+        if (!rc && e == cudaSuccess && herr) rc = fail(VVQ2_ERR_CUDA, "gemm wait timed out (%d)", herr);
+        if (!rc && e == cudaSuccess) e = cudaMemcpy(y, dy, sizeof(float) * t * n, cudaMemcpyDefault);
+    }
+    for (void* p : tmp.allocs) cudaFree(p);
+    if (rc) return rc;
+    if (e != cudaSuccess) return fail(VVQ2_ERR_CUDA, "debug gemm: %s", cudaGetErrorString(e));
     return 0;
 }
 

@@ -1,0 +1,418 @@
+// gemm_tc.cu -- prefill-sized (> 8 rows) dequant GEMM on the 5th-generation
+// tensor cores (tcgen05 + TMEM), sm_100a.
+//
+// Y[T, N] = X[T, K] . W[N, K]^T for every linear of the Qwen2 layer when a
+// call carries more token rows than the decode GEMV handles
+// (src/qwen2.cpp:19-26,274-276,349, the SwiGLU FFN at :33-40).  GGUF blocks
+// cannot feed the tensor cores directly, so the weight operand is produced in
+// shared memory by dequantizing warps: ggml's dequantize_row_* values (exact
+// f32) rounded once to f16, written in the K-major 128-byte-swizzled layout
+// the UMMA descriptor expects.  Activations arrive as f16 via TMA (same
+// swizzle).  One thread issues tcgen05.mma (kind::f16, f32 accumulate) into
+// two 128x128 TMEM accumulators, so each dequantized weight tile serves 256
+// token rows.  Epilogue warps read TMEM with tcgen05.ld and apply the fused
+// epilogue: QKV (+bias, NEOX RoPE, K/V into the f16 paged cache), residual
+// add, SwiGLU (gate/up tiles interleaved), or a plain store.
+//
+// CTA: 6 warps.  warp 0: TMEM allocation + TMA producer (lane 0);
+// warp 1: MMA issuer (lane 0); warps 2-5: weight producers, then epilogue.
+// Pipeline: 4 stages of {A0, A1, B} 16 KB tiles (BK = 64), mbarriers full/empty.
+// Every wait is bounded; a timeout sets args.err and unwinds without leaving
+// TMEM allocated.
+#include "common.cuh"
+#include "kernels.h"
+#include "tc.cuh"
+
+namespace vvq2 {
+
+namespace {
+
+constexpr int BM = 128;       // token rows per accumulator (two accumulators per CTA)
+constexpr int BN = 128;       // output features per CTA
+constexpr int BK = 64;        // K per stage (128 bytes of f16: one swizzle row)
+constexpr int STAGES = 4;
+constexpr int TILE_BYTES = BM * BK * 2;                 // 16 KB
+constexpr int STAGE_BYTES = 3 * TILE_BYTES;             // A0, A1, B
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 256;
+
+__device__ __forceinline__ void store_chunk(uint8_t* btile, int p, int j, uint4 v) {
+    *reinterpret_cast<uint4*>(btile + p * 128 + ((j ^ (p & 7)) * 16)) = v;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t wsel(const uint4& v, int t) {
+    return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w;
+}
+
+// Dequantize elements [k0, k0 + 64) of weight row `row` into 8 swizzled
+// 16-byte chunks of row p of the B tile (exact ggml values, then f16 RNE).
+template <int WT>
+__device__ __forceinline__ void produce_row(const DevW& W, int row, int k0, uint8_t* btile, int p) {
+    if (row < 0 || row >= W.rows) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) store_chunk(btile, p, j, make_uint4(0, 0, 0, 0));
+        return;
+    }
+    const uint8_t* rp = W.q + (size_t)row * W.row_stride;
+    if constexpr (WT == W_Q8_0) {
+        const uint4* qp = reinterpret_cast<const uint4*>(rp + k0);
+        uint4 q[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q[i] = __ldg(qp + i);
+        const __half2 dd = *reinterpret_cast<const __half2*>(W.d + (size_t)row * (W.cols / 32) + k0 / 32);
+        const float d0 = __low2float(dd), d1 = __high2float(dd);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float d = j < 4 ? d0 : d1;
+            const uint32_t w0 = wsel(q[j / 2], (j % 2) * 2), w1 = wsel(q[j / 2], (j % 2) * 2 + 1);
+            uint4 o;
+            o.x = pack_h2(__fmul_rn((float)(int8_t)(w0 & 0xff), d), __fmul_rn((float)(int8_t)((w0 >> 8) & 0xff), d));
+            o.y = pack_h2(__fmul_rn((float)(int8_t)((w0 >> 16) & 0xff), d), __fmul_rn((float)(int8_t)(w0 >> 24), d));
+            o.z = pack_h2(__fmul_rn((float)(int8_t)(w1 & 0xff), d), __fmul_rn((float)(int8_t)((w1 >> 8) & 0xff), d));
+            o.w = pack_h2(__fmul_rn((float)(int8_t)((w1 >> 16) & 0xff), d), __fmul_rn((float)(int8_t)(w1 >> 24), d));
+            store_chunk(btile, p, j, o);
+        }
+    } else if constexpr (WT == W_Q5_K) {
+        const int sb = k0 / 256, qq = (k0 % 256) / 64;    // 64-element chunk qq of the super-block
+        const uint8_t* b = rp + (size_t)sb * Q5K_BYTES;
+        const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(b));
+        uint4 qs[2], qh[2];
+        qs[0] = __ldg(reinterpret_cast<const uint4*>(b + 48 + 32 * qq));
+        qs[1] = __ldg(reinterpret_cast<const uint4*>(b + 48 + 32 * qq) + 1);
+        qh[0] = __ldg(reinterpret_cast<const uint4*>(b + 16));
+        qh[1] = __ldg(reinterpret_cast<const uint4*>(b + 16) + 1);
+        const uint8_t* scb = reinterpret_cast<const uint8_t*>(&hdr) + 4;
+        const __half2 dh = *reinterpret_cast<const __half2*>(&hdr.x);
+        float d1[2], m1[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int j = 2 * qq + h;
+            int s, m;
+            if (j < 4) {
+                s = scb[j] & 63;
+                m = scb[j + 4] & 63;
+            } else {
+                s = (scb[j + 4] & 0xF) | ((scb[j - 4] >> 6) << 4);
+                m = (scb[j + 4] >> 4) | ((scb[j] >> 6) << 4);
+            }
+            d1[h] = __fmul_rn(__low2float(dh), (float)s);
+            m1[h] = __fmul_rn(__high2float(dh), (float)m);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int h = j / 4;                 // first or second 32 elements
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int l = (j % 4) * 8 + e;   // 0..31 within the sub-block
+                const uint32_t qsw = wsel(qs[l / 16], (l % 16) / 4), qhw = wsel(qh[l / 16], (l % 16) / 4);
+                const int qb = (qsw >> (8 * (l % 4))) & 0xff, hb = (qhw >> (8 * (l % 4))) & 0xff;
+                const int q = ((qb >> (4 * h)) & 0xF) + (((hb >> (2 * qq + h)) & 1) ? 16 : 0);
+                f[e] = __fsub_rn(__fmul_rn(d1[h], (float)q), m1[h]);
+            }
+            store_chunk(btile, p, j, make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
+                                                pack_h2(f[6], f[7])));
+        }
+    } else if constexpr (WT == W_Q6_K) {
+        const int sb = k0 / 256, qq = (k0 % 256) / 64, hf = qq >> 1, k0q = (qq & 1) * 2;
+        const uint8_t* b = rp + (size_t)sb * Q6K_PACKED;
+        uint4 ql[4], qh[2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ql[i] = __ldg(reinterpret_cast<const uint4*>(b + hf * 64) + i);
+        qh[0] = __ldg(reinterpret_cast<const uint4*>(b + 128 + hf * 32));
+        qh[1] = __ldg(reinterpret_cast<const uint4*>(b + 128 + hf * 32) + 1);
+        const int8_t* scl = reinterpret_cast<const int8_t*>(b + 192);
+        const float dsb = __half2float(W.d[(size_t)row * (W.cols / 256) + sb]);
+        float ds[4];   // (k - k0q) * 2 + l/16
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) ds[kk * 2 + hh] = __fmul_rn(dsb, (float)scl[hf * 8 + hh + 2 * (k0q + kk)]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int kk = j / 4;                // quarter k = k0q + kk
+            const int k = k0q + kk;
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int l = (j % 4) * 8 + e;   // 0..31
+                const int qlbyte_idx = (k & 1) * 32 + l;   // within the 64 ql bytes of this half
+                const uint32_t lw = wsel(ql[qlbyte_idx / 16], (qlbyte_idx % 16) / 4);
+                const uint32_t hw = wsel(qh[l / 16], (l % 16) / 4);
+                const int lb = (lw >> (8 * (qlbyte_idx % 4))) & 0xff, hb = (hw >> (8 * (l % 4))) & 0xff;
+                const int q = (int)(((lb >> (4 * (k >> 1))) & 0xF) | (((hb >> (2 * k)) & 3) << 4)) - 32;
+                f[e] = __fmul_rn(ds[kk * 2 + l / 16], (float)q);
+            }
+            store_chunk(btile, p, j, make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
+                                                pack_h2(f[6], f[7])));
+        }
+    } else if constexpr (WT == W_F16) {
+        const uint4* hp = reinterpret_cast<const uint4*>(rp + (size_t)k0 * 2);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) store_chunk(btile, p, j, __ldg(hp + j));
+    } else {
+        const float4* fp = reinterpret_cast<const float4*>(rp + (size_t)k0 * 4);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 a = __ldg(fp + 2 * j), c = __ldg(fp + 2 * j + 1);
+            store_chunk(btile, p, j, make_uint4(pack_h2(a.x, a.y), pack_h2(a.z, a.w), pack_h2(c.x, c.y),
+                                                pack_h2(c.z, c.w)));
+        }
+    }
+}
+
+template <int WT, int EPI>
+__global__ void __launch_bounds__(THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], done;
+    __shared__ uint32_t tmem_base;
+    __shared__ int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, t0 = blockIdx.y * (2 * BM);
+    const bool two = t0 + BM < a.T;
+    const int nk = a.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            tc::mbar_init(&full[s], 1 + 128);
+            tc::mbar_init(&empty[s], 1);
+        }
+        tc::mbar_init(&done, 1);
+        abort_flag = 0;
+        tc::mbar_fence_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(&tmem_base, TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    auto fail = [&]() {
+        if (a.err) atomicExch(a.err, 2);
+        atomicExch(&abort_flag, 1);
+    };
+
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer: activation tiles A0 (rows t0..) and A1 (rows t0+128..)
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); break; }
+            if (*(volatile int*)&abort_flag) break;
+            uint8_t* st = smem + s * STAGE_BYTES;
+            tc::mbar_arrive_expect_tx(&full[s], (two ? 2 : 1) * TILE_BYTES);
+            tc::tma_load_2d(st, &tmA, kb * BK, t0, &full[s]);
+            if (two) tc::tma_load_2d(st + TILE_BYTES, &tmA, kb * BK, t0 + BM, &full[s]);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer
+        constexpr uint32_t idesc = tc::idesc_f16(BM, BN);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            if (!tc::mbar_wait(&full[s], (kb / STAGES) & 1)) { fail(); ok = false; break; }
+            if (*(volatile int*)&abort_flag) { ok = false; break; }
+            tc::tc_fence_after();
+            uint8_t* st = smem + s * STAGE_BYTES;
+            const uint64_t da0 = tc::desc_sw128(st), da1 = tc::desc_sw128(st + TILE_BYTES);
+            const uint64_t db = tc::desc_sw128(st + 2 * TILE_BYTES);
+#pragma unroll
+            for (int k16 = 0; k16 < BK / 16; ++k16) {
+                const uint32_t acc = (kb | k16) != 0;
+                tc::mma_f16(tmem, da0 + 2 * k16, db + 2 * k16, idesc, acc);
+                if (two) tc::mma_f16(tmem + BN, da1 + 2 * k16, db + 2 * k16, idesc, acc);
+            }
+            tc::mma_commit(&empty[s]);   // stage s free once these MMAs complete
+        }
+        tc::mma_commit(&done);          // all issued MMAs complete (also on the abort path)
+        (void)ok;
+    } else if (warp >= 2) {
+        // ---- weight producers: thread p owns row p of the B tile
+        const int p = threadIdx.x - 64;
+        int wrow;
+        const DevW* W;
+        if (EPI == EPI_SWIGLU) {
+            W = p < 64 ? &a.w0 : &a.w1;
+            wrow = blockIdx.x * 64 + (p & 63);
+        } else {
+            W = &a.w0;
+            wrow = n0 + p;
+        }
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); break; }
+            if (*(volatile int*)&abort_flag) break;
+            uint8_t* bt = smem + s * STAGE_BYTES + 2 * TILE_BYTES;
+            produce_row<WT>(*W, wrow, kb * BK, bt, p);
+            tc::fence_proxy_async_smem();
+            tc::mbar_arrive(&full[s]);
+        }
+        // ---- epilogue: wait for the accumulators
+        bool ok = tc::mbar_wait(&done, 0);
+        if (!ok) fail();
+        tc::tc_fence_after();
+        const int quarter = warp & 3;    // TMEM lanes 32*quarter .. +31
+        const int r = quarter * 32 + lane;
+        // tcgen05.ld is warp-collective: decide per warp
+        ok = __all_sync(0xffffffffu, ok && !*(volatile int*)&abort_flag);
+        if (ok) {
+            for (int acc = 0; acc < (two ? 2 : 1); ++acc) {
+                const int t = t0 + acc * BM + r;
+                const bool valid = t < a.T;
+                const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+                if constexpr (EPI == EPI_RESID || EPI == EPI_STORE) {
+                    for (int c = 0; c < BN; c += 32) {
+                        float v[32];
+                        tc::tmem_ld32(tbase + c, v);
+                        if (!valid) continue;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            const int n = n0 + c + e;
+                            if (n < a.N) {
+                                float x = v[e];
+                                if (a.bias) x = __fadd_rn(x, a.bias[n]);
+                                float* dst = a.y + (size_t)t * a.y_stride + n;
+                                *dst = (EPI == EPI_RESID) ? __fadd_rn(*dst, x) : x;
+                            }
+                        }
+                    }
+                } else if constexpr (EPI == EPI_SWIGLU) {
+                    for (int c = 0; c < 64; c += 32) {
+                        float g[32], u[32];
+                        tc::tmem_ld32(tbase + c, g);
+                        tc::tmem_ld32(tbase + 64 + c, u);
+                        if (!valid) continue;
+                        const int i0 = blockIdx.x * 64 + c;
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2) {
+                            if (i0 + e + 1 < a.N) {
+                                *reinterpret_cast<__half2*>(a.yh + (size_t)t * a.yh_stride + i0 + e) =
+                                    __floats2half2_rn(__fmul_rn(silu_ref(g[e]), u[e]), __fmul_rn(silu_ref(g[e + 1]), u[e + 1]));
+                            } else if (i0 + e < a.N) {
+                                a.yh[(size_t)t * a.yh_stride + i0 + e] = __float2half_rn(__fmul_rn(silu_ref(g[e]), u[e]));
+                            }
+                        }
+                    }
+                } else if constexpr (EPI == EPI_QKV) {
+                    const int hd = a.hd, half = hd / 2;
+                    const RowMeta rm = valid ? a.meta[t] : RowMeta{0, 0, 0, 0};
+                    for (int hb = 0; hb < BN; hb += hd) {          // heads within the tile
+                        for (int i0 = 0; i0 < half; i0 += 32) {
+                            float x0[32], x1[32];
+                            int npair;
+                            if (half >= 32) {
+                                tc::tmem_ld32(tbase + hb + i0, x0);
+                                tc::tmem_ld32(tbase + hb + half + i0, x1);
+                                npair = 32;
+                            } else {   // hd 32: one load holds both halves
+                                float v[32];
+                                tc::tmem_ld32(tbase + hb, v);
+#pragma unroll
+                                for (int e = 0; e < 16; ++e) {
+                                    x0[e] = v[e];
+                                    x1[e] = v[e + 16];
+                                }
+                                npair = 16;
+                            }
+                            const int f0 = n0 + hb;                // first feature of this head
+                            if (!valid || f0 >= a.N) continue;
+                            const int h = f0 / hd;
+                            for (int e = 0; e < npair; ++e) {
+                                const int i = i0 + e;
+                                float v0 = x0[e], v1 = x1[e];
+                                if (a.bias) {
+                                    v0 = __fadd_rn(v0, a.bias[f0 + i]);
+                                    v1 = __fadd_rn(v1, a.bias[f0 + i + half]);
+                                }
+                                if (h < a.nq + a.nkv) {
+                                    const float2 cs = a.rope_cs[(size_t)t * half + i];
+                                    const float y0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+                                    const float y1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+                                    v0 = y0;
+                                    v1 = y1;
+                                }
+                                if (h < a.nq) {
+                                    float* q = a.y + (size_t)t * a.y_stride + h * hd;
+                                    q[i] = v0;
+                                    q[i + half] = v1;
+                                } else {
+                                    const bool is_k = h < a.nq + a.nkv;
+                                    const int kvh = is_k ? h - a.nq : h - a.nq - a.nkv;
+                                    __half* dst = (is_k ? a.kv.k : a.kv.v) + kv_offset(a.kv, rm.seq, rm.cidx, kvh);
+                                    dst[i] = __float2half_rn(v0);
+                                    dst[i + half] = __float2half_rn(v1);
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+template <int EPI>
+cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, cudaStream_t st) {
+    dim3 grid((EPI == EPI_SWIGLU ? (a.N + 63) / 64 : (a.N + BN - 1) / BN), (a.T + 2 * BM - 1) / (2 * BM));
+    switch (a.w0.type) {
+        case W_Q8_0: k_gemm_tc<W_Q8_0, EPI><<<grid, THREADS, SMEM_BYTES, st>>>(tm, a); break;
+        case W_Q5_K: k_gemm_tc<W_Q5_K, EPI><<<grid, THREADS, SMEM_BYTES, st>>>(tm, a); break;
+        case W_Q6_K: k_gemm_tc<W_Q6_K, EPI><<<grid, THREADS, SMEM_BYTES, st>>>(tm, a); break;
+        case W_F16: k_gemm_tc<W_F16, EPI><<<grid, THREADS, SMEM_BYTES, st>>>(tm, a); break;
+        case W_F32: k_gemm_tc<W_F32, EPI><<<grid, THREADS, SMEM_BYTES, st>>>(tm, a); break;
+        default: return cudaErrorInvalidValue;
+    }
+    note_launch();
+    return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t prepare_epi() {
+    const void* fns[] = {(const void*)k_gemm_tc<W_Q8_0, EPI>, (const void*)k_gemm_tc<W_Q5_K, EPI>,
+                         (const void*)k_gemm_tc<W_Q6_K, EPI>, (const void*)k_gemm_tc<W_F16, EPI>,
+                         (const void*)k_gemm_tc<W_F32, EPI>};
+    for (const void* f : fns) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t gemm_tc_prepare() {
+    cudaError_t e;
+    if ((e = prepare_epi<EPI_QKV>()) != cudaSuccess) return e;
+    if ((e = prepare_epi<EPI_RESID>()) != cudaSuccess) return e;
+    if ((e = prepare_epi<EPI_SWIGLU>()) != cudaSuccess) return e;
+    return prepare_epi<EPI_STORE>();
+}
+
+cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st) {
+    if (a.K % BK || a.T <= 0 || a.N <= 0) return cudaErrorInvalidValue;
+    if (a.epi == EPI_QKV && (BN % a.hd || (a.hd != 32 && a.hd != 64 && a.hd != 128))) return cudaErrorInvalidValue;
+    switch (a.epi) {
+        case EPI_QKV: return launch_epi<EPI_QKV>(a, tmA, st);
+        case EPI_RESID: return launch_epi<EPI_RESID>(a, tmA, st);
+        case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(a, tmA, st);
+        case EPI_STORE: return launch_epi<EPI_STORE>(a, tmA, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace vvq2

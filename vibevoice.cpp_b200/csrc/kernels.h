@@ -1,6 +1,7 @@
 // kernels.h -- launch interfaces of the sm_100a kernels (host side).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -44,6 +45,25 @@ size_t gemv_smem_bytes(int wt, int M, int K);
 cudaError_t gemv_prepare();
 int gemv_max_rows(int K);   // activation rows that fit the GEMV's shared memory
 
+// ------------------------------------------------------ tcgen05 GEMM (prefill)
+struct GemmArgs {
+    DevW w0, w1;                   // weights; SwiGLU interleaves gate (w0) and up (w1) tiles
+    int T = 0, N = 0, K = 0;       // token rows, output features, input dim
+    int epi = 0;                   // EPI_QKV / EPI_RESID / EPI_SWIGLU / EPI_STORE
+    const float* bias = nullptr;
+    float* y = nullptr;            // f32 out: RESID/STORE [T][y_stride]; QKV: Q [T][nq*hd]
+    int y_stride = 0;
+    __half* yh = nullptr;          // f16 out: SwiGLU [T][yh_stride]
+    int yh_stride = 0;
+    const RowMeta* meta = nullptr; // per token row
+    KvLayer kv;
+    int nq = 0, nkv = 0, hd = 0;
+    const float2* rope_cs = nullptr;   // [T][hd/2] (cos, sin)
+    int* err = nullptr;
+};
+cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st);
+cudaError_t gemm_tc_prepare();
+
 // ------------------------------------------------------ decode attention
 struct AttnDecodeArgs {
     const float* q = nullptr;      // [M][nq*hd] (roped)
@@ -58,6 +78,7 @@ struct AttnDecodeArgs {
     float* part_ml = nullptr;      // [M][max_splits][nq][2] (running max, sum)
     int* counters = nullptr;       // [M][nkv], zero between launches
     int* err = nullptr;            // set to nonzero if a bounded wait gave up
+    __half* out_h = nullptr;       // if set, write f16 output here instead of `out`
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st);
 cudaError_t attn_decode_prepare();
@@ -70,6 +91,13 @@ cudaError_t rope_launch(const float* x, int n_tok, int n_heads, int hd, const in
                         float ts, float* y, cudaStream_t st);
 cudaError_t rmsnorm_launch(const float* x, const float* w, int rows, int n, float eps, float* y,
                            cudaStream_t st);
+// RMSNorm to f16 (the tensor-core GEMM's activation operand)
+cudaError_t rmsnorm_f16_launch(const float* x, const float* w, int rows, int n, float eps, __half* y,
+                               cudaStream_t st);
+// NEOX (cos, sin) per (row, pair) with ggml's CPU theta recurrence: [rows][hd/2]
+cudaError_t rope_table_launch(const RowMeta* meta, int rows, int hd, float ts, float2* cs, cudaStream_t st);
+// f32 -> f16 copy
+cudaError_t to_f16_launch(const float* x, int64_t n, __half* y, cudaStream_t st);
 // rows of a tok_embd table (any weight type) -> f32 [n][cols]
 cudaError_t embed_launch(const DevW& t, const int32_t* tok, int n, float* out, cudaStream_t st);
 // f32 [n_pos][n_kv][hd] -> f16 paged cache of one sequence / layer

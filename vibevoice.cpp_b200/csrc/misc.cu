@@ -61,6 +61,42 @@ __global__ void k_rmsnorm(const float* x, const float* w, int n, float eps, floa
         y[(size_t)blockIdx.x * n + k] = __fmul_rn(__fmul_rn(xr[k], sc), w[k]);
 }
 
+// RMSNorm rows to f16: one CTA per row
+__global__ void k_rmsnorm_f16(const float* x, const float* w, int n, float eps, __half* y) {
+    __shared__ float red[32];
+    __shared__ float scale_s;
+    const float* xr = x + (size_t)blockIdx.x * n;
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) ss = fmaf(xr[k], xr[k], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+        scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)n), eps)));
+    }
+    __syncthreads();
+    const float sc = scale_s;
+    for (int k = threadIdx.x; k < n; k += blockDim.x)
+        y[(size_t)blockIdx.x * n + k] = __float2half_rn(__fmul_rn(__fmul_rn(xr[k], sc), w[k]));
+}
+
+__global__ void k_rope_table(const RowMeta* meta, int rows, int half, float ts, float2* cs) {
+    const int64_t n = (int64_t)rows * half;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(t / half), i = (int)(t % half);
+        float th = (float)meta[r].pos;
+        for (int k = 0; k < i; ++k) th = __fmul_rn(th, ts);
+        cs[t] = make_float2(cosf(th), sinf(th));
+    }
+}
+
+__global__ void k_to_f16(const float* x, int64_t n, __half* y) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = __float2half_rn(x[i]);
+}
+
 __global__ void k_embed(DevW t, const int32_t* tok, int n, float* out) {
     const int i = blockIdx.x;
     const int r = tok[i];
@@ -137,6 +173,26 @@ cudaError_t rope_launch(const float* x, int n_tok, int n_heads, int hd, const in
 cudaError_t rmsnorm_launch(const float* x, const float* w, int rows, int n, float eps, float* y,
                            cudaStream_t st) {
     k_rmsnorm<<<rows, 256, 0, st>>>(x, w, n, eps, y);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_f16_launch(const float* x, const float* w, int rows, int n, float eps, __half* y,
+                               cudaStream_t st) {
+    k_rmsnorm_f16<<<rows, 256, 0, st>>>(x, w, n, eps, y);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t rope_table_launch(const RowMeta* meta, int rows, int hd, float ts, float2* cs, cudaStream_t st) {
+    const int64_t n = (int64_t)rows * (hd / 2);
+    k_rope_table<<<grid_for(n, 256), 256, 0, st>>>(meta, rows, hd / 2, ts, cs);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t to_f16_launch(const float* x, int64_t n, __half* y, cudaStream_t st) {
+    k_to_f16<<<grid_for(n, 256), 256, 0, st>>>(x, n, y);
     note_launch();
     return cudaGetLastError();
 }

@@ -72,6 +72,7 @@ def lib() -> C.CDLL:
             "vvq2_last_error": (C.c_char_p, []),
             "vvq2_kernel_launches": (I64, []),
             "vvq2_profile": (I, [P, I]),
+            "vvq2_debug_gemm": (I, [I, P, I, I, P, I, P]),
             "vvq2_profile_read": (I, [P, I, P, P, P]),
         }
         for name, (res, args) in sig.items():
@@ -268,4 +269,13 @@ def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     y = np.empty_like(x)
     rows = x.size // x.shape[-1]
     _chk(lib().vvq2_rms_norm(_p(x), _p(w), rows, x.shape[-1], eps, _p(y)))
+    return y
+
+
+def debug_gemm(qtype: int, raw: np.ndarray, n: int, k: int, x: np.ndarray) -> np.ndarray:
+    """y = x . W^T through the tcgen05 prefill GEMM (test hook)."""
+    raw = np.ascontiguousarray(raw)
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty((x.shape[0], n), np.float32)
+    _chk(lib().vvq2_debug_gemm(qtype, _p(raw), n, k, _p(x), x.shape[0], _p(y)))
     return y
