@@ -198,6 +198,33 @@ int64_t vvq2_kernel_launches(void);
  * dequantized exactly and rounded to f16, f32 accumulation.  k % 64 == 0. */
 int  vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int t, float* y);
 
+/* ---- allocation-free decode attention (no counterpart in the reference) --
+ * For callers that cannot call cudaMalloc -- an engine whose pool owns all GPU
+ * memory, code inside another framework's context or a graph capture, a
+ * real-time thread that must not enter the allocator: the split-K decode
+ * attention of this library with its scratch (partial O, per-split max/sum,
+ * arrival counters, error word) in one fixed file-scope device array instead
+ * of allocations.  The caller passes device pointers it owns:
+ *   q          f32 [n_rows][n_heads*head_dim], RoPE already applied
+ *   k_pages,
+ *   v_pages    f16 pages [page][n_kv_heads][64][head_dim]
+ *   block_table int32 [seq][max_pages] logical -> physical page
+ *   row_meta   int32 [n_rows][4] = {seq, pos, (unused), kv_len}; keys j < kv_len
+ *              with j <= pos are attended
+ *   max_kv     an upper bound of every row's kv_len (sizes the split grid)
+ *   out        f32 [n_rows][n_heads*head_dim]
+ * Limits: n_rows <= 8, n_heads*head_dim <= 4096, n_heads <= 64, n_kv_heads
+ * <= 16, head_dim 32/64/128, n_heads/n_kv_heads <= 8; beyond them it returns
+ * VVQ2_ERR_INVALID_ARG.  The array (about 2.1 MB) stays allocated on every GPU
+ * that loads the library until exit.  Calls share it: calls that overlap on
+ * the GPU race and must be serialized by the caller.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make that
+ * first call before any stream capture.  Allocates nothing. */
+int  vvq2_attention_decode_noalloc(const float* q, const void* k_pages, const void* v_pages,
+                                   const int* block_table, int max_pages, const int* row_meta,
+                                   int n_rows, int max_kv, int n_heads, int n_kv_heads,
+                                   int head_dim, float* out, void* stream);
+
 /* ---- measurement (no counterpart in the reference, which has no profiler
  * hooks; used by bench.py for the roofline figure) -------------------------
  * While enabled, vvq2_decode_step brackets every GEMV (kind 0) and attention

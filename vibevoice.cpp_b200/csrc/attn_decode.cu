@@ -353,4 +353,102 @@ cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st) {
     return cudaErrorInvalidValue;
 }
 
+// ===================================================================== no-alloc
+// Decode attention for callers that cannot allocate device memory.
+//
+// Some hosts of this library run where cudaMalloc is not available to them:
+// an engine that hands every byte of the GPU to its own memory pool up front,
+// code running inside a CUDA-graph capture or a context owned by another
+// framework, or a real-time audio thread that must not enter the driver's
+// allocator.  They own the inputs (Q, the paged K/V, block table, row
+// metadata) and the output, but not the kernel's scratch: the split-K partial
+// O, the per-split max/sum, the per-(row, head) arrival counters and the
+// error word.  That scratch lives here, in one fixed file-scope device array.
+//
+// Limits (checked, VVQ2_ERR_INVALID_ARG beyond them): up to NA_MAX_ROWS query
+// rows, NA_MAX_SPLITS splits per row, n_heads * head_dim <= NA_MAX_QW,
+// n_heads <= NA_MAX_HEADS, n_kv_heads <= NA_MAX_KV.  Size: about 2.1 MB per
+// GPU, held by every GPU that loads the library until the process exits.
+//
+// The array is shared by every call: calls that overlap on the GPU (two
+// streams, two threads) race on it and must be serialized by the caller.  Each
+// call clears the counters and the error word it relies on before launching.
+// The device address of the array is looked up once per device, on that
+// device's first call (cudaGetSymbolAddress); make that first call before any
+// stream capture.
+namespace {
+
+constexpr int NA_MAX_ROWS = 8;
+constexpr int NA_MAX_SPLITS = 16;
+constexpr int NA_MAX_QW = 4096;
+constexpr int NA_MAX_HEADS = 64;
+constexpr int NA_MAX_KV = 16;
+constexpr size_t NA_PART = (size_t)NA_MAX_ROWS * NA_MAX_SPLITS * NA_MAX_QW * sizeof(float);
+constexpr size_t NA_ML = (size_t)NA_MAX_ROWS * NA_MAX_SPLITS * NA_MAX_HEADS * 2 * sizeof(float);
+constexpr size_t NA_COUNTERS = (size_t)NA_MAX_ROWS * NA_MAX_KV * sizeof(int);
+constexpr size_t NA_BYTES = NA_PART + NA_ML + NA_COUNTERS + 256;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_BYTES];
+
+constexpr int NA_MAX_DEVICES = 64;
+unsigned char* g_noalloc_ptr[NA_MAX_DEVICES] = {};
+
+}  // namespace
+
 }  // namespace vvq2
+
+extern "C" int vvq2_attention_decode_noalloc(const float* q, const void* k_pages, const void* v_pages,
+                                             const int* block_table, int max_pages, const int* row_meta,
+                                             int n_rows, int max_kv, int n_heads, int n_kv_heads,
+                                             int head_dim, float* out, void* stream) {
+    using namespace vvq2;
+    if (!q || !k_pages || !v_pages || !block_table || !row_meta || !out || n_rows <= 0 || max_kv <= 0 ||
+        max_pages <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
+        return -2;   // VVQ2_ERR_INVALID_ARG
+    if (n_rows > NA_MAX_ROWS || n_heads * head_dim > NA_MAX_QW || n_heads > NA_MAX_HEADS ||
+        n_kv_heads > NA_MAX_KV || n_heads / n_kv_heads > AD_MAXG ||
+        (head_dim != 32 && head_dim != 64 && head_dim != 128) || max_kv > max_pages * KV_PAGE)
+        return -2;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= NA_MAX_DEVICES) return -10;
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+            cudaGetLastError();
+            return -9;   // VVQ2_ERR_CUDA
+        }
+        if (attn_decode_prepare() != cudaSuccess) return -9;
+        g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+    }
+    unsigned char* base = g_noalloc_ptr[dev];
+    // whole pages per split, at most NA_MAX_SPLITS splits over max_kv keys
+    int split = (max_kv + NA_MAX_SPLITS - 1) / NA_MAX_SPLITS;
+    split = (split + KV_PAGE - 1) / KV_PAGE * KV_PAGE;
+    if (split < KV_PAGE) split = KV_PAGE;
+    AttnDecodeArgs a;
+    a.q = q;
+    a.out = out;
+    a.meta = reinterpret_cast<const RowMeta*>(row_meta);
+    a.kv.k = static_cast<__half*>(const_cast<void*>(k_pages));
+    a.kv.v = static_cast<__half*>(const_cast<void*>(v_pages));
+    a.kv.block_table = block_table;
+    a.kv.max_pages = max_pages;
+    a.kv.n_kv = n_kv_heads;
+    a.kv.hd = head_dim;
+    a.M = n_rows;
+    a.nq = n_heads;
+    a.nkv = n_kv_heads;
+    a.hd = head_dim;
+    a.split = split;
+    a.max_splits = (max_kv + split - 1) / split;
+    a.scale = 1.0f / sqrtf((float)head_dim);
+    a.part = reinterpret_cast<float*>(base);
+    a.part_ml = reinterpret_cast<float*>(base + NA_PART);
+    a.counters = reinterpret_cast<int*>(base + NA_PART + NA_ML);
+    a.err = reinterpret_cast<int*>(base + NA_PART + NA_ML + NA_COUNTERS);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // counters and the error word must start at zero; partials are written before read
+    if (cudaMemsetAsync(a.counters, 0, NA_COUNTERS + sizeof(int), st) != cudaSuccess) return -9;
+    if (attn_decode_launch(a, st) != cudaSuccess) return -9;
+    return 0;
+}
