@@ -234,6 +234,14 @@ int  vvq2_attention_decode_noalloc(const float* q, const void* k_pages, const vo
 int  vvq2_profile(vvq2_ctx* ctx, int enable);
 int  vvq2_profile_read(vvq2_ctx* ctx, int kind, double* ms, double* bytes, int64_t* launches);
 
+/* Phase timeline of the persistent decode-step kernel (no reference
+ * counterpart).  With VVQ2_MEGA_TRACE=1 in the environment when a decode
+ * graph is built, every CTA stamps %globaltimer (ns) at kernel start, at
+ * arrival at / release from each grid barrier, and at the end of the last
+ * step.  Layout [slots][grid]: slot 0 start, 1+2b arrive b, 2+2b release b,
+ * slots-1 end.  `out` may be null to query grid and slots only. */
+int  vvq2_mega_trace(vvq2_ctx* ctx, uint64_t* out, int64_t cap, int* grid, int* slots);
+
 #ifdef __cplusplus
 }
 #endif

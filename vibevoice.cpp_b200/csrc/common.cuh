@@ -26,8 +26,9 @@ struct DevW {
     int type = -1;
     int rows = 0, cols = 0;
     const uint8_t* q = nullptr;
-    const __half* d = nullptr;
+    const __half* d = nullptr;     // block scales: row r at d + r * d_stride
     int64_t row_stride = 0;        // bytes per row of q
+    int64_t d_stride = 0;          // halves per row of d
 };
 
 // Per activation row (token of a sequence) metadata for the decode/prefill step.

@@ -16,7 +16,7 @@ __device__ __forceinline__ float deq_elem(const DevW& w, int row, int e) {
     switch (w.type) {
         case W_Q8_0: {
             const int8_t q = reinterpret_cast<const int8_t*>(w.q + (size_t)row * w.row_stride)[e];
-            const float d = __half2float(w.d[(size_t)row * (w.cols / 32) + e / 32]);
+            const float d = __half2float(w.d[(size_t)row * w.d_stride + e / 32]);
             return __fmul_rn((float)q, d);
         }
         case W_Q5_K: {
@@ -47,7 +47,7 @@ __device__ __forceinline__ float deq_elem(const DevW& w, int row, int e) {
             const uint8_t qhb = b[128 + hf * 32 + l];
             const int q = (int)(((qlb >> (4 * (k >> 1))) & 0xF) | (((qhb >> (2 * k)) & 3) << 4)) - 32;
             const int8_t sc = reinterpret_cast<const int8_t*>(b + 192)[hf * 8 + l / 16 + 2 * k];
-            const float d = __half2float(w.d[(size_t)row * (w.cols / 256) + sb]);
+            const float d = __half2float(w.d[(size_t)row * w.d_stride + sb]);
             return __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
         }
         case W_F16:

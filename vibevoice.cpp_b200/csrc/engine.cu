@@ -132,6 +132,7 @@ struct vvq2_ctx {
     std::vector<void*> allocs;
     // scratch for up to GEMV_MAX_M activation rows
     float *X = nullptr, *Q = nullptr, *ATT = nullptr, *FA = nullptr, *LOGITS = nullptr;
+    float* QKVr = nullptr;         // persistent step: raw q|k|v rows [GEMV_MAX_M][qkv rows]
     // prefill (tensor-core) scratch for up to PREFILL_ROWS token rows
     __half *Xh = nullptr, *ATTh = nullptr, *Ah = nullptr;
     float2* rope_cs = nullptr;
@@ -145,6 +146,19 @@ struct vvq2_ctx {
     int max_rows = GEMV_MAX_M;     // activation rows per GEMV launch (shared-memory bound)
     int* err = nullptr;            // device error word written by bounded waits
     std::vector<vvq2_kv*> kvs;   // caches created on this context (released with it)
+
+    // persistent decode-step kernel state: per-KV device layer tables, grid
+    // barrier counter / launch epoch / abort flag
+    unsigned long long* bar_count = nullptr;
+    unsigned int* epoch = nullptr;
+    int* abort_flag = nullptr;
+    unsigned long long* mega_trace = nullptr;   // VVQ2_MEGA_TRACE=1: phase timeline of the last step
+    int mega_grid = 0;
+    struct MegaTable {
+        vvq2_kv* kv;
+        MegaLayer* d_layers;
+    };
+    std::vector<MegaTable> mega_tables;
 
     // measurement: per-launch CUDA events (captured into decode graphs when on)
     struct Rec { int kind; int e0, e1; double bytes; };
@@ -205,6 +219,14 @@ struct vvq2_kv {
 
 namespace {
 
+// Host <-> device copy ordered on `st` and complete on return.  (A pageable
+// cudaMemcpy may return before its DMA has landed, and the engine's
+// non-blocking stream does not wait for the legacy stream.)
+cudaError_t copy_on(void* dst, const void* src, size_t n, cudaStream_t st) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, n, cudaMemcpyDefault, st);
+    return e == cudaSuccess ? cudaStreamSynchronize(st) : e;
+}
+
 // Host repack of one GGUF tensor into the device layout (DevW).
 int upload_tensor(vvq2_ctx* c, const vvq2_tensor& t, DevW* out, int expect_ne0, int expect_ne1,
                   const char* name) {
@@ -225,18 +247,21 @@ int upload_tensor(vvq2_ctx* c, const vvq2_tensor& t, DevW* out, int expect_ne0, 
     std::vector<uint16_t> d;
     switch (t.type) {
         case W_Q8_0:
-            w.row_stride = cols;
-            q.resize((size_t)rows * cols);
-            d.resize((size_t)rows * nb);
+            // one row = [cols quants][nb f16 scales, padded to 16 bytes]: a run of
+            // rows is one contiguous, 16-byte aligned range (one bulk copy)
+            w.row_stride = cols + (nb * 2 + 15) / 16 * 16;
+            w.d_stride = w.row_stride / 2;
+            q.assign((size_t)rows * w.row_stride, 0);
             for (int64_t r = 0; r < rows; ++r)
                 for (int64_t b = 0; b < nb; ++b) {
                     const uint8_t* blk = src + ((size_t)r * nb + b) * 34;
-                    memcpy(&d[(size_t)r * nb + b], blk, 2);
-                    memcpy(&q[(size_t)r * cols + b * 32], blk + 2, 32);
+                    memcpy(&q[(size_t)r * w.row_stride + cols + b * 2], blk, 2);
+                    memcpy(&q[(size_t)r * w.row_stride + b * 32], blk + 2, 32);
                 }
             break;
         case W_Q6_K:
             w.row_stride = nb * Q6K_PACKED;
+            w.d_stride = nb;
             q.resize((size_t)rows * w.row_stride);
             d.resize((size_t)rows * nb);
             for (int64_t r = 0; r < rows; ++r)
@@ -253,12 +278,13 @@ int upload_tensor(vvq2_ctx* c, const vvq2_tensor& t, DevW* out, int expect_ne0, 
     }
     uint8_t* dq = nullptr;
     if (int rc = c->alloc(&dq, q.size())) return rc;
-    CU(cudaMemcpy(dq, q.data(), q.size(), cudaMemcpyHostToDevice));
+    CU(copy_on(dq, q.data(), q.size(), c->stream));
     w.q = dq;
+    if (t.type == W_Q8_0) w.d = reinterpret_cast<const __half*>(dq + cols);
     if (!d.empty()) {
         __half* dd = nullptr;
         if (int rc = c->alloc(&dd, d.size())) return rc;
-        CU(cudaMemcpy(dd, d.data(), d.size() * 2, cudaMemcpyHostToDevice));
+        CU(copy_on(dd, d.data(), d.size() * 2, c->stream));
         w.d = dd;
     }
     *out = w;
@@ -279,7 +305,7 @@ int upload_vec(vvq2_ctx* c, const vvq2_tensor& t, int n, float** out, const char
         return fail(VVQ2_ERR_NOT_IMPLEMENTED, "%s: vector type %d", name, t.type);
     }
     if (int rc = c->alloc(out, (size_t)n)) return rc;
-    CU(cudaMemcpy(*out, h.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+    CU(copy_on(*out, h.data(), (size_t)n * 4, c->stream));
     return 0;
 }
 
@@ -296,7 +322,13 @@ int check_device_error(vvq2_ctx* c) {
     int e = 0;
     CU(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {
-        cudaMemset(c->err, 0, sizeof(int));
+        cudaMemsetAsync(c->err, 0, sizeof(int), c->stream);
+        // a persistent kernel that gave up leaves its barrier bookkeeping mid-launch
+        if (c->bar_count) cudaMemsetAsync(c->bar_count, 0, sizeof(unsigned long long), c->stream);
+        if (c->epoch) cudaMemsetAsync(c->epoch, 0, sizeof(unsigned int), c->stream);
+        if (c->abort_flag) cudaMemsetAsync(c->abort_flag, 0, sizeof(int), c->stream);
+        if (c->counters) cudaMemsetAsync(c->counters, 0, sizeof(int) * GEMV_MAX_M * c->hp.n_kv_heads, c->stream);
+        cudaStreamSynchronize(c->stream);
         return fail(VVQ2_ERR_CUDA, "a device-side wait timed out (code %d)", e);
     }
     return 0;
@@ -313,11 +345,11 @@ void choose_split(const vvq2_ctx* c, int M, int max_lim, int* split, int* nsplit
     *nsplit = (max_lim + s - 1) / s;
 }
 
+// Algorithmic bytes of a weight matrix: its GGUF size (the padding of the
+// device layout is not counted).
 size_t weight_bytes(const DevW& w) {
     if (w.type < 0) return 0;
-    size_t b = (size_t)w.rows * w.row_stride;
-    if (w.d) b += (size_t)w.rows * (w.cols / (w.type == W_Q8_0 ? 32 : 256)) * 2;
-    return b;
+    return (size_t)w.rows * (size_t)(w.cols / block_elems(w.type)) * block_bytes(w.type);
 }
 
 // Records CUDA events around launches when profiling (kind 0 GEMV, 1 attention).
@@ -557,6 +589,176 @@ int enqueue_decode(vvq2_ctx* c, vvq2_kv* kv, int M, int split, int nsplit, cudaS
     return 0;
 }
 
+// Shared-memory and tile plan of the persistent decode step for M rows.
+struct MegaPlan {
+    bool ok = false;
+    int nstage = 0, slot = 0, uni = 0, t_qkv = 1, t_o = 1, t_gu = 1, t_down = 1, t_lm = 1;
+    size_t smem = 0;
+};
+
+MegaPlan mega_plan(const vvq2_ctx* c, int M) {
+    MegaPlan p;
+    const vvq2_hparams& hp = c->hp;
+    const int grid = c->mega_grid, ncw = decode_mega_consumer_warps();
+    if (grid <= 0 || M < 1 || M > 2 || c->layers.empty()) return p;
+    const vvq2_ctx::Layer& L0 = c->layers[0];
+    const int kmax = std::max({hp.hidden_size, hp.intermediate_size, hp.n_heads * hp.head_dim});
+    p.uni = decode_mega_union_bytes(hp.head_dim, M, kmax);
+    const int lim = decode_mega_smem_limit();
+    // The ring has a multiple of `ncw` slots and tile i goes to consumer warp
+    // i % ncw, so every slot is always read by the same warp, in order.
+    for (int k = decode_mega_max_stages() / ncw; k >= 1; --k) {
+        const int nst = k * ncw;
+        const int64_t slot_max = (int64_t)(lim - p.uni) / nst / 128 * 128;
+        // rows per tile: a power of two that gives every consumer warp a tile
+        // and fits a slot
+        bool fits = true;
+        auto pick = [&](const DevW& w, int cap, int mats) {
+            const int rpc = (w.rows + grid - 1) / grid;
+            int t = 1;
+            while (t * 2 <= cap && t * 2 * ncw <= rpc && (int64_t)t * 2 * mats * w.row_stride <= slot_max) t *= 2;
+            if ((int64_t)t * mats * w.row_stride > slot_max) fits = false;
+            return t;
+        };
+        p.t_qkv = pick(L0.qkv, 8, 1);
+        p.t_o = pick(L0.o, 8, 1);
+        p.t_gu = pick(L0.gate, 4, 2);
+        p.t_down = pick(L0.down, 8, 1);
+        p.t_lm = pick(c->lm_head, 8, 1);
+        if (!fits) continue;
+        int64_t slot = std::max<int64_t>({p.t_qkv * L0.qkv.row_stride, p.t_o * L0.o.row_stride,
+                                          2 * p.t_gu * L0.gate.row_stride, p.t_down * L0.down.row_stride,
+                                          p.t_lm * c->lm_head.row_stride});
+        slot = (slot + 127) / 128 * 128;
+        p.slot = (int)slot;
+        p.nstage = nst;
+        p.smem = (size_t)p.uni + (size_t)p.nstage * p.slot;
+        p.ok = true;
+        return p;
+    }
+    return p;
+}
+
+// The persistent decode-step kernel covers Q8_0 models with head_dim 64/128,
+// at most 8 q heads per KV head and up to 2 rows (the CFG pair);
+// VVQ2_MEGA=0 forces the per-phase graph.
+bool mega_eligible(const vvq2_ctx* c, int M) {
+    const char* env = std::getenv("VVQ2_MEGA");
+    if (env && env[0] == '0') return false;
+    if (c->mega_grid <= 0 || M < 1 || M > 2) return false;
+    if (c->hp.head_dim != 64 && c->hp.head_dim != 128) return false;
+    if (c->hp.n_heads % c->hp.n_kv_heads || c->hp.n_heads / c->hp.n_kv_heads > 8) return false;
+    if (c->lm_head.type != W_Q8_0 || c->tok_embd.type != W_Q8_0) return false;
+    for (const auto& L : c->layers)
+        if (L.qkv.type != W_Q8_0 || L.o.type != W_Q8_0 || L.gate.type != W_Q8_0 || L.up.type != W_Q8_0 ||
+            L.down.type != W_Q8_0)
+            return false;
+    return mega_plan(c, M).ok;
+}
+
+// Attention split of the persistent step: every (row, KV head) gets up to
+// (attention groups on the GPU) / (rows x KV heads) splits of whole pages.
+void mega_split(const vvq2_ctx* c, int M, int max_lim, int* split, int* nsplit) {
+    const int groups = (c->hp.head_dim >= 128 ? 2 : 3) * c->mega_grid;
+    const int per_row = std::max(1, std::min(64, groups / std::max(1, M * c->hp.n_kv_heads)));
+    int s = (max_lim + per_row - 1) / per_row;
+    s = (std::max(s, KV_PAGE) + KV_PAGE - 1) / KV_PAGE * KV_PAGE;
+    while ((max_lim + s - 1) / s > 64) s += KV_PAGE;
+    *split = s;
+    *nsplit = (max_lim + s - 1) / s;
+}
+
+// Device table of layer descriptors for (ctx, kv); built outside stream capture.
+int ensure_mega_table(vvq2_ctx* c, vvq2_kv* kv, MegaLayer** out) {
+    MegaLayer* dl = nullptr;
+    for (const auto& t : c->mega_tables)
+        if (t.kv == kv) dl = t.d_layers;
+    if (!dl) {
+        std::vector<MegaLayer> h(c->hp.n_layers);
+        for (int li = 0; li < c->hp.n_layers; ++li) {
+            const vvq2_ctx::Layer& L = c->layers[li];
+            h[li].qkv = L.qkv;
+            h[li].o = L.o;
+            h[li].gate = L.gate;
+            h[li].up = L.up;
+            h[li].down = L.down;
+            h[li].attn_norm = L.attn_norm;
+            h[li].ffn_norm = L.ffn_norm;
+            h[li].qkv_bias = L.qkv_bias;
+            h[li].kv = kv->layer(li);
+        }
+        if (int rc = c->alloc(&dl, h.size())) return rc;
+        CU(copy_on(dl, h.data(), sizeof(MegaLayer) * h.size(), c->stream));
+        c->mega_tables.push_back({kv, dl});
+    }
+    const char* tr = std::getenv("VVQ2_MEGA_TRACE");
+    if (tr && tr[0] == '1' && !c->mega_trace) {
+        const size_t n = (size_t)mega_trace_slots(c->hp.n_layers) * c->mega_grid;
+        if (int rc = c->alloc(&c->mega_trace, n)) return rc;
+        CU(cudaMemsetAsync(c->mega_trace, 0, n * sizeof(unsigned long long), c->stream));
+        CU(cudaStreamSynchronize(c->stream));
+    }
+    *out = dl;
+    return 0;
+}
+
+int enqueue_decode_mega(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, cudaStream_t st,
+                        std::vector<vvq2_ctx::Rec>* recs, double step_bytes) {
+    MegaLayer* dl = nullptr;
+    for (const auto& t : c->mega_tables)
+        if (t.kv == kv) dl = t.d_layers;
+    if (!dl) return fail(VVQ2_ERR_GENERIC, "decode layer table missing");
+    const MegaPlan p = mega_plan(c, M);
+    if (!p.ok) return fail(VVQ2_ERR_GENERIC, "no shared-memory plan for the persistent step");
+    const vvq2_hparams& hp = c->hp;
+    MegaArgs a;
+    a.layers = dl;
+    a.n_layers = hp.n_layers;
+    a.H = hp.hidden_size;
+    a.F = hp.intermediate_size;
+    a.nq = hp.n_heads;
+    a.nkv = hp.n_kv_heads;
+    a.hd = hp.head_dim;
+    a.M = M;
+    a.grid = c->mega_grid;
+    a.lm_head = c->lm_head;
+    a.tok_embd = c->tok_embd;
+    a.out_norm = c->out_norm;
+    a.X = c->X;
+    a.ATT = c->ATT;
+    a.FA = c->FA;
+    a.QKV = c->QKVr;
+    a.qkv_rows = c->layers[0].qkv.rows;
+    a.part = c->part;
+    a.part_ml = c->part_ml;
+    a.counters = c->counters;
+    a.meta = c->meta;
+    a.tok = c->tok;
+    a.amax = c->amax;
+    a.bar_count = c->bar_count;
+    a.epoch = c->epoch;
+    a.abort = c->abort_flag;
+    mega_split(c, M, max_lim, &a.split, &a.nsplit);
+    a.eps = hp.rms_norm_eps;
+    a.rope_ts = c->rope_ts;
+    a.scale = 1.0f / sqrtf((float)hp.head_dim);
+    a.err = c->err;
+    a.trace = c->mega_trace;
+    a.nstage = p.nstage;
+    a.slot_bytes = p.slot;
+    a.union_bytes = p.uni;
+    a.t_qkv = p.t_qkv;
+    a.t_o = p.t_o;
+    a.t_gu = p.t_gu;
+    a.t_down = p.t_down;
+    a.t_lm = p.t_lm;
+    Recorder R{c, st, recs};
+    CU(R.begin());
+    CU(decode_mega_launch(a, p.smem, st));
+    CU(R.end(0, step_bytes));
+    return 0;
+}
+
 }  // namespace
 
 // ======================================================================= C ABI
@@ -610,6 +812,7 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     if (p.major != 10) return fail(VVQ2_ERR_NO_DEVICE, "device %d is sm_%d%d, need sm_100", device, p.major, p.minor);
     CU(cudaSetDevice(device));
     CU(gemv_prepare());
+    CU(decode_mega_prepare());
     CU(attn_decode_prepare());
     vvq2_ctx* c = new vvq2_ctx();
     c->hp = *hp;
@@ -635,6 +838,7 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     rc = rc ? rc : c->alloc(&c->rope_cs, (size_t)P * hp->head_dim / 2);
     rc = rc ? rc : c->alloc(&c->ATT, (size_t)M * qw);
     rc = rc ? rc : c->alloc(&c->FA, (size_t)M * F);
+    rc = rc ? rc : c->alloc(&c->QKVr, (size_t)M * (hp->n_heads + 2 * hp->n_kv_heads) * hp->head_dim);
     rc = rc ? rc : c->alloc(&c->part, (size_t)M * c->max_splits_cap * qw);
     rc = rc ? rc : c->alloc(&c->part_ml, (size_t)M * c->max_splits_cap * hp->n_heads * 2);
     rc = rc ? rc : c->alloc(&c->counters, (size_t)M * hp->n_kv_heads);
@@ -642,12 +846,20 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     rc = rc ? rc : c->alloc(&c->amax, (size_t)M);
     rc = rc ? rc : c->alloc(&c->tok, (size_t)M);
     rc = rc ? rc : c->alloc(&c->err, (size_t)1);
+    rc = rc ? rc : c->alloc(&c->bar_count, (size_t)1);
+    rc = rc ? rc : c->alloc(&c->epoch, (size_t)1);
+    rc = rc ? rc : c->alloc(&c->abort_flag, (size_t)1);
+    c->mega_grid = decode_mega_grid();
     c->max_rows = std::min(GEMV_MAX_M, gemv_max_rows(std::max({hp->hidden_size, qw, F})));
     if (!rc && hp->vocab_size > 0) rc = c->alloc(&c->LOGITS, (size_t)M * hp->vocab_size);
     if (!rc && cudaMallocHost(&c->meta_host, sizeof(RowMeta) * P) != cudaSuccess)
         rc = fail(VVQ2_ERR_OUT_OF_MEMORY, "pinned alloc failed");
     if (!rc && (cudaMemset(c->counters, 0, sizeof(int) * M * hp->n_kv_heads) != cudaSuccess ||
-                cudaMemset(c->err, 0, sizeof(int)) != cudaSuccess))
+                cudaMemset(c->err, 0, sizeof(int)) != cudaSuccess ||
+                cudaMemset(c->bar_count, 0, sizeof(unsigned long long)) != cudaSuccess ||
+                cudaMemset(c->epoch, 0, sizeof(unsigned int)) != cudaSuccess ||
+                cudaMemset(c->abort_flag, 0, sizeof(int)) != cudaSuccess ||
+                cudaDeviceSynchronize() != cudaSuccess))   // the engine stream does not wait for these
         rc = fail(VVQ2_ERR_CUDA, "memset failed");
     if (rc) {
         vvq2_free(c);
@@ -719,7 +931,7 @@ int vvq2_set_layer(vvq2_ctx* c, int li, const vvq2_layer_weights* w) {
         }
         if (any) {
             if (int rc = c->alloc(&L.qkv_bias, bias.size())) return rc;
-            CU(cudaMemcpy(L.qkv_bias, bias.data(), bias.size() * 4, cudaMemcpyHostToDevice));
+            CU(copy_on(L.qkv_bias, bias.data(), bias.size() * 4, c->stream));
         }
     }
     if (int rc = upload_tensor(c, w->attn_o, &L.o, qw, H, "attn_o")) return rc;
@@ -773,10 +985,10 @@ int vvq2_kv_init(vvq2_ctx* c, int n_seqs, int max_seq, vvq2_kv** out) {
     // the indirection so pages can later be shared or reassigned
     std::vector<int> bt(pages);
     for (size_t i = 0; i < pages; ++i) bt[i] = (int)i;
-    cudaMemcpy(kv->block_table, bt.data(), pages * sizeof(int), cudaMemcpyHostToDevice);
-    cudaMemset(kv->k, 0, bytes);
-    cudaMemset(kv->v, 0, bytes);
-    if (cudaGetLastError() != cudaSuccess) {
+    cudaError_t e = cudaMemsetAsync(kv->k, 0, bytes, c->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(kv->v, 0, bytes, c->stream);
+    if (e == cudaSuccess) e = copy_on(kv->block_table, bt.data(), pages * sizeof(int), c->stream);
+    if (e != cudaSuccess || cudaGetLastError() != cudaSuccess) {
         vvq2_kv_free(kv);
         return fail(VVQ2_ERR_CUDA, "kv init copy failed");
     }
@@ -799,6 +1011,9 @@ void vvq2_kv_free(vvq2_kv* kv) {
                         c->graphs.end());
         if (c->meta_kv == kv) c->meta_kv = nullptr;
         c->kvs.erase(std::remove(c->kvs.begin(), c->kvs.end(), kv), c->kvs.end());
+        c->mega_tables.erase(std::remove_if(c->mega_tables.begin(), c->mega_tables.end(),
+                                            [kv](const vvq2_ctx::MegaTable& t) { return t.kv == kv; }),
+                             c->mega_tables.end());
     }
     if (kv->k) cudaFree(kv->k);
     if (kv->v) cudaFree(kv->v);
@@ -829,6 +1044,8 @@ static int kv_xfer(vvq2_kv* kv, int seq, int layer, float* k, float* v, const fl
     if (n_pos == 0) return 0;
     const size_t n = (size_t)n_pos * c->hp.n_kv_heads * c->hp.head_dim;
     float *dk = nullptr, *dv = nullptr;
+    // device-resident k/v may still be being written on another stream
+    if (upload && (is_device_ptr(kc) || is_device_ptr(vc))) CU(cudaDeviceSynchronize());
     CU(cudaMalloc(&dk, n * 4));
     if (cudaMalloc(&dv, n * 4) != cudaSuccess) {
         cudaFree(dk);
@@ -836,15 +1053,15 @@ static int kv_xfer(vvq2_kv* kv, int seq, int layer, float* k, float* v, const fl
     }
     cudaError_t e = cudaSuccess;
     if (upload) {
-        e = cudaMemcpy(dk, kc, n * 4, cudaMemcpyDefault);
-        if (e == cudaSuccess) e = cudaMemcpy(dv, vc, n * 4, cudaMemcpyDefault);
+        e = cudaMemcpyAsync(dk, kc, n * 4, cudaMemcpyDefault, c->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dv, vc, n * 4, cudaMemcpyDefault, c->stream);
         if (e == cudaSuccess) e = kv_upload_launch(kv->layer(layer), seq, dk, dv, n_pos, c->stream);
         if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     } else {
         e = kv_download_launch(kv->layer(layer), seq, dk, dv, n_pos, c->stream);
         if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
-        if (e == cudaSuccess) e = cudaMemcpy(k, dk, n * 4, cudaMemcpyDefault);
-        if (e == cudaSuccess) e = cudaMemcpy(v, dv, n * 4, cudaMemcpyDefault);
+        if (e == cudaSuccess) e = copy_on(k, dk, n * 4, c->stream);
+        if (e == cudaSuccess) e = copy_on(v, dv, n * 4, c->stream);
     }
     cudaFree(dk);
     cudaFree(dv);
@@ -1048,8 +1265,22 @@ int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, cons
         vvq2_ctx::Graph g{kv, sv, bucket, c->prof_on, nullptr, 0, {}};
         const long long k0 = launch_count();
         cudaGraph_t graph = nullptr;
+        if (mega_eligible(c, M)) {
+            MegaLayer* dl = nullptr;
+            if (int rc = ensure_mega_table(c, kv, &dl)) return rc;
+        }
         CU(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-        int rc = enqueue_decode(c, kv, M, split, nsplit, st, c->prof_on ? &g.recs : nullptr, attn_bytes);
+        int rc;
+        if (mega_eligible(c, M)) {
+            double step_bytes = attn_bytes + (double)weight_bytes(c->lm_head);
+            for (const auto& L : c->layers)
+                step_bytes += (double)(weight_bytes(L.qkv) + weight_bytes(L.o) + weight_bytes(L.gate) +
+                                       weight_bytes(L.up) + weight_bytes(L.down));
+            step_bytes += (double)attn_bytes * (c->hp.n_layers - 1);   // attn_bytes covers one layer
+            rc = enqueue_decode_mega(c, kv, M, bucket, st, c->prof_on ? &g.recs : nullptr, step_bytes);
+        } else {
+            rc = enqueue_decode(c, kv, M, split, nsplit, st, c->prof_on ? &g.recs : nullptr, attn_bytes);
+        }
         cudaError_t e = cudaStreamEndCapture(st, &graph);
         if (rc) {
             if (graph) cudaGraphDestroy(graph);
@@ -1104,6 +1335,20 @@ int vvq2_profile_read(vvq2_ctx* c, int kind, double* ms, double* bytes, int64_t*
     if (ms) *ms = c->prof_ms[kind];
     if (bytes) *bytes = c->prof_bytes[kind];
     if (launches) *launches = c->prof_n[kind];
+    return 0;
+}
+
+int vvq2_mega_trace(vvq2_ctx* c, uint64_t* out, int64_t cap, int* grid, int* slots) {
+    if (int rc = check_ctx(c)) return rc;
+    if (!c->mega_trace) return fail(VVQ2_ERR_INVALID_ARG, "no persistent-step trace (set VVQ2_MEGA_TRACE=1)");
+    const int sl = mega_trace_slots(c->hp.n_layers);
+    const int64_t n = (int64_t)sl * c->mega_grid;
+    if (grid) *grid = c->mega_grid;
+    if (slots) *slots = sl;
+    if (!out) return 0;
+    if (cap < n) return fail(VVQ2_ERR_INVALID_ARG, "trace buffer too small");
+    CU(cudaDeviceSynchronize());
+    CU(cudaMemcpy(out, c->mega_trace, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost));
     return 0;
 }
 

@@ -65,7 +65,7 @@ __device__ __forceinline__ void produce_row(const DevW& W, int row, int k0, uint
         uint4 q[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) q[i] = __ldg(qp + i);
-        const __half2 dd = *reinterpret_cast<const __half2*>(W.d + (size_t)row * (W.cols / 32) + k0 / 32);
+        const __half2 dd = *reinterpret_cast<const __half2*>(W.d + (size_t)row * W.d_stride + k0 / 32);
         const float d0 = __low2float(dd), d1 = __high2float(dd);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -128,7 +128,7 @@ __device__ __forceinline__ void produce_row(const DevW& W, int row, int k0, uint
         qh[0] = __ldg(reinterpret_cast<const uint4*>(b + 128 + hf * 32));
         qh[1] = __ldg(reinterpret_cast<const uint4*>(b + 128 + hf * 32) + 1);
         const int8_t* scl = reinterpret_cast<const int8_t*>(b + 192);
-        const float dsb = __half2float(W.d[(size_t)row * (W.cols / 256) + sb]);
+        const float dsb = __half2float(W.d[(size_t)row * W.d_stride + sb]);
         float ds[4];   // (k - k0q) * 2 + l/16
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk)

@@ -23,11 +23,17 @@
 // warp starts pulling its first unit's weights into L2 before
 // griddepcontrol.wait, overlapping the previous kernel's tail.
 #include "common.cuh"
+#include "gemv_dev.cuh"
 #include "kernels.h"
 
 namespace vvq2 {
 
 namespace {
+
+using gd::Chunk;
+using gd::load_chunk;
+using gd::expand4;
+using gd::clear_chunk;
 
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
@@ -36,109 +42,6 @@ constexpr size_t GEMV_SMEM_MAX = 200 * 1024;
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
-
-// One 16-element chunk of one weight row, as loaded (raw bits + block scales).
-struct Chunk {
-    uint4 r0, r1, r2, r3;   // raw: Q8_0 q in r0; Q5_K qs/qh in r0/r1; Q6_K ql/qh in r0/r1;
-                            // F16 in r0/r1; F32 in r0..r3
-    float scale;            // Q8_0 d; Q5_K d*sc; Q6_K d*sc
-    float mscale;           // Q5_K dmin*m
-    int shift;              // Q5_K sub-block j; Q6_K quarter k
-};
-
-template <int WT>
-__device__ __forceinline__ void load_chunk(const DevW& W, int row, int c, Chunk& ch) {
-    const uint8_t* rp = W.q + (size_t)row * W.row_stride;
-    if constexpr (WT == W_Q8_0) {
-        ch.r0 = __ldg(reinterpret_cast<const uint4*>(rp) + c);
-        ch.scale = __half2float(W.d[(size_t)row * (W.cols / 32) + c / 2]);
-    } else if constexpr (WT == W_Q5_K) {
-        const int sb = c >> 4, e0 = (c & 15) * 16, j = e0 / 32, l0 = e0 & 31;
-        const uint8_t* b = rp + (size_t)sb * Q5K_BYTES;
-        const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(b));
-        ch.r0 = __ldg(reinterpret_cast<const uint4*>(b + 48 + 32 * (j >> 1) + l0));
-        ch.r1 = __ldg(reinterpret_cast<const uint4*>(b + 16 + l0));
-        const uint8_t* scb = reinterpret_cast<const uint8_t*>(&hdr) + 4;
-        int sc, m;
-        if (j < 4) {
-            sc = scb[j] & 63;
-            m = scb[j + 4] & 63;
-        } else {
-            sc = (scb[j + 4] & 0xF) | ((scb[j - 4] >> 6) << 4);
-            m = (scb[j + 4] >> 4) | ((scb[j] >> 6) << 4);
-        }
-        const __half2 dh = *reinterpret_cast<const __half2*>(&hdr.x);
-        ch.scale = __fmul_rn(__low2float(dh), (float)sc);    // d1 = d*sc   (dequantize_row_q5_K)
-        ch.mscale = __fmul_rn(__high2float(dh), (float)m);   // m1 = dmin*m
-        ch.shift = j;
-    } else if constexpr (WT == W_Q6_K) {
-        const int sb = c >> 4, e0 = (c & 15) * 16;
-        const int hf = e0 >> 7, r = e0 & 127, k = r >> 5, l0 = r & 31;
-        const uint8_t* b = rp + (size_t)sb * Q6K_PACKED;
-        ch.r0 = __ldg(reinterpret_cast<const uint4*>(b + hf * 64 + (k & 1) * 32 + l0));
-        ch.r1 = __ldg(reinterpret_cast<const uint4*>(b + 128 + hf * 32 + l0));
-        const int8_t sc = reinterpret_cast<const int8_t*>(b + 192)[hf * 8 + (l0 >> 4) + 2 * k];
-        ch.scale = __fmul_rn(__half2float(W.d[(size_t)row * (W.cols / 256) + sb]), (float)sc);  // d*sc
-        ch.shift = k;
-    } else if constexpr (WT == W_F16) {
-        const uint4* p = reinterpret_cast<const uint4*>(rp) + 2 * c;
-        ch.r0 = __ldg(p);
-        ch.r1 = __ldg(p + 1);
-    } else {
-        const uint4* p = reinterpret_cast<const uint4*>(rp) + 4 * c;
-        ch.r0 = __ldg(p);
-        ch.r1 = __ldg(p + 1);
-        ch.r2 = __ldg(p + 2);
-        ch.r3 = __ldg(p + 3);
-    }
-}
-
-__device__ __forceinline__ uint32_t word(const uint4& v, int t) {
-    return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w;
-}
-
-// Dequantized weights g*4 .. g*4+3 of the chunk, bit-exact with ggml's
-// dequantize_row_*: Q8_0 q*d; Q5_K d1*q - m1; Q6_K (d*sc)*(q-32); F16/F32 as is.
-template <int WT>
-__device__ __forceinline__ void expand4(const Chunk& ch, int g, float* w) {
-    if constexpr (WT == W_Q8_0) {
-        const uint32_t q = word(ch.r0, g);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) w[e] = __fmul_rn((float)(int8_t)((q >> (8 * e)) & 0xff), ch.scale);
-    } else if constexpr (WT == W_Q5_K) {
-        const int j = ch.shift;
-        const uint32_t q = ((word(ch.r0, g) >> (4 * (j & 1))) & 0x0F0F0F0Fu) |
-                           (((word(ch.r1, g) >> j) & 0x01010101u) << 4);
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-            w[e] = __fsub_rn(__fmul_rn(ch.scale, (float)((q >> (8 * e)) & 0xff)), ch.mscale);
-    } else if constexpr (WT == W_Q6_K) {
-        const int k = ch.shift;
-        const uint32_t q = ((word(ch.r0, g) >> (4 * (k >> 1))) & 0x0F0F0F0Fu) |
-                           (((word(ch.r1, g) >> (2 * k)) & 0x03030303u) << 4);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) w[e] = __fmul_rn(ch.scale, (float)((int)((q >> (8 * e)) & 0xff) - 32));
-    } else if constexpr (WT == W_F16) {
-        const uint4& v = g < 2 ? ch.r0 : ch.r1;
-        const uint32_t a = word(v, (g & 1) * 2), b = word(v, (g & 1) * 2 + 1);
-        const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&a));
-        const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&b));
-        w[0] = f0.x; w[1] = f0.y; w[2] = f1.x; w[3] = f1.y;
-    } else {
-        const uint4& v = g == 0 ? ch.r0 : g == 1 ? ch.r1 : g == 2 ? ch.r2 : ch.r3;
-        w[0] = __uint_as_float(v.x); w[1] = __uint_as_float(v.y);
-        w[2] = __uint_as_float(v.z); w[3] = __uint_as_float(v.w);
-    }
-}
-
-// L2 prefetch of the chunks a lane will read for one weight row
-template <int WT>
-__device__ __forceinline__ void prefetch_row(const DevW& W, int row, int lane, int nchunk) {
-    const uint8_t* rp = W.q + (size_t)row * W.row_stride;
-    const int bytes_per_chunk = (int)(W.row_stride / nchunk);
-    for (int c = lane; c < nchunk; c += 32)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + (size_t)c * bytes_per_chunk));
-}
 
 // Row r of unit u: (tensor, row).  QKV: two NEOX pairs (i0, i0+1) of one head;
 // SwiGLU: gate rows i0, i0+1 then up rows i0, i0+1; else 4 consecutive rows.
@@ -232,17 +135,6 @@ __device__ void stage_activations(const GemvArgs& a, float* act) {
         }
     }
     __syncthreads();
-}
-
-// zero only the fields the type uses, so unused ones stay dead in registers
-template <int WT>
-__device__ __forceinline__ void clear_chunk(Chunk& ch) {
-    ch.r0 = make_uint4(0, 0, 0, 0);
-    if constexpr (WT != W_Q8_0) ch.r1 = make_uint4(0, 0, 0, 0);
-    if constexpr (WT == W_F32) ch.r2 = ch.r3 = make_uint4(0, 0, 0, 0);
-    if constexpr (WT == W_Q8_0 || WT == W_Q5_K || WT == W_Q6_K) ch.scale = 0.f;
-    if constexpr (WT == W_Q5_K) ch.mscale = 0.f;
-    if constexpr (WT == W_Q5_K || WT == W_Q6_K) ch.shift = 0;
 }
 
 // Work decomposition.  A unit is NR weight rows; a unit is split across `wpu`

@@ -64,6 +64,50 @@ struct GemmArgs {
 cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st);
 cudaError_t gemm_tc_prepare();
 
+// ------------------------------------------------------ persistent decode step
+struct MegaLayer {
+    DevW qkv, o, gate, up, down;
+    const float* attn_norm = nullptr;
+    const float* ffn_norm = nullptr;
+    const float* qkv_bias = nullptr;
+    KvLayer kv;
+};
+
+struct MegaArgs {
+    const MegaLayer* layers = nullptr;   // device array
+    int n_layers = 0, H = 0, F = 0, nq = 0, nkv = 0, hd = 0, M = 0, grid = 0;
+    DevW lm_head, tok_embd;
+    const float* out_norm = nullptr;
+    float *X = nullptr, *ATT = nullptr, *FA = nullptr;
+    float* QKV = nullptr;                // [M][qkv_rows] raw q|k|v (+bias), before RoPE
+    int qkv_rows = 0;
+    float *part = nullptr, *part_ml = nullptr;   // [M][64][nq][hd], [M][64][nq][2]
+    int* counters = nullptr;
+    RowMeta* meta = nullptr;
+    int32_t* tok = nullptr;
+    unsigned long long* amax = nullptr;
+    unsigned long long* bar_count = nullptr;
+    unsigned int* epoch = nullptr;
+    int* abort = nullptr;
+    int split = 0, nsplit = 0;
+    float eps = 0.f, rope_ts = 0.f, scale = 0.f;
+    int* err = nullptr;
+    // shared-memory plan: [union_bytes: activations | attention][nstage x slot_bytes ring]
+    int nstage = 0, slot_bytes = 0, union_bytes = 0;
+    int t_qkv = 1, t_o = 1, t_gu = 1, t_down = 1, t_lm = 1;   // weight rows per ring tile
+    // optional phase timeline: [slot][grid] %globaltimer ns; slot 0 = start,
+    // 1 + 2b / 2 + 2b = arrival at / release from grid barrier b, last = end
+    unsigned long long* trace = nullptr;
+};
+__host__ __device__ constexpr int mega_trace_slots(int n_layers) { return 2 * (5 * n_layers + 2) + 2; }
+cudaError_t decode_mega_prepare();
+cudaError_t decode_mega_launch(const MegaArgs& a, size_t smem, cudaStream_t st);
+int decode_mega_union_bytes(int hd, int M, int kmax);
+int decode_mega_max_stages();
+int decode_mega_consumer_warps();
+int decode_mega_smem_limit();
+int decode_mega_grid();
+
 // ------------------------------------------------------ decode attention
 struct AttnDecodeArgs {
     const float* q = nullptr;      // [M][nq*hd] (roped)

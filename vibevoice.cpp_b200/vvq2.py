@@ -75,6 +75,7 @@ def lib() -> C.CDLL:
             "vvq2_debug_gemm": (I, [I, P, I, I, P, I, P]),
             "vvq2_attention_decode_noalloc": (I, [P, P, P, P, I, P, I, I, I, I, I, P, P]),
             "vvq2_profile_read": (I, [P, I, P, P, P]),
+            "vvq2_mega_trace": (I, [P, P, C.c_int64, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -161,6 +162,14 @@ class Engine:
         ms, by, n = C.c_double(), C.c_double(), C.c_int64()
         _chk(lib().vvq2_profile_read(self.ctx, kind, C.byref(ms), C.byref(by), C.byref(n)))
         return ms.value, by.value, n.value
+
+    def mega_trace(self) -> np.ndarray:
+        """[slots][grid] %globaltimer stamps of the last persistent decode step."""
+        g, sl = C.c_int(), C.c_int()
+        _chk(lib().vvq2_mega_trace(self.ctx, None, 0, C.byref(g), C.byref(sl)))
+        out = np.zeros((sl.value, g.value), np.uint64)
+        _chk(lib().vvq2_mega_trace(self.ctx, _p(out), out.size, None, None))
+        return out
 
     def kv(self, n_seqs: int, max_seq: int) -> "KV":
         return KV(self, n_seqs, max_seq)
