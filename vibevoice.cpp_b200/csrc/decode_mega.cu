@@ -7,21 +7,23 @@
 // its weight stream cold.  Here one CTA per SM walks the phase list,
 // separated by grid-wide barriers, and the weight stream does not stop:
 //
-//  * warp 15 of every CTA is a producer.  Its lane 0 walks the CTA's weight
-//    tiles of the WHOLE step in consumption order (this CTA's contiguous row
-//    slice of every matrix, cut into tiles of T rows) and bulk-copies them
-//    (cp.async.bulk; a run of Q8_0 rows with their scales is one contiguous
-//    range) into a ring of shared-memory slots, gated only by free slots.
-//    Weights do not depend on activations, so while the consumers wait in a
-//    grid barrier or run attention, the next phases' weights are landing.
-//  * warps 0..14 consume: stage the phase's activation rows (RMSNorm'd where
-//    the layer norms) from L2 into shared memory; then each warp takes whole
-//    tiles (round robin), computes T x M dot products over the full K (exact
-//    dequantized int8 weights x f32 activations, packed FFMA2), reduces them
-//    with one transposing butterfly and applies the epilogue (bias, residual
-//    add, SwiGLU, running argmax) straight to global memory.
+//  * weights: every warp owns D slots of a shared-memory ring (D = 1 or 2)
+//    and streams its own share of the CTA's weight tiles: the CTA's
+//    contiguous row slice of every matrix of the WHOLE step, cut into tiles
+//    of T rows, goes round robin over the 16 warps (tile i -> warp i % 16).
+//    Right after computing a tile a warp bulk-copies (cp.async.bulk; a run
+//    of Q8_0 rows with their scales is one contiguous range) its next tile
+//    into the freed slot.  Weights do not depend on activations, so a warp's
+//    next tiles -- often of the next phase -- are in flight while it waits in
+//    a grid barrier or runs attention, and no warp waits for another's slot.
+//  * each warp stages nothing of its own: the CTA stages the phase's
+//    activation rows (RMSNorm'd where the layer norms) from L2 into shared
+//    memory, then each warp computes its tiles' T x M dot products over the
+//    full K (exact dequantized int8 weights x f32 activations, packed FFMA2),
+//    reduces them with one transposing butterfly and applies the epilogue
+//    (bias, residual add, SwiGLU, running argmax) straight to global memory.
 //  * attention: one item per (row, KV head, split of whole 64-key pages) on
-//    128-thread groups.  The first pages of each group's first item are
+//    128-thread groups.  The first page of each group's first item is
 //    requested by TMA BEFORE the QKV -> attention barrier (past keys do not
 //    depend on this step).  The item applies RoPE to this step's raw q/k,
 //    patches the new key/value row into its tile, appends it to the paged
@@ -30,7 +32,7 @@
 // Every wait is bounded.  A wait that gives up records an error code, raises
 // the global abort flag and this CTA's `fail` flag; all warps then skip the
 // remaining work (control flow only changes at grid barriers, where it is
-// uniform) and the producer waits for its copies in flight before returning.
+// uniform) and wait for their copies in flight before returning.
 #include <algorithm>
 
 #include "common.cuh"
@@ -42,11 +44,9 @@ namespace vvq2 {
 namespace {
 
 constexpr int MT = 512;                 // threads per CTA
-constexpr int NCW = 15;                 // consumer warps
-constexpr int NCT = NCW * 32;           // consumer threads
-constexpr int PRODUCER = 15;            // producer warp
-constexpr int BAR_CONS = 1;             // named barrier of the consumer threads (2.. = attention groups)
-constexpr int MAX_STAGES = 32;
+constexpr int NCW = 16;                 // warps (all compute and stream)
+constexpr int NCT = NCW * 32;
+constexpr int MAX_STAGES = 32;          // ring slots: NCW x D
 constexpr int ATT_THREADS = 128;
 constexpr int MAXG = 8;                 // q heads per KV head
 constexpr int PAGE = KV_PAGE;           // keys per page / tile
@@ -58,9 +58,9 @@ enum { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DOWN = 3, PH_LM = 4 };
 
 template <int HD>
 struct AttConst {
-    static constexpr int NG = HD >= 128 ? 2 : 3;                 // attention groups per CTA
+    static constexpr int NG = 2;                                 // attention groups per CTA
     static constexpr int TILE_BYTES = PAGE * HD * 2;             // one page of K (or V) of one head
-    static constexpr int GROUP_BYTES = 4 * TILE_BYTES;           // K, V x 2 stages
+    static constexpr int GROUP_BYTES = 2 * TILE_BYTES;           // K and V of one page
 };
 
 // per-group attention state (in the phase-shared dynamic region)
@@ -71,7 +71,6 @@ struct __align__(16) AttSh {
     float run_max[MAXG], run_sum[MAXG], alpha[MAXG];
     float wts[MAXG][MAX_MERGE];
     float inv_den[MAXG];
-    float2 cs[HD / 2];             // RoPE (cos, sin) of this row's position
     __half kn[HD], vn[HD];         // this step's key (roped) and value row
     int is_last, failed;
 };
@@ -93,7 +92,7 @@ __device__ __forceinline__ void trace_mark(const MegaArgs& a, int slot) {
     if (a.trace) a.trace[(size_t)slot * gridDim.x + blockIdx.x] = gtimer();
 }
 
-__device__ __forceinline__ void cbar() { asm volatile("bar.sync %0, %1;" ::"n"(BAR_CONS), "n"(NCT) : "memory"); }
+__device__ __forceinline__ void cbar() { __syncthreads(); }
 
 struct GroupSync {
     int id;
@@ -135,16 +134,15 @@ __device__ void raise_fail(const MegaArgs& a, Ctl& ctl, int code) {
     *(volatile int*)&ctl.fail = 1;
 }
 
-// Grid barrier over the consumer threads of every CTA.
+// Grid barrier over the consumer threads of every CTA.  The arrival is one
+// release reduction (orders this CTA's writes, observed through the CTA
+// barrier, before it); the wait polls with acquire loads.
 __device__ void grid_sync(const MegaArgs& a, Ctl& ctl) {
-    // generic global writes (K/V rows) are read by TMA in later steps
-    asm volatile("fence.proxy.async.global;" ::: "memory");
     cbar();
     if (threadIdx.x == 0) {
         trace_mark(a, 1 + 2 * ctl.nbar);
         ctl.target += gridDim.x;
-        __threadfence();
-        atomicAdd(a.bar_count, 1ull);
+        asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(a.bar_count), "l"(1ull) : "memory");
         uint32_t i = 0;
         while (true) {
             unsigned long long v;
@@ -156,7 +154,6 @@ __device__ void grid_sync(const MegaArgs& a, Ctl& ctl) {
                 atomicExch(a.abort, 1);
                 break;
             }
-            __nanosleep(20);
         }
         __threadfence();
         if (*(volatile int*)a.abort) {
@@ -177,6 +174,7 @@ struct Geo {
     int r0, n;             // slice rows
     int T;                 // rows per tile (per matrix)
     int K;
+    int ntiles;
 };
 
 __device__ __forceinline__ Geo phase_geo(const MegaArgs& a, int li, int ph) {
@@ -204,40 +202,43 @@ __device__ __forceinline__ Geo phase_geo(const MegaArgs& a, int li, int ph) {
     g.p1 = w1 ? w1->q + (size_t)g.r0 * g.rs : nullptr;
     g.T = T;
     g.K = w0->cols;
+    g.ntiles = (g.n + T - 1) / T;
     return g;
 }
 
-// ------------------------------------------------------------ producer
-__device__ void producer(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint64_t* empty, Ctl& ctl) {
-    const volatile int* fl = &ctl.fail;
-    const int nst = a.nstage;
-    uint32_t seq = 0;
-    bool ok = true;
-    for (int li = 0; li <= a.n_layers && ok; ++li) {
-        const int nph = li == a.n_layers ? 1 : 4;
-        for (int ph = 0; ph < nph && ok; ++ph) {
-            const Geo g = phase_geo(a, li, li == a.n_layers ? PH_LM : ph);
-            for (int r = 0; r < g.n; r += g.T) {
-                const int slot = (int)(seq % nst);
-                if (seq >= (uint32_t)nst && !wait_or_fail(&empty[slot], ((seq / nst) - 1) & 1, fl)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t b0 = (uint32_t)(min(g.T, g.n - r) * g.rs);
-                uint8_t* dst = ring + (size_t)slot * a.slot_bytes;
-                tc::fence_proxy_async_smem();   // consumers' generic reads of the slot are ordered before
-                tc::mbar_arrive_expect_tx(&full[slot], g.p1 ? 2 * b0 : b0);
-                bulk_g2s(dst, g.p0 + (size_t)r * g.rs, b0, &full[slot]);
-                if (g.p1) bulk_g2s(dst + (size_t)g.T * g.rs, g.p1 + (size_t)r * g.rs, b0, &full[slot]);
-                ++seq;
-            }
-        }
+// ------------------------------------------------------------ weight ring
+// Per-warp streaming state (identical in all lanes; lane 0 issues).
+struct WarpRing {
+    uint32_t used;         // tiles this warp has consumed
+    uint32_t issued;       // tiles this warp has requested
+    int ip, ij;            // next tile to request: phase-table index, tile in phase
+};
+
+__device__ __forceinline__ void ring_normalize(WarpRing& w, const Geo* tab, int nph) {
+    while (w.ip < nph && w.ij >= tab[w.ip].ntiles) {
+        w.ij -= tab[w.ip].ntiles;
+        ++w.ip;
     }
-    // drain: every issued copy has landed before the CTA exits.  (Slot i is
-    // always consumed by warp i % NCW: a consumer never polls a slot's
-    // barrier before the slot's previous tile has landed and been released.)
-    const uint32_t lo = seq > (uint32_t)nst ? seq - nst : 0;
-    for (uint32_t s = lo; s < seq; ++s) tc::mbar_wait(&full[s % nst], (s / nst) & 1, 1u << 20);
+}
+
+// Request this warp's next tile into slot warp + NCW * (issued % D).
+__device__ __forceinline__ void ring_issue(WarpRing& w, const Geo* tab, int nph, uint8_t* ring, uint64_t* full,
+                                           int warp, int lane, int D, int slot_bytes) {
+    if (w.ip >= nph) return;
+    const Geo& e = tab[w.ip];
+    const int slot = warp + NCW * (int)(w.issued % D);
+    if (lane == 0) {
+        const int r = w.ij * e.T;
+        const uint32_t b0 = (uint32_t)(min(e.T, e.n - r) * e.rs);
+        uint8_t* dst = ring + (size_t)slot * slot_bytes;
+        tc::fence_proxy_async_smem();   // this warp's generic reads of the slot come first
+        tc::mbar_arrive_expect_tx(&full[slot], e.p1 ? 2 * b0 : b0);
+        bulk_g2s(dst, e.p0 + (size_t)r * e.rs, b0, &full[slot]);
+        if (e.p1) bulk_g2s(dst + (size_t)e.T * e.rs, e.p1 + (size_t)r * e.rs, b0, &full[slot]);
+    }
+    w.issued += 1;
+    w.ij += NCW;
+    ring_normalize(w, tab, nph);
 }
 
 // ------------------------------------------------------------ activations
@@ -253,6 +254,59 @@ __device__ void stage(const MegaArgs& a, const float* x, const float* norm_w, in
     float ss[MB];
 #pragma unroll
     for (int m = 0; m < MB; ++m) ss[m] = 0.f;
+    if (norm_w && K4 <= 2 * NCT) {
+        // rows go to shared memory; the norm weights are loaded in the same
+        // round trip and kept in registers for the scaling pass
+        float4 w[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int k4 = tid + i * NCT;
+            if (k4 < K4) {
+                w[i] = __ldg(reinterpret_cast<const float4*>(norm_w) + k4);
+                const int c = k4 >> 2, g = k4 & 3;
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    const float4 v = __ldcg(reinterpret_cast<const float4*>(x + (size_t)m * K) + k4);
+                    ss[m] = fmaf(v.x, v.x, ss[m]);
+                    ss[m] = fmaf(v.y, v.y, ss[m]);
+                    ss[m] = fmaf(v.z, v.z, ss[m]);
+                    ss[m] = fmaf(v.w, v.w, ss[m]);
+                    act4[(m * 4 + g) * NC + c] = v;
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            const float t = warp_sum(ss[m]);
+            if (lane == 0) red[m * NCW + warp] = t;
+        }
+        cbar();
+        if (tid < MB) {
+            float t = 0.f;
+            for (int i = 0; i < NCW; ++i) t += red[tid * NCW + i];
+            scl[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps)));
+        }
+        cbar();
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int k4 = tid + i * NCT;
+            if (k4 < K4) {
+                const int c = k4 >> 2, g = k4 & 3;
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    const float sc = scl[m];
+                    float4 t = act4[(m * 4 + g) * NC + c];
+                    t.x = __fmul_rn(__fmul_rn(t.x, sc), w[i].x);   // (x * scale) * w: ggml_rms_norm, then ggml_mul
+                    t.y = __fmul_rn(__fmul_rn(t.y, sc), w[i].y);
+                    t.z = __fmul_rn(__fmul_rn(t.z, sc), w[i].z);
+                    t.w = __fmul_rn(__fmul_rn(t.w, sc), w[i].w);
+                    act4[(m * 4 + g) * NC + c] = t;
+                }
+            }
+        }
+        cbar();
+        return;
+    }
     for (int k4 = tid; k4 < K4; k4 += NCT) {
         const int c = k4 >> 2, g = k4 & 3;
 #pragma unroll
@@ -376,76 +430,88 @@ __device__ __forceinline__ float warp_transpose_sum(float (&v)[NV], int lane) {
     return v[0];
 }
 
-// One tile of a GEMV phase: math + epilogue.
+// One tile of a GEMV phase: math + epilogue.  The epilogue's global
+// operands (old residual, bias) are loaded before the math so their latency
+// overlaps it.  For lm_head the writer lanes keep a running argmax key.
 template <int PH, int T, int MB>
 __device__ __forceinline__ void tile_epilogue(const MegaArgs& a, const MegaLayer* L, const uint8_t* tile,
                                               const Geo& g, int r, const float4* act4, int lane,
-                                              unsigned long long* best) {
+                                              unsigned long long& kbest) {
     constexpr int NR = PH == PH_GU ? 2 * T : T;
     constexpr int NV = NR * MB;
     constexpr int SH = 5 - Log2<NV>::v;
-    float acc[NV];
-    tile_dot<NR, MB>(tile, (int)g.rs, g.K, act4, lane, acc);
-    float v = warp_transpose_sum<NV>(acc, lane);
     const int idx = lane >> SH;              // = t * MB + m
     const int t = idx / MB, m = idx % MB;
     const bool writer = (lane & ((1 << SH) - 1)) == 0;
     const int nr = min(T, g.n - r);
+    const int row = g.r0 + r + t;
+    const bool w_ok = writer && t < nr;
+    float pre = 0.f;
+    if constexpr (PH == PH_O || PH == PH_DOWN) {
+        if (w_ok) pre = __ldcg(a.X + (size_t)m * a.H + row);
+    } else if constexpr (PH == PH_QKV) {
+        if (w_ok && L->qkv_bias) pre = L->qkv_bias[row];
+    }
+    float acc[NV];
+    tile_dot<NR, MB>(tile, (int)g.rs, g.K, act4, lane, acc);
+    float v = warp_transpose_sum<NV>(acc, lane);
     if constexpr (PH == PH_GU) {
         const float u = __shfl_sync(0xffffffffu, v, (lane + ((T * MB) << SH)) & 31);
-        if (writer && t < nr) a.FA[(size_t)m * a.F + g.r0 + r + t] = __fmul_rn(silu_ref(v), u);   // silu(g) * u
+        if (w_ok) a.FA[(size_t)m * a.F + row] = __fmul_rn(silu_ref(v), u);   // ggml_swiglu_split: silu(g) * u
     } else if constexpr (PH == PH_QKV) {
-        if (writer && t < nr) {
-            const int row = g.r0 + r + t;
-            if (L->qkv_bias) v = __fadd_rn(v, L->qkv_bias[row]);
-            a.QKV[(size_t)m * a.qkv_rows + row] = v;
-        }
+        if (w_ok) a.QKV[(size_t)m * a.qkv_rows + row] = L->qkv_bias ? __fadd_rn(v, pre) : v;
     } else if constexpr (PH == PH_LM) {
-        if (writer && t < nr) atomicMax(&best[m], argmax_key(v, g.r0 + r + t));
-    } else {   // O-proj / down: residual add into X (ggml_add(x, o))
-        if (writer && t < nr) {
-            float* dst = a.X + (size_t)m * a.H + g.r0 + r + t;
-            *dst = __fadd_rn(__ldcg(dst), v);
+        if (w_ok) {
+            const unsigned long long k = argmax_key(v, row);
+            kbest = k > kbest ? k : kbest;
         }
+    } else {   // O-proj / down: residual add into X (ggml_add(x, o))
+        if (w_ok) a.X[(size_t)m * a.H + row] = __fadd_rn(pre, v);
     }
 }
 
 template <int PH, int MB>
-__device__ void gemv_tiles(const MegaArgs& a, int li, const uint8_t* ring, uint64_t* full, uint64_t* empty,
-                           const float* act, uint32_t& seq, Ctl& ctl, unsigned long long* best) {
+__device__ void gemv_tiles(const MegaArgs& a, int li, const Geo* tab, int nph, uint8_t* ring, uint64_t* full,
+                           const float* act, uint32_t& seq, WarpRing& wr, int D, Ctl& ctl,
+                           unsigned long long* best) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const Geo g = phase_geo(a, li, PH);
+    const Geo& g = tab[PH == PH_LM ? 4 * a.n_layers : 4 * li + PH];
     const MegaLayer* L = PH == PH_LM ? nullptr : &a.layers[li];
-    const int ntiles = (g.n + g.T - 1) / g.T;
     const float4* act4 = reinterpret_cast<const float4*>(act);
     const int j0 = (warp - (int)(seq % NCW) + NCW) % NCW;
     const volatile int* fl = &ctl.fail;
-    for (int j = j0; j < ntiles; j += NCW) {
-        const uint32_t s = seq + j;
-        const int slot = (int)(s % a.nstage);
-        if (!wait_or_fail(&full[slot], (s / a.nstage) & 1, fl)) {
+    unsigned long long kbest = 0ull;
+    for (int j = j0; j < g.ntiles; j += NCW) {
+        const int slot = warp + NCW * (int)(wr.used % D);
+        if (!wait_or_fail(&full[slot], (wr.used / D) & 1, fl)) {
             if (lane == 0 && !*fl) raise_fail(a, ctl, 4);
             break;
         }
         const uint8_t* tile = ring + (size_t)slot * a.slot_bytes;
         const int r = j * g.T;
         switch (g.T) {
-            case 1: tile_epilogue<PH, 1, MB>(a, L, tile, g, r, act4, lane, best); break;
-            case 2: tile_epilogue<PH, 2, MB>(a, L, tile, g, r, act4, lane, best); break;
-            case 4: tile_epilogue<PH, 4, MB>(a, L, tile, g, r, act4, lane, best); break;
+            case 1: tile_epilogue<PH, 1, MB>(a, L, tile, g, r, act4, lane, kbest); break;
+            case 2: tile_epilogue<PH, 2, MB>(a, L, tile, g, r, act4, lane, kbest); break;
             default:
-                if constexpr (PH != PH_GU) tile_epilogue<PH, 8, MB>(a, L, tile, g, r, act4, lane, best);
+                if constexpr (PH != PH_GU) tile_epilogue<PH, 4, MB>(a, L, tile, g, r, act4, lane, kbest);
                 break;
         }
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&empty[slot]);
+        wr.used += 1;
+        ring_issue(wr, tab, nph, ring, full, warp, lane, D, a.slot_bytes);   // refill the slot just freed
     }
-    seq += ntiles;
+    if constexpr (PH == PH_LM) {
+        // writer lanes hold one row's running best; the row index m is a function of the lane and T
+        const int sh = 5 - (g.T == 1 ? 0 : g.T == 2 ? 1 : 2) - (MB == 2 ? 1 : 0);
+        if (kbest) atomicMax(&best[(lane >> sh) % MB], kbest);
+    }
+    seq += g.ntiles;
 }
 
 // ------------------------------------------------------------ attention
 struct AttItem {
     int m, g, s, nsplit, j0, j1, ntiles;
+    int page0;             // physical page of the first tile
     RowMeta rm;
 };
 
@@ -460,26 +526,29 @@ __device__ __forceinline__ bool att_item_geo(const MegaArgs& a, int it, AttItem&
     x.j0 = x.s * a.split;
     x.j1 = min(lim, x.j0 + a.split);
     x.ntiles = (x.j1 - x.j0 + PAGE - 1) / PAGE;
+    x.page0 = __ldg(a.layers[0].kv.block_table + (size_t)x.rm.seq * a.layers[0].kv.max_pages + x.j0 / PAGE);
     return true;
 }
 
+// K and V of page `tile` of the item into the group's single stage.
 template <int HD>
 __device__ __forceinline__ void att_issue(const KvLayer& kv, const AttItem& x, int tile, __half* kt, __half* vt,
                                           uint64_t* bar) {
     constexpr int TB = AttConst<HD>::TILE_BYTES;
-    const int b = tile & 1;
-    const int page = __ldg(kv.block_table + (size_t)x.rm.seq * kv.max_pages + (x.j0 + tile * PAGE) / PAGE);
+    const int page =
+        tile == 0 ? x.page0 : __ldg(kv.block_table + (size_t)x.rm.seq * kv.max_pages + (x.j0 + tile * PAGE) / PAGE);
     const size_t off = ((size_t)page * kv.n_kv + x.g) * PAGE * HD;
-    tc::mbar_arrive_expect_tx(&bar[b], 2 * TB);
-    bulk_g2s(kt + b * PAGE * HD, kv.k + off, TB, &bar[b]);
-    bulk_g2s(vt + b * PAGE * HD, kv.v + off, TB, &bar[b]);
+    tc::mbar_arrive_expect_tx(bar, 2 * TB);
+    bulk_g2s(kt, kv.k + off, TB, bar);
+    bulk_g2s(vt, kv.v + off, TB, bar);
 }
 
-// One attention item on a 128-thread group.  The first two tiles may already
-// be in flight (`prefetched`).  Returns false after a timed-out wait.
+// One attention item on a 128-thread group.  The first tile may already be
+// in flight (`prefetched`).  Returns false after a timed-out wait.
 template <int HD>
 __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x, int tid, __half* kt, __half* vt,
-                         AttSh<HD>& sh, uint64_t* bar, uint32_t (&uses)[2], bool prefetched, GroupSync sync) {
+                         AttSh<HD>& sh, const float2* cs_row, uint64_t* bar, uint32_t& uses, bool prefetched,
+                         GroupSync sync) {
     const int lane = tid & 31, warp = tid >> 5;
     const int G = a.nq / a.nkv;
     constexpr int half = HD / 2;
@@ -489,43 +558,55 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
     const bool has_new = newj >= x.j0 && newj < x.j1;
 
     if (tid == 0) sh.failed = 0;
-    // RoPE table of this row's position (ggml CPU theta recurrence)
-    for (int i = tid; i < half; i += ATT_THREADS) {
-        float th = (float)rm.pos;
-        for (int k = 0; k < i; ++k) th = __fmul_rn(th, a.rope_ts);
-        sh.cs[i] = make_float2(cosf(th), sinf(th));
-    }
     if (tid < MAXG) {
         sh.run_max[tid] = -INFINITY;
         sh.run_sum[tid] = 0.f;
     }
     sync();
+    // this step's raw q (and new k, v) rows: all loads issued before any use
     const float* qkv = a.QKV + (size_t)m * a.qkv_rows;
-    for (int t = tid; t < G * half; t += ATT_THREADS) {
-        const int h = t / half, i = t % half;
-        const float* q = qkv + (size_t)(g * G + h) * HD;
-        const float x0 = __ldcg(q + i), x1 = __ldcg(q + i + half);
-        const float2 cs = sh.cs[i];
-        const float y0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-        const float y1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-        sh.qs[h][i] = __half2float(__float2half_rn(y0));
-        sh.qs[h][i + half] = __half2float(__float2half_rn(y1));
+    constexpr int QI = (MAXG * half + ATT_THREADS - 1) / ATT_THREADS;
+    float qa[QI], qb[QI], ka = 0.f, kb = 0.f, vv = 0.f;
+#pragma unroll
+    for (int it = 0; it < QI; ++it) {
+        const int t = tid + it * ATT_THREADS;
+        if (t < G * half) {
+            const float* q = qkv + (size_t)(g * G + t / half) * HD + t % half;
+            qa[it] = __ldcg(q);
+            qb[it] = __ldcg(q + half);
+        }
     }
     if (has_new) {
-        const float* k = qkv + (size_t)(a.nq + g) * HD;
-        const float* v = qkv + (size_t)(a.nq + a.nkv + g) * HD;
-        for (int i = tid; i < half; i += ATT_THREADS) {
-            const float x0 = __ldcg(k + i), x1 = __ldcg(k + i + half);
-            const float2 cs = sh.cs[i];
-            sh.kn[i] = __float2half_rn(__fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y)));
-            sh.kn[i + half] = __float2half_rn(__fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x)));
+        if (tid < half) {
+            const float* k = qkv + (size_t)(a.nq + g) * HD + tid;
+            ka = __ldcg(k);
+            kb = __ldcg(k + half);
         }
-        for (int d = tid; d < HD; d += ATT_THREADS) sh.vn[d] = __float2half_rn(__ldcg(v + d));
+        if (tid < HD) vv = __ldcg(qkv + (size_t)(a.nq + a.nkv + g) * HD + tid);
+    }
+#pragma unroll
+    for (int it = 0; it < QI; ++it) {
+        const int t = tid + it * ATT_THREADS;
+        if (t < G * half) {
+            const int h = t / half, i = t % half;
+            const float2 cs = cs_row[i];
+            const float y0 = __fsub_rn(__fmul_rn(qa[it], cs.x), __fmul_rn(qb[it], cs.y));
+            const float y1 = __fadd_rn(__fmul_rn(qa[it], cs.y), __fmul_rn(qb[it], cs.x));
+            sh.qs[h][i] = __half2float(__float2half_rn(y0));
+            sh.qs[h][i + half] = __half2float(__float2half_rn(y1));
+        }
+    }
+    if (has_new) {
+        if (tid < half) {
+            const float2 cs = cs_row[tid];
+            sh.kn[tid] = __float2half_rn(__fsub_rn(__fmul_rn(ka, cs.x), __fmul_rn(kb, cs.y)));
+            sh.kn[tid + half] = __float2half_rn(__fadd_rn(__fmul_rn(ka, cs.y), __fmul_rn(kb, cs.x)));
+        }
+        if (tid < HD) sh.vn[tid] = __float2half_rn(vv);
     }
     if (tid == 0 && !prefetched) {
         tc::fence_proxy_async_smem();
         att_issue<HD>(kv, x, 0, kt, vt, bar);
-        if (x.ntiles > 1) att_issue<HD>(kv, x, 1, kt, vt, bar);
     }
 
     constexpr int NCH = HD / 8;
@@ -540,16 +621,15 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
     const int rot = kk % NCH;
 
     for (int t = 0; t < x.ntiles; ++t) {
-        const int b = t & 1;
-        if (!tc::mbar_wait(&bar[b], uses[b] & 1)) {
+        if (!tc::mbar_wait(bar, uses & 1)) {
             atomicCAS(a.err, 0, 1);
             sh.failed = 1;
         }
-        uses[b] += 1;
+        uses += 1;
         sync();
         if (sh.failed) return false;   // uniform after the group barrier
-        __half* K = kt + b * PAGE * HD;
-        __half* V = vt + b * PAGE * HD;
+        __half* K = kt;
+        __half* V = vt;
         const int tj0 = x.j0 + t * PAGE;
         const int nk = min(PAGE, x.j1 - tj0);
         if (has_new && newj >= tj0 && newj < tj0 + PAGE) {
@@ -639,10 +719,10 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
                 }
             }
         }
-        sync();   // tile buffer b and sc are free again
-        if (tid == 0 && t + 2 < x.ntiles) {
+        sync();   // the stage and sc are free again
+        if (tid == 0 && t + 1 < x.ntiles) {
             tc::fence_proxy_async_smem();
-            att_issue<HD>(kv, x, t + 2, kt, vt, bar);
+            att_issue<HD>(kv, x, t + 1, kt, vt, bar);
         }
     }
     // append this step's K/V row to the paged cache (read by later steps)
@@ -688,7 +768,7 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
     if (!sh.is_last) return true;
     __threadfence();
     const int ns = x.nsplit;
-    float* ml = reinterpret_cast<float*>(kt);   // [G][ns][2]: the K stages are free now
+    float* ml = reinterpret_cast<float*>(kt);   // [G][ns][2]: the K stage is free now
     for (int i = tid; i < G * ns; i += ATT_THREADS) {
         const int h = i / ns, ss = i % ns;
         const float2 v = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + ((size_t)m * MAX_MERGE + ss) * a.nq +
@@ -715,12 +795,19 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
         const int h = t / PAIRS, d2 = t % PAIRS;
         const int qh = g * G + h;
         float2 num = make_float2(0.f, 0.f);
-#pragma unroll 8
-        for (int ss = 0; ss < ns; ++ss) {
-            const float2 p = __ldcg(reinterpret_cast<const float2*>(
-                                        a.part + (((size_t)m * MAX_MERGE + ss) * a.nq + qh) * HD) + d2);
-            num.x = fmaf(sh.wts[h][ss], p.x, num.x);
-            num.y = fmaf(sh.wts[h][ss], p.y, num.y);
+        for (int s0 = 0; s0 < ns; s0 += 8) {   // 8 independent loads in flight per batch
+            float2 p[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (s0 + i < ns)
+                    p[i] = __ldcg(reinterpret_cast<const float2*>(
+                                      a.part + (((size_t)m * MAX_MERGE + s0 + i) * a.nq + qh) * HD) + d2);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (s0 + i < ns) {
+                    num.x = fmaf(sh.wts[h][s0 + i], p[i].x, num.x);
+                    num.y = fmaf(sh.wts[h][s0 + i], p[i].y, num.y);
+                }
         }
         reinterpret_cast<float2*>(out + (size_t)qh * HD)[d2] =
             make_float2(num.x * sh.inv_den[h], num.y * sh.inv_den[h]);
@@ -735,15 +822,19 @@ template <int HD, int MB>
 __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
     extern __shared__ __align__(1024) uint8_t dyn[];
     using AC = AttConst<HD>;
-    __shared__ __align__(8) uint64_t full[MAX_STAGES], empty[MAX_STAGES];
-    __shared__ __align__(8) uint64_t abar[AC::NG][2];
+    __shared__ __align__(8) uint64_t full[MAX_STAGES];
+    __shared__ __align__(8) uint64_t abar[AC::NG];
     __shared__ float red[2 * NCW];
     __shared__ float scl[2];
     __shared__ unsigned long long best[2];
+    __shared__ float2 rope_cs[2][64];              // RoPE (cos, sin) per row: positions are fixed for the launch
     __shared__ Ctl ctl;
     const int tid = threadIdx.x, warp = tid >> 5;
     uint8_t* region = dyn;                         // activations | attention tiles + state
     uint8_t* ring = dyn + a.union_bytes;
+    Geo* tab = reinterpret_cast<Geo*>(ring + (size_t)a.nstage * a.slot_bytes);   // [4 * n_layers + 1]
+    const int nph = 4 * a.n_layers + 1;
+    const int D = a.nstage / NCW;
     float* act = reinterpret_cast<float*>(region);
 
     if (tid == 0) {
@@ -753,24 +844,25 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
         ctl.fail = 0;
         ctl.nbar = 0;
         trace_mark(a, 0);
-        for (int i = 0; i < a.nstage; ++i) {
-            tc::mbar_init(&full[i], 1);
-            tc::mbar_init(&empty[i], 1);
-        }
-        for (int i = 0; i < AC::NG; ++i) {
-            tc::mbar_init(&abar[i][0], 1);
-            tc::mbar_init(&abar[i][1], 1);
-        }
+        for (int i = 0; i < a.nstage; ++i) tc::mbar_init(&full[i], 1);
+        for (int i = 0; i < AC::NG; ++i) tc::mbar_init(&abar[i], 1);
         tc::mbar_fence_init();
     }
     if (tid < 2) best[tid] = 0ull;
     if (blockIdx.x == 0 && tid < MB) a.amax[tid] = 0ull;
+    // this CTA's tile geometry of every phase of the step
+    for (int p = tid; p < nph; p += NCT)
+        tab[p] = phase_geo(a, p == nph - 1 ? 0 : p / 4, p == nph - 1 ? PH_LM : p % 4);
     __syncthreads();
 
-    if (warp == PRODUCER) {
-        if ((tid & 31) == 0) producer(a, ring, full, empty, ctl);
-        return;
-    }
+    // every warp requests its first D tiles (layer 0's weights land during the embedding)
+    const int lane = tid & 31;
+    WarpRing wr;
+    wr.used = wr.issued = 0;
+    wr.ip = 0;
+    wr.ij = warp;
+    ring_normalize(wr, tab, nph);
+    for (int d = 0; d < D; ++d) ring_issue(wr, tab, nph, ring, full, warp, lane, D, a.slot_bytes);
 
     // ---- token embedding: X[m] = dequant(tok_embd[tok[m]])
     {
@@ -789,14 +881,26 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
         }
     }
 
+    // RoPE table of each row's position (ggml CPU theta recurrence)
+    for (int t = tid; t < MB * (HD / 2); t += NCT) {
+        const int m = t / (HD / 2), i = t % (HD / 2);
+        float th = (float)a.meta[m].pos;
+        for (int k = 0; k < i; ++k) th = __fmul_rn(th, a.rope_ts);
+        rope_cs[m][i] = make_float2(cosf(th), sinf(th));
+    }
+
     uint32_t seq = 0;                    // ring tiles consumed so far
-    uint32_t uses[2] = {0, 0};           // completed phases of this group's attention barriers
+    uint32_t uses = 0;                   // completed phases of this group's attention barrier
     const int qw = a.nq * HD;
     const int grp = tid / ATT_THREADS, gtid = tid % ATT_THREADS;
     const int n_att = a.nsplit * a.nkv * MB;
     AttSh<HD>* ash = reinterpret_cast<AttSh<HD>*>(region + AC::NG * AC::GROUP_BYTES);
     __half* kt = reinterpret_cast<__half*>(region + (size_t)grp * AC::GROUP_BYTES);
-    __half* vt = kt + 2 * PAGE * HD;
+    __half* vt = kt + PAGE * HD;
+    // this group's first attention item: the same in every layer of the launch
+    const int it0 = blockIdx.x + grp * gridDim.x;
+    AttItem x0;
+    const bool pre = grp < AC::NG && it0 < n_att && att_item_geo(a, it0, x0);   // uniform in the group
 
     for (int li = 0; li < a.n_layers; ++li) {
         const MegaLayer& L = a.layers[li];
@@ -804,17 +908,13 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
         grid_sync(a, ctl);
         if (ctl.aborted) break;
         stage<MB>(a, a.X, L.attn_norm, a.H, act, red, scl);
-        gemv_tiles<PH_QKV, MB>(a, li, ring, full, empty, act, seq, ctl, best);
-        // 2. attention: the first pages of each group's first item are requested
+        gemv_tiles<PH_QKV, MB>(a, li, tab, nph, ring, full, act, seq, wr, D, ctl, best);
+        // 2. attention: the first page of each group's first item is requested
         //    before the barrier (activations are dead: the region is free)
         cbar();
-        const int it0 = blockIdx.x + grp * gridDim.x;
-        AttItem x0;
-        const bool pre = grp < AC::NG && it0 < n_att && att_item_geo(a, it0, x0);   // uniform in the group
         if (pre && gtid == 0) {
             tc::fence_proxy_async_smem();
-            att_issue<HD>(L.kv, x0, 0, kt, vt, abar[grp]);
-            if (x0.ntiles > 1) att_issue<HD>(L.kv, x0, 1, kt, vt, abar[grp]);
+            att_issue<HD>(L.kv, x0, 0, kt, vt, &abar[grp]);
         }
         grid_sync(a, ctl);
         if (grp < AC::NG) {
@@ -825,8 +925,8 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
                 else if (!att_item_geo(a, it, x)) continue;
                 // a prefetched item runs even when aborting, so its copies are waited for
                 if (ctl.aborted && !(first && pre)) break;
-                if (!att_item<HD>(a, L.kv, x, gtid, kt, vt, ash[grp], abar[grp], uses, first && pre,
-                                  GroupSync{2 + grp})) {
+                if (!att_item<HD>(a, L.kv, x, gtid, kt, vt, ash[grp], rope_cs[x.m], &abar[grp], uses,
+                                  first && pre, GroupSync{1 + grp})) {
                     if (gtid == 0) raise_fail(a, ctl, 1);
                     break;
                 }
@@ -837,24 +937,24 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
         grid_sync(a, ctl);
         if (ctl.aborted) break;
         stage<MB>(a, a.ATT, nullptr, qw, act, red, scl);
-        gemv_tiles<PH_O, MB>(a, li, ring, full, empty, act, seq, ctl, best);
+        gemv_tiles<PH_O, MB>(a, li, tab, nph, ring, full, act, seq, wr, D, ctl, best);
         // 4. RMSNorm + gate/up + SwiGLU
         grid_sync(a, ctl);
         if (ctl.aborted) break;
         stage<MB>(a, a.X, L.ffn_norm, a.H, act, red, scl);
-        gemv_tiles<PH_GU, MB>(a, li, ring, full, empty, act, seq, ctl, best);
+        gemv_tiles<PH_GU, MB>(a, li, tab, nph, ring, full, act, seq, wr, D, ctl, best);
         // 5. down + residual
         grid_sync(a, ctl);
         if (ctl.aborted) break;
         stage<MB>(a, a.FA, nullptr, a.F, act, red, scl);
-        gemv_tiles<PH_DOWN, MB>(a, li, ring, full, empty, act, seq, ctl, best);
+        gemv_tiles<PH_DOWN, MB>(a, li, tab, nph, ring, full, act, seq, wr, D, ctl, best);
     }
     // output norm + lm_head + argmax
     if (!ctl.aborted) {
         grid_sync(a, ctl);
         if (!ctl.aborted) {
             stage<MB>(a, a.X, a.out_norm, a.H, act, red, scl);
-            gemv_tiles<PH_LM, MB>(a, 0, ring, full, empty, act, seq, ctl, best);
+            gemv_tiles<PH_LM, MB>(a, 0, tab, nph, ring, full, act, seq, wr, D, ctl, best);
             cbar();
             if (tid < MB && best[tid]) atomicMax(a.amax + tid, best[tid]);
             grid_sync(a, ctl);
@@ -868,6 +968,9 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
         r.kvlen += 1;
         a.meta[tid] = r;
     }
+    // copies still in flight (only after an abort): wait for them before exiting
+    for (uint32_t k = wr.used; k < wr.issued; ++k)
+        tc::mbar_wait(&full[warp + NCW * (int)(k % D)], (k / D) & 1, 1u << 20);
     if (tid == 0) {
         if (blockIdx.x == 0) {
             __threadfence();
@@ -899,6 +1002,10 @@ int decode_mega_max_stages() { return MAX_STAGES; }
 
 int decode_mega_consumer_warps() { return NCW; }
 
+int decode_mega_att_groups() { return AttConst<64>::NG; }
+
+int decode_mega_table_bytes(int n_layers) { return (int)((4 * n_layers + 1) * sizeof(Geo)); }
+
 // dynamic shared memory available to the kernel: opt-in limit minus its static shared memory
 int decode_mega_smem_limit() {
     int dev = 0, optin = 0;
@@ -929,11 +1036,11 @@ int decode_mega_grid() {
 }
 
 cudaError_t decode_mega_launch(const MegaArgs& a, size_t smem, cudaStream_t st) {
-    const bool t_ok = (a.t_gu == 1 || a.t_gu == 2 || a.t_gu == 4);
-    auto pow2_le8 = [](int t) { return t == 1 || t == 2 || t == 4 || t == 8; };
+    auto pow2_le4 = [](int t) { return t == 1 || t == 2 || t == 4; };
+    const bool t_ok = a.t_gu == 1 || a.t_gu == 2;   // gate + up rows: at most 4 per tile
     if (a.M < 1 || a.M > 2 || a.nstage < NCW || a.nstage > MAX_STAGES || a.nstage % NCW || a.nsplit < 1 ||
         a.nsplit > MAX_MERGE ||
-        !t_ok || !pow2_le8(a.t_qkv) || !pow2_le8(a.t_o) || !pow2_le8(a.t_down) || !pow2_le8(a.t_lm) ||
+        !t_ok || !pow2_le4(a.t_qkv) || !pow2_le4(a.t_o) || !pow2_le4(a.t_down) || !pow2_le4(a.t_lm) ||
         a.slot_bytes % 16 || a.union_bytes % 1024)
         return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};

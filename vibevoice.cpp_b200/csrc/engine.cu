@@ -604,9 +604,9 @@ MegaPlan mega_plan(const vvq2_ctx* c, int M) {
     const vvq2_ctx::Layer& L0 = c->layers[0];
     const int kmax = std::max({hp.hidden_size, hp.intermediate_size, hp.n_heads * hp.head_dim});
     p.uni = decode_mega_union_bytes(hp.head_dim, M, kmax);
-    const int lim = decode_mega_smem_limit();
-    // The ring has a multiple of `ncw` slots and tile i goes to consumer warp
-    // i % ncw, so every slot is always read by the same warp, in order.
+    const int lim = decode_mega_smem_limit() - decode_mega_table_bytes(hp.n_layers);
+    // The ring has D slots per warp (D = 2 preferred): tile i of a CTA goes
+    // to warp i % ncw, which streams it into one of its own slots.
     for (int k = decode_mega_max_stages() / ncw; k >= 1; --k) {
         const int nst = k * ncw;
         const int64_t slot_max = (int64_t)(lim - p.uni) / nst / 128 * 128;
@@ -620,11 +620,11 @@ MegaPlan mega_plan(const vvq2_ctx* c, int M) {
             if ((int64_t)t * mats * w.row_stride > slot_max) fits = false;
             return t;
         };
-        p.t_qkv = pick(L0.qkv, 8, 1);
-        p.t_o = pick(L0.o, 8, 1);
-        p.t_gu = pick(L0.gate, 4, 2);
-        p.t_down = pick(L0.down, 8, 1);
-        p.t_lm = pick(c->lm_head, 8, 1);
+        p.t_qkv = pick(L0.qkv, 4, 1);
+        p.t_o = pick(L0.o, 4, 1);
+        p.t_gu = pick(L0.gate, 2, 2);
+        p.t_down = pick(L0.down, 4, 1);
+        p.t_lm = pick(c->lm_head, 4, 1);
         if (!fits) continue;
         int64_t slot = std::max<int64_t>({p.t_qkv * L0.qkv.row_stride, p.t_o * L0.o.row_stride,
                                           2 * p.t_gu * L0.gate.row_stride, p.t_down * L0.down.row_stride,
@@ -632,7 +632,7 @@ MegaPlan mega_plan(const vvq2_ctx* c, int M) {
         slot = (slot + 127) / 128 * 128;
         p.slot = (int)slot;
         p.nstage = nst;
-        p.smem = (size_t)p.uni + (size_t)p.nstage * p.slot;
+        p.smem = (size_t)p.uni + (size_t)p.nstage * p.slot + decode_mega_table_bytes(hp.n_layers);
         p.ok = true;
         return p;
     }
@@ -659,7 +659,7 @@ bool mega_eligible(const vvq2_ctx* c, int M) {
 // Attention split of the persistent step: every (row, KV head) gets up to
 // (attention groups on the GPU) / (rows x KV heads) splits of whole pages.
 void mega_split(const vvq2_ctx* c, int M, int max_lim, int* split, int* nsplit) {
-    const int groups = (c->hp.head_dim >= 128 ? 2 : 3) * c->mega_grid;
+    const int groups = decode_mega_att_groups() * c->mega_grid;
     const int per_row = std::max(1, std::min(64, groups / std::max(1, M * c->hp.n_kv_heads)));
     int s = (max_lim + per_row - 1) / per_row;
     s = (std::max(s, KV_PAGE) + KV_PAGE - 1) / KV_PAGE * KV_PAGE;

@@ -92,7 +92,7 @@ struct MegaArgs {
     int split = 0, nsplit = 0;
     float eps = 0.f, rope_ts = 0.f, scale = 0.f;
     int* err = nullptr;
-    // shared-memory plan: [union_bytes: activations | attention][nstage x slot_bytes ring]
+    // shared-memory plan: [union_bytes: activations | attention][nstage x slot_bytes ring][phase table]
     int nstage = 0, slot_bytes = 0, union_bytes = 0;
     int t_qkv = 1, t_o = 1, t_gu = 1, t_down = 1, t_lm = 1;   // weight rows per ring tile
     // optional phase timeline: [slot][grid] %globaltimer ns; slot 0 = start,
@@ -105,6 +105,8 @@ cudaError_t decode_mega_launch(const MegaArgs& a, size_t smem, cudaStream_t st);
 int decode_mega_union_bytes(int hd, int M, int kmax);
 int decode_mega_max_stages();
 int decode_mega_consumer_warps();
+int decode_mega_table_bytes(int n_layers);
+int decode_mega_att_groups();
 int decode_mega_smem_limit();
 int decode_mega_grid();
 
