@@ -69,8 +69,6 @@ struct __align__(16) AttSh {
     float qs[MAXG][HD];            // roped q, rounded to f16 (ggml FA converts Q to the K type)
     float sc[MAXG][PAGE];
     float run_max[MAXG], run_sum[MAXG], alpha[MAXG];
-    float wts[MAXG][MAX_MERGE];
-    float inv_den[MAXG];
     __half kn[HD], vn[HD];         // this step's key (roped) and value row
     int is_last, failed;
 };
@@ -245,109 +243,55 @@ __device__ __forceinline__ void ring_issue(WarpRing& w, const Geo* tab, int nph,
 // act layout: float4 index ((m * 4 + g) * NC + c) holds elements
 // 16c + 4g .. 16c + 4g + 3 of row m, so the lanes of a warp (consecutive
 // chunks c) read consecutive 16-byte words.
+//
+// Where the phase RMSNorms its input, act = x * w (the norm weight) and the
+// per-warp partial sums of squares go to red[m][warp]; the row scale
+// 1/sqrt(mean(x^2) + eps) is applied to the dot products instead
+// (W (x s o w) = s W (x o w)), so no second pass over act is needed.
 template <int MB>
-__device__ void stage(const MegaArgs& a, const float* x, const float* norm_w, int K, float* act, float* red,
-                      float* scl) {
+__device__ void stage(const float* x, const float* norm_w, int K, float* act, float* red) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int NC = K / 16, K4 = K / 4;
     float4* act4 = reinterpret_cast<float4*>(act);
     float ss[MB];
 #pragma unroll
     for (int m = 0; m < MB; ++m) ss[m] = 0.f;
-    if (norm_w && K4 <= 2 * NCT) {
-        // rows go to shared memory; the norm weights are loaded in the same
-        // round trip and kept in registers for the scaling pass
-        float4 w[2];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int k4 = tid + i * NCT;
-            if (k4 < K4) {
-                w[i] = __ldg(reinterpret_cast<const float4*>(norm_w) + k4);
-                const int c = k4 >> 2, g = k4 & 3;
-#pragma unroll
-                for (int m = 0; m < MB; ++m) {
-                    const float4 v = __ldcg(reinterpret_cast<const float4*>(x + (size_t)m * K) + k4);
-                    ss[m] = fmaf(v.x, v.x, ss[m]);
-                    ss[m] = fmaf(v.y, v.y, ss[m]);
-                    ss[m] = fmaf(v.z, v.z, ss[m]);
-                    ss[m] = fmaf(v.w, v.w, ss[m]);
-                    act4[(m * 4 + g) * NC + c] = v;
-                }
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < MB; ++m) {
-            const float t = warp_sum(ss[m]);
-            if (lane == 0) red[m * NCW + warp] = t;
-        }
-        cbar();
-        if (tid < MB) {
-            float t = 0.f;
-            for (int i = 0; i < NCW; ++i) t += red[tid * NCW + i];
-            scl[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps)));
-        }
-        cbar();
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int k4 = tid + i * NCT;
-            if (k4 < K4) {
-                const int c = k4 >> 2, g = k4 & 3;
-#pragma unroll
-                for (int m = 0; m < MB; ++m) {
-                    const float sc = scl[m];
-                    float4 t = act4[(m * 4 + g) * NC + c];
-                    t.x = __fmul_rn(__fmul_rn(t.x, sc), w[i].x);   // (x * scale) * w: ggml_rms_norm, then ggml_mul
-                    t.y = __fmul_rn(__fmul_rn(t.y, sc), w[i].y);
-                    t.z = __fmul_rn(__fmul_rn(t.z, sc), w[i].z);
-                    t.w = __fmul_rn(__fmul_rn(t.w, sc), w[i].w);
-                    act4[(m * 4 + g) * NC + c] = t;
-                }
-            }
-        }
-        cbar();
-        return;
-    }
+#pragma unroll 4
     for (int k4 = tid; k4 < K4; k4 += NCT) {
         const int c = k4 >> 2, g = k4 & 3;
+        const float4 w = norm_w ? __ldg(reinterpret_cast<const float4*>(norm_w) + k4) : make_float4(1.f, 1.f, 1.f, 1.f);
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(x + (size_t)m * K) + k4);
-            ss[m] = fmaf(v.x, v.x, ss[m]);
-            ss[m] = fmaf(v.y, v.y, ss[m]);
-            ss[m] = fmaf(v.z, v.z, ss[m]);
-            ss[m] = fmaf(v.w, v.w, ss[m]);
+            float4 v = __ldcg(reinterpret_cast<const float4*>(x + (size_t)m * K) + k4);
+            if (norm_w) {
+                ss[m] = fmaf(v.x, v.x, ss[m]);
+                ss[m] = fmaf(v.y, v.y, ss[m]);
+                ss[m] = fmaf(v.z, v.z, ss[m]);
+                ss[m] = fmaf(v.w, v.w, ss[m]);
+                v.x = __fmul_rn(v.x, w.x);
+                v.y = __fmul_rn(v.y, w.y);
+                v.z = __fmul_rn(v.z, w.z);
+                v.w = __fmul_rn(v.w, w.w);
+            }
             act4[(m * 4 + g) * NC + c] = v;
         }
     }
     if (norm_w) {
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
-            const float w = warp_sum(ss[m]);
-            if (lane == 0) red[m * NCW + warp] = w;
-        }
-        cbar();
-        if (tid < MB) {
-            float t = 0.f;
-            for (int w = 0; w < NCW; ++w) t += red[tid * NCW + w];
-            scl[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps)));
-        }
-        cbar();
-        for (int k4 = tid; k4 < K4; k4 += NCT) {
-            const int c = k4 >> 2, g = k4 & 3;
-            const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w) + k4);
-#pragma unroll
-            for (int m = 0; m < MB; ++m) {
-                float4 t = act4[(m * 4 + g) * NC + c];
-                const float s = scl[m];
-                t.x = __fmul_rn(__fmul_rn(t.x, s), w.x);   // (x * scale) * w: ggml_rms_norm, then ggml_mul
-                t.y = __fmul_rn(__fmul_rn(t.y, s), w.y);
-                t.z = __fmul_rn(__fmul_rn(t.z, s), w.z);
-                t.w = __fmul_rn(__fmul_rn(t.w, s), w.w);
-                act4[(m * 4 + g) * NC + c] = t;
-            }
+            const float t = warp_sum(ss[m]);
+            if (lane == 0) red[m * NCW + warp] = t;
         }
     }
     cbar();
+}
+
+// RMSNorm row scale from the staged partial sums (ggml_rms_norm: 1/sqrt(mean + eps)).
+__device__ __forceinline__ float norm_scale(const float* red, int m, int K, float eps) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) t += red[m * NCW + w];
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), eps)));
 }
 
 // ------------------------------------------------------------ tile math
@@ -435,7 +379,7 @@ __device__ __forceinline__ float warp_transpose_sum(float (&v)[NV], int lane) {
 // overlaps it.  For lm_head the writer lanes keep a running argmax key.
 template <int PH, int T, int MB>
 __device__ __forceinline__ void tile_epilogue(const MegaArgs& a, const MegaLayer* L, const uint8_t* tile,
-                                              const Geo& g, int r, const float4* act4, int lane,
+                                              const Geo& g, int r, const float4* act4, int lane, float nsc,
                                               unsigned long long& kbest) {
     constexpr int NR = PH == PH_GU ? 2 * T : T;
     constexpr int NV = NR * MB;
@@ -455,6 +399,7 @@ __device__ __forceinline__ void tile_epilogue(const MegaArgs& a, const MegaLayer
     float acc[NV];
     tile_dot<NR, MB>(tile, (int)g.rs, g.K, act4, lane, acc);
     float v = warp_transpose_sum<NV>(acc, lane);
+    if constexpr (PH == PH_QKV || PH == PH_GU || PH == PH_LM) v = __fmul_rn(v, nsc);   // RMSNorm scale of row m
     if constexpr (PH == PH_GU) {
         const float u = __shfl_sync(0xffffffffu, v, (lane + ((T * MB) << SH)) & 31);
         if (w_ok) a.FA[(size_t)m * a.F + row] = __fmul_rn(silu_ref(v), u);   // ggml_swiglu_split: silu(g) * u
@@ -472,7 +417,7 @@ __device__ __forceinline__ void tile_epilogue(const MegaArgs& a, const MegaLayer
 
 template <int PH, int MB>
 __device__ void gemv_tiles(const MegaArgs& a, int li, const Geo* tab, int nph, uint8_t* ring, uint64_t* full,
-                           const float* act, uint32_t& seq, WarpRing& wr, int D, Ctl& ctl,
+                           const float* act, const float* red, uint32_t& seq, WarpRing& wr, int D, Ctl& ctl,
                            unsigned long long* best) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const Geo& g = tab[PH == PH_LM ? 4 * a.n_layers : 4 * li + PH];
@@ -481,6 +426,13 @@ __device__ void gemv_tiles(const MegaArgs& a, int li, const Geo* tab, int nph, u
     const int j0 = (warp - (int)(seq % NCW) + NCW) % NCW;
     const volatile int* fl = &ctl.fail;
     unsigned long long kbest = 0ull;
+    // this lane's row m is fixed by the lane and T; its RMSNorm scale where the phase norms
+    float nsc = 1.f;
+    if constexpr (PH == PH_QKV || PH == PH_GU || PH == PH_LM) {
+        const int nv = (PH == PH_GU ? 2 : 1) * g.T * MB;
+        const int sh = 5 - (nv == 1 ? 0 : nv == 2 ? 1 : nv == 4 ? 2 : nv == 8 ? 3 : 4);
+        nsc = norm_scale(red, (lane >> sh) % MB, g.K, a.eps);
+    }
     for (int j = j0; j < g.ntiles; j += NCW) {
         const int slot = warp + NCW * (int)(wr.used % D);
         if (!wait_or_fail(&full[slot], (wr.used / D) & 1, fl)) {
@@ -490,10 +442,10 @@ __device__ void gemv_tiles(const MegaArgs& a, int li, const Geo* tab, int nph, u
         const uint8_t* tile = ring + (size_t)slot * a.slot_bytes;
         const int r = j * g.T;
         switch (g.T) {
-            case 1: tile_epilogue<PH, 1, MB>(a, L, tile, g, r, act4, lane, kbest); break;
-            case 2: tile_epilogue<PH, 2, MB>(a, L, tile, g, r, act4, lane, kbest); break;
+            case 1: tile_epilogue<PH, 1, MB>(a, L, tile, g, r, act4, lane, nsc, kbest); break;
+            case 2: tile_epilogue<PH, 2, MB>(a, L, tile, g, r, act4, lane, nsc, kbest); break;
             default:
-                if constexpr (PH != PH_GU) tile_epilogue<PH, 4, MB>(a, L, tile, g, r, act4, lane, kbest);
+                if constexpr (PH != PH_GU) tile_epilogue<PH, 4, MB>(a, L, tile, g, r, act4, lane, nsc, kbest);
                 break;
         }
         __syncwarp();
@@ -548,7 +500,7 @@ __device__ __forceinline__ void att_issue(const KvLayer& kv, const AttItem& x, i
 template <int HD>
 __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x, int tid, __half* kt, __half* vt,
                          AttSh<HD>& sh, const float2* cs_row, uint64_t* bar, uint32_t& uses, bool prefetched,
-                         GroupSync sync) {
+                         GroupSync sync, int* merge_n, int4* merges) {
     const int lane = tid & 31, warp = tid >> 5;
     const int G = a.nq / a.nkv;
     constexpr int half = HD / 2;
@@ -758,63 +710,93 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
         a.part_ml[(pbase + g * G + tid) * 2 + 0] = sh.run_max[tid];
         a.part_ml[(pbase + g * G + tid) * 2 + 1] = sh.run_sum[tid];
     }
-    __threadfence();
     sync();
     if (tid == 0) {
-        const int prev = atomicAdd(a.counters + m * a.nkv + g, 1);
-        sh.is_last = (prev == x.nsplit - 1);
+        // release the partials (written by the group, ordered by the group
+        // barrier), count the split; the last one queues the merge for its CTA
+        int prev;
+        asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
+                     : "=r"(prev)
+                     : "l"(a.counters + m * a.nkv + g)
+                     : "memory");
+        if (prev == x.nsplit - 1) {
+            const int e = atomicAdd(merge_n, 1);
+            merges[e] = make_int4(m, g, x.nsplit, 0);
+        }
     }
     sync();
-    if (!sh.is_last) return true;
-    __threadfence();
-    const int ns = x.nsplit;
-    float* ml = reinterpret_cast<float*>(kt);   // [G][ns][2]: the K stage is free now
-    for (int i = tid; i < G * ns; i += ATT_THREADS) {
+    return true;
+}
+
+// Log-sum-exp merge of the ns partials of (row m, KV head g) by the whole
+// CTA (all partial loads in one round trip), then ATT[m][heads of g].
+// `scr`: shared scratch of at least mega_merge_scratch bytes.
+template <int HD>
+__device__ void cta_merge(const MegaArgs& a, int m, int g, int ns, float* scr) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = a.nq / a.nkv;
+    constexpr int PAIRS = HD / 2;
+    float* ml = scr;                                  // [G][ns][2]
+    float* wts = ml + 2 * MAXG * MAX_MERGE;           // [G][ns]
+    float* inv = wts + MAXG * MAX_MERGE;              // [G]
+    float2* num = reinterpret_cast<float2*>(inv + 2 * MAXG);   // [Q][G * PAIRS]
+    const float2* pml = reinterpret_cast<const float2*>(a.part_ml);
+    for (int i = tid; i < G * ns; i += NCT) {
         const int h = i / ns, ss = i % ns;
-        const float2 v = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + ((size_t)m * MAX_MERGE + ss) * a.nq +
-                                g * G + h);
+        const float2 v = __ldcg(pml + ((size_t)m * MAX_MERGE + ss) * a.nq + g * G + h);
         ml[2 * i] = v.x;
         ml[2 * i + 1] = v.y;
     }
-    sync();
-    for (int h = warp; h < G; h += 4) {
+    cbar();
+    for (int h = warp; h < G; h += NCW) {
         float mx = -INFINITY;
         for (int ss = lane; ss < ns; ss += 32) mx = fmaxf(mx, ml[2 * (h * ns + ss)]);
         mx = warp_max(mx);
         float den = 0.f;
         for (int ss = lane; ss < ns; ss += 32) {
             const float w = expf(ml[2 * (h * ns + ss)] - mx);
-            sh.wts[h][ss] = w;
+            wts[h * ns + ss] = w;
             den = fmaf(w, ml[2 * (h * ns + ss) + 1], den);
         }
         den = warp_sum(den);
-        if (lane == 0) sh.inv_den[h] = 1.0f / den;
+        if (lane == 0) inv[h] = 1.0f / den;
     }
-    sync();
-    for (int t = tid; t < G * PAIRS; t += ATT_THREADS) {
-        const int h = t / PAIRS, d2 = t % PAIRS;
-        const int qh = g * G + h;
-        float2 num = make_float2(0.f, 0.f);
-        for (int s0 = 0; s0 < ns; s0 += 8) {   // 8 independent loads in flight per batch
+    cbar();
+    const int np = G * PAIRS, Q = NCT / np;          // Q threads share one (head, column pair)
+    if (tid < Q * np) {
+        const int pidx = tid % np, qi = tid / np;
+        const int h = pidx / PAIRS, d2 = pidx % PAIRS;
+        const float2* src = reinterpret_cast<const float2*>(a.part + (size_t)(g * G + h) * HD) + d2;
+        const size_t sstride = (size_t)a.nq * HD / 2;   // float2 per split
+        float2 acc = make_float2(0.f, 0.f);
+        for (int s0 = qi; s0 < ns; s0 += 8 * Q) {      // 8 independent loads in flight per batch
             float2 p[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-                if (s0 + i < ns)
-                    p[i] = __ldcg(reinterpret_cast<const float2*>(
-                                      a.part + (((size_t)m * MAX_MERGE + s0 + i) * a.nq + qh) * HD) + d2);
+                if (s0 + i * Q < ns) p[i] = __ldcg(src + ((size_t)m * MAX_MERGE + s0 + i * Q) * sstride);
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-                if (s0 + i < ns) {
-                    num.x = fmaf(sh.wts[h][s0 + i], p[i].x, num.x);
-                    num.y = fmaf(sh.wts[h][s0 + i], p[i].y, num.y);
+                if (s0 + i * Q < ns) {
+                    const float w = wts[h * ns + s0 + i * Q];
+                    acc.x = fmaf(w, p[i].x, acc.x);
+                    acc.y = fmaf(w, p[i].y, acc.y);
                 }
         }
-        reinterpret_cast<float2*>(out + (size_t)qh * HD)[d2] =
-            make_float2(num.x * sh.inv_den[h], num.y * sh.inv_den[h]);
+        num[qi * np + pidx] = acc;
+    }
+    cbar();
+    float* out = a.ATT + (size_t)m * a.nq * HD;
+    for (int pidx = tid; pidx < np; pidx += NCT) {
+        float2 t = num[pidx];
+        for (int qi = 1; qi < Q; ++qi) {
+            t.x += num[qi * np + pidx].x;
+            t.y += num[qi * np + pidx].y;
+        }
+        const int h = pidx / PAIRS, d2 = pidx % PAIRS;
+        reinterpret_cast<float2*>(out + (size_t)(g * G + h) * HD)[d2] = make_float2(t.x * inv[h], t.y * inv[h]);
     }
     if (tid == 0) a.counters[m * a.nkv + g] = 0;   // ready for the next layer / launch
-    sync();
-    return true;
+    cbar();
 }
 
 // ------------------------------------------------------------ kernel
@@ -825,9 +807,10 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
     __shared__ __align__(8) uint64_t full[MAX_STAGES];
     __shared__ __align__(8) uint64_t abar[AC::NG];
     __shared__ float red[2 * NCW];
-    __shared__ float scl[2];
     __shared__ unsigned long long best[2];
     __shared__ float2 rope_cs[2][64];              // RoPE (cos, sin) per row: positions are fixed for the launch
+    __shared__ int merge_n;                        // attention merges this CTA owes in the current layer
+    __shared__ int4 merges[16];                    // (m, g, nsplit)
     __shared__ Ctl ctl;
     const int tid = threadIdx.x, warp = tid >> 5;
     uint8_t* region = dyn;                         // activations | attention tiles + state
@@ -907,11 +890,12 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
         // 1. RMSNorm + QKV (+bias) -> raw q/k/v rows
         grid_sync(a, ctl);
         if (ctl.aborted) break;
-        stage<MB>(a, a.X, L.attn_norm, a.H, act, red, scl);
-        gemv_tiles<PH_QKV, MB>(a, li, tab, nph, ring, full, act, seq, wr, D, ctl, best);
+        stage<MB>(a.X, L.attn_norm, a.H, act, red);
+        gemv_tiles<PH_QKV, MB>(a, li, tab, nph, ring, full, act, red, seq, wr, D, ctl, best);
         // 2. attention: the first page of each group's first item is requested
         //    before the barrier (activations are dead: the region is free)
         cbar();
+        if (tid == 0) merge_n = 0;
         if (pre && gtid == 0) {
             tc::fence_proxy_async_smem();
             att_issue<HD>(L.kv, x0, 0, kt, vt, &abar[grp]);
@@ -926,35 +910,39 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
                 // a prefetched item runs even when aborting, so its copies are waited for
                 if (ctl.aborted && !(first && pre)) break;
                 if (!att_item<HD>(a, L.kv, x, gtid, kt, vt, ash[grp], rope_cs[x.m], &abar[grp], uses,
-                                  first && pre, GroupSync{1 + grp})) {
+                                  first && pre, GroupSync{1 + grp}, &merge_n, merges)) {
                     if (gtid == 0) raise_fail(a, ctl, 1);
                     break;
                 }
             }
         }
+        cbar();
+        // splits that finished last merge with the whole CTA (the tiles are free now)
+        for (int e = 0; e < merge_n && !ctl.aborted; ++e)
+            cta_merge<HD>(a, merges[e].x, merges[e].y, merges[e].z, reinterpret_cast<float*>(region));
         if (ctl.aborted) break;
         // 3. O-proj + residual
         grid_sync(a, ctl);
         if (ctl.aborted) break;
-        stage<MB>(a, a.ATT, nullptr, qw, act, red, scl);
-        gemv_tiles<PH_O, MB>(a, li, tab, nph, ring, full, act, seq, wr, D, ctl, best);
+        stage<MB>(a.ATT, nullptr, qw, act, red);
+        gemv_tiles<PH_O, MB>(a, li, tab, nph, ring, full, act, red, seq, wr, D, ctl, best);
         // 4. RMSNorm + gate/up + SwiGLU
         grid_sync(a, ctl);
         if (ctl.aborted) break;
-        stage<MB>(a, a.X, L.ffn_norm, a.H, act, red, scl);
-        gemv_tiles<PH_GU, MB>(a, li, tab, nph, ring, full, act, seq, wr, D, ctl, best);
+        stage<MB>(a.X, L.ffn_norm, a.H, act, red);
+        gemv_tiles<PH_GU, MB>(a, li, tab, nph, ring, full, act, red, seq, wr, D, ctl, best);
         // 5. down + residual
         grid_sync(a, ctl);
         if (ctl.aborted) break;
-        stage<MB>(a, a.FA, nullptr, a.F, act, red, scl);
-        gemv_tiles<PH_DOWN, MB>(a, li, tab, nph, ring, full, act, seq, wr, D, ctl, best);
+        stage<MB>(a.FA, nullptr, a.F, act, red);
+        gemv_tiles<PH_DOWN, MB>(a, li, tab, nph, ring, full, act, red, seq, wr, D, ctl, best);
     }
     // output norm + lm_head + argmax
     if (!ctl.aborted) {
         grid_sync(a, ctl);
         if (!ctl.aborted) {
-            stage<MB>(a, a.X, a.out_norm, a.H, act, red, scl);
-            gemv_tiles<PH_LM, MB>(a, 0, tab, nph, ring, full, act, seq, wr, D, ctl, best);
+            stage<MB>(a.X, a.out_norm, a.H, act, red);
+            gemv_tiles<PH_LM, MB>(a, 0, tab, nph, ring, full, act, red, seq, wr, D, ctl, best);
             cbar();
             if (tid < MB && best[tid]) atomicMax(a.amax + tid, best[tid]);
             grid_sync(a, ctl);
