@@ -41,6 +41,74 @@ C2 = dict(hidden=896, n_heads=14, n_kv_heads=2, head_dim=64, ffn=4864, n_layers=
 SEED = 20261201
 
 
+C5_LAYER = dict(hidden=3584, n_heads=28, n_kv_heads=4, head_dim=128, ffn=18944, n_layers=1, vocab=152064,
+                rope_theta=1.0e6, rms_eps=1.0e-6)
+
+
+def measured_tensor_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    return 1590.0, 1400.0, "fallback"
+
+
+def prefill_measure(vvq2, synth, torch, local, sh, n_tok, reps=3):
+    """One 7B-shaped Q8_0 layer (config 5 dims) over an n_tok causal prompt,
+    one tensor-core chunk: CUDA events around the whole layer forward, and
+    per-launch events (engine profiling) around the flash-attention and GEMM
+    kernels.  Flops: 2*T*N*K per linear, 4*nq*hd*(pos+1) per query row for
+    attention (the causal half)."""
+    hp = C5_LAYER
+    rng = np.random.default_rng(SEED + 5)
+    layer = synth.layer_q8_0(rng, hp)
+    os.environ["VVQ2_PREFILL_ROWS"] = str(n_tok)   # the whole prompt in one chunk
+    eng = vvq2.Engine(hp, device=local)
+    del os.environ["VVQ2_PREFILL_ROWS"]
+    eng.set_layer(0, layer)
+    kv = eng.kv(1, n_tok + 64)
+    g = torch.Generator(device="cuda").manual_seed(SEED + 5)
+    x = torch.randn((1, n_tok, hp["hidden"]), generator=g, device="cuda", dtype=torch.float32)
+    y = torch.empty_like(x)
+
+    def run():
+        kv.set_past_len(0, 0)
+        eng.forward(kv, [0], x, [0], flags=0, y=y, stream=sh)
+
+    run()
+    torch.cuda.synchronize()
+    eng.profile(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream()
+    e0.record(stream)
+    for _ in range(reps):
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    a_ms, a_fl, a_n = eng.profile_read(2)
+    g_ms, g_fl, g_n = eng.profile_read(3)
+    eng.profile(False)
+    burst, sustained, kind = measured_tensor_peak()
+    attn_tf = a_fl / (a_ms / 1000.0) / 1e12 if a_n else None
+    gemm_tf = g_fl / (g_ms / 1000.0) / 1e12 if g_n else None
+    layer_tf = (a_fl + g_fl) / reps / (ms / 1000.0) / 1e12
+    return {
+        "workload": f"config-5-shaped layer (7B dims: hidden 3584, 28/4 heads, hd 128, ffn 18944, Q8_0), "
+                    f"{n_tok}-token causal prompt, batch 1, one tensor-core chunk",
+        "tokens_per_s": round(n_tok / (ms / 1000.0), 1), "ms_per_layer": round(ms, 3),
+        "layer_tflops": round(layer_tf, 1),
+        "attn": {"kernel": "k_fa_prefill<128> (tcgen05 causal flash attention)",
+                 "tflops": round(attn_tf, 1) if attn_tf else None,
+                 "frac": round(attn_tf / burst, 4) if attn_tf else None,
+                 "ms": round(a_ms / max(a_n, 1), 3), "flops_per_launch": a_fl / max(a_n, 1)},
+        "gemm": {"kernel": "k_gemm_tc (tcgen05 dequant GEMM, fused epilogues)",
+                 "tflops": round(gemm_tf, 1) if gemm_tf else None,
+                 "frac": round(gemm_tf / burst, 4) if gemm_tf else None},
+        "peak_tflops": burst, "peak_kind": f"{kind} bf16 dense burst (sustained {sustained})",
+    }
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -162,6 +230,8 @@ def main():
     ap.add_argument("--kv", type=int, default=1024)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=16384)
+    ap.add_argument("--no-prefill", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, local, world = dist_env()
@@ -288,6 +358,8 @@ def main():
                      "step_hbm_gbs": round(synth.weight_bytes(model) * 1.0 / (ms / args.steps / 1000.0) / 1e9, 1)},
         "clocks": clk.summary(),
     }
+    if not args.no_prefill:
+        line["prefill"] = prefill_measure(vvq2, synth, torch, local, sh, args.prefill_tokens)
     if rank == 0 and world == 1 and not args.no_cpu:
         rate, n, cores = cpu_decode_rate(model, hp, args.kv)
         line["cpu_baseline"] = {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",

@@ -226,10 +226,12 @@ int  vvq2_attention_decode_noalloc(const float* q, const void* k_pages, const vo
                                    int head_dim, float* out, void* stream);
 
 /* ---- measurement (no counterpart in the reference, which has no profiler
- * hooks; used by bench.py for the roofline figure) -------------------------
- * While enabled, vvq2_decode_step brackets every GEMV (kind 0) and attention
- * (kind 1) launch with CUDA events on the launching stream, synchronizes after
- * each step, and accumulates per-kind device time, algorithmic bytes and
+ * hooks; used by bench.py for the roofline figures) ------------------------
+ * While enabled, vvq2_decode_step brackets the persistent decode-step kernel
+ * or every GEMV (kind 0) and attention (kind 1) launch, and vvq2_forward on the
+ * tensor-core path every flash-attention (kind 2) and GEMM (kind 3) launch,
+ * with CUDA events on the launching stream; per kind it accumulates device
+ * time, algorithmic work (bytes for kinds 0/1, flops for kinds 2/3) and
  * launch counts.  Enabling resets the totals. */
 int  vvq2_profile(vvq2_ctx* ctx, int enable);
 int  vvq2_profile_read(vvq2_ctx* ctx, int kind, double* ms, double* bytes, int64_t* launches);

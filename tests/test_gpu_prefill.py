@@ -61,3 +61,41 @@ def test_prefill_golden_layer(vv, golden):
     kv = eng.kv(1, 80)
     got = eng.forward(kv, [0], x, [0])
     assert np.max(np.abs(got - y)) < 5e-3
+
+
+@pytest.mark.parametrize("hd,std", [(64, 0.02), (64, 0.08), (128, 0.02), (128, 0.08)])
+def test_prefill_flash_attention_vs_oracle(vv, hd, std):
+    """Chunked prefill on the tcgen05 flash-attention path: 2 sequences with a
+    100-position N(0,1) KV prefix, then 650 prompt tokens each (three chunks:
+    later chunks attend to earlier ones, the last q tile is partial).  A
+    larger weight scale gives sharp attention rows (scores of several units),
+    which exercises the running-max rescale."""
+    from fixtures_util import C4
+    hp = dict(C1, n_layers=1) if hd == 64 else dict(C4, n_layers=1, ffn=2048)
+    rng = np.random.default_rng(1000 + hd + int(std * 100))
+    t = random_layer(rng, hp, O.Q8_0, std=std)
+    eng = vv.Engine(hp)
+    eng.set_layer(0, t)
+    past, n = 100, 650
+    kv = eng.kv(2, past + n + 8)
+    ora = O.Model(hp, 2, past + n + 8, GPU_MODE)
+    ora.set_layer(0, t)
+    w = hp["n_kv_heads"] * hp["head_dim"]
+    for s in range(2):
+        k = rng.standard_normal((past, w)).astype(np.float32)
+        v = rng.standard_normal((past, w)).astype(np.float32)
+        kv.load_prefix(s, 0, k, v)
+        ora.kv_load(s, 0, k, v)
+        kv.set_past_len(s, past)
+        ora.set_past_len(s, past)
+    x = rng.standard_normal((2, n, hp["hidden"])).astype(np.float32)
+    got = eng.forward(kv, [0, 1], x, [past, past])
+    ref = ora.forward([0, 1], x, [past, past])
+    err = rel_err(got, ref)
+    print(f"hd {hd} std {std}: prefill rel err {err:.2e}")
+    assert err < 5e-3
+    # the K/V rows it appended serve the next decode step
+    x1 = rng.standard_normal((2, 1, hp["hidden"])).astype(np.float32)
+    g1 = eng.forward(kv, [0, 1], x1, [past + n, past + n])
+    r1 = ora.forward([0, 1], x1, [past + n, past + n])
+    assert rel_err(g1, r1) < 5e-3

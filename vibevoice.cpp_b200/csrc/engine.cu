@@ -27,7 +27,7 @@ using namespace vvq2;
 
 namespace {
 
-constexpr int PREFILL_ROWS = 512;   // token rows per tensor-core chunk
+constexpr int PREFILL_ROWS_DEFAULT = 4096;   // token rows per tensor-core chunk (VVQ2_PREFILL_ROWS overrides)
 
 // cuTensorMapEncodeTiled from the driver, fetched through the runtime (no -lcuda)
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -54,6 +54,20 @@ bool make_act_map(CUtensorMap* m, const __half* base, int rows, int cols) {
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
     const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// One layer's K or V pool as a 2-D f16 [rows][hd] TMA map: 64-key x 64-column
+// boxes, 128-byte swizzle (the prefill flash-attention operand layout).
+bool make_kv_map(CUtensorMap* m, const __half* base, int64_t rows, int hd) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || hd % 64 || ((uintptr_t)base & 15)) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
+    const cuuint32_t box[2] = {64, 64};
     const cuuint32_t es[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -133,7 +147,8 @@ struct vvq2_ctx {
     // scratch for up to GEMV_MAX_M activation rows
     float *X = nullptr, *Q = nullptr, *ATT = nullptr, *FA = nullptr, *LOGITS = nullptr;
     float* QKVr = nullptr;         // persistent step: raw q|k|v rows [GEMV_MAX_M][qkv rows]
-    // prefill (tensor-core) scratch for up to PREFILL_ROWS token rows
+    // prefill (tensor-core) scratch for up to prefill_rows token rows
+    int prefill_rows = PREFILL_ROWS_DEFAULT;
     __half *Xh = nullptr, *ATTh = nullptr, *Ah = nullptr;
     float2* rope_cs = nullptr;
     float *part = nullptr, *part_ml = nullptr;
@@ -164,8 +179,8 @@ struct vvq2_ctx {
     struct Rec { int kind; int e0, e1; double bytes; };
     bool prof_on = false;
     std::vector<cudaEvent_t> events;
-    double prof_ms[3] = {0, 0, 0}, prof_bytes[3] = {0, 0, 0};
-    int64_t prof_n[3] = {0, 0, 0};
+    double prof_ms[4] = {0, 0, 0, 0}, prof_bytes[4] = {0, 0, 0, 0};
+    int64_t prof_n[4] = {0, 0, 0, 0};
 
     // decode-step CUDA graphs, keyed by (kv, sequence set, length bucket, profiling)
     struct Graph {
@@ -358,16 +373,23 @@ struct Recorder {
     cudaStream_t st;
     std::vector<vvq2_ctx::Rec>* recs;
     int e0 = -1;
+    // inside stream capture an event record must be an external node
+    cudaError_t record(cudaEvent_t e) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) return cudaErrorInvalidValue;
+        return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(e, st, cudaEventRecordExternal)
+                                                   : cudaEventRecord(e, st);
+    }
     cudaError_t begin() {
         if (!recs) return cudaSuccess;
         const int need = (int)recs->size() * 2 + 2;
-        if ((int)c->events.size() < need) return cudaErrorInvalidValue;   // vvq2_profile pre-creates
+        if ((int)c->events.size() < need) return cudaErrorInvalidValue;   // created before any capture
         e0 = (int)recs->size() * 2;
-        return cudaEventRecordWithFlags(c->events[e0], st, cudaEventRecordExternal);
+        return record(c->events[e0]);
     }
     cudaError_t end(int kind, double bytes) {
         if (!recs) return cudaSuccess;
-        cudaError_t err = cudaEventRecordWithFlags(c->events[e0 + 1], st, cudaEventRecordExternal);
+        cudaError_t err = record(c->events[e0 + 1]);
         recs->push_back({kind, e0, e0 + 1, bytes});
         return err;
     }
@@ -476,11 +498,20 @@ int run_layers_decode(vvq2_ctx* c, vvq2_kv* kv, int M, int split, int nsplit, in
     return 0;
 }
 
-// One pass over layers for M (<= PREFILL_ROWS) rows in c->X with metadata in
+// One pass over layers for M (<= prefill_rows) rows in c->X with metadata in
 // c->meta, on the tensor-core path: RMSNorm->f16, tcgen05 GEMMs with fused
 // epilogues, and flash attention over each row's causal prefix.
-int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, int first, int n_layers, cudaStream_t st) {
+int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int max_lim, int first, int n_layers,
+                       cudaStream_t st, std::vector<vvq2_ctx::Rec>* recs, double attn_flops) {
     const vvq2_hparams& hp = c->hp;
+    Recorder R{c, st, recs};
+    auto gemm = [&](const GemmArgs& g, const CUtensorMap& map) -> int {
+        CU(R.begin());
+        CU(gemm_tc_launch(g, map, st));
+        const double n = g.epi == EPI_SWIGLU ? 2.0 * g.N : (double)g.N;
+        CU(R.end(3, 2.0 * g.T * n * g.K));
+        return 0;
+    };
     const int H = hp.hidden_size, nq = hp.n_heads, nkv = hp.n_kv_heads, hd = hp.head_dim;
     const int F = hp.intermediate_size, qw = nq * hd;
     CU(rope_table_launch(c->meta, M, hd, c->rope_ts, c->rope_cs, st));
@@ -509,8 +540,32 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, int first, 
         q.bias = L.qkv_bias;
         q.y = c->Q;
         q.y_stride = qw;
-        CU(gemm_tc_launch(q, mapX, st));
-        // 2. causal attention, one CTA per (row, kv head), f16 output
+        if (int rc = gemm(q, mapX)) return rc;
+        // 2. causal attention, f16 output: tcgen05 flash attention for head_dim
+        //    64/128, else one split-K decode CTA per (row, kv head)
+        if (hd == 64 || hd == 128) {
+            const int64_t kv_rows = (int64_t)kv->n_seqs * kv->max_pages * nkv * KV_PAGE;
+            CUtensorMap mk, mv;
+            if (!make_kv_map(&mk, kvl.k, kv_rows, hd) || !make_kv_map(&mv, kvl.v, kv_rows, hd))
+                return fail(VVQ2_ERR_CUDA, "kv tensor map");
+            FaArgs fa;
+            fa.q = c->Q;
+            fa.out = c->ATTh;
+            fa.meta = c->meta;
+            fa.block_table = kvl.block_table;
+            fa.max_pages = kvl.max_pages;
+            fa.kv_rows = (int)kv_rows;
+            fa.n_seqs = n_seqs;
+            fa.nt = nt;
+            fa.nq = nq;
+            fa.nkv = nkv;
+            fa.hd = hd;
+            fa.scale = 1.0f / sqrtf((float)hd);
+            fa.err = c->err;
+            CU(R.begin());
+            CU(fa_prefill_launch(fa, mk, mv, st));
+            CU(R.end(2, attn_flops));
+        } else {
         AttnDecodeArgs ad;
         ad.q = c->Q;
         ad.out_h = c->ATTh;
@@ -528,6 +583,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, int first, 
         ad.counters = c->counters;
         ad.err = c->err;
         CU(attn_decode_launch(ad, st));
+        }
         // 3. O-proj + residual
         GemmArgs o = g;
         o.w0 = L.o;
@@ -536,7 +592,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, int first, 
         o.epi = EPI_RESID;
         o.y = c->X;
         o.y_stride = H;
-        CU(gemm_tc_launch(o, mapA, st));
+        if (int rc = gemm(o, mapA)) return rc;
         // 4. RMSNorm -> f16, gate/up GEMM with SwiGLU epilogue (f16 out)
         CU(rmsnorm_f16_launch(c->X, L.ffn_norm, M, H, hp.rms_norm_eps, c->Xh, st));
         GemmArgs f = g;
@@ -547,7 +603,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, int first, 
         f.epi = EPI_SWIGLU;
         f.yh = c->Ah;
         f.yh_stride = F;
-        CU(gemm_tc_launch(f, mapX, st));
+        if (int rc = gemm(f, mapX)) return rc;
         // 5. down + residual
         GemmArgs d = g;
         d.w0 = L.down;
@@ -556,7 +612,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, int first, 
         d.epi = EPI_RESID;
         d.y = c->X;
         d.y_stride = H;
-        CU(gemm_tc_launch(d, mapF, st));
+        if (int rc = gemm(d, mapF)) return rc;
     }
     return 0;
 }
@@ -824,11 +880,16 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
         return fail(VVQ2_ERR_CUDA, "stream create failed");
     }
     const int M = GEMV_MAX_M;
-    const int P = PREFILL_ROWS;
+    if (const char* pr = std::getenv("VVQ2_PREFILL_ROWS")) {
+        const int v = atoi(pr);
+        if (v >= 256 && v <= 65536) c->prefill_rows = v / 128 * 128;
+    }
+    const int P = c->prefill_rows;
     const int qw = hp->n_heads * hp->head_dim;
     const int F = std::max(hp->intermediate_size, 1);
     int rc = 0;
     if (cudaSuccess != gemm_tc_prepare()) rc = fail(VVQ2_ERR_CUDA, "gemm prepare failed");
+    if (!rc && cudaSuccess != fa_prefill_prepare()) rc = fail(VVQ2_ERR_CUDA, "flash attention prepare failed");
     if (!encode_fn()) rc = rc ? rc : fail(VVQ2_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     rc = rc ? rc : c->alloc(&c->X, (size_t)P * hp->hidden_size);
     rc = rc ? rc : c->alloc(&c->Q, (size_t)P * qw);
@@ -1107,11 +1168,11 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
     // runs through every layer before the next (resident chunked prefill,
     // the ordering tests/test_qwen2_resident.cpp checks).
     // Few rows: decode GEMV path.  Otherwise tensor-core chunks of up to
-    // PREFILL_ROWS rows.
+    // prefill_rows rows.
     const bool tc_path = n_seqs * n_tok > c->max_rows;
-    if (n_seqs > PREFILL_ROWS)
-        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "more than %d sequences per call", PREFILL_ROWS);
-    const int tok_per_chunk = std::max(1, (tc_path ? PREFILL_ROWS : c->max_rows) / n_seqs);
+    if (n_seqs > c->prefill_rows)
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "more than %d sequences per call", c->prefill_rows);
+    const int tok_per_chunk = std::max(1, (tc_path ? c->prefill_rows : c->max_rows) / n_seqs);
     for (int t0 = 0; t0 < n_tok; t0 += tok_per_chunk) {
         const int nt = std::min(tok_per_chunk, n_tok - t0);
         const int M = n_seqs * nt;
@@ -1130,8 +1191,23 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
             CU(cudaMemcpyAsync(c->X + (size_t)s * nt * H, x + ((size_t)s * n_tok + t0) * H,
                                sizeof(float) * nt * H, x_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
         c->meta_kv = nullptr;   // c->meta no longer describes a decode step
+        std::vector<vvq2_ctx::Rec> recs;
         if (tc_path && M > c->max_rows) {
-            if (int rc = run_layers_prefill(c, kv, M, max_lim, first_layer, n_layers, st)) return rc;
+            // causal attention flops of one layer: QK^T and PV, 2 flops per (head, dim, key)
+            double attn_flops = 0.0;
+            for (int r = 0; r < M; ++r)
+                attn_flops += 4.0 * c->hp.n_heads * c->hp.head_dim *
+                              std::min(c->meta_host[r].pos + 1, c->meta_host[r].kvlen);
+            if (c->prof_on && c->events.size() < 2 * (5 * (size_t)n_layers + 2)) {
+                for (size_t i = c->events.size(); i < 2 * (5 * (size_t)n_layers + 2); ++i) {
+                    cudaEvent_t e;
+                    CU(cudaEventCreate(&e));
+                    c->events.push_back(e);
+                }
+            }
+            if (int rc = run_layers_prefill(c, kv, M, n_seqs, nt, max_lim, first_layer, n_layers, st,
+                                            c->prof_on ? &recs : nullptr, attn_flops))
+                return rc;
         } else {
             int split = 0, nsplit = 0;
             choose_split(c, M, max_lim, &split, &nsplit);
@@ -1151,6 +1227,13 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
         // the meta staging buffer is reused by the next chunk
         CU(cudaStreamSynchronize(st));
         if (int rc = check_device_error(c)) return rc;
+        for (const auto& r : recs) {
+            float ms = 0.f;
+            CU(cudaEventElapsedTime(&ms, c->events[r.e0], c->events[r.e1]));
+            c->prof_ms[r.kind] += ms;
+            c->prof_bytes[r.kind] += r.bytes;
+            c->prof_n[r.kind] += 1;
+        }
     }
     if (flags & VVQ2_ADVANCE)
         for (int s = 0; s < n_seqs; ++s) kv->past[seqs[s]] += n_tok;
@@ -1318,7 +1401,7 @@ int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, cons
 int vvq2_profile(vvq2_ctx* c, int enable) {
     if (int rc = check_ctx(c)) return rc;
     c->prof_on = enable != 0;
-    for (int k = 0; k < 3; ++k) c->prof_ms[k] = c->prof_bytes[k] = 0.0, c->prof_n[k] = 0;
+    for (int k = 0; k < 4; ++k) c->prof_ms[k] = c->prof_bytes[k] = 0.0, c->prof_n[k] = 0;
     // events are created here, never during stream capture
     const size_t need = 2 * (6 * (size_t)c->hp.n_layers + 8);
     while (c->prof_on && c->events.size() < need) {
@@ -1331,7 +1414,7 @@ int vvq2_profile(vvq2_ctx* c, int enable) {
 
 int vvq2_profile_read(vvq2_ctx* c, int kind, double* ms, double* bytes, int64_t* launches) {
     if (int rc = check_ctx(c)) return rc;
-    if (kind < 0 || kind > 2) return fail(VVQ2_ERR_INVALID_ARG, "bad profile kind");
+    if (kind < 0 || kind > 3) return fail(VVQ2_ERR_INVALID_ARG, "bad profile kind");
     if (ms) *ms = c->prof_ms[kind];
     if (bytes) *bytes = c->prof_bytes[kind];
     if (launches) *launches = c->prof_n[kind];

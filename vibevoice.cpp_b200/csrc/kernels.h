@@ -129,6 +129,23 @@ struct AttnDecodeArgs {
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st);
 cudaError_t attn_decode_prepare();
 
+// ------------------------------------------------------ prefill attention
+struct FaArgs {
+    const float* q = nullptr;            // [rows][nq*hd] roped Q, row = seq_slot * nt + t
+    __half* out = nullptr;               // [rows][nq*hd]
+    const RowMeta* meta = nullptr;
+    const int* block_table = nullptr;    // [seq][max_pages]
+    int max_pages = 0;
+    int kv_rows = 0;                     // rows of the K/V tensor maps (pages * n_kv * 64)
+    int n_seqs = 0, nt = 0;              // sequences in the chunk, rows per sequence
+    int nq = 0, nkv = 0, hd = 0;
+    float scale = 0.f;
+    int* err = nullptr;
+};
+cudaError_t fa_prefill_prepare();
+// mk / mv: the layer's K / V pool as 2-D f16 [kv_rows][hd], box 64 x 64, 128-byte swizzle
+cudaError_t fa_prefill_launch(const FaArgs& a, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st);
+
 // ------------------------------------------------------------- misc
 long long launch_count();
 // dequantize a repacked device weight matrix to f32 [rows][cols]
