@@ -74,6 +74,20 @@ bool make_kv_map(CUtensorMap* m, const __half* base, int64_t rows, int hd) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// f16 weight matrix [rows][cols] (dequantized copy) as a TMA map: 64 x box_rows
+// boxes, 128-byte swizzle (the GEMM's B operand layout)
+bool make_w_map(CUtensorMap* m, const __half* base, int rows, int cols, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || cols % 64 || ((uintptr_t)base & 15)) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 thread_local std::string g_err;
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
@@ -150,6 +164,8 @@ struct vvq2_ctx {
     // prefill (tensor-core) scratch for up to prefill_rows token rows
     int prefill_rows = PREFILL_ROWS_DEFAULT;
     __half *Xh = nullptr, *ATTh = nullptr, *Ah = nullptr;
+    __half* Wh = nullptr;          // f16 copy of the weight matrix the current prefill GEMM uses
+    size_t wh_elems = 0;
     float2* rope_cs = nullptr;
     float *part = nullptr, *part_ml = nullptr;
     int* counters = nullptr;
@@ -505,9 +521,35 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
                        cudaStream_t st, std::vector<vvq2_ctx::Rec>* recs, double attn_flops) {
     const vvq2_hparams& hp = c->hp;
     Recorder R{c, st, recs};
+    // Chunks of more than 256 rows first make an f16 copy of the weights
+    // (read once), then the GEMM loads both operands with TMA; smaller
+    // chunks dequantize weight tiles inside the GEMM.
+    const bool tma_b = M > 256;
+    if (tma_b) {
+        const vvq2_ctx::Layer& L0 = c->layers[first];
+        const size_t need = std::max({(size_t)L0.qkv.rows * L0.qkv.cols, (size_t)L0.o.rows * L0.o.cols,
+                                      (size_t)L0.gate.rows * L0.gate.cols + (size_t)L0.up.rows * L0.up.cols,
+                                      (size_t)L0.down.rows * L0.down.cols});
+        if (need > c->wh_elems) {
+            if (int rc = c->alloc(&c->Wh, need)) return rc;
+            c->wh_elems = need;
+        }
+    }
     auto gemm = [&](const GemmArgs& g, const CUtensorMap& map) -> int {
+        CUtensorMap b0, b1;
+        if (tma_b) {
+            const bool sw = g.epi == EPI_SWIGLU;
+            CU(dequant_f16_launch(g.w0, c->Wh, st));
+            if (!make_w_map(&b0, c->Wh, g.w0.rows, g.w0.cols, sw ? 64 : 128))
+                return fail(VVQ2_ERR_CUDA, "weight tensor map");
+            if (sw) {
+                __half* up = c->Wh + (size_t)g.w0.rows * g.w0.cols;
+                CU(dequant_f16_launch(g.w1, up, st));
+                if (!make_w_map(&b1, up, g.w1.rows, g.w1.cols, 64)) return fail(VVQ2_ERR_CUDA, "weight tensor map");
+            }
+        }
         CU(R.begin());
-        CU(gemm_tc_launch(g, map, st));
+        CU(gemm_tc_launch(g, map, st, tma_b ? &b0 : nullptr, tma_b && g.epi == EPI_SWIGLU ? &b1 : nullptr));
         const double n = g.epi == EPI_SWIGLU ? 2.0 * g.N : (double)g.N;
         CU(R.end(3, 2.0 * g.T * n * g.K));
         return 0;
@@ -1525,7 +1567,16 @@ int vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int t
             g.y = dy;
             g.y_stride = n;
             g.err = derr;
-            e = gemm_tc_launch(g, map, 0);
+            if (t > 256) {   // the prefill engine's path for large chunks: f16 weight copy + TMA
+                __half* wh = nullptr;
+                rc = tmp.alloc(&wh, (size_t)n * k);
+                CUtensorMap bmap;
+                if (!rc) e = dequant_f16_launch(dw, wh, 0);
+                if (!rc && e == cudaSuccess && !make_w_map(&bmap, wh, n, k, 128)) rc = fail(VVQ2_ERR_CUDA, "tensor map");
+                if (!rc && e == cudaSuccess) e = gemm_tc_launch(g, map, 0, &bmap, nullptr);
+            } else {
+                e = gemm_tc_launch(g, map, 0);
+            }
         }
         if (!rc && e == cudaSuccess) e = cudaDeviceSynchronize();
         int herr = 0;

@@ -16,6 +16,11 @@
 //
 // CTA: 6 warps.  warp 0: TMEM allocation + TMA producer (lane 0);
 // warp 1: MMA issuer (lane 0); warps 2-5: weight producers, then epilogue.
+//
+// Large prefill chunks instead take the weight operand from an f16 copy made
+// once per chunk (dequant_f16_launch: the same exact-then-f16 values) through
+// TMA as well (TMAB variant): the producer warps then only run the epilogue,
+// and no weight tile is dequantized once per 256-row block of tokens.
 // Pipeline: 4 stages of {A0, A1, B} 16 KB tiles (BK = 64), mbarriers full/empty.
 // Every wait is bounded; a timeout sets args.err and unwinds without leaving
 // TMEM allocated.
@@ -167,8 +172,10 @@ __device__ __forceinline__ void produce_row(const DevW& W, int row, int k0, uint
     }
 }
 
-template <int WT, int EPI>
-__global__ void __launch_bounds__(THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const GemmArgs a) {
+template <int WT, int EPI, bool TMAB>
+__global__ void __launch_bounds__(THREADS, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+              const __grid_constant__ CUtensorMap tmB1, const GemmArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], done;
@@ -181,7 +188,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_tc(const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            tc::mbar_init(&full[s], 1 + 128);
+            tc::mbar_init(&full[s], TMAB ? 1 : 1 + 128);
             tc::mbar_init(&empty[s], 1);
         }
         tc::mbar_init(&done, 1);
@@ -209,9 +216,17 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_tc(const __grid_constant__ 
             if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); break; }
             if (*(volatile int*)&abort_flag) break;
             uint8_t* st = smem + s * STAGE_BYTES;
-            tc::mbar_arrive_expect_tx(&full[s], (two ? 2 : 1) * TILE_BYTES);
+            tc::mbar_arrive_expect_tx(&full[s], ((two ? 2 : 1) + (TMAB ? 1 : 0)) * TILE_BYTES);
             tc::tma_load_2d(st, &tmA, kb * BK, t0, &full[s]);
             if (two) tc::tma_load_2d(st + TILE_BYTES, &tmA, kb * BK, t0 + BM, &full[s]);
+            if constexpr (TMAB) {
+                if constexpr (EPI == EPI_SWIGLU) {   // 64 gate rows, then the same 64 up rows
+                    tc::tma_load_2d(st + 2 * TILE_BYTES, &tmB0, kb * BK, blockIdx.x * 64, &full[s]);
+                    tc::tma_load_2d(st + 2 * TILE_BYTES + 64 * 128, &tmB1, kb * BK, blockIdx.x * 64, &full[s]);
+                } else {
+                    tc::tma_load_2d(st + 2 * TILE_BYTES, &tmB0, kb * BK, n0, &full[s]);
+                }
+            }
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer
@@ -247,7 +262,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_tc(const __grid_constant__ 
             W = &a.w0;
             wrow = n0 + p;
         }
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = 0; !TMAB && kb < nk; ++kb) {
             const int s = kb % STAGES;
             if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); break; }
             if (*(volatile int*)&abort_flag) break;
@@ -256,6 +271,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_tc(const __grid_constant__ 
             tc::fence_proxy_async_smem();
             tc::mbar_arrive(&full[s]);
         }
+        (void)W;
+        (void)wrow;
         // ---- epilogue: wait for the accumulators
         bool ok = tc::mbar_wait(&done, 0);
         if (!ok) fail();
@@ -367,15 +384,20 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_tc(const __grid_constant__ 
 }
 
 template <int EPI>
-cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, cudaStream_t st) {
+cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, const CUtensorMap* b0, const CUtensorMap* b1,
+                       cudaStream_t st) {
     dim3 grid((EPI == EPI_SWIGLU ? (a.N + 63) / 64 : (a.N + BN - 1) / BN), (a.T + 2 * BM - 1) / (2 * BM));
-    switch (a.w0.type) {
-        case W_Q8_0: k_gemm_tc<W_Q8_0, EPI><<<grid, THREADS, SMEM_BYTES, st>>>(tm, a); break;
-        case W_Q5_K: k_gemm_tc<W_Q5_K, EPI><<<grid, THREADS, SMEM_BYTES, st>>>(tm, a); break;
-        case W_Q6_K: k_gemm_tc<W_Q6_K, EPI><<<grid, THREADS, SMEM_BYTES, st>>>(tm, a); break;
-        case W_F16: k_gemm_tc<W_F16, EPI><<<grid, THREADS, SMEM_BYTES, st>>>(tm, a); break;
-        case W_F32: k_gemm_tc<W_F32, EPI><<<grid, THREADS, SMEM_BYTES, st>>>(tm, a); break;
-        default: return cudaErrorInvalidValue;
+    if (b0) {
+        k_gemm_tc<W_F16, EPI, true><<<grid, THREADS, SMEM_BYTES, st>>>(tm, *b0, b1 ? *b1 : *b0, a);
+    } else {
+        switch (a.w0.type) {
+            case W_Q8_0: k_gemm_tc<W_Q8_0, EPI, false><<<grid, THREADS, SMEM_BYTES, st>>>(tm, tm, tm, a); break;
+            case W_Q5_K: k_gemm_tc<W_Q5_K, EPI, false><<<grid, THREADS, SMEM_BYTES, st>>>(tm, tm, tm, a); break;
+            case W_Q6_K: k_gemm_tc<W_Q6_K, EPI, false><<<grid, THREADS, SMEM_BYTES, st>>>(tm, tm, tm, a); break;
+            case W_F16: k_gemm_tc<W_F16, EPI, false><<<grid, THREADS, SMEM_BYTES, st>>>(tm, tm, tm, a); break;
+            case W_F32: k_gemm_tc<W_F32, EPI, false><<<grid, THREADS, SMEM_BYTES, st>>>(tm, tm, tm, a); break;
+            default: return cudaErrorInvalidValue;
+        }
     }
     note_launch();
     return cudaGetLastError();
@@ -383,9 +405,9 @@ cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, cudaStream_t st
 
 template <int EPI>
 cudaError_t prepare_epi() {
-    const void* fns[] = {(const void*)k_gemm_tc<W_Q8_0, EPI>, (const void*)k_gemm_tc<W_Q5_K, EPI>,
-                         (const void*)k_gemm_tc<W_Q6_K, EPI>, (const void*)k_gemm_tc<W_F16, EPI>,
-                         (const void*)k_gemm_tc<W_F32, EPI>};
+    const void* fns[] = {(const void*)k_gemm_tc<W_Q8_0, EPI, false>, (const void*)k_gemm_tc<W_Q5_K, EPI, false>,
+                         (const void*)k_gemm_tc<W_Q6_K, EPI, false>, (const void*)k_gemm_tc<W_F16, EPI, false>,
+                         (const void*)k_gemm_tc<W_F32, EPI, false>, (const void*)k_gemm_tc<W_F16, EPI, true>};
     for (const void* f : fns) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
@@ -403,14 +425,16 @@ cudaError_t gemm_tc_prepare() {
     return prepare_epi<EPI_STORE>();
 }
 
-cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st) {
+cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st, const CUtensorMap* tmB0,
+                           const CUtensorMap* tmB1) {
     if (a.K % BK || a.T <= 0 || a.N <= 0) return cudaErrorInvalidValue;
     if (a.epi == EPI_QKV && (BN % a.hd || (a.hd != 32 && a.hd != 64 && a.hd != 128))) return cudaErrorInvalidValue;
+    if (a.epi == EPI_SWIGLU && tmB0 && !tmB1) return cudaErrorInvalidValue;
     switch (a.epi) {
-        case EPI_QKV: return launch_epi<EPI_QKV>(a, tmA, st);
-        case EPI_RESID: return launch_epi<EPI_RESID>(a, tmA, st);
-        case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(a, tmA, st);
-        case EPI_STORE: return launch_epi<EPI_STORE>(a, tmA, st);
+        case EPI_QKV: return launch_epi<EPI_QKV>(a, tmA, tmB0, tmB1, st);
+        case EPI_RESID: return launch_epi<EPI_RESID>(a, tmA, tmB0, tmB1, st);
+        case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(a, tmA, tmB0, tmB1, st);
+        case EPI_STORE: return launch_epi<EPI_STORE>(a, tmA, tmB0, tmB1, st);
         default: return cudaErrorInvalidValue;
     }
 }

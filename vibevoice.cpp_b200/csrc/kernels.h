@@ -61,7 +61,11 @@ struct GemmArgs {
     const float2* rope_cs = nullptr;   // [T][hd/2] (cos, sin)
     int* err = nullptr;
 };
-cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st);
+// tmB0/tmB1 (optional): f16 weight maps [N][K], box 64 x 128 (SwiGLU: gate and
+// up, box 64 x 64); when given, weights are loaded by TMA instead of being
+// dequantized in the kernel
+cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st,
+                           const CUtensorMap* tmB0 = nullptr, const CUtensorMap* tmB1 = nullptr);
 cudaError_t gemm_tc_prepare();
 
 // ------------------------------------------------------ persistent decode step
@@ -150,6 +154,8 @@ cudaError_t fa_prefill_launch(const FaArgs& a, const CUtensorMap& mk, const CUte
 long long launch_count();
 // dequantize a repacked device weight matrix to f32 [rows][cols]
 cudaError_t dequant_rows_launch(const DevW& w, float* dst, cudaStream_t st);
+// ... to f16 [rows][cols] (exact dequantized value, rounded once)
+cudaError_t dequant_f16_launch(const DevW& w, __half* dst, cudaStream_t st);
 cudaError_t rope_launch(const float* x, int n_tok, int n_heads, int hd, const int32_t* pos,
                         float ts, float* y, cudaStream_t st);
 cudaError_t rmsnorm_launch(const float* x, const float* w, int rows, int n, float eps, float* y,
