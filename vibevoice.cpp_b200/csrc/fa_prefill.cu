@@ -10,16 +10,17 @@
 //   warp 0: TMA producer of 128-key K and V tiles (two 64-key pages each,
 //           pages resolved through the block table, 128-byte swizzle)
 //   warp 1: MMA issuer: S_j = Q K_j^T into one of two 128-column TMEM
-//           buffers; O += P_j V_j (V as an MN-major operand, no transpose)
-//           into the TMEM output accumulator
-//   warps 2-5: one query row per thread: Q staging (f32 -> f16), then per
+//           buffers (Q read from TMEM); O += P_j V_j with P read from TMEM
+//           and V from shared memory as an MN-major operand (no transpose)
+//   warps 2-5: one query row per thread: Q staged as f16 into TMEM, then per
 //           key tile the softmax from TMEM against a per-row reference max:
-//           P = exp2((S - m_ref) log2e/sqrt(hd)) written as f16 into the
-//           A-operand tile.  O is only rescaled (TMEM load, scale, store)
-//           when a row's max exceeds its reference by more than 2^8, so P
-//           stays <= 256 and most tiles need no correction pass.
-// Tiles are double buffered: S_{j+1}, the loads of tile j+2 and P_{j-1} V_{j-1}
-// overlap the softmax of tile j.  Every wait is bounded; a timeout records args.err and
+//           P = exp2((S - m_ref) log2e/sqrt(hd)) written as f16 over the
+//           tile's own S columns.  O is only rescaled (TMEM load, scale,
+//           store) when a row's max exceeds its reference by more than 2^8,
+//           so P stays <= 256 and most tiles need no correction pass.
+// Shared memory holds only K and V (3 stages); Q and P never touch it, which
+// halves the shared-memory traffic of the two MMAs.  S_{j+1}, the loads of
+// later tiles and P_{j-1} V_{j-1} overlap the softmax of tile j.  Every wait is bounded; a timeout records args.err and
 // the CTA unwinds, still freeing its TMEM.
 #include "common.cuh"
 #include "kernels.h"
@@ -34,17 +35,18 @@ constexpr int BQ = 128;        // query rows per CTA
 constexpr int BKV = 128;       // keys per tile
 constexpr int BLK = 16384;     // one [128 rows][128 bytes] swizzled block
 constexpr int PAGE_BYTES = KV_PAGE * 128;   // one 64-key box of 64 f16 columns
-constexpr uint32_t TMEM_COLS = 512;         // S0 | S1 | O
+constexpr uint32_t TMEM_COLS = 512;         // S0 | S1 | O | Q
+constexpr int NST = 3;                      // K/V stages
 
 template <int HD>
 struct FaCfg {
-    static constexpr int NB = HD / 64;                  // 64-column blocks along hd
-    static constexpr int Q_OFF = 0;
-    static constexpr int K_OFF = NB * BLK;              // 2 stages
-    static constexpr int V_OFF = K_OFF + 2 * NB * BLK;  // 2 stages
-    static constexpr int P_OFF = V_OFF + 2 * NB * BLK;  // 2 buffers x 2 key blocks
-    static constexpr int SMEM = P_OFF + 4 * BLK + 1024;
+    static constexpr int NB = HD / 64;                    // 64-column blocks along hd
+    static constexpr int K_OFF = 0;                       // NST stages
+    static constexpr int V_OFF = K_OFF + NST * NB * BLK;  // NST stages
+    static constexpr int SMEM = V_OFF + NST * NB * BLK + 1024;
     static constexpr uint32_t TILE_TX = NB * 2 * PAGE_BYTES;   // one K (or V) tile
+    static constexpr uint32_t O_COL = 2 * BKV;            // output accumulator columns
+    static constexpr uint32_t Q_COL = O_COL + HD;         // Q: HD/2 columns of f16 pairs
 };
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
@@ -59,16 +61,14 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// 16-byte chunk j (0..7) of row r of a [128][128 B] 128-byte-swizzled block
-__device__ __forceinline__ uint8_t* swz(uint8_t* blk, int r, int j) { return blk + r * 128 + ((j ^ (r & 7)) << 4); }
-
 template <int HD>
 __global__ void __launch_bounds__(FT, 1)
     k_fa_prefill(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, const FaArgs a) {
     using C = FaCfg<HD>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full, o_full[2], q_full;
+    __shared__ __align__(8) uint64_t k_full[NST], k_empty[NST], v_full[NST], v_empty[NST], s_full[2], p_full, o_full[2];
+    __shared__ __align__(8) uint64_t q_full;
     __shared__ __align__(8) uint64_t mma_done;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
@@ -84,13 +84,14 @@ __global__ void __launch_bounds__(FT, 1)
     const int nkt = (klim + BKV - 1) / BKV;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < NST; ++i) {
             tc::mbar_init(&k_full[i], 1);
             tc::mbar_init(&k_empty[i], 1);
             tc::mbar_init(&v_full[i], 1);
             tc::mbar_init(&v_empty[i], 1);
-            tc::mbar_init(&s_full[i], 1);
         }
+        tc::mbar_init(&s_full[0], 1);
+        tc::mbar_init(&s_full[1], 1);
         tc::mbar_init(&p_full, 128);
         tc::mbar_init(&o_full[0], 1);
         tc::mbar_init(&o_full[1], 1);
@@ -115,8 +116,8 @@ __global__ void __launch_bounds__(FT, 1)
     auto aborted = [&]() { return *(volatile int*)&abort_flag != 0; };
 
     if (warp == 0 && lane == 0) {
-        // ---- TMA producer: K tile j after S_{j-2} finished with its stage,
-        //      V tile j after O_{j-2}
+        // ---- TMA producer: K tile j after S_{j-NST} finished with its stage,
+        //      V tile j after P V of tile j-NST
         auto load = [&](const CUtensorMap* map, uint8_t* stage, uint64_t* bar, int j) {
             tc::mbar_arrive_expect_tx(bar, C::TILE_TX);
             for (int ps = 0; ps < 2; ++ps) {
@@ -131,39 +132,38 @@ __global__ void __launch_bounds__(FT, 1)
         };
         int nk = 0, nv = 0;
         for (int j = 0; j < nkt; ++j) {
-            const int st = j & 1;
-            if (j >= 2 && !tc::mbar_wait(&k_empty[st], ((j >> 1) - 1) & 1)) { fail(); break; }
+            const int st = j % NST;
+            if (j >= NST && !tc::mbar_wait(&k_empty[st], ((j / NST) - 1) & 1)) { fail(); break; }
             if (aborted()) break;
             load(&mk, sm + C::K_OFF + st * C::NB * BLK, &k_full[st], j);
             ++nk;
-            if (j >= 2 && !tc::mbar_wait(&v_empty[st], ((j >> 1) - 1) & 1)) { fail(); break; }
+            if (j >= NST && !tc::mbar_wait(&v_empty[st], ((j / NST) - 1) & 1)) { fail(); break; }
             if (aborted()) break;
             load(&mv, sm + C::V_OFF + st * C::NB * BLK, &v_full[st], j);
             ++nv;
         }
         // copies still in flight land before the CTA exits
-        for (int j = max(0, nk - 2); j < nk; ++j) tc::mbar_wait(&k_full[j & 1], (j >> 1) & 1, 1u << 20);
-        for (int j = max(0, nv - 2); j < nv; ++j) tc::mbar_wait(&v_full[j & 1], (j >> 1) & 1, 1u << 20);
+        for (int j = max(0, nk - NST); j < nk; ++j) tc::mbar_wait(&k_full[j % NST], (j / NST) & 1, 1u << 20);
+        for (int j = max(0, nv - NST); j < nv; ++j) tc::mbar_wait(&v_full[j % NST], (j / NST) & 1, 1u << 20);
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer
         constexpr uint32_t idS = tc::idesc_f16(BQ, BKV);
         constexpr uint32_t idO = tc::idesc_f16_bmn(BQ, HD);
-        uint8_t* q = sm + C::Q_OFF;
         bool ok = tc::mbar_wait(&q_full, 0);
         auto issue_s = [&](int j) -> bool {
-            const int st = j & 1;
-            if (!tc::mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
+            const int ks = j % NST;
+            if (!tc::mbar_wait(&k_full[ks], (j / NST) & 1)) return false;
             if (aborted()) return false;
             tc::tc_fence_after();
-            uint8_t* kt = sm + C::K_OFF + st * C::NB * BLK;
+            uint8_t* kt = sm + C::K_OFF + ks * C::NB * BLK;
 #pragma unroll
             for (int k16 = 0; k16 < HD / 16; ++k16) {
                 const int kb = k16 >> 2, w = k16 & 3;
-                tc::mma_f16(tmem + st * BKV, tc::desc_sw128(q + kb * BLK) + 2 * w, tc::desc_sw128(kt + kb * BLK) + 2 * w,
-                            idS, k16 > 0);
+                tc::mma_f16_ts(tmem + (j & 1) * BKV, tmem + C::Q_COL + k16 * 8, tc::desc_sw128(kt + kb * BLK) + 2 * w,
+                               idS, k16 > 0);
             }
-            tc::mma_commit(&k_empty[st]);
-            tc::mma_commit(&s_full[st]);
+            tc::mma_commit(&k_empty[ks]);
+            tc::mma_commit(&s_full[j & 1]);
             return true;
         };
         if (ok) {
@@ -171,21 +171,20 @@ __global__ void __launch_bounds__(FT, 1)
             ok = issue_s(0) && (nkt < 2 || issue_s(1));
         }
         for (int j = 0; ok && j < nkt; ++j) {
-            const int st = j & 1;
-            if (!tc::mbar_wait(&p_full, j & 1) || !tc::mbar_wait(&v_full[st], (j >> 1) & 1) || aborted()) {
+            const int vs = j % NST;
+            if (!tc::mbar_wait(&p_full, j & 1) || !tc::mbar_wait(&v_full[vs], (j / NST) & 1) || aborted()) {
                 ok = false;
                 break;
             }
             tc::tc_fence_after();
-            uint8_t* vt = sm + C::V_OFF + st * C::NB * BLK;
-            uint8_t* p = sm + C::P_OFF + (j & 1) * 2 * BLK;
+            uint8_t* vt = sm + C::V_OFF + vs * C::NB * BLK;
 #pragma unroll
             for (int k16 = 0; k16 < BKV / 16; ++k16) {
-                // A = P (K-major, keys), B = V (MN-major: hd contiguous per key)
-                tc::mma_f16(tmem + 2 * BKV, tc::desc_sw128(p + (k16 >> 2) * BLK) + 2 * (k16 & 3),
-                            tc::desc_sw128_mn(vt + k16 * 16 * 128, BLK), idO, (j | k16) > 0);
+                // A = P (TMEM, over the tile's S columns), B = V (MN-major: hd contiguous per key)
+                tc::mma_f16_ts(tmem + C::O_COL, tmem + (j & 1) * BKV + k16 * 8,
+                               tc::desc_sw128_mn(vt + k16 * 16 * 128, BLK), idO, (j | k16) > 0);
             }
-            tc::mma_commit(&v_empty[st]);
+            tc::mma_commit(&v_empty[vs]);
             tc::mma_commit(&o_full[j & 1]);
             if (j + 2 < nkt && !issue_s(j + 2)) ok = false;
         }
@@ -202,31 +201,31 @@ __global__ void __launch_bounds__(FT, 1)
             const RowMeta rm = a.meta[grow];
             kl = min(rm.pos + 1, rm.kvlen);
         }
-        // Q row -> f16, swizzled K-major A operand
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+        // Q row -> f16 pairs in this row's TMEM lane (the S MMA's A operand)
         {
             const float* qr = a.q + (size_t)grow * a.nq * HD + (size_t)h * HD;
 #pragma unroll
-            for (int b = 0; b < C::NB; ++b)
+            for (int cc = 0; cc < HD / 64; ++cc) {
+                float qp[32];   // 32 columns = 64 elements, packed as f16 pairs
+                uint32_t* qu = reinterpret_cast<uint32_t*>(qp);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    uint4 v = make_uint4(0, 0, 0, 0);
-                    if (valid) {
-                        const float4 x0 = __ldg(reinterpret_cast<const float4*>(qr + b * 64 + j * 8));
-                        const float4 x1 = __ldg(reinterpret_cast<const float4*>(qr + b * 64 + j * 8 + 4));
-                        v = make_uint4(pack_h2(x0.x, x0.y), pack_h2(x0.z, x0.w), pack_h2(x1.x, x1.y),
-                                       pack_h2(x1.z, x1.w));
-                    }
-                    *reinterpret_cast<uint4*>(swz(sm + C::Q_OFF + b * BLK, rr, j)) = v;
+                for (int e = 0; e < 64; e += 4) {
+                    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (valid) x = __ldg(reinterpret_cast<const float4*>(qr + cc * 64 + e));
+                    qu[e / 2] = pack_h2(x.x, x.y);
+                    qu[e / 2 + 1] = pack_h2(x.z, x.w);
                 }
+                tc::tmem_st32(lane_base + C::Q_COL + cc * 32, qp);
+            }
         }
-        tc::fence_proxy_async_smem();
+        tc::tc_fence_before();
         tc::mbar_arrive(&q_full);
 
         const float c = a.scale * 1.4426950408889634f;   // scores to log2 units
         constexpr float RESCALE_LOG2 = 8.f;                 // P <= 2^8 between rescales
         float m_ref = -INFINITY, l = 0.f;
-        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
-        const uint32_t to = lane_base + 2 * BKV;            // this row's output accumulator
+        const uint32_t to = lane_base + C::O_COL;           // this row's output accumulator
         int o_seen = 0;                                     // tiles whose P V is known complete
         bool ok = true;
         // Wait for P V of tiles < upto, in order.  o_full[t & 1] completes for
@@ -284,29 +283,30 @@ __global__ void __launch_bounds__(FT, 1)
                     m_ref = mx;
                 }
             }
-            // P buffer j % 2 was last read by P V of tile j - 2: wait for it (in
-            // order, so the parity of every o_full wait stays unambiguous)
+            // arrivals stay within one tile of the o_full phases seen (parity tracking)
             wait_o(j - 1);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
-            // P = 2^(S c - m_ref c) (masked keys: 2^-inf = 0), f16, into buffer j % 2
+            // P = 2^(S c - m_ref c) (masked keys: 2^-inf = 0) as f16 pairs over
+            // the first 64 of this tile's S columns (already read above)
             const float mc = m_ref == -INFINITY ? 0.f : m_ref * c;
             float sum0 = 0.f, sum1 = 0.f;
-            uint8_t* pb = sm + C::P_OFF + (j & 1) * 2 * BLK;
 #pragma unroll
-            for (int q8 = 0; q8 < BKV / 8; ++q8) {
-                float pe[8];
+            for (int cc = 0; cc < 2; ++cc) {
+                float pp[32];
+                uint32_t* pu = reinterpret_cast<uint32_t*>(pp);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) pe[e] = ex2(fmaf(sv[q8 * 8 + e], c, -mc));
-                sum0 += (pe[0] + pe[1]) + (pe[2] + pe[3]);
-                sum1 += (pe[4] + pe[5]) + (pe[6] + pe[7]);
-                // keys q8*8 .. q8*8+7: block (q8*8)/64, chunk q8 % 8
-                *reinterpret_cast<uint4*>(swz(pb + (q8 >> 3) * BLK, rr, q8 & 7)) =
-                    make_uint4(pack_h2(pe[0], pe[1]), pack_h2(pe[2], pe[3]), pack_h2(pe[4], pe[5]), pack_h2(pe[6], pe[7]));
+                for (int e = 0; e < 64; e += 2) {
+                    const float p0 = ex2(fmaf(sv[cc * 64 + e], c, -mc));
+                    const float p1 = ex2(fmaf(sv[cc * 64 + e + 1], c, -mc));
+                    if (e & 2) sum1 += p0 + p1;
+                    else sum0 += p0 + p1;
+                    pu[e / 2] = pack_h2(p0, p1);
+                }
+                tc::tmem_st32(lane_base + st * BKV + cc * 32, pp);
             }
             l += sum0 + sum1;
-            tc::fence_proxy_async_smem();   // P visible to the tensor core
-            tc::tc_fence_before();          // S reads and O rescale done before the MMA reuses them
+            tc::tc_fence_before();          // S reads, P stores and O rescale done before the MMA reuses them
             tc::mbar_arrive(&p_full);
         }
         wait_o(nkt);
