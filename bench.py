@@ -110,6 +110,57 @@ def prefill_measure(vvq2, synth, torch, local, sh, n_tok, reps=3):
     }
 
 
+def c3_measure(eng, hp, torch, dist, rank, world, sh, steps, warmup=2):
+    """Config 3: 64 independent TTS streams (128 rows with their CFG pairs),
+    ragged KV lengths uniform in [64, 2048] (a pair shares its length), one
+    greedy decode step per stream per iteration.  The streams are split over
+    the ranks (data parallel, no collective on the data path); each rank
+    decodes its rows as one batched step (tensor-core path, split-K attention
+    over each row's own length).  Value: all ranks' rows per second, timed as
+    the max over ranks."""
+    streams = 64
+    mine = [s for s in range(streams) if s % world == rank]
+    rows = 2 * len(mine)
+    rng = np.random.default_rng(SEED + 3)
+    lens_all = rng.integers(64, 2049, size=streams)
+    lens = np.repeat(lens_all[mine], 2)
+    kv = eng.kv(rows, int(lens.max()) + warmup + steps + 8)
+    w = hp["n_kv_heads"] * hp["head_dim"]
+    g = torch.Generator(device="cuda").manual_seed(SEED + 3 + rank)
+    for r in range(rows):
+        L = int(lens[r])
+        for li in range(hp["n_layers"]):
+            k = torch.randn((L, w), generator=g, device="cuda", dtype=torch.float32)
+            v = torch.randn((L, w), generator=g, device="cuda", dtype=torch.float32)
+            kv.load_prefix(r, li, k, v)
+        kv.set_past_len(r, L)
+    seqs = list(range(rows))
+    tok = torch.randint(0, hp["vocab"], (rows,), dtype=torch.int32, device="cuda", generator=g)
+    for _ in range(warmup):
+        eng.decode_step(kv, seqs, tok, tok, stream=sh)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        eng.decode_step(kv, seqs, tok, tok, stream=sh)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    kv.close()
+    return {"workload": "config 3: 64 streams x CFG pair (128 rows) of the 0.5B-shaped Q8_0 stack, ragged KV "
+                        "64..2048, one greedy step per stream per iteration",
+            "value": round(2 * streams * steps / (ms / 1000.0), 1), "unit": "tokens/s",
+            "ms_per_step": round(ms / steps, 3), "rows_per_gpu": rows, "n_gpus": world, "steps": steps,
+            "scaling": "strong", "parallelism": f"data parallel over {world} GPU(s), no collectives"}
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -233,6 +284,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--prefill-tokens", type=int, default=16384)
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-c3", action="store_true")
+    ap.add_argument("--c3-steps", type=int, default=10)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, local, world = dist_env()
@@ -359,6 +412,8 @@ def main():
                      "step_hbm_gbs": round(synth.weight_bytes(model) * 1.0 / (ms / args.steps / 1000.0) / 1e9, 1)},
         "clocks": clk.summary(),
     }
+    if not args.no_c3:
+        line["c3"] = c3_measure(eng, hp, torch, dist, rank, world, sh, args.c3_steps)
     if not args.no_prefill:
         line["prefill"] = prefill_measure(vvq2, synth, torch, local, sh, args.prefill_tokens)
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -358,7 +358,7 @@ int check_device_error(vvq2_ctx* c) {
         if (c->bar_count) cudaMemsetAsync(c->bar_count, 0, sizeof(unsigned long long), c->stream);
         if (c->epoch) cudaMemsetAsync(c->epoch, 0, sizeof(unsigned int), c->stream);
         if (c->abort_flag) cudaMemsetAsync(c->abort_flag, 0, sizeof(int), c->stream);
-        if (c->counters) cudaMemsetAsync(c->counters, 0, sizeof(int) * GEMV_MAX_M * c->hp.n_kv_heads, c->stream);
+        if (c->counters) cudaMemsetAsync(c->counters, 0, sizeof(int) * c->prefill_rows * c->hp.n_kv_heads, c->stream);
         cudaStreamSynchronize(c->stream);
         return fail(VVQ2_ERR_CUDA, "a device-side wait timed out (code %d)", e);
     }
@@ -583,9 +583,10 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         q.y = c->Q;
         q.y_stride = qw;
         if (int rc = gemm(q, mapX)) return rc;
-        // 2. causal attention, f16 output: tcgen05 flash attention for head_dim
-        //    64/128, else one split-K decode CTA per (row, kv head)
-        if (hd == 64 || hd == 128) {
+        // 2. causal attention, f16 output: tcgen05 flash attention for prompt
+        //    chunks (head_dim 64/128); rows of one token each (batched decode
+        //    of many streams) and other head sizes use the split-K decode kernel
+        if ((hd == 64 || hd == 128) && nt > 1) {
             const int64_t kv_rows = (int64_t)kv->n_seqs * kv->max_pages * nkv * KV_PAGE;
             CUtensorMap mk, mv;
             if (!make_kv_map(&mk, kvl.k, kv_rows, hd) || !make_kv_map(&mv, kvl.v, kv_rows, hd))
@@ -617,8 +618,20 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         ad.nq = nq;
         ad.nkv = nkv;
         ad.hd = hd;
-        ad.split = (max_lim + KV_PAGE - 1) / KV_PAGE * KV_PAGE;
-        ad.max_splits = 1;
+        if (nt == 1) {
+            // partials [row][split] share the decode scratch: rows x splits <= its capacity
+            int split = 0, nsplit = 0;
+            choose_split(c, M, max_lim, &split, &nsplit);
+            while (nsplit > 1 && M * nsplit > GEMV_MAX_M * c->max_splits_cap) {
+                split += KV_PAGE;
+                nsplit = (max_lim + split - 1) / split;
+            }
+            ad.split = split;
+            ad.max_splits = nsplit;
+        } else {
+            ad.split = (max_lim + KV_PAGE - 1) / KV_PAGE * KV_PAGE;
+            ad.max_splits = 1;
+        }
         ad.scale = 1.0f / sqrtf((float)hd);
         ad.part = c->part;
         ad.part_ml = c->part_ml;
@@ -764,6 +777,71 @@ void mega_split(const vvq2_ctx* c, int M, int max_lim, int* split, int* nsplit) 
     while ((max_lim + s - 1) / s > 64) s += KV_PAGE;
     *split = s;
     *nsplit = (max_lim + s - 1) / s;
+}
+
+// Greedy decode step for more rows than the GEMV paths take (many streams at
+// once): embedding, the stack on the tensor-core path (split-K decode
+// attention over each row's ragged KV length), final RMSNorm, and the lm_head
+// as a tcgen05 GEMM whose epilogue keeps each row's argmax.
+int decode_step_batched(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, const int32_t* tokens_in,
+                        int32_t* tokens_out, cudaStream_t st) {
+    const vvq2_hparams& hp = c->hp;
+    const int M = n_seqs, H = hp.hidden_size;
+    if (M > c->prefill_rows) return fail(VVQ2_ERR_INVALID_ARG, "%d rows > %d per decode step", M, c->prefill_rows);
+    int max_lim = 1;
+    double attn_flops = 0.0;
+    for (int s = 0; s < M; ++s) {
+        const int past = kv->past[seqs[s]];
+        c->meta_host[s] = RowMeta{seqs[s], past, past, past + 1};
+        max_lim = std::max(max_lim, past + 1);
+        attn_flops += 4.0 * hp.n_heads * hp.head_dim * (past + 1);
+    }
+    CU(cudaMemcpyAsync(c->meta, c->meta_host, sizeof(RowMeta) * M, cudaMemcpyHostToDevice, st));
+    c->meta_kv = nullptr;   // c->meta no longer describes a graph-captured decode step
+    CU(cudaMemcpyAsync(c->tok, tokens_in, sizeof(int32_t) * M, cudaMemcpyDefault, st));
+    CU(embed_launch(c->tok_embd, c->tok, M, c->X, st));
+    std::vector<vvq2_ctx::Rec> recs;
+    if (c->prof_on && c->events.size() < 2 * (5 * (size_t)hp.n_layers + 4)) {
+        for (size_t i = c->events.size(); i < 2 * (5 * (size_t)hp.n_layers + 4); ++i) {
+            cudaEvent_t e;
+            CU(cudaEventCreate(&e));
+            c->events.push_back(e);
+        }
+    }
+    if (int rc = run_layers_prefill(c, kv, M, M, 1, max_lim, 0, hp.n_layers, st, c->prof_on ? &recs : nullptr,
+                                    attn_flops))
+        return rc;
+    CU(rmsnorm_f16_launch(c->X, c->out_norm, M, H, hp.rms_norm_eps, c->Xh, st));
+    CUtensorMap mapX;
+    if (!make_act_map(&mapX, c->Xh, M, H)) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "hidden %d not a multiple of 64", H);
+    CU(argmax_init_launch(c->amax, M, st));
+    GemmArgs g;
+    g.w0 = c->lm_head;
+    g.T = M;
+    g.N = c->lm_head.rows;
+    g.K = H;
+    g.epi = EPI_ARGMAX;
+    g.amax = c->amax;
+    g.err = c->err;
+    {
+        Recorder R{c, st, c->prof_on ? &recs : nullptr};
+        CU(R.begin());
+        CU(gemm_tc_launch(g, mapX, st));
+        CU(R.end(3, 2.0 * M * (double)g.N * H));
+    }
+    CU(argmax_final_launch(c->amax, M, c->tok, st));
+    CU(cudaMemcpyAsync(tokens_out, c->tok, sizeof(int32_t) * M, cudaMemcpyDefault, st));
+    CU(cudaStreamSynchronize(st));   // the meta staging buffer is reused by the next call
+    if (int rc = check_device_error(c)) return rc;
+    for (const auto& r : recs) {
+        float ms = 0.f;
+        CU(cudaEventElapsedTime(&ms, c->events[r.e0], c->events[r.e1]));
+        c->prof_ms[r.kind] += ms;
+        c->prof_bytes[r.kind] += r.bytes;
+        c->prof_n[r.kind] += 1;
+    }
+    for (int s = 0; s < M; ++s) kv->past[seqs[s]] += 1;
+    return 0;
 }
 
 // Device table of layer descriptors for (ctx, kv); built outside stream capture.
@@ -944,10 +1022,10 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     rc = rc ? rc : c->alloc(&c->QKVr, (size_t)M * (hp->n_heads + 2 * hp->n_kv_heads) * hp->head_dim);
     rc = rc ? rc : c->alloc(&c->part, (size_t)M * c->max_splits_cap * qw);
     rc = rc ? rc : c->alloc(&c->part_ml, (size_t)M * c->max_splits_cap * hp->n_heads * 2);
-    rc = rc ? rc : c->alloc(&c->counters, (size_t)M * hp->n_kv_heads);
+    rc = rc ? rc : c->alloc(&c->counters, (size_t)P * hp->n_kv_heads);   // batched decode: one per (row, KV head)
     rc = rc ? rc : c->alloc(&c->meta, (size_t)P);
-    rc = rc ? rc : c->alloc(&c->amax, (size_t)M);
-    rc = rc ? rc : c->alloc(&c->tok, (size_t)M);
+    rc = rc ? rc : c->alloc(&c->amax, (size_t)P);   // batched decode: one key / token per row
+    rc = rc ? rc : c->alloc(&c->tok, (size_t)P);
     rc = rc ? rc : c->alloc(&c->err, (size_t)1);
     rc = rc ? rc : c->alloc(&c->bar_count, (size_t)1);
     rc = rc ? rc : c->alloc(&c->epoch, (size_t)1);
@@ -957,7 +1035,7 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     if (!rc && hp->vocab_size > 0) rc = c->alloc(&c->LOGITS, (size_t)M * hp->vocab_size);
     if (!rc && cudaMallocHost(&c->meta_host, sizeof(RowMeta) * P) != cudaSuccess)
         rc = fail(VVQ2_ERR_OUT_OF_MEMORY, "pinned alloc failed");
-    if (!rc && (cudaMemset(c->counters, 0, sizeof(int) * M * hp->n_kv_heads) != cudaSuccess ||
+    if (!rc && (cudaMemset(c->counters, 0, sizeof(int) * P * hp->n_kv_heads) != cudaSuccess ||
                 cudaMemset(c->err, 0, sizeof(int)) != cudaSuccess ||
                 cudaMemset(c->bar_count, 0, sizeof(unsigned long long)) != cudaSuccess ||
                 cudaMemset(c->epoch, 0, sizeof(unsigned int)) != cudaSuccess ||
@@ -1343,7 +1421,7 @@ int vvq2_embed(vvq2_ctx* c, int n, const int32_t* tokens, float* out, void* stre
 int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, const int32_t* tokens_in,
                      int32_t* tokens_out, void* stream) {
     if (int rc = check_ctx(c)) return rc;
-    if (!kv || kv->ctx != c || !seqs || !tokens_in || !tokens_out || n_seqs <= 0 || n_seqs > c->max_rows)
+    if (!kv || kv->ctx != c || !seqs || !tokens_in || !tokens_out || n_seqs <= 0)
         return fail(VVQ2_ERR_INVALID_ARG, "bad decode_step arguments");
     if (c->tok_embd.type < 0 || c->lm_head.type < 0 || !c->out_norm)
         return fail(VVQ2_ERR_INVALID_ARG, "decode_step needs output_norm, lm_head and tok_embd");
@@ -1357,6 +1435,7 @@ int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, cons
         if (kv->past[seqs[s]] + 1 > kv->max_seq) return fail(VVQ2_ERR_INVALID_ARG, "KV overflow");
     }
     cudaStream_t st = pick_stream(c, stream);
+    if (n_seqs > c->max_rows) return decode_step_batched(c, kv, seqs, n_seqs, tokens_in, tokens_out, st);
     const int M = n_seqs;
     std::vector<int> sv(seqs, seqs + n_seqs);
     int max_lim = 1;

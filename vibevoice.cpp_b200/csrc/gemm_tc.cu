@@ -286,7 +286,23 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int t = t0 + acc * BM + r;
                 const bool valid = t < a.T;
                 const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-                if constexpr (EPI == EPI_RESID || EPI == EPI_STORE) {
+                if constexpr (EPI == EPI_ARGMAX) {
+                    // lm_head: this row's best (logit, feature) over the tile, one atomic per row
+                    unsigned long long best = 0ull;
+                    for (int c = 0; c < BN; c += 32) {
+                        float v[32];
+                        tc::tmem_ld32(tbase + c, v);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            const int n = n0 + c + e;
+                            if (n < a.N) {
+                                const unsigned long long k = argmax_key(v[e], n);
+                                best = k > best ? k : best;
+                            }
+                        }
+                    }
+                    if (valid && best) atomicMax(a.amax + t, best);
+                } else if constexpr (EPI == EPI_RESID || EPI == EPI_STORE) {
                     for (int c = 0; c < BN; c += 32) {
                         float v[32];
                         tc::tmem_ld32(tbase + c, v);
@@ -422,6 +438,7 @@ cudaError_t gemm_tc_prepare() {
     if ((e = prepare_epi<EPI_QKV>()) != cudaSuccess) return e;
     if ((e = prepare_epi<EPI_RESID>()) != cudaSuccess) return e;
     if ((e = prepare_epi<EPI_SWIGLU>()) != cudaSuccess) return e;
+    if ((e = prepare_epi<EPI_ARGMAX>()) != cudaSuccess) return e;
     return prepare_epi<EPI_STORE>();
 }
 
@@ -435,6 +452,7 @@ cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream
         case EPI_RESID: return launch_epi<EPI_RESID>(a, tmA, tmB0, tmB1, st);
         case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(a, tmA, tmB0, tmB1, st);
         case EPI_STORE: return launch_epi<EPI_STORE>(a, tmA, tmB0, tmB1, st);
+        case EPI_ARGMAX: return a.amax ? launch_epi<EPI_ARGMAX>(a, tmA, tmB0, tmB1, st) : cudaErrorInvalidValue;
         default: return cudaErrorInvalidValue;
     }
 }

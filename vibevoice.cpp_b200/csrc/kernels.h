@@ -59,6 +59,7 @@ struct GemmArgs {
     KvLayer kv;
     int nq = 0, nkv = 0, hd = 0;
     const float2* rope_cs = nullptr;   // [T][hd/2] (cos, sin)
+    unsigned long long* amax = nullptr;   // ARGMAX: [T] running (logit, index) keys
     int* err = nullptr;
 };
 // tmB0/tmB1 (optional): f16 weight maps [N][K], box 64 x 128 (SwiGLU: gate and

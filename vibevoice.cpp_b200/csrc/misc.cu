@@ -153,11 +153,13 @@ __global__ void k_advance_meta(RowMeta* meta, int n) {
 }
 
 __global__ void k_argmax_init(unsigned long long* keys, int n) {
-    if (threadIdx.x < n) keys[threadIdx.x] = 0ull;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) keys[i] = 0ull;
 }
 
 __global__ void k_argmax_final(const unsigned long long* keys, int n, int32_t* out) {
-    if (threadIdx.x < n) out[threadIdx.x] = argmax_key_index(keys[threadIdx.x]);
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = argmax_key_index(keys[i]);
 }
 
 int grid_for(int64_t n, int threads) {
@@ -248,13 +250,13 @@ cudaError_t advance_meta_launch(RowMeta* meta, int n, cudaStream_t st) {
 }
 
 cudaError_t argmax_init_launch(unsigned long long* keys, int n, cudaStream_t st) {
-    k_argmax_init<<<1, 32, 0, st>>>(keys, n);
+    k_argmax_init<<<(n + 127) / 128, 128, 0, st>>>(keys, n);
     note_launch();
     return cudaGetLastError();
 }
 
 cudaError_t argmax_final_launch(const unsigned long long* keys, int n, int32_t* out, cudaStream_t st) {
-    k_argmax_final<<<1, 32, 0, st>>>(keys, n, out);
+    k_argmax_final<<<(n + 127) / 128, 128, 0, st>>>(keys, n, out);
     note_launch();
     return cudaGetLastError();
 }
