@@ -27,6 +27,7 @@ using namespace vvq2;
 
 namespace {
 
+constexpr int PART_SLOTS = 1024;   // (row, split) attention partial slots (>= GEMV_MAX_M x 64 splits)
 constexpr int PREFILL_ROWS_DEFAULT = 4096;   // token rows per tensor-core chunk (VVQ2_PREFILL_ROWS overrides)
 
 // cuTensorMapEncodeTiled from the driver, fetched through the runtime (no -lcuda)
@@ -166,6 +167,8 @@ struct vvq2_ctx {
     __half *Xh = nullptr, *ATTh = nullptr, *Ah = nullptr;
     __half* Wh = nullptr;          // f16 copy of the weight matrix the current prefill GEMM uses
     size_t wh_elems = 0;
+    float* kpart = nullptr;        // split-K partials of the tensor-core GEMMs
+    size_t kpart_elems = 0;
     float2* rope_cs = nullptr;
     float *part = nullptr, *part_ml = nullptr;
     int* counters = nullptr;
@@ -548,8 +551,25 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
                 if (!make_w_map(&b1, up, g.w1.rows, g.w1.cols, 64)) return fail(VVQ2_ERR_CUDA, "weight tensor map");
             }
         }
+        // few output tiles (small N, few rows): split K over more CTAs, then an
+        // in-order reduction applies the epilogue
+        GemmArgs gg = g;
+        const int tiles = (g.N + 127) / 128 * ((g.T + 255) / 256);
+        if ((g.epi == EPI_QKV || g.epi == EPI_RESID) && tiles < 74) {
+            const int ks = std::min(g.K / 64 / 2, std::max(1, 148 / tiles));
+            if (ks > 1) {
+                const size_t need = (size_t)ks * g.T * g.N;
+                if (need > c->kpart_elems) {
+                    if (int rc = c->alloc(&c->kpart, need)) return rc;
+                    c->kpart_elems = need;
+                }
+                gg.kpart = c->kpart;
+                gg.k_splits = ks;
+            }
+        }
         CU(R.begin());
-        CU(gemm_tc_launch(g, map, st, tma_b ? &b0 : nullptr, tma_b && g.epi == EPI_SWIGLU ? &b1 : nullptr));
+        CU(gemm_tc_launch(gg, map, st, tma_b ? &b0 : nullptr, tma_b && g.epi == EPI_SWIGLU ? &b1 : nullptr));
+        if (gg.kpart) CU(splitk_epilogue_launch(gg, st));
         const double n = g.epi == EPI_SWIGLU ? 2.0 * g.N : (double)g.N;
         CU(R.end(3, 2.0 * g.T * n * g.K));
         return 0;
@@ -620,9 +640,12 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         ad.hd = hd;
         if (nt == 1) {
             // partials [row][split] share the decode scratch: rows x splits <= its capacity
-            int split = 0, nsplit = 0;
-            choose_split(c, M, max_lim, &split, &nsplit);
-            while (nsplit > 1 && M * nsplit > GEMV_MAX_M * c->max_splits_cap) {
+            // ~4 CTAs per SM over (row, KV head, split), whole pages per split
+            const int want = std::max(1, (4 * 148 + M * nkv - 1) / (M * nkv));
+            int split = (max_lim + want - 1) / want;
+            split = (std::max(split, KV_PAGE) + KV_PAGE - 1) / KV_PAGE * KV_PAGE;
+            int nsplit = (max_lim + split - 1) / split;
+            while (nsplit > 1 && (M * nsplit > PART_SLOTS || nsplit > c->max_splits_cap)) {
                 split += KV_PAGE;
                 nsplit = (max_lim + split - 1) / split;
             }
@@ -1020,8 +1043,9 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     rc = rc ? rc : c->alloc(&c->ATT, (size_t)M * qw);
     rc = rc ? rc : c->alloc(&c->FA, (size_t)M * F);
     rc = rc ? rc : c->alloc(&c->QKVr, (size_t)M * (hp->n_heads + 2 * hp->n_kv_heads) * hp->head_dim);
-    rc = rc ? rc : c->alloc(&c->part, (size_t)M * c->max_splits_cap * qw);
-    rc = rc ? rc : c->alloc(&c->part_ml, (size_t)M * c->max_splits_cap * hp->n_heads * 2);
+    // attention partials: decode rows x splits, or batched-decode rows x splits (<= PART_SLOTS)
+    rc = rc ? rc : c->alloc(&c->part, (size_t)PART_SLOTS * qw);
+    rc = rc ? rc : c->alloc(&c->part_ml, (size_t)PART_SLOTS * hp->n_heads * 2);
     rc = rc ? rc : c->alloc(&c->counters, (size_t)P * hp->n_kv_heads);   // batched decode: one per (row, KV head)
     rc = rc ? rc : c->alloc(&c->meta, (size_t)P);
     rc = rc ? rc : c->alloc(&c->amax, (size_t)P);   // batched decode: one key / token per row

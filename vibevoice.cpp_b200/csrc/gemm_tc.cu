@@ -24,6 +24,8 @@
 // Pipeline: 4 stages of {A0, A1, B} 16 KB tiles (BK = 64), mbarriers full/empty.
 // Every wait is bounded; a timeout sets args.err and unwinds without leaving
 // TMEM allocated.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
@@ -184,7 +186,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, t0 = blockIdx.y * (2 * BM);
     const bool two = t0 + BM < a.T;
-    const int nk = a.K / BK;
+    // split-K: CTA z of gridDim.z takes k-blocks [kb0, kb0 + nk) and writes a
+    // raw f32 partial (a.kpart); splitk_epilogue_launch sums them in order
+    const int nk_all = a.K / BK;
+    const int kb0 = (int)((long long)nk_all * blockIdx.z / gridDim.z);
+    const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -211,20 +217,20 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (warp == 0 && lane == 0) {
         // ---- TMA producer: activation tiles A0 (rows t0..) and A1 (rows t0+128..)
-        for (int kb = 0; kb < nk; ++kb) {
-            const int s = kb % STAGES;
-            if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); break; }
+        for (int i = 0; i < nk; ++i) {
+            const int s = i % STAGES, kx = (kb0 + i) * BK;
+            if (i >= STAGES && !tc::mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) { fail(); break; }
             if (*(volatile int*)&abort_flag) break;
             uint8_t* st = smem + s * STAGE_BYTES;
             tc::mbar_arrive_expect_tx(&full[s], ((two ? 2 : 1) + (TMAB ? 1 : 0)) * TILE_BYTES);
-            tc::tma_load_2d(st, &tmA, kb * BK, t0, &full[s]);
-            if (two) tc::tma_load_2d(st + TILE_BYTES, &tmA, kb * BK, t0 + BM, &full[s]);
+            tc::tma_load_2d(st, &tmA, kx, t0, &full[s]);
+            if (two) tc::tma_load_2d(st + TILE_BYTES, &tmA, kx, t0 + BM, &full[s]);
             if constexpr (TMAB) {
                 if constexpr (EPI == EPI_SWIGLU) {   // 64 gate rows, then the same 64 up rows
-                    tc::tma_load_2d(st + 2 * TILE_BYTES, &tmB0, kb * BK, blockIdx.x * 64, &full[s]);
-                    tc::tma_load_2d(st + 2 * TILE_BYTES + 64 * 128, &tmB1, kb * BK, blockIdx.x * 64, &full[s]);
+                    tc::tma_load_2d(st + 2 * TILE_BYTES, &tmB0, kx, blockIdx.x * 64, &full[s]);
+                    tc::tma_load_2d(st + 2 * TILE_BYTES + 64 * 128, &tmB1, kx, blockIdx.x * 64, &full[s]);
                 } else {
-                    tc::tma_load_2d(st + 2 * TILE_BYTES, &tmB0, kb * BK, n0, &full[s]);
+                    tc::tma_load_2d(st + 2 * TILE_BYTES, &tmB0, kx, n0, &full[s]);
                 }
             }
         }
@@ -232,7 +238,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---- MMA issuer
         constexpr uint32_t idesc = tc::idesc_f16(BM, BN);
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = 0; kb < nk; ++kb) {   // local k-block index
             const int s = kb % STAGES;
             if (!tc::mbar_wait(&full[s], (kb / STAGES) & 1)) { fail(); ok = false; break; }
             if (*(volatile int*)&abort_flag) { ok = false; break; }
@@ -262,12 +268,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             W = &a.w0;
             wrow = n0 + p;
         }
-        for (int kb = 0; !TMAB && kb < nk; ++kb) {
+        for (int kb = 0; !TMAB && kb < nk; ++kb) {   // local k-block index
             const int s = kb % STAGES;
             if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); break; }
             if (*(volatile int*)&abort_flag) break;
             uint8_t* bt = smem + s * STAGE_BYTES + 2 * TILE_BYTES;
-            produce_row<WT>(*W, wrow, kb * BK, bt, p);
+            produce_row<WT>(*W, wrow, (kb0 + kb) * BK, bt, p);
             tc::fence_proxy_async_smem();
             tc::mbar_arrive(&full[s]);
         }
@@ -286,7 +292,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int t = t0 + acc * BM + r;
                 const bool valid = t < a.T;
                 const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-                if constexpr (EPI == EPI_ARGMAX) {
+                if (a.kpart && EPI != EPI_ARGMAX && EPI != EPI_SWIGLU) {
+                    // split-K partial [z][T][N], summed by splitk_epilogue_launch
+                    for (int c = 0; c < BN; c += 32) {
+                        float v[32];
+                        tc::tmem_ld32(tbase + c, v);
+                        if (!valid) continue;
+                        float* dst = a.kpart + ((size_t)blockIdx.z * a.T + t) * a.N + n0 + c;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (n0 + c + e < a.N) dst[e] = v[e];
+                    }
+                } else if constexpr (EPI == EPI_ARGMAX) {
                     // lm_head: this row's best (logit, feature) over the tile, one atomic per row
                     unsigned long long best = 0ull;
                     for (int c = 0; c < BN; c += 32) {
@@ -402,7 +419,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 template <int EPI>
 cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, const CUtensorMap* b0, const CUtensorMap* b1,
                        cudaStream_t st) {
-    dim3 grid((EPI == EPI_SWIGLU ? (a.N + 63) / 64 : (a.N + BN - 1) / BN), (a.T + 2 * BM - 1) / (2 * BM));
+    dim3 grid((EPI == EPI_SWIGLU ? (a.N + 63) / 64 : (a.N + BN - 1) / BN), (a.T + 2 * BM - 1) / (2 * BM),
+              a.kpart ? a.k_splits : 1);
     if (b0) {
         k_gemm_tc<W_F16, EPI, true><<<grid, THREADS, SMEM_BYTES, st>>>(tm, *b0, b1 ? *b1 : *b0, a);
     } else {
@@ -431,7 +449,67 @@ cudaError_t prepare_epi() {
     return cudaSuccess;
 }
 
+// Sum the split-K partials in split order and apply the epilogue: one thread
+// per (row, column) for RESID / STORE, per (row, rotation pair) for QKV.
+__global__ void k_splitk_epilogue(const GemmArgs a) {
+    const int64_t per_row = a.epi == EPI_QKV ? a.N / 2 : a.N;
+    const int64_t total = (int64_t)a.T * per_row;
+    const int ks = a.k_splits;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / per_row);
+        auto sum = [&](int n) {
+            float v = 0.f;
+            for (int z = 0; z < ks; ++z) v += a.kpart[((size_t)z * a.T + t) * a.N + n];
+            return v;
+        };
+        if (a.epi == EPI_QKV) {
+            const int hd = a.hd, half = hd / 2;
+            const int pr = (int)(i % per_row);
+            const int h = pr / half, ii = pr % half, f0 = h * hd;
+            float v0 = sum(f0 + ii), v1 = sum(f0 + ii + half);
+            if (a.bias) {
+                v0 = __fadd_rn(v0, a.bias[f0 + ii]);
+                v1 = __fadd_rn(v1, a.bias[f0 + ii + half]);
+            }
+            if (h < a.nq + a.nkv) {
+                const float2 cs = a.rope_cs[(size_t)t * half + ii];
+                const float y0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+                const float y1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+                v0 = y0;
+                v1 = y1;
+            }
+            if (h < a.nq) {
+                float* q = a.y + (size_t)t * a.y_stride + f0;
+                q[ii] = v0;
+                q[ii + half] = v1;
+            } else {
+                const RowMeta rm = a.meta[t];
+                const bool is_k = h < a.nq + a.nkv;
+                const int kvh = is_k ? h - a.nq : h - a.nq - a.nkv;
+                __half* dst = (is_k ? a.kv.k : a.kv.v) + kv_offset(a.kv, rm.seq, rm.cidx, kvh);
+                dst[ii] = __float2half_rn(v0);
+                dst[ii + half] = __float2half_rn(v1);
+            }
+        } else {
+            const int n = (int)(i % per_row);
+            float v = sum(n);
+            if (a.bias) v = __fadd_rn(v, a.bias[n]);
+            float* dst = a.y + (size_t)t * a.y_stride + n;
+            *dst = a.epi == EPI_RESID ? __fadd_rn(*dst, v) : v;
+        }
+    }
+}
+
 }  // namespace
+
+cudaError_t splitk_epilogue_launch(const GemmArgs& a, cudaStream_t st) {
+    if (!a.kpart || a.k_splits < 1) return cudaErrorInvalidValue;
+    const int64_t total = (int64_t)a.T * (a.epi == EPI_QKV ? a.N / 2 : a.N);
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 8);
+    k_splitk_epilogue<<<(unsigned)blocks, 256, 0, st>>>(a);
+    note_launch();
+    return cudaGetLastError();
+}
 
 cudaError_t gemm_tc_prepare() {
     cudaError_t e;
@@ -447,6 +525,8 @@ cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream
     if (a.K % BK || a.T <= 0 || a.N <= 0) return cudaErrorInvalidValue;
     if (a.epi == EPI_QKV && (BN % a.hd || (a.hd != 32 && a.hd != 64 && a.hd != 128))) return cudaErrorInvalidValue;
     if (a.epi == EPI_SWIGLU && tmB0 && !tmB1) return cudaErrorInvalidValue;
+    if (a.kpart && (a.k_splits < 1 || a.k_splits > a.K / BK || a.epi == EPI_SWIGLU || a.epi == EPI_ARGMAX))
+        return cudaErrorInvalidValue;
     switch (a.epi) {
         case EPI_QKV: return launch_epi<EPI_QKV>(a, tmA, tmB0, tmB1, st);
         case EPI_RESID: return launch_epi<EPI_RESID>(a, tmA, tmB0, tmB1, st);

@@ -60,6 +60,8 @@ struct GemmArgs {
     int nq = 0, nkv = 0, hd = 0;
     const float2* rope_cs = nullptr;   // [T][hd/2] (cos, sin)
     unsigned long long* amax = nullptr;   // ARGMAX: [T] running (logit, index) keys
+    float* kpart = nullptr;        // split-K: [k_splits][T][N] f32 partials (then splitk_epilogue_launch)
+    int k_splits = 1;
     int* err = nullptr;
 };
 // tmB0/tmB1 (optional): f16 weight maps [N][K], box 64 x 128 (SwiGLU: gate and
@@ -68,6 +70,8 @@ struct GemmArgs {
 cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st,
                            const CUtensorMap* tmB0 = nullptr, const CUtensorMap* tmB1 = nullptr);
 cudaError_t gemm_tc_prepare();
+// sum split-K partials in order and apply a.epi (QKV / RESID / STORE)
+cudaError_t splitk_epilogue_launch(const GemmArgs& a, cudaStream_t st);
 
 // ------------------------------------------------------ persistent decode step
 struct MegaLayer {
