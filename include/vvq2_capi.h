@@ -236,6 +236,25 @@ int  vvq2_attention_decode_noalloc(const float* q, const void* k_pages, const vo
 int  vvq2_profile(vvq2_ctx* ctx, int enable);
 int  vvq2_profile_read(vvq2_ctx* ctx, int kind, double* ms, double* bytes, int64_t* launches);
 
+/* ---- multi-GPU partition of the attention (config 5: long-context ASR) ----
+ * No reference counterpart (the reference runs one process on one device).
+ * One context per GPU and process.  `world` = head_groups x seq_parts ranks;
+ * rank r holds KV-head group r / seq_parts (the QKV rows and attention of its
+ * q heads) and sequence part r % seq_parts of every sequence's keys (part 1
+ * starts at a page-aligned split fixed by the sequence's first write: half
+ * of it).  Each rank computes normalized attention output and its
+ * log-sum-exp over its keys; the two parts of a head group merge (O, LSE)
+ * through an NCCL all-gather, head groups all-gather the output rows, and
+ * O-proj, FFN, final norm and lm_head run replicated, so every rank returns
+ * the same hidden states and tokens.  Call after vvq2_init and before
+ * vvq2_set_layer / vvq2_kv_init, on all ranks at once (NCCL init is
+ * collective); every rank must then make the same calls with the same
+ * inputs.  `nccl_id`: VVQ2_NCCL_ID_BYTES from vvq2_nccl_unique_id on one
+ * rank, shared with the others by the host. */
+#define VVQ2_NCCL_ID_BYTES 128
+int  vvq2_nccl_unique_id(void* out);
+int  vvq2_partition(vvq2_ctx* ctx, int rank, int world, int seq_parts, const void* nccl_id);
+
 /* Phase timeline of the persistent decode-step kernel (no reference
  * counterpart).  With VVQ2_MEGA_TRACE=1 in the environment when a decode
  * graph is built, every CTA stamps %globaltimer (ns) at kernel start, at

@@ -48,6 +48,19 @@ __device__ bool item(const AttnDecodeArgs& a, int s, int g, int m, int tid, __ha
     const int G = a.nq / a.nkv;
     const RowMeta rm = a.meta[m];
     const int lim = min(rm.pos + 1, rm.kvlen);
+    if (lim <= 0) {
+        // no keys for this row here (another rank holds its part of the
+        // sequence): zeros and LSE -inf, written once (split 0)
+        if (s == 0) {
+            for (int t = tid; t < G * HD; t += THREADS) {
+                const size_t off = (size_t)m * a.nq * HD + (size_t)g * G * HD + t;
+                if (a.out_h) a.out_h[off] = __float2half_rn(0.f);
+                else a.out[off] = 0.f;
+            }
+            if (a.lse && tid < G) a.lse[(size_t)m * a.nq + g * G + tid] = -INFINITY;
+        }
+        return true;
+    }
     const int nsplit = (lim + a.split - 1) / a.split;
     if (s >= nsplit) return true;
     const int j0 = s * a.split, j1 = min(lim, j0 + a.split);
@@ -206,6 +219,7 @@ __device__ bool item(const AttnDecodeArgs& a, int s, int g, int m, int tid, __ha
     }
 
     if (nsplit == 1) {
+        if (a.lse && tid < G) a.lse[(size_t)m * a.nq + g * G + tid] = sh.run_max[tid] + logf(sh.run_sum[tid]);
 #pragma unroll
         for (int k = 0; k < HPER; ++k) {
             const int h = hs + k * HSUB;
@@ -264,7 +278,10 @@ __device__ bool item(const AttnDecodeArgs& a, int s, int g, int m, int tid, __ha
             den = fmaf(w, ml_s[2 * (h * nsplit + ss) + 1], den);
         }
         den = warp_sum(den);
-        if (lane == 0) sh.inv_den[h] = 1.0f / den;
+        if (lane == 0) {
+            sh.inv_den[h] = 1.0f / den;
+            if (a.lse) a.lse[(size_t)m * a.nq + g * G + h] = mx + logf(den);
+        }
     }
     sync();
     for (int t = tid; t < G * PAIRS; t += THREADS) {

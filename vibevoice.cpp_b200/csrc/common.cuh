@@ -34,8 +34,10 @@ struct DevW {
 // Per activation row (token of a sequence) metadata for the decode/prefill step.
 struct RowMeta {
     int seq;    // KV sequence id
-    int pos;    // absolute position (RoPE, causal limit: keys j <= pos)
-    int cidx;   // cache index the new K/V row is written to
+    int pos;    // absolute position (RoPE, causal limit: keys j <= pos).  A rank that
+                // holds a later part of a sequence's keys sees pos - part_start here
+                // (its cache indices start at the part) and gets RoPE from its own table
+    int cidx;   // cache index the new K/V row is written to (< 0: another rank stores it)
     int kvlen;  // keys present after the step's writes (past_len + n_tok)
 };
 

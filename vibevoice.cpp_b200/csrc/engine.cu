@@ -8,6 +8,7 @@
 // pool, positions and the causal mask are computed by the kernels, and a step
 // is a fixed sequence of launches on one stream.
 #include <cuda_runtime.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cctype>
@@ -146,6 +147,18 @@ struct Owned {
 struct vvq2_ctx {
     vvq2_hparams hp{};
     int device = 0;
+    // Multi-GPU partition of the attention (vvq2_partition): rank (g, s) holds
+    // KV-head group g (its q heads' QKV rows and attention) and part s of every
+    // sequence's keys; O-proj, FFN and lm_head are replicated.
+    struct Part {
+        int rank = 0, world = 1, seq_parts = 1, head_parts = 1, g = 0, s = 0;
+        int nq = 0, nkv = 0;                // heads held locally
+        ncclComm_t comm = nullptr, pair = nullptr, heads = nullptr;
+        bool on() const { return world > 1; }
+    } pt;
+    __half *ATTl = nullptr, *ATTg = nullptr;   // local / gathered attention output (partitioned)
+    float *LSEl = nullptr, *LSEg = nullptr;
+    RowMeta* meta_rope = nullptr;              // true positions for the RoPE table (partitioned)
     cudaStream_t stream = nullptr;
     float rope_ts = 0.f;
     struct Layer {
@@ -238,6 +251,9 @@ struct vvq2_kv {
     __half* v = nullptr;
     int* block_table = nullptr;
     std::vector<int> past;
+    // partitioned contexts, 2 sequence parts: first position of part 1 per
+    // sequence (-1: not yet fixed; set by the sequence's first write)
+    std::vector<int> split;
 
     KvLayer layer(int li) const {
         KvLayer L;
@@ -245,7 +261,7 @@ struct vvq2_kv {
         L.v = v + (size_t)li * layer_elems;
         L.block_table = block_table;
         L.max_pages = max_pages;
-        L.n_kv = ctx->hp.n_kv_heads;
+        L.n_kv = ctx->pt.nkv;
         L.hd = ctx->hp.head_dim;
         return L;
     }
@@ -574,9 +590,12 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         CU(R.end(3, 2.0 * g.T * n * g.K));
         return 0;
     };
-    const int H = hp.hidden_size, nq = hp.n_heads, nkv = hp.n_kv_heads, hd = hp.head_dim;
-    const int F = hp.intermediate_size, qw = nq * hd;
-    CU(rope_table_launch(c->meta, M, hd, c->rope_ts, c->rope_cs, st));
+    const int H = hp.hidden_size, hd = hp.head_dim;
+    const int nq = c->pt.nq, nkv = c->pt.nkv;          // heads this rank holds (all, unpartitioned)
+    const int F = hp.intermediate_size, qw = hp.n_heads * hd, qw_l = nq * hd;
+    const bool parted = c->pt.on();
+    // RoPE from true positions (a later sequence part shifts meta.pos for its keys)
+    CU(rope_table_launch(parted ? c->meta_rope : c->meta, M, hd, c->rope_ts, c->rope_cs, st));
     CUtensorMap mapX, mapA, mapF;
     if (!make_act_map(&mapX, c->Xh, M, H) || !make_act_map(&mapA, c->ATTh, M, qw) || !make_act_map(&mapF, c->Ah, M, F))
         return fail(VVQ2_ERR_NOT_IMPLEMENTED, "activation tensor map (dims %d/%d/%d must be multiples of 64)", H, qw, F);
@@ -601,8 +620,10 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         q.epi = EPI_QKV;
         q.bias = L.qkv_bias;
         q.y = c->Q;
-        q.y_stride = qw;
+        q.y_stride = qw_l;
         if (int rc = gemm(q, mapX)) return rc;
+        __half* att_out = parted ? c->ATTl : c->ATTh;        // this rank's heads
+        float* att_lse = c->pt.seq_parts > 1 ? c->LSEl : nullptr;
         // 2. causal attention, f16 output: tcgen05 flash attention for prompt
         //    chunks (head_dim 64/128); rows of one token each (batched decode
         //    of many streams) and other head sizes use the split-K decode kernel
@@ -613,7 +634,8 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
                 return fail(VVQ2_ERR_CUDA, "kv tensor map");
             FaArgs fa;
             fa.q = c->Q;
-            fa.out = c->ATTh;
+            fa.out = att_out;
+            fa.lse = att_lse;
             fa.meta = c->meta;
             fa.block_table = kvl.block_table;
             fa.max_pages = kvl.max_pages;
@@ -631,7 +653,8 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         } else {
         AttnDecodeArgs ad;
         ad.q = c->Q;
-        ad.out_h = c->ATTh;
+        ad.out_h = att_out;
+        ad.lse = att_lse;
         ad.meta = c->meta;
         ad.kv = kvl;
         ad.M = M;
@@ -662,7 +685,26 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         ad.err = c->err;
         CU(attn_decode_launch(ad, st));
         }
-        // 3. O-proj + residual
+        if (parted) {
+            // the two sequence parts of this head group: (O, LSE) all-gather, merge
+            if (c->pt.seq_parts > 1) {
+                if (ncclGroupStart() != ncclSuccess ||
+                    ncclAllGather(c->ATTl, c->ATTg, (size_t)M * qw_l, ncclHalf, c->pt.pair, st) != ncclSuccess ||
+                    ncclAllGather(c->LSEl, c->LSEg, (size_t)M * nq, ncclFloat, c->pt.pair, st) != ncclSuccess ||
+                    ncclGroupEnd() != ncclSuccess)
+                    return fail(VVQ2_ERR_CUDA, "NCCL all-gather of (O, LSE) failed");
+                CU(lse_merge_launch(c->ATTg, c->LSEg, M, nq, hd, c->ATTl, st));
+            }
+            // head groups: all-gather the output rows, then [group][row][w] -> [row][all heads]
+            if (c->pt.head_parts > 1) {
+                if (ncclAllGather(c->ATTl, c->ATTg, (size_t)M * qw_l, ncclHalf, c->pt.heads, st) != ncclSuccess)
+                    return fail(VVQ2_ERR_CUDA, "NCCL all-gather of attention rows failed");
+                CU(gather_rows_launch(c->ATTg, M, c->pt.head_parts, qw_l, c->ATTh, st));
+            } else {
+                CU(cudaMemcpyAsync(c->ATTh, c->ATTl, sizeof(__half) * M * qw, cudaMemcpyDeviceToDevice, st));
+            }
+        }
+        // 3. O-proj + residual (replicated on partitioned ranks)
         GemmArgs o = g;
         o.w0 = L.o;
         o.N = H;
@@ -802,6 +844,35 @@ void mega_split(const vvq2_ctx* c, int M, int max_lim, int* split, int* nsplit) 
     *nsplit = (max_lim + s - 1) / s;
 }
 
+// A token row as this rank sees it.  `rope` gets the true position (RoPE
+// table); the returned row has the cache index and key limits of the rank's
+// sequence part: part 0 holds positions [0, split), part 1 [split, ...) at
+// cache index pos - split (pos is shifted the same way so the kernels'
+// causal limit min(pos + 1, kvlen) stays right); cidx < 0 when the other
+// part stores the row.
+RowMeta local_row(const vvq2_ctx* c, const vvq2_kv* kv, int seq, int pos, int cidx, int kvlen, RowMeta* rope) {
+    RowMeta r{seq, pos, cidx, kvlen};
+    if (rope) *rope = r;
+    if (c->pt.seq_parts < 2) return r;
+    const int S0 = kv->split[seq];
+    if (c->pt.s == 0) {
+        r.cidx = cidx < S0 ? cidx : -1;
+        r.kvlen = std::min(kvlen, S0);
+    } else {
+        r.pos = pos - S0;
+        r.cidx = cidx >= S0 ? cidx - S0 : -1;
+        r.kvlen = std::max(0, kvlen - S0);
+    }
+    return r;
+}
+
+// Fix a sequence's part split at its first write of n positions (half of it,
+// page aligned); later writes keep it.
+void fix_split(const vvq2_ctx* c, vvq2_kv* kv, int seq, int n) {
+    if (c->pt.seq_parts > 1 && kv->split[seq] < 0)
+        kv->split[seq] = std::max(KV_PAGE, ((n + 1) / 2 + KV_PAGE - 1) / KV_PAGE * KV_PAGE);
+}
+
 // Greedy decode step for more rows than the GEMV paths take (many streams at
 // once): embedding, the stack on the tensor-core path (split-K decode
 // attention over each row's ragged KV length), final RMSNorm, and the lm_head
@@ -813,13 +884,17 @@ int decode_step_batched(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, c
     if (M > c->prefill_rows) return fail(VVQ2_ERR_INVALID_ARG, "%d rows > %d per decode step", M, c->prefill_rows);
     int max_lim = 1;
     double attn_flops = 0.0;
+    std::vector<RowMeta> rope(c->pt.on() ? M : 0);
     for (int s = 0; s < M; ++s) {
         const int past = kv->past[seqs[s]];
-        c->meta_host[s] = RowMeta{seqs[s], past, past, past + 1};
-        max_lim = std::max(max_lim, past + 1);
-        attn_flops += 4.0 * hp.n_heads * hp.head_dim * (past + 1);
+        fix_split(c, kv, seqs[s], 1);
+        const RowMeta r = local_row(c, kv, seqs[s], past, past, past + 1, c->pt.on() ? &rope[s] : nullptr);
+        c->meta_host[s] = r;
+        max_lim = std::max(max_lim, std::min(r.pos + 1, r.kvlen));
+        attn_flops += 4.0 * c->pt.nq * hp.head_dim * std::max(0, std::min(r.pos + 1, r.kvlen));
     }
     CU(cudaMemcpyAsync(c->meta, c->meta_host, sizeof(RowMeta) * M, cudaMemcpyHostToDevice, st));
+    if (c->pt.on()) CU(copy_on(c->meta_rope, rope.data(), sizeof(RowMeta) * M, st));
     c->meta_kv = nullptr;   // c->meta no longer describes a graph-captured decode step
     CU(cudaMemcpyAsync(c->tok, tokens_in, sizeof(int32_t) * M, cudaMemcpyDefault, st));
     CU(embed_launch(c->tok_embd, c->tok, M, c->X, st));
@@ -1017,6 +1092,8 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     c->hp = *hp;
     c->device = device;
     c->layers.resize(hp->n_layers);
+    c->pt.nq = hp->n_heads;
+    c->pt.nkv = hp->n_kv_heads;
     c->rope_ts = powf(hp->rope_theta, -2.0f / (float)hp->head_dim);
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
         delete c;
@@ -1092,8 +1169,61 @@ void vvq2_free(vvq2_ctx* c) {
         kv->ctx = nullptr;
     }
     if (c->meta_host) cudaFreeHost(c->meta_host);
+    for (ncclComm_t m : {c->pt.heads, c->pt.pair, c->pt.comm})
+        if (m) ncclCommDestroy(m);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
+}
+
+int vvq2_nccl_unique_id(void* out) {
+    if (!out) return fail(VVQ2_ERR_INVALID_ARG, "null id buffer");
+    static_assert(sizeof(ncclUniqueId) == VVQ2_NCCL_ID_BYTES, "NCCL unique id size");
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess) return fail(VVQ2_ERR_CUDA, "ncclGetUniqueId failed");
+    memcpy(out, &id, sizeof id);
+    return 0;
+}
+
+int vvq2_partition(vvq2_ctx* c, int rank, int world, int seq_parts, const void* nccl_id) {
+    if (int rc = check_ctx(c)) return rc;
+    const vvq2_hparams& hp = c->hp;
+    if (world < 1 || rank < 0 || rank >= world || (seq_parts != 1 && seq_parts != 2) || world % seq_parts)
+        return fail(VVQ2_ERR_INVALID_ARG, "bad partition rank %d / world %d / seq_parts %d", rank, world, seq_parts);
+    const int hp_parts = world / seq_parts;
+    if (hp.n_kv_heads % hp_parts) return fail(VVQ2_ERR_INVALID_ARG, "%d KV heads over %d head groups", hp.n_kv_heads, hp_parts);
+    for (const auto& L : c->layers)
+        if (L.set) return fail(VVQ2_ERR_INVALID_ARG, "vvq2_partition must precede vvq2_set_layer");
+    if (!c->kvs.empty()) return fail(VVQ2_ERR_INVALID_ARG, "vvq2_partition must precede vvq2_kv_init");
+    if (c->pt.on()) return fail(VVQ2_ERR_INVALID_ARG, "context already partitioned");
+    if (world == 1) return 0;
+    if (!nccl_id) return fail(VVQ2_ERR_INVALID_ARG, "null NCCL id");
+    vvq2_ctx::Part P;
+    P.rank = rank;
+    P.world = world;
+    P.seq_parts = seq_parts;
+    P.head_parts = hp_parts;
+    P.g = rank / seq_parts;
+    P.s = rank % seq_parts;
+    P.nq = hp.n_heads / hp_parts;
+    P.nkv = hp.n_kv_heads / hp_parts;
+    CU(cudaSetDevice(c->device));
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, sizeof id);
+    if (ncclCommInitRank(&P.comm, world, id, rank) != ncclSuccess) return fail(VVQ2_ERR_CUDA, "ncclCommInitRank failed");
+    // the two ranks of a head group (sequence parts), and the ranks of one part across head groups
+    if (seq_parts > 1 && ncclCommSplit(P.comm, P.g, P.s, &P.pair, nullptr) != ncclSuccess)
+        return fail(VVQ2_ERR_CUDA, "ncclCommSplit (pair) failed");
+    if (hp_parts > 1 && ncclCommSplit(P.comm, P.s, P.g, &P.heads, nullptr) != ncclSuccess)
+        return fail(VVQ2_ERR_CUDA, "ncclCommSplit (heads) failed");
+    c->pt = P;
+    const size_t rows = (size_t)c->prefill_rows;
+    const int qw = hp.n_heads * hp.head_dim;
+    if (int rc = c->alloc(&c->ATTl, rows * qw)) return rc;
+    if (int rc = c->alloc(&c->ATTg, 2 * rows * qw)) return rc;
+    if (int rc = c->alloc(&c->LSEl, rows * hp.n_heads)) return rc;
+    if (int rc = c->alloc(&c->LSEg, 2 * rows * hp.n_heads)) return rc;
+    if (int rc = c->alloc(&c->meta_rope, rows)) return rc;
+    return 0;
 }
 
 int vvq2_set_layer(vvq2_ctx* c, int li, const vvq2_layer_weights* w) {
@@ -1115,13 +1245,18 @@ int vvq2_set_layer(vvq2_ctx* c, int li, const vvq2_layer_weights* w) {
             if (!tt->data || tt->ne0 != H) return fail(VVQ2_ERR_INVALID_ARG, "attn q/k/v shape");
         if (w->attn_q.ne1 != qw || w->attn_k.ne1 != kvw || w->attn_v.ne1 != kvw)
             return fail(VVQ2_ERR_INVALID_ARG, "attn q/k/v rows");
-        std::vector<uint8_t> cat(rb * (qw + 2 * kvw));
-        memcpy(cat.data(), w->attn_q.data, rb * qw);
-        memcpy(cat.data() + rb * qw, w->attn_k.data, rb * kvw);
-        memcpy(cat.data() + rb * (qw + kvw), w->attn_v.data, rb * kvw);
-        vvq2_tensor tc{cat.data(), t, H, qw + 2 * kvw};
-        if (int rc = upload_tensor(c, tc, &L.qkv, H, qw + 2 * kvw, "attn_qkv")) return rc;
-        std::vector<float> bias(qw + 2 * kvw, 0.0f);
+        // a partitioned rank keeps the rows of its own heads: q heads
+        // [g*nq_l, (g+1)*nq_l), k and v heads [g*nkv_l, (g+1)*nkv_l)
+        const int hd = hp.head_dim;
+        const int qw_l = c->pt.nq * hd, kvw_l = c->pt.nkv * hd;
+        const size_t q0 = (size_t)c->pt.g * qw_l, k0 = (size_t)c->pt.g * kvw_l;
+        std::vector<uint8_t> cat(rb * (qw_l + 2 * kvw_l));
+        memcpy(cat.data(), static_cast<const uint8_t*>(w->attn_q.data) + rb * q0, rb * qw_l);
+        memcpy(cat.data() + rb * qw_l, static_cast<const uint8_t*>(w->attn_k.data) + rb * k0, rb * kvw_l);
+        memcpy(cat.data() + rb * (qw_l + kvw_l), static_cast<const uint8_t*>(w->attn_v.data) + rb * k0, rb * kvw_l);
+        vvq2_tensor tc{cat.data(), t, H, qw_l + 2 * kvw_l};
+        if (int rc = upload_tensor(c, tc, &L.qkv, H, qw_l + 2 * kvw_l, "attn_qkv")) return rc;
+        std::vector<float> bias_full(qw + 2 * kvw, 0.0f);
         bool any = false;
         const vvq2_tensor* bs[3] = {&w->attn_q_bias, &w->attn_k_bias, &w->attn_v_bias};
         const int off[3] = {0, qw, qw + kvw}, n[3] = {qw, kvw, kvw};
@@ -1129,11 +1264,16 @@ int vvq2_set_layer(vvq2_ctx* c, int li, const vvq2_layer_weights* w) {
             if (!bs[i]->data) continue;
             any = true;
             if (bs[i]->ne0 * std::max<int64_t>(bs[i]->ne1, 1) != n[i]) return fail(VVQ2_ERR_INVALID_ARG, "bias size");
-            if (bs[i]->type == W_F32) memcpy(&bias[off[i]], bs[i]->data, (size_t)n[i] * 4);
+            if (bs[i]->type == W_F32) memcpy(&bias_full[off[i]], bs[i]->data, (size_t)n[i] * 4);
             else if (bs[i]->type == W_F16)
-                for (int j = 0; j < n[i]; ++j) bias[off[i] + j] = __half2float(static_cast<const __half*>(bs[i]->data)[j]);
+                for (int j = 0; j < n[i]; ++j) bias_full[off[i] + j] = __half2float(static_cast<const __half*>(bs[i]->data)[j]);
             else return fail(VVQ2_ERR_NOT_IMPLEMENTED, "bias type");
         }
+        std::vector<float> bias(qw_l + 2 * kvw_l);
+        std::copy(bias_full.begin() + q0, bias_full.begin() + q0 + qw_l, bias.begin());
+        std::copy(bias_full.begin() + qw + k0, bias_full.begin() + qw + k0 + kvw_l, bias.begin() + qw_l);
+        std::copy(bias_full.begin() + qw + kvw + k0, bias_full.begin() + qw + kvw + k0 + kvw_l,
+                  bias.begin() + qw_l + kvw_l);
         if (any) {
             if (int rc = c->alloc(&L.qkv_bias, bias.size())) return rc;
             CU(copy_on(L.qkv_bias, bias.data(), bias.size() * 4, c->stream));
@@ -1178,7 +1318,7 @@ int vvq2_kv_init(vvq2_ctx* c, int n_seqs, int max_seq, vvq2_kv** out) {
     kv->max_seq = max_seq;
     kv->max_pages = (max_seq + KV_PAGE - 1) / KV_PAGE;
     const size_t pages = (size_t)n_seqs * kv->max_pages;
-    kv->layer_elems = pages * c->hp.n_kv_heads * KV_PAGE * c->hp.head_dim;
+    kv->layer_elems = pages * c->pt.nkv * KV_PAGE * c->hp.head_dim;   // this rank's KV heads
     const size_t bytes = kv->layer_elems * c->hp.n_layers * sizeof(__half);
     if (cudaMalloc(&kv->k, bytes) != cudaSuccess || cudaMalloc(&kv->v, bytes) != cudaSuccess ||
         cudaMalloc(&kv->block_table, pages * sizeof(int)) != cudaSuccess) {
@@ -1198,6 +1338,7 @@ int vvq2_kv_init(vvq2_ctx* c, int n_seqs, int max_seq, vvq2_kv** out) {
         return fail(VVQ2_ERR_CUDA, "kv init copy failed");
     }
     kv->past.assign(n_seqs, 0);
+    kv->split.assign(n_seqs, c->pt.seq_parts > 1 ? -1 : INT32_MAX);
     c->kvs.push_back(kv);
     *out = kv;
     return 0;
@@ -1247,7 +1388,33 @@ static int kv_xfer(vvq2_kv* kv, int seq, int layer, float* k, float* v, const fl
     if (seq < 0 || seq >= kv->n_seqs || layer < 0 || layer >= c->hp.n_layers || n_pos < 0 || n_pos > kv->max_seq)
         return fail(VVQ2_ERR_INVALID_ARG, "bad kv transfer");
     if (n_pos == 0) return 0;
-    const size_t n = (size_t)n_pos * c->hp.n_kv_heads * c->hp.head_dim;
+    std::vector<float> lk, lv;   // partitioned upload: this rank's heads and sequence part
+    if (c->pt.on()) {
+        if (!upload) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "kv read on a partitioned context");
+        fix_split(c, kv, seq, n_pos);
+        const int W = c->hp.n_kv_heads * c->hp.head_dim, wl = c->pt.nkv * c->hp.head_dim, c0 = c->pt.g * wl;
+        int p0 = 0, p1 = n_pos;
+        if (c->pt.seq_parts > 1) {
+            if (c->pt.s == 0) p1 = std::min(n_pos, kv->split[seq]);
+            else p0 = std::min(n_pos, kv->split[seq]);
+        }
+        std::vector<float> hk((size_t)n_pos * W), hv((size_t)n_pos * W);
+        if (is_device_ptr(kc) || is_device_ptr(vc)) CU(cudaDeviceSynchronize());
+        CU(copy_on(hk.data(), kc, hk.size() * 4, c->stream));
+        CU(copy_on(hv.data(), vc, hv.size() * 4, c->stream));
+        lk.resize((size_t)(p1 - p0) * wl);
+        lv.resize(lk.size());
+        for (int p = p0; p < p1; ++p)
+            for (int j = 0; j < wl; ++j) {
+                lk[(size_t)(p - p0) * wl + j] = hk[(size_t)p * W + c0 + j];
+                lv[(size_t)(p - p0) * wl + j] = hv[(size_t)p * W + c0 + j];
+            }
+        n_pos = p1 - p0;
+        kc = lk.data();
+        vc = lv.data();
+        if (n_pos == 0) return 0;
+    }
+    const size_t n = (size_t)n_pos * c->pt.nkv * c->hp.head_dim;
     float *dk = nullptr, *dv = nullptr;
     // device-resident k/v may still be being written on another stream
     if (upload && (is_device_ptr(kc) || is_device_ptr(vc))) CU(cudaDeviceSynchronize());
@@ -1313,7 +1480,7 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
     // the ordering tests/test_qwen2_resident.cpp checks).
     // Few rows: decode GEMV path.  Otherwise tensor-core chunks of up to
     // prefill_rows rows.
-    const bool tc_path = n_seqs * n_tok > c->max_rows;
+    const bool tc_path = n_seqs * n_tok > c->max_rows || c->pt.on();   // partitioned: NCCL on the tensor-core path
     if (n_seqs > c->prefill_rows)
         return fail(VVQ2_ERR_NOT_IMPLEMENTED, "more than %d sequences per call", c->prefill_rows);
     const int tok_per_chunk = std::max(1, (tc_path ? c->prefill_rows : c->max_rows) / n_seqs);
@@ -1321,27 +1488,30 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
         const int nt = std::min(tok_per_chunk, n_tok - t0);
         const int M = n_seqs * nt;
         int max_lim = 1;
-        for (int s = 0; s < n_seqs; ++s)
+        std::vector<RowMeta> rope(c->pt.on() ? M : 0);
+        for (int s = 0; s < n_seqs; ++s) {
+            fix_split(c, kv, seqs[s], kv->past[seqs[s]] + n_tok);
             for (int t = 0; t < nt; ++t) {
                 RowMeta& r = c->meta_host[s * nt + t];
-                r.seq = seqs[s];
-                r.pos = pos_start[s] + t0 + t;
-                r.cidx = kv->past[seqs[s]] + t0 + t;
-                r.kvlen = kv->past[seqs[s]] + t0 + nt;
+                r = local_row(c, kv, seqs[s], pos_start[s] + t0 + t, kv->past[seqs[s]] + t0 + t,
+                              kv->past[seqs[s]] + t0 + nt, c->pt.on() ? &rope[s * nt + t] : nullptr);
                 max_lim = std::max(max_lim, std::min(r.pos + 1, r.kvlen));
             }
+        }
         CU(cudaMemcpyAsync(c->meta, c->meta_host, sizeof(RowMeta) * M, cudaMemcpyHostToDevice, st));
+        if (c->pt.on()) CU(copy_on(c->meta_rope, rope.data(), sizeof(RowMeta) * M, st));
         for (int s = 0; s < n_seqs; ++s)
             CU(cudaMemcpyAsync(c->X + (size_t)s * nt * H, x + ((size_t)s * n_tok + t0) * H,
                                sizeof(float) * nt * H, x_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
         c->meta_kv = nullptr;   // c->meta no longer describes a decode step
         std::vector<vvq2_ctx::Rec> recs;
-        if (tc_path && M > c->max_rows) {
-            // causal attention flops of one layer: QK^T and PV, 2 flops per (head, dim, key)
+        if (tc_path && (M > c->max_rows || c->pt.on())) {
+            // causal attention flops of one layer (this rank's heads and keys):
+            // QK^T and PV, 2 flops per (head, dim, key)
             double attn_flops = 0.0;
             for (int r = 0; r < M; ++r)
-                attn_flops += 4.0 * c->hp.n_heads * c->hp.head_dim *
-                              std::min(c->meta_host[r].pos + 1, c->meta_host[r].kvlen);
+                attn_flops += 4.0 * c->pt.nq * c->hp.head_dim *
+                              std::max(0, std::min(c->meta_host[r].pos + 1, c->meta_host[r].kvlen));
             if (c->prof_on && c->events.size() < 2 * (5 * (size_t)n_layers + 2)) {
                 for (size_t i = c->events.size(); i < 2 * (5 * (size_t)n_layers + 2); ++i) {
                     cudaEvent_t e;
@@ -1459,7 +1629,8 @@ int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, cons
         if (kv->past[seqs[s]] + 1 > kv->max_seq) return fail(VVQ2_ERR_INVALID_ARG, "KV overflow");
     }
     cudaStream_t st = pick_stream(c, stream);
-    if (n_seqs > c->max_rows) return decode_step_batched(c, kv, seqs, n_seqs, tokens_in, tokens_out, st);
+    // partitioned contexts exchange attention through NCCL on the tensor-core path
+    if (n_seqs > c->max_rows || c->pt.on()) return decode_step_batched(c, kv, seqs, n_seqs, tokens_in, tokens_out, st);
     const int M = n_seqs;
     std::vector<int> sv(seqs, seqs + n_seqs);
     int max_lim = 1;

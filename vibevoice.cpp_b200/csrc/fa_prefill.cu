@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(FT, 1)
     const int row0 = s * a.nt + qt * BQ, nrows = min(BQ, a.nt - qt * BQ);
     const RowMeta last = a.meta[row0 + nrows - 1];
     const int klim = min(last.pos + 1, last.kvlen);    // keys any row of the tile may see
-    const int nkt = (klim + BKV - 1) / BKV;
+    const int nkt = klim > 0 ? (klim + BKV - 1) / BKV : 0;   // 0: no keys here (another rank's part)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NST; ++i) {
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(FT, 1)
         };
         if (ok) {
             tc::tc_fence_after();
-            ok = issue_s(0) && (nkt < 2 || issue_s(1));
+            ok = nkt == 0 || (issue_s(0) && (nkt < 2 || issue_s(1)));
         }
         for (int j = 0; ok && j < nkt; ++j) {
             const int vs = j % NST;
@@ -315,12 +315,20 @@ __global__ void __launch_bounds__(FT, 1)
             fail();
         } else {
             tc::tc_fence_after();
+            // a row without keys (l == 0) writes zeros and LSE -inf; its TMEM
+            // accumulator may never have been written
             const float inv = l > 0.f ? 1.0f / l : 0.f;
+            if (valid && a.lse)   // log-sum-exp of the scaled scores, natural log
+                a.lse[(size_t)grow * a.nq + h] = l > 0.f ? fmaf(m_ref, a.scale, logf(l)) : -INFINITY;
             __half* dst = a.out + (size_t)grow * a.nq * HD + (size_t)h * HD;
 #pragma unroll
             for (int cc = 0; cc < HD / 32; ++cc) {
                 float v[32];
                 tc::tmem_ld32(to + cc * 32, v);
+                if (l == 0.f) {
+#pragma unroll
+                    for (int d = 0; d < 32; ++d) v[d] = 0.f;
+                }
                 if (valid) {
 #pragma unroll
                     for (int d = 0; d < 32; d += 8)

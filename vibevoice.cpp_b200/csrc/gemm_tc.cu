@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                     float* q = a.y + (size_t)t * a.y_stride + h * hd;
                                     q[i] = v0;
                                     q[i + half] = v1;
-                                } else {
+                                } else if (rm.cidx >= 0) {   // cidx < 0: another rank stores this position
                                     const bool is_k = h < a.nq + a.nkv;
                                     const int kvh = is_k ? h - a.nq : h - a.nq - a.nkv;
                                     __half* dst = (is_k ? a.kv.k : a.kv.v) + kv_offset(a.kv, rm.seq, rm.cidx, kvh);
@@ -482,7 +482,7 @@ __global__ void k_splitk_epilogue(const GemmArgs a) {
                 float* q = a.y + (size_t)t * a.y_stride + f0;
                 q[ii] = v0;
                 q[ii + half] = v1;
-            } else {
+            } else if (a.meta[t].cidx >= 0) {   // cidx < 0: another rank stores this position
                 const RowMeta rm = a.meta[t];
                 const bool is_k = h < a.nq + a.nkv;
                 const int kvh = is_k ? h - a.nq : h - a.nq - a.nkv;

@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
                         float* q = a.y + (size_t)mm * a.y_stride + h * a.hd;
                         q[i2] = x0;
                         q[i2 + a.hd / 2] = x1;
-                    } else {
+                    } else if (rm.cidx >= 0) {   // cidx < 0: another rank stores this position
                         const bool is_k = h < a.n_q_heads + a.n_kv_heads;
                         const int kvh = is_k ? h - a.n_q_heads : h - a.n_q_heads - a.n_kv_heads;
                         __half* dst = (is_k ? a.kv.k : a.kv.v) + kv_offset(a.kv, rm.seq, rm.cidx, kvh);

@@ -134,6 +134,7 @@ struct AttnDecodeArgs {
     int* counters = nullptr;       // [M][nkv], zero between launches
     int* err = nullptr;            // set to nonzero if a bounded wait gave up
     __half* out_h = nullptr;       // if set, write f16 output here instead of `out`
+    float* lse = nullptr;          // optional [M][nq]: log-sum-exp of the scaled scores (-inf: no keys)
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st);
 cudaError_t attn_decode_prepare();
@@ -149,6 +150,7 @@ struct FaArgs {
     int n_seqs = 0, nt = 0;              // sequences in the chunk, rows per sequence
     int nq = 0, nkv = 0, hd = 0;
     float scale = 0.f;
+    float* lse = nullptr;                // optional [rows][nq]: log-sum-exp of the scaled scores
     int* err = nullptr;
 };
 cudaError_t fa_prefill_prepare();
@@ -159,6 +161,12 @@ cudaError_t fa_prefill_launch(const FaArgs& a, const CUtensorMap& mk, const CUte
 long long launch_count();
 // dequantize a repacked device weight matrix to f32 [rows][cols]
 cudaError_t dequant_rows_launch(const DevW& w, float* dst, cudaStream_t st);
+// log-sum-exp merge of two partial attention outputs over disjoint key sets:
+// o2 [2][rows][nh*hd] f16, l2 [2][rows][nh] -> out [rows][nh*hd] f16
+cudaError_t lse_merge_launch(const __half* o2, const float* l2, int64_t rows, int nh, int hd, __half* out,
+                             cudaStream_t st);
+// [parts][rows][w] -> [rows][parts*w]
+cudaError_t gather_rows_launch(const __half* in, int64_t rows, int parts, int w, __half* out, cudaStream_t st);
 // ... to f16 [rows][cols] (exact dequantized value, rounded once)
 cudaError_t dequant_f16_launch(const DevW& w, __half* dst, cudaStream_t st);
 cudaError_t rope_launch(const float* x, int n_tok, int n_heads, int hd, const int32_t* pos,

@@ -184,6 +184,49 @@ cudaError_t dequant_f16_launch(const DevW& w, __half* dst, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// Merge two attention results over disjoint key sets (log-sum-exp):
+// o = (e^(l0-l) o0 + e^(l1-l) o1) / (e^(l0-l) + e^(l1-l)), l = max(l0, l1).
+// o2: [2][rows][nh*hd] f16 (normalized parts), l2: [2][rows][nh] natural-log LSE.
+__global__ void k_lse_merge(const __half* o2, const float* l2, int64_t rows, int nh, int hd, __half* out) {
+    const int64_t n = rows * nh * hd;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t rh = i / hd;                        // row * nh + head
+        const float l0 = l2[rh], l1 = l2[rows * nh + rh];
+        const float mx = fmaxf(l0, l1);
+        float v = 0.f;
+        if (mx != -INFINITY) {
+            const float w0 = expf(l0 - mx), w1 = expf(l1 - mx);
+            v = (w0 * __half2float(o2[i]) + w1 * __half2float(o2[rows * nh * hd + i])) / (w0 + w1);
+        }
+        out[i] = __float2half_rn(v);
+    }
+}
+
+// [parts][rows][w] -> [rows][parts * w] (all-gathered per-rank head blocks into rows)
+__global__ void k_gather_rows(const __half* in, int64_t rows, int parts, int w, __half* out) {
+    const int64_t n = rows * parts * w;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / ((int64_t)parts * w);
+        const int c = (int)(i % ((int64_t)parts * w)), p = c / w, e = c % w;
+        out[i] = in[((int64_t)p * rows + r) * w + e];
+    }
+}
+
+cudaError_t lse_merge_launch(const __half* o2, const float* l2, int64_t rows, int nh, int hd, __half* out,
+                             cudaStream_t st) {
+    const int64_t n = rows * nh * hd;
+    k_lse_merge<<<grid_for(n, 256), 256, 0, st>>>(o2, l2, rows, nh, hd, out);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t gather_rows_launch(const __half* in, int64_t rows, int parts, int w, __half* out, cudaStream_t st) {
+    const int64_t n = rows * parts * w;
+    k_gather_rows<<<grid_for(n, 256), 256, 0, st>>>(in, rows, parts, w, out);
+    note_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t rope_launch(const float* x, int n_tok, int n_heads, int hd, const int32_t* pos, float ts,
                         float* y, cudaStream_t st) {
     const int64_t n = (int64_t)n_tok * n_heads * (hd / 2);

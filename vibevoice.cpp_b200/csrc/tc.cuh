@@ -52,7 +52,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 }
 
 // ---------------------------------------------------------------- TMA
-// 2-D tiled load, no multicast: box lands at `dst`, completion counted in bytes on `bar`.
+// 2-D tiled load into this CTA only: box lands at `dst`, completion counted in bytes on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

@@ -76,6 +76,8 @@ def lib() -> C.CDLL:
             "vvq2_attention_decode_noalloc": (I, [P, P, P, P, I, P, I, I, I, I, I, P, P]),
             "vvq2_profile_read": (I, [P, I, P, P, P]),
             "vvq2_mega_trace": (I, [P, P, C.c_int64, P, P]),
+            "vvq2_nccl_unique_id": (I, [P]),
+            "vvq2_partition": (I, [P, I, I, I, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -162,6 +164,13 @@ class Engine:
         ms, by, n = C.c_double(), C.c_double(), C.c_int64()
         _chk(lib().vvq2_profile_read(self.ctx, kind, C.byref(ms), C.byref(by), C.byref(n)))
         return ms.value, by.value, n.value
+
+    def partition(self, rank: int, world: int, seq_parts: int, nccl_id: bytes) -> None:
+        """Attention partition over `world` GPUs (one Engine per process and GPU):
+        rank r holds KV-head group r // seq_parts and sequence part r % seq_parts.
+        Call on every rank before set_layer / kv()."""
+        buf = C.create_string_buffer(bytes(nccl_id), NCCL_ID_BYTES)
+        _chk(lib().vvq2_partition(self.ctx, rank, world, seq_parts, C.cast(buf, C.c_void_p)))
 
     def mega_trace(self) -> np.ndarray:
         """[slots][grid] %globaltimer stamps of the last persistent decode step."""
@@ -255,6 +264,16 @@ class KV:
 
     def past_len(self, seq: int) -> int:
         return _chk(lib().vvq2_kv_past_len(self.kv, seq))
+
+
+NCCL_ID_BYTES = 128
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id (make it on one rank, share it with the others)."""
+    buf = C.create_string_buffer(NCCL_ID_BYTES)
+    _chk(lib().vvq2_nccl_unique_id(C.cast(buf, C.c_void_p)))
+    return buf.raw
 
 
 def dequantize(qtype: int, raw: np.ndarray, n: int) -> np.ndarray:
