@@ -161,6 +161,96 @@ def c3_measure(eng, hp, torch, dist, rank, world, sh, steps, warmup=2):
             "scaling": "strong", "parallelism": f"data parallel over {world} GPU(s), no collectives"}
 
 
+C5 = dict(hidden=3584, n_heads=28, n_kv_heads=4, head_dim=128, ffn=18944, n_layers=28, vocab=152064,
+          rope_theta=1.0e6, rms_eps=1.0e-6)
+
+
+def run_c5(args, rank, local, world):
+    """Config 5: the 7B-shaped Q8_0 ASR stack, causal prefill of
+    args.c5_tokens prompt embeddings, then greedy decode steps.  At N > 1 the
+    attention is partitioned (vvq2_partition): KV heads over 2/4 GPUs, KV heads
+    x sequence halves over 8, with NCCL (O, LSE) combines; each rank decodes
+    the same single stream.  Times are CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import synth
+    import vvq2
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+    hp = C5
+    eng = vvq2.Engine(hp, device=local)
+    seq_parts = 2 if world == 8 else 1
+    if world > 1:
+        ids = [vvq2.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        eng.partition(rank, world, seq_parts, ids[0])
+    rng = np.random.default_rng(SEED + 55)
+    for li in range(hp["n_layers"]):
+        eng.set_layer(li, synth.layer_q8_0_fast(rng, hp))
+    head = synth.q8_0_random_tensor(rng, hp["vocab"], hp["hidden"])
+    norm = synth.f32_tensor(1.0 + rng.standard_normal(hp["hidden"], dtype=np.float32) * 0.02)
+    eng.set_output(norm, head, head)
+    T, steps = args.c5_tokens, args.c5_steps
+    # warm-up on a separate cache (NCCL connections, lazily created scratch)
+    kvw = eng.kv(1, 512)
+    eng.forward(kvw, [0], np.zeros((1, 256, hp["hidden"]), np.float32), [0])
+    kvw.close()
+    kv = eng.kv(1, T + steps + 16)
+    g = torch.Generator(device="cuda").manual_seed(SEED + 5)
+    x = torch.randn((1, T, hp["hidden"]), generator=g, device="cuda", dtype=torch.float32)
+    y = torch.empty((1, hp["hidden"]), device="cuda", dtype=torch.float32)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sh = stream.cuda_stream
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    pre_ms = timed(lambda: eng.forward(kv, [0], x, [0], flags=vvq2.ADVANCE | vvq2.LAST_ONLY, y=y, stream=sh))
+    tok = torch.randint(0, hp["vocab"], (1,), dtype=torch.int32, device="cuda", generator=g)
+    for _ in range(2):
+        eng.decode_step(kv, [0], tok, tok, stream=sh)
+    dec_ms = timed(lambda: [eng.decode_step(kv, [0], tok, tok, stream=sh) for _ in range(steps)])
+    lin = 2.0 * T * hp["n_layers"] * hp["hidden"] * (
+        hp["n_heads"] * hp["head_dim"] + 2 * hp["n_kv_heads"] * hp["head_dim"] + hp["n_heads"] * hp["head_dim"]
+        + 3 * hp["ffn"])
+    att = 4.0 * hp["n_heads"] * hp["head_dim"] * T * (T + 1) / 2 * hp["n_layers"]
+    burst, _, kind = measured_tensor_peak()
+    line = {"impl": "ours", "metric": "qwen2_c5_prefill_decode", "workload":
+            f"config 5: 7B-shaped Q8_0 stack (28 layers), causal prefill of {T} prompt embeddings, "
+            f"then {steps} greedy decode steps, batch 1", "n_gpus": world,
+            "partition": "none" if world == 1 else (f"KV heads over {world} GPUs" if seq_parts == 1 else
+                                                     f"KV heads x sequence halves over {world} GPUs"),
+            "prefill": {"tokens_per_s": round(T / (pre_ms / 1000.0), 1), "ms": round(pre_ms, 1),
+                        "tflops_per_gpu": round((lin + att) / (pre_ms / 1000.0) / 1e12 / world, 1),
+                        "peak_tflops": burst, "peak_kind": kind},
+            "decode": {"tokens_per_s": round(steps / (dec_ms / 1000.0), 2), "ms_per_step": round(dec_ms / steps, 3)},
+            "data": "synthetic (random Q8_0 blocks, N(0,1) embeddings)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -285,12 +375,17 @@ def main():
     ap.add_argument("--prefill-tokens", type=int, default=16384)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-c3", action="store_true")
+    ap.add_argument("--workload", default="c2", choices=["c2", "c5"])
+    ap.add_argument("--c5-tokens", type=int, default=27000)
+    ap.add_argument("--c5-steps", type=int, default=32)
     ap.add_argument("--c3-steps", type=int, default=10)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, local, world = dist_env()
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.workload == "c5":
+        return run_c5(args, rank, local, world)
 
     import torch
     import torch.distributed as dist

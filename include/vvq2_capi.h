@@ -244,9 +244,12 @@ int  vvq2_profile_read(vvq2_ctx* ctx, int kind, double* ms, double* bytes, int64
  * starts at a page-aligned split fixed by the sequence's first write: half
  * of it).  Each rank computes normalized attention output and its
  * log-sum-exp over its keys; the two parts of a head group merge (O, LSE)
- * through an NCCL all-gather, head groups all-gather the output rows, and
- * O-proj, FFN, final norm and lm_head run replicated, so every rank returns
- * the same hidden states and tokens.  Call after vvq2_init and before
+ * through an NCCL all-gather, head groups all-gather the output rows, O-proj
+ * runs replicated, the FFN is split over all ranks (gate/up rows, down
+ * columns; intermediate_size / world must be a multiple of 64 and of the
+ * down weight's block size) with an NCCL
+ * all-reduce of the down projection, and final norm and lm_head run
+ * replicated, so every rank returns the same hidden states and tokens.  Call after vvq2_init and before
  * vvq2_set_layer / vvq2_kv_init, on all ranks at once (NCCL init is
  * collective); every rank must then make the same calls with the same
  * inputs.  `nccl_id`: VVQ2_NCCL_ID_BYTES from vvq2_nccl_unique_id on one

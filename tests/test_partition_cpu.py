@@ -34,6 +34,11 @@ def test_plan_covers_each_head_and_key_once():
     assert len(k0) + len(k1) == n and k0.stop == k1.start
     with pytest.raises(ValueError):
         PT.plan(0, 3, 1, 28, 4)
+    for world in (2, 4, 8):
+        feats = [f for r in range(world) for f in PT.ffn_range(r, world, 18944)]
+        assert feats == list(range(18944))
+    with pytest.raises(ValueError):
+        PT.ffn_range(0, 8, 4864 + 64)
 
 
 def _worker(rank, world, port, seq_parts, q_all, k_all, v_all, q_pos, out):

@@ -153,12 +153,14 @@ struct vvq2_ctx {
     struct Part {
         int rank = 0, world = 1, seq_parts = 1, head_parts = 1, g = 0, s = 0;
         int nq = 0, nkv = 0;                // heads held locally
+        int ffn = 0;                        // FFN intermediate features held locally (split over all ranks)
         ncclComm_t comm = nullptr, pair = nullptr, heads = nullptr;
         bool on() const { return world > 1; }
     } pt;
     __half *ATTl = nullptr, *ATTg = nullptr;   // local / gathered attention output (partitioned)
     float *LSEl = nullptr, *LSEg = nullptr;
     RowMeta* meta_rope = nullptr;              // true positions for the RoPE table (partitioned)
+    float* Xp = nullptr;                       // partial down-projection rows before the all-reduce
     cudaStream_t stream = nullptr;
     float rope_ts = 0.f;
     struct Layer {
@@ -592,7 +594,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
     };
     const int H = hp.hidden_size, hd = hp.head_dim;
     const int nq = c->pt.nq, nkv = c->pt.nkv;          // heads this rank holds (all, unpartitioned)
-    const int F = hp.intermediate_size, qw = hp.n_heads * hd, qw_l = nq * hd;
+    const int F = c->pt.ffn, qw = hp.n_heads * hd, qw_l = nq * hd;   // F: this rank's FFN features
     const bool parted = c->pt.on();
     // RoPE from true positions (a later sequence part shifts meta.pos for its keys)
     CU(rope_table_launch(parted ? c->meta_rope : c->meta, M, hd, c->rope_ts, c->rope_cs, st));
@@ -724,15 +726,21 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         f.yh = c->Ah;
         f.yh_stride = F;
         if (int rc = gemm(f, mapX)) return rc;
-        // 5. down + residual
+        // 5. down + residual (partitioned: partial sums over this rank's features,
+        //    NCCL all-reduce, then the residual add)
         GemmArgs d = g;
         d.w0 = L.down;
         d.N = H;
         d.K = F;
-        d.epi = EPI_RESID;
-        d.y = c->X;
+        d.epi = parted ? EPI_STORE : EPI_RESID;
+        d.y = parted ? c->Xp : c->X;
         d.y_stride = H;
         if (int rc = gemm(d, mapF)) return rc;
+        if (parted) {
+            if (ncclAllReduce(c->Xp, c->Xp, (size_t)M * H, ncclFloat, ncclSum, c->pt.comm, st) != ncclSuccess)
+                return fail(VVQ2_ERR_CUDA, "NCCL all-reduce of the down projection failed");
+            CU(add_rows_launch(c->X, c->Xp, (int64_t)M * H, st));
+        }
     }
     return 0;
 }
@@ -1094,6 +1102,7 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     c->layers.resize(hp->n_layers);
     c->pt.nq = hp->n_heads;
     c->pt.nkv = hp->n_kv_heads;
+    c->pt.ffn = hp->intermediate_size;
     c->rope_ts = powf(hp->rope_theta, -2.0f / (float)hp->head_dim);
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
         delete c;
@@ -1191,6 +1200,10 @@ int vvq2_partition(vvq2_ctx* c, int rank, int world, int seq_parts, const void* 
         return fail(VVQ2_ERR_INVALID_ARG, "bad partition rank %d / world %d / seq_parts %d", rank, world, seq_parts);
     const int hp_parts = world / seq_parts;
     if (hp.n_kv_heads % hp_parts) return fail(VVQ2_ERR_INVALID_ARG, "%d KV heads over %d head groups", hp.n_kv_heads, hp_parts);
+    // 64-feature multiples per rank (GEMM K blocks, SwiGLU tiles); the weight
+    // type's block alignment of the down columns is checked at vvq2_set_layer
+    if (hp.intermediate_size % (world * 64))
+        return fail(VVQ2_ERR_INVALID_ARG, "ffn %d not a multiple of %d (64 per rank)", hp.intermediate_size, world * 64);
     for (const auto& L : c->layers)
         if (L.set) return fail(VVQ2_ERR_INVALID_ARG, "vvq2_partition must precede vvq2_set_layer");
     if (!c->kvs.empty()) return fail(VVQ2_ERR_INVALID_ARG, "vvq2_partition must precede vvq2_kv_init");
@@ -1206,6 +1219,7 @@ int vvq2_partition(vvq2_ctx* c, int rank, int world, int seq_parts, const void* 
     P.s = rank % seq_parts;
     P.nq = hp.n_heads / hp_parts;
     P.nkv = hp.n_kv_heads / hp_parts;
+    P.ffn = hp.intermediate_size / world;
     CU(cudaSetDevice(c->device));
     ncclUniqueId id;
     memcpy(&id, nccl_id, sizeof id);
@@ -1223,6 +1237,7 @@ int vvq2_partition(vvq2_ctx* c, int rank, int world, int seq_parts, const void* 
     if (int rc = c->alloc(&c->LSEl, rows * hp.n_heads)) return rc;
     if (int rc = c->alloc(&c->LSEg, 2 * rows * hp.n_heads)) return rc;
     if (int rc = c->alloc(&c->meta_rope, rows)) return rc;
+    if (int rc = c->alloc(&c->Xp, rows * hp.hidden_size)) return rc;
     return 0;
 }
 
@@ -1280,10 +1295,36 @@ int vvq2_set_layer(vvq2_ctx* c, int li, const vvq2_layer_weights* w) {
         }
     }
     if (int rc = upload_tensor(c, w->attn_o, &L.o, qw, H, "attn_o")) return rc;
-    if (int rc = upload_tensor(c, w->ffn_gate, &L.gate, H, F, "ffn_gate")) return rc;
-    if (int rc = upload_tensor(c, w->ffn_up, &L.up, H, F, "ffn_up")) return rc;
+    if (c->pt.on()) {
+        // FFN split over all ranks: gate/up rows and down columns [rank*F_l, (rank+1)*F_l)
+        const int Fl = c->pt.ffn;
+        const size_t f0 = (size_t)c->pt.rank * Fl;
+        for (const vvq2_tensor* tt : {&w->ffn_gate, &w->ffn_up, &w->ffn_down})
+            if (!tt->data || !type_ok(tt->type)) return fail(VVQ2_ERR_INVALID_ARG, "ffn tensor");
+        if (w->ffn_gate.ne0 != H || w->ffn_gate.ne1 != F || w->ffn_up.ne0 != H || w->ffn_up.ne1 != F ||
+            w->ffn_down.ne0 != F || w->ffn_down.ne1 != H)
+            return fail(VVQ2_ERR_INVALID_ARG, "ffn shapes");
+        const size_t rb_g = (size_t)(H / block_elems(w->ffn_gate.type)) * block_bytes(w->ffn_gate.type);
+        const size_t rb_u = (size_t)(H / block_elems(w->ffn_up.type)) * block_bytes(w->ffn_up.type);
+        vvq2_tensor tg{static_cast<const uint8_t*>(w->ffn_gate.data) + rb_g * f0, w->ffn_gate.type, H, Fl};
+        vvq2_tensor tu{static_cast<const uint8_t*>(w->ffn_up.data) + rb_u * f0, w->ffn_up.type, H, Fl};
+        if (int rc = upload_tensor(c, tg, &L.gate, H, Fl, "ffn_gate")) return rc;
+        if (int rc = upload_tensor(c, tu, &L.up, H, Fl, "ffn_up")) return rc;
+        const int dt = w->ffn_down.type, be = block_elems(dt), bb = block_bytes(dt);
+        if (f0 % be || Fl % be) return fail(VVQ2_ERR_INVALID_ARG, "ffn slice not block aligned");
+        const size_t rb_d = (size_t)(F / be) * bb, sl = (size_t)(Fl / be) * bb;
+        std::vector<uint8_t> cols((size_t)H * sl);
+        for (int r = 0; r < H; ++r)
+            memcpy(cols.data() + (size_t)r * sl,
+                   static_cast<const uint8_t*>(w->ffn_down.data) + (size_t)r * rb_d + f0 / be * bb, sl);
+        vvq2_tensor td{cols.data(), dt, Fl, H};
+        if (int rc = upload_tensor(c, td, &L.down, Fl, H, "ffn_down")) return rc;
+    } else {
+        if (int rc = upload_tensor(c, w->ffn_gate, &L.gate, H, F, "ffn_gate")) return rc;
+        if (int rc = upload_tensor(c, w->ffn_up, &L.up, H, F, "ffn_up")) return rc;
+        if (int rc = upload_tensor(c, w->ffn_down, &L.down, F, H, "ffn_down")) return rc;
+    }
     if (L.gate.type != L.up.type) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "ffn_gate/up types differ");
-    if (int rc = upload_tensor(c, w->ffn_down, &L.down, F, H, "ffn_down")) return rc;
     if (int rc = upload_vec(c, w->attn_norm, H, &L.attn_norm, "attn_norm")) return rc;
     if (int rc = upload_vec(c, w->ffn_norm, H, &L.ffn_norm, "ffn_norm")) return rc;
     L.set = true;

@@ -165,6 +165,8 @@ cudaError_t dequant_rows_launch(const DevW& w, float* dst, cudaStream_t st);
 // o2 [2][rows][nh*hd] f16, l2 [2][rows][nh] -> out [rows][nh*hd] f16
 cudaError_t lse_merge_launch(const __half* o2, const float* l2, int64_t rows, int nh, int hd, __half* out,
                              cudaStream_t st);
+// x += y over n floats
+cudaError_t add_rows_launch(float* x, const float* y, int64_t n, cudaStream_t st);
 // [parts][rows][w] -> [rows][parts*w]
 cudaError_t gather_rows_launch(const __half* in, int64_t rows, int parts, int w, __half* out, cudaStream_t st);
 // ... to f16 [rows][cols] (exact dequantized value, rounded once)

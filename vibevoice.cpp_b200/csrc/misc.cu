@@ -212,6 +212,18 @@ __global__ void k_gather_rows(const __half* in, int64_t rows, int parts, int w, 
     }
 }
 
+// x += y (residual add of an all-reduced partial projection)
+__global__ void k_add_rows(float* x, const float* y, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        x[i] = __fadd_rn(x[i], y[i]);
+}
+
+cudaError_t add_rows_launch(float* x, const float* y, int64_t n, cudaStream_t st) {
+    k_add_rows<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
+    note_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t lse_merge_launch(const __half* o2, const float* l2, int64_t rows, int nh, int hd, __half* out,
                              cudaStream_t st) {
     const int64_t n = rows * nh * hd;

@@ -7,6 +7,9 @@ every sequence's keys.  Part 1 starts at a page-aligned split fixed by the
 sequence's first write of n positions: max(64, roundup((n + 1) // 2, 64)).
 Each rank's attention output is normalized over its own keys and carries its
 log-sum-exp; two parts merge as o = sum_i e^(l_i - l) o_i / sum_i e^(l_i - l).
+The FFN is split over all ranks: rank r holds intermediate features
+[r F/world, (r+1) F/world) (gate/up rows, down columns); the partial down
+projections are all-reduced.
 
 Pure Python/numpy: the host side of the partition (plan, id exchange) and a
 restatement of the merge used by the tests."""
@@ -34,6 +37,14 @@ def plan(rank: int, world: int, seq_parts: int, n_heads: int, n_kv_heads: int) -
     nq = n_heads // groups
     return {"group": g, "part": s, "kv_heads": range(g * nkv, (g + 1) * nkv),
             "q_heads": range(g * nq, (g + 1) * nq), "groups": groups, "seq_parts": seq_parts}
+
+
+def ffn_range(rank: int, world: int, ffn: int) -> range:
+    """Intermediate FFN features one rank holds."""
+    if ffn % (world * 64):
+        raise ValueError(f"ffn {ffn} not a multiple of {world * 64}")
+    f = ffn // world
+    return range(rank * f, (rank + 1) * f)
 
 
 def keys_of_part(part: int, seq_parts: int, split: int, n_keys: int) -> range:

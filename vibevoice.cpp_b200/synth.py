@@ -66,6 +66,38 @@ def layer_q8_0(rng, hp: dict, bias: bool = True) -> dict:
     }
 
 
+def q8_0_random_tensor(rng, rows: int, cols: int, std: float = 0.02):
+    """Random Q8_0 blocks without a float pass (for large timing models):
+    uniform int8 quants and f16 scales ~ std*2.5/127, the scale a block of
+    N(0, std) values gets.  Statistically close to q8_0_tensor, much faster."""
+    nb = rows * (cols // 32)
+    raw = np.frombuffer(rng.bytes(nb * 34), np.uint8).reshape(nb, 34).copy()
+    d = (rng.uniform(0.8, 1.2, size=nb) * std * 2.5 / 127).astype(np.float16)
+    raw[:, :2] = d.view(np.uint8).reshape(-1, 2)
+    raw[:, 2:] = np.where(raw[:, 2:] == 128, 127, raw[:, 2:])   # int8 -128 excluded, as in ggml's quantizer
+    return (raw.reshape(-1), Q8_0, cols, rows)
+
+
+def layer_q8_0_fast(rng, hp: dict) -> dict:
+    """layer_q8_0 with random Q8_0 bytes (q8_0_random_tensor)."""
+    H, nq, nkv, hd, F = hp["hidden"], hp["n_heads"], hp["n_kv_heads"], hp["head_dim"], hp["ffn"]
+    g = lambda *s: (rng.standard_normal(s, dtype=np.float32) * 0.02)
+    return {
+        "attn_norm": f32_tensor(1.0 + g(H)),
+        "attn_q": q8_0_random_tensor(rng, nq * hd, H),
+        "attn_k": q8_0_random_tensor(rng, nkv * hd, H),
+        "attn_v": q8_0_random_tensor(rng, nkv * hd, H),
+        "attn_o": q8_0_random_tensor(rng, H, nq * hd),
+        "attn_q_bias": f32_tensor(g(nq * hd)),
+        "attn_k_bias": f32_tensor(g(nkv * hd)),
+        "attn_v_bias": f32_tensor(g(nkv * hd)),
+        "ffn_norm": f32_tensor(1.0 + g(H)),
+        "ffn_gate": q8_0_random_tensor(rng, F, H),
+        "ffn_up": q8_0_random_tensor(rng, F, H),
+        "ffn_down": q8_0_random_tensor(rng, H, F),
+    }
+
+
 def model_q8_0(seed: int, hp: dict, n_layers: int | None = None) -> dict:
     """Full LM: layers, output_norm, tied Q8_0 lm_head / token embedding."""
     rng = np.random.default_rng(seed)
