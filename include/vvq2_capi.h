@@ -228,8 +228,10 @@ int  vvq2_attention_decode_noalloc(const float* q, const void* k_pages, const vo
 /* ---- measurement (no counterpart in the reference, which has no profiler
  * hooks; used by bench.py for the roofline figures) ------------------------
  * While enabled, vvq2_decode_step brackets the persistent decode-step kernel
- * or every GEMV (kind 0) and attention (kind 1) launch, and vvq2_forward on the
+ * or every GEMV (kind 0) and attention (kind 1) launch, vvq2_forward on the
  * tensor-core path every flash-attention (kind 2) and GEMM (kind 3) launch,
+ * and a decode step of many rows (tensor-core path) its split-K attention
+ * (kind 1) and GEMM (kind 3) launches,
  * with CUDA events on the launching stream; per kind it accumulates device
  * time, algorithmic work (bytes for kinds 0/1, flops for kinds 2/3) and
  * launch counts.  Enabling resets the totals. */

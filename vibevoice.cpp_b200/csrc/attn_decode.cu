@@ -45,12 +45,95 @@ __global__ void __launch_bounds__(ad::THREADS) k_attn_decode(const AttnDecodeArg
     ad::item<HD>(a, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, kt, vt, sh, uses, CtaSync{});
 }
 
+// Log-sum-exp merge of many splits, one CTA per (query head, row): thread
+// (split group sg, 4 columns d4) loads the partials of splits sg, sg + SG, ...
+// all at once (one round of independent loads), then the CTA combines
+//   O = sum_s e^{m_s - M} O_s / sum_s e^{m_s - M} l_s,   M = max_s m_s.
+constexpr int MG_SG = 8;                          // split groups per head
+constexpr int MG_PER = ad::MAX_MERGE / MG_SG;     // splits per thread
+constexpr int MERGE_INLINE = 4;                   // up to this many splits the last CTA merges
+
 template <int HD>
-cudaError_t launch_hd(const AttnDecodeArgs& a, cudaStream_t st) {
+__global__ void __launch_bounds__(HD / 4 * MG_SG) k_attn_merge(const AttnDecodeArgs a) {
+    constexpr int D4 = HD / 4;
+    __shared__ float s_mx[MG_SG], s_den[MG_SG];
+    __shared__ float4 s_num[MG_SG][D4];
+    const int h = blockIdx.x, m = blockIdx.y;
+    const int tid = threadIdx.x, d4 = tid % D4, sg = tid / D4;
+    const RowMeta rm = a.meta[m];
+    const int lim = min(rm.pos + 1, rm.kvlen);
+    const int ns = lim > 0 ? (lim + a.split - 1) / a.split : 0;
+    if (ns <= 1) return;   // no keys, or one split: the attention kernel wrote the output
+    float4 p[MG_PER];
+    float2 ml[MG_PER];
+#pragma unroll
+    for (int k = 0; k < MG_PER; ++k) {
+        const int s = sg + k * MG_SG;
+        if (s < ns) {
+            const size_t r = ((size_t)m * a.max_splits + s) * a.nq + h;
+            ml[k] = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + r);
+            p[k] = __ldcg(reinterpret_cast<const float4*>(a.part + r * HD) + d4);
+        }
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < MG_PER; ++k)
+        if (sg + k * MG_SG < ns) mx = fmaxf(mx, ml[k].x);
+    if (d4 == 0) s_mx[sg] = mx;
+    __syncthreads();
+    mx = s_mx[0];
+#pragma unroll
+    for (int i = 1; i < MG_SG; ++i) mx = fmaxf(mx, s_mx[i]);
+    float den = 0.f;
+    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < MG_PER; ++k) {
+        if (sg + k * MG_SG < ns) {
+            const float w = expf(ml[k].x - mx);
+            den = fmaf(w, ml[k].y, den);
+            num.x = fmaf(w, p[k].x, num.x);
+            num.y = fmaf(w, p[k].y, num.y);
+            num.z = fmaf(w, p[k].z, num.z);
+            num.w = fmaf(w, p[k].w, num.w);
+        }
+    }
+    if (d4 == 0) s_den[sg] = den;
+    s_num[sg][d4] = num;
+    __syncthreads();
+    if (sg != 0) return;
+    float dt = 0.f;
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < MG_SG; ++i) {
+        dt += s_den[i];
+        t.x += s_num[i][d4].x;
+        t.y += s_num[i][d4].y;
+        t.z += s_num[i][d4].z;
+        t.w += s_num[i][d4].w;
+    }
+    const float inv = 1.0f / dt;
+    const size_t off = (size_t)m * a.nq * HD + (size_t)h * HD + d4 * 4;
+    if (a.out_h) {
+        reinterpret_cast<__half2*>(a.out_h + off)[0] = __floats2half2_rn(t.x * inv, t.y * inv);
+        reinterpret_cast<__half2*>(a.out_h + off)[1] = __floats2half2_rn(t.z * inv, t.w * inv);
+    } else {
+        *reinterpret_cast<float4*>(a.out + off) = make_float4(t.x * inv, t.y * inv, t.z * inv, t.w * inv);
+    }
+    if (a.lse && d4 == 0) a.lse[(size_t)m * a.nq + h] = mx + logf(dt);
+}
+
+template <int HD>
+cudaError_t launch_hd(const AttnDecodeArgs& a0, cudaStream_t st) {
     const size_t smem = ad::tile_smem_bytes(HD);   // attn_decode_prepare() opted in
+    AttnDecodeArgs a = a0;
+    a.defer_merge = a.max_splits > MERGE_INLINE;
     dim3 grid(a.max_splits, a.nkv, a.M);
     k_attn_decode<HD><<<grid, ad::THREADS, smem, st>>>(a);
     note_launch();
+    if (a.defer_merge) {
+        k_attn_merge<HD><<<dim3(a.nq, a.M), HD / 4 * MG_SG, 0, st>>>(a);
+        note_launch();
+    }
     return cudaGetLastError();
 }
 

@@ -246,6 +246,10 @@ __device__ bool item(const AttnDecodeArgs& a, int s, int g, int m, int tid, __ha
         a.part_ml[(pbase + g * G + tid) * 2 + 0] = sh.run_max[tid];
         a.part_ml[(pbase + g * G + tid) * 2 + 1] = sh.run_sum[tid];
     }
+    if (a.defer_merge) {   // many splits: k_attn_merge combines them after this launch
+        sync();            // sh is reused by the next item
+        return true;
+    }
     __threadfence();
     sync();
     if (tid == 0) {

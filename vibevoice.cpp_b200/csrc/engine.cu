@@ -685,7 +685,10 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         ad.part_ml = c->part_ml;
         ad.counters = c->counters;
         ad.err = c->err;
+        CU(R.begin());
         CU(attn_decode_launch(ad, st));
+        // f16 K and V read: 4 bytes per key and head dimension of each KV head
+        CU(R.end(1, attn_flops * nkv / nq));
         }
         if (parted) {
             // the two sequence parts of this head group: (O, LSE) all-gather, merge

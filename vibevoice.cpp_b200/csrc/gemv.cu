@@ -22,6 +22,8 @@
 // and argmax.  Kernels are launched with programmatic dependent launch: each
 // warp starts pulling its first unit's weights into L2 before
 // griddepcontrol.wait, overlapping the previous kernel's tail.
+#include <type_traits>
+
 #include "common.cuh"
 #include "gemv_dev.cuh"
 #include "kernels.h"
@@ -339,6 +341,372 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     }
 }
 
+// ------------------------------------------------------------------------
+// Streaming GEMV for one or two activation rows (a decode step of one
+// sequence or of a CFG pair): the bandwidth-bound case.
+//
+// One CTA of 16 warps per SM.  CTA b owns a contiguous range of units (NR
+// weight rows each, grouped by unit_rows), cut into (unit, item) pairs; an
+// item is 512 consecutive K elements of the unit's rows, one 16-element chunk
+// per lane.  Warp w takes pairs w, w + 16, w + 32, ... and keeps the weight
+// loads of its next SP pairs in flight in registers -- the first ones are
+// issued before the activations are even staged (programmatic dependent
+// launch), and there is no block-wide barrier in the main loop, so every SM
+// keeps ~SP x 2 KB per warp outstanding.  Q8_0/K-quant values become exact
+// floats without I2F (the unsigned byte in the mantissa of 2^23, minus 2^23 +
+// offset) and the block scale multiplies each 16-element partial sum.  Per
+// pair the warp reduces its NR x MB sums with one transposing butterfly into
+// shared memory; after one block barrier each row's per-item partials are
+// summed in item order (deterministic), scaled by the row's RMSNorm factor
+// (the staged activations are x * w; W (x s o w) = s W (x o w)), and the
+// epilogue applied.
+constexpr int S_THREADS = 512;
+constexpr int S_WARPS = S_THREADS / 32;
+constexpr size_t S_SMEM_MAX = 220 * 1024;
+
+struct Q8Raw {
+    uint4 q;        // 16 quants
+    uint32_t d;     // f16 block scale bits
+};
+
+template <int WT>
+using SChunk = typename std::conditional<WT == W_Q8_0, Q8Raw, Chunk>::type;
+
+// register stages of weight loads per warp (by type and activation rows)
+template <int WT, int MB>
+struct SPipe {
+    static constexpr int P = WT == W_Q8_0 ? (MB == 1 ? 4 : 3) : WT == W_F32 ? 1 : 2;
+};
+
+template <int WT>
+__device__ __forceinline__ void s_load(const DevW& W, int row, int c, bool ok, SChunk<WT>& ch) {
+    if constexpr (WT == W_Q8_0) {
+        if (ok) {
+            const uint8_t* rp = W.q + (size_t)row * W.row_stride;
+            ch.q = __ldg(reinterpret_cast<const uint4*>(rp) + c);
+            ch.d = __ldg(reinterpret_cast<const unsigned short*>(W.d) + (size_t)row * W.d_stride + c / 2);
+        } else {
+            ch.q = make_uint4(0, 0, 0, 0);
+            ch.d = 0;
+        }
+    } else {
+        if (ok) load_chunk<WT>(W, row, c, ch);
+        else clear_chunk<WT>(ch);
+    }
+}
+
+// exact floats of the four unsigned bytes of w: 2^23 + byte (then an FFMA2 removes the offset)
+__device__ __forceinline__ void magic4(uint32_t w, float2& f01, float2& f23) {
+    f01 = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440)),
+                      __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441)));
+    f23 = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7442)),
+                      __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7443)));
+}
+
+// Dot of one lane's 16-element chunk of one weight row with MB activation
+// chunks (av[m][g] = elements 4g .. 4g+3 of row m).
+template <int WT, int MB>
+__device__ __forceinline__ void s_dot(const SChunk<WT>& ch, const float4 (&av)[MB][4], float (&out)[MB]) {
+    const float2 one2 = make_float2(1.0f, 1.0f);
+    float2 s[MB];
+#pragma unroll
+    for (int m = 0; m < MB; ++m) s[m] = make_float2(0.f, 0.f);
+    if constexpr (WT == W_Q8_0 || WT == W_Q5_K || WT == W_Q6_K) {
+        // Q8_0: signed quant, stored as q + 128; Q5_K: 0..31; Q6_K: q - 32 with q in 0..63
+        constexpr float OFF = WT == W_Q8_0 ? -8388736.0f : WT == W_Q5_K ? -8388608.0f : -8388640.0f;
+        const float2 off2 = make_float2(OFF, OFF);
+        float2 as[MB];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) as[m] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            uint32_t w;
+            if constexpr (WT == W_Q8_0) {
+                w = gd::word(ch.q, g) ^ 0x80808080u;
+            } else if constexpr (WT == W_Q5_K) {
+                const int j = ch.shift;
+                w = ((gd::word(ch.r0, g) >> (4 * (j & 1))) & 0x0F0F0F0Fu) |
+                    (((gd::word(ch.r1, g) >> j) & 0x01010101u) << 4);
+            } else {
+                const int k = ch.shift;
+                w = ((gd::word(ch.r0, g) >> (4 * (k >> 1))) & 0x0F0F0F0Fu) |
+                    (((gd::word(ch.r1, g) >> (2 * k)) & 0x03030303u) << 4);
+            }
+            float2 f01, f23;
+            magic4(w, f01, f23);
+            f01 = __ffma2_rn(f01, one2, off2);
+            f23 = __ffma2_rn(f23, one2, off2);
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                const float2 a01 = make_float2(av[m][g].x, av[m][g].y), a23 = make_float2(av[m][g].z, av[m][g].w);
+                s[m] = __ffma2_rn(f01, a01, s[m]);
+                s[m] = __ffma2_rn(f23, a23, s[m]);
+                if constexpr (WT == W_Q5_K) {
+                    as[m] = __fadd2_rn(as[m], a01);
+                    as[m] = __fadd2_rn(as[m], a23);
+                }
+            }
+        }
+        float d;
+        if constexpr (WT == W_Q8_0) d = __half2float(__ushort_as_half((unsigned short)ch.d));
+        else d = ch.scale;
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            out[m] = __fmul_rn(d, s[m].x + s[m].y);
+            // Q5_K: w = d1 q - m1, so w.a = d1 (q.a) - m1 (sum a)
+            if constexpr (WT == W_Q5_K) out[m] = fmaf(-ch.mscale, as[m].x + as[m].y, out[m]);
+        }
+    } else {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            float w[4];
+            expand4<WT>(ch, g, w);
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                s[m] = __ffma2_rn(make_float2(w[0], w[1]), make_float2(av[m][g].x, av[m][g].y), s[m]);
+                s[m] = __ffma2_rn(make_float2(w[2], w[3]), make_float2(av[m][g].z, av[m][g].w), s[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MB; ++m) out[m] = s[m].x + s[m].y;
+    }
+}
+
+template <int N>
+struct SLog2 {
+    static constexpr int v = 1 + SLog2<N / 2>::v;
+};
+template <>
+struct SLog2<1> {
+    static constexpr int v = 0;
+};
+
+// Sum NV (a power of two) per-lane values over the warp; lane l returns the
+// total of value index l >> (5 - log2 NV).
+template <int NV>
+__device__ __forceinline__ float s_transpose_sum(float (&v)[NV], int lane) {
+#pragma unroll
+    for (int n = NV, o = 16; n > 1; n >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float keep = up ? v[i + n / 2] : v[i];
+            const float send = up ? v[i] : v[i + n / 2];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+#pragma unroll
+    for (int o = 16 >> SLog2<NV>::v; o >= 1; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    return v[0];
+}
+
+template <int WT, int EPI, int MB>
+__global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) {
+    constexpr int P = SPipe<WT, MB>::P;
+    constexpr int NV = NR * MB;
+    constexpr int SH = 5 - SLog2<NV>::v;
+    extern __shared__ __align__(16) float sm_act[];
+    __shared__ float red[MB * S_WARPS];
+    __shared__ unsigned long long best[MB];
+    __shared__ float rope_c[EPI == EPI_QKV ? MB : 1][EPI == EPI_QKV ? 64 : 1];
+    __shared__ float rope_s[EPI == EPI_QKV ? MB : 1][EPI == EPI_QKV ? 64 : 1];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = a.K, NC = K / 16, niter = (NC + 31) / 32;
+    const int U = a.n_units;
+    const int u0 = (int)((long long)U * blockIdx.x / gridDim.x);
+    const int nu = (int)((long long)U * (blockIdx.x + 1) / gridDim.x) - u0;
+    const int npairs = nu * niter;
+    float4* act4 = reinterpret_cast<float4*>(sm_act);            // [(m * 4 + g) * NC + c]
+    float* part = sm_act + (size_t)MB * K;                        // [(ul * NR + j) * niter + it][MB]
+
+    auto load_pair = [&](int p, SChunk<WT> (&dst)[NR]) {
+        const int ul = p / niter, it = p - ul * niter;
+        const int u = u0 + ul, c = it * 32 + lane;
+        int r[NR], wh[NR];
+        unit_rows<EPI>(a, u, r, wh);
+#pragma unroll
+        for (int j = 0; j < NR; ++j) {
+            const DevW& W = wh[j] ? a.w1 : a.w0;
+            s_load<WT>(W, r[j], c, c < NC && r[j] < W.rows, dst[j]);
+        }
+    };
+
+    // weights do not depend on the previous kernel: start the stream first
+    SChunk<WT> buf[P][NR];
+#pragma unroll
+    for (int s = 0; s < P; ++s)
+        if (warp + s * S_WARPS < npairs) load_pair(warp + s * S_WARPS, buf[s]);
+    pdl_launch();
+    pdl_wait();
+    if (EPI == EPI_ARGMAX && tid < MB) best[tid] = 0ull;
+    if constexpr (EPI == EPI_QKV) {
+        // NEOX cos/sin per (row, pair) with ggml's CPU theta recurrence, once per CTA
+        const int half = a.hd / 2;
+        for (int t = tid; t < MB * half; t += S_THREADS) {
+            const int m = t / half, i = t % half;
+            float th = (float)a.meta[m].pos;
+            for (int k = 0; k < i; ++k) th = __fmul_rn(th, a.rope_ts);
+            rope_c[m][i] = cosf(th);
+            rope_s[m][i] = sinf(th);
+        }
+    }
+    // stage x (times the norm weight where the linear follows an RMSNorm)
+    {
+        float ss[MB];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) ss[m] = 0.f;
+        const int K4 = K / 4;
+        for (int k4 = tid; k4 < K4; k4 += S_THREADS) {
+            const int c = k4 >> 2, g = k4 & 3;
+            const float4 w = a.norm_w ? __ldg(reinterpret_cast<const float4*>(a.norm_w) + k4)
+                                      : make_float4(1.f, 1.f, 1.f, 1.f);
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                float4 v = __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)m * a.x_stride) + k4);
+                if (a.norm_w) {
+                    ss[m] = fmaf(v.x, v.x, ss[m]);
+                    ss[m] = fmaf(v.y, v.y, ss[m]);
+                    ss[m] = fmaf(v.z, v.z, ss[m]);
+                    ss[m] = fmaf(v.w, v.w, ss[m]);
+                    v.x = __fmul_rn(v.x, w.x);
+                    v.y = __fmul_rn(v.y, w.y);
+                    v.z = __fmul_rn(v.z, w.z);
+                    v.w = __fmul_rn(v.w, w.w);
+                }
+                act4[(m * 4 + g) * NC + c] = v;
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            const float t = warp_sum(ss[m]);
+            if (lane == 0) red[m * S_WARPS + warp] = t;
+        }
+    }
+    __syncthreads();
+
+    // main loop: pair warp + (n + s) * 16 sits in register stage s
+    for (int n = 0; warp + n * S_WARPS < npairs; n += P) {
+#pragma unroll
+        for (int s = 0; s < P; ++s) {
+            const int p = warp + (n + s) * S_WARPS;
+            if (p < npairs) {
+                const int ul = p / niter, it = p - ul * niter;
+                const int c = it * 32 + lane;
+                float acc[NV];
+                if (c < NC) {
+                    float4 av[MB][4];
+#pragma unroll
+                    for (int m = 0; m < MB; ++m)
+#pragma unroll
+                        for (int g = 0; g < 4; ++g) av[m][g] = act4[(m * 4 + g) * NC + c];
+#pragma unroll
+                    for (int j = 0; j < NR; ++j) {
+                        float o[MB];
+                        s_dot<WT, MB>(buf[s][j], av, o);
+#pragma unroll
+                        for (int m = 0; m < MB; ++m) acc[j * MB + m] = o[m];
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < NV; ++i) acc[i] = 0.f;
+                }
+                // the stage is free: request the pair P rounds ahead
+                const int pn = p + P * S_WARPS;
+                if (pn < npairs) load_pair(pn, buf[s]);
+                const float v = s_transpose_sum<NV>(acc, lane);
+                if ((lane & ((1 << SH) - 1)) == 0) {
+                    const int idx = lane >> SH, j = idx / MB, m = idx % MB;
+                    part[((size_t)(ul * NR + j) * niter + it) * MB + m] = v;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- epilogue: per-row sums in item order, RMSNorm scale, fused op
+    float nsc[MB];
+#pragma unroll
+    for (int m = 0; m < MB; ++m) {
+        nsc[m] = 1.f;
+        if (a.norm_w) {
+            float t = 0.f;
+#pragma unroll
+            for (int w = 0; w < S_WARPS; ++w) t += red[m * S_WARPS + w];
+            nsc[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps)));
+        }
+    }
+    auto rowsum = [&](int ul, int j, int m) {
+        const float* pp = part + (size_t)(ul * NR + j) * niter * MB + m;
+        float v = 0.f;
+        for (int it = 0; it < niter; ++it) v += pp[it * MB];
+        return a.norm_w ? __fmul_rn(v, m == 0 ? nsc[0] : nsc[MB - 1]) : v;
+    };
+    if constexpr (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
+        // thread: (unit, pair jp in {0, 1}, row m); partners are unit rows jp and jp + 2
+        for (int t = tid; t < nu * 2 * MB; t += S_THREADS) {
+            const int m = t % MB, jp = (t / MB) & 1, ul = t / (2 * MB);
+            const int u = u0 + ul;
+            int row[NR], which[NR];
+            unit_rows<EPI>(a, u, row, which);
+            float v0 = rowsum(ul, jp, m), v1 = rowsum(ul, jp + 2, m);
+            if constexpr (EPI == EPI_SWIGLU) {
+                if (row[jp] < a.w0.rows) a.y[(size_t)m * a.y_stride + row[jp]] = __fmul_rn(silu_ref(v0), v1);
+            } else {
+                if (a.bias) {
+                    v0 = __fadd_rn(v0, a.bias[row[jp]]);
+                    v1 = __fadd_rn(v1, a.bias[row[jp + 2]]);
+                }
+                const int h = row[jp] / a.hd, i2 = row[jp] % a.hd;
+                const RowMeta rm = a.meta[m];
+                if (h < a.n_q_heads + a.n_kv_heads) {
+                    const float cc = rope_c[m][i2], sn = rope_s[m][i2];
+                    const float y0 = __fsub_rn(__fmul_rn(v0, cc), __fmul_rn(v1, sn));
+                    const float y1 = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, cc));
+                    v0 = y0;
+                    v1 = y1;
+                }
+                if (h < a.n_q_heads) {
+                    float* q = a.y + (size_t)m * a.y_stride + h * a.hd;
+                    q[i2] = v0;
+                    q[i2 + a.hd / 2] = v1;
+                } else if (rm.cidx >= 0) {   // cidx < 0: another rank stores this position
+                    const bool is_k = h < a.n_q_heads + a.n_kv_heads;
+                    const int kvh = is_k ? h - a.n_q_heads : h - a.n_q_heads - a.n_kv_heads;
+                    __half* dst = (is_k ? a.kv.k : a.kv.v) + kv_offset(a.kv, rm.seq, rm.cidx, kvh);
+                    dst[i2] = __float2half_rn(v0);
+                    dst[i2 + a.hd / 2] = __float2half_rn(v1);
+                }
+            }
+        }
+    } else {
+        for (int t = tid; t < nu * NR * MB; t += S_THREADS) {
+            const int m = t % MB, j = (t / MB) % NR, ul = t / (NR * MB);
+            const int row = (u0 + ul) * NR + j;
+            if (row >= a.w0.rows) continue;
+            float v = rowsum(ul, j, m);
+            if constexpr (EPI == EPI_ARGMAX) {
+                if (a.y) a.y[(size_t)m * a.y_stride + row] = v;
+                atomicMax(&best[m], argmax_key(v, row));
+            } else {
+                if (a.bias) v = __fadd_rn(v, a.bias[row]);
+                float* dst = a.y + (size_t)m * a.y_stride + row;
+                if (EPI == EPI_RESID) *dst = __fadd_rn(*dst, v);   // ggml_add(x, o)
+                else *dst = v;
+            }
+        }
+        if constexpr (EPI == EPI_ARGMAX) {
+            __syncthreads();
+            if (tid < MB && best[tid]) atomicMax(a.argmax + tid, best[tid]);
+        }
+    }
+}
+
+size_t stream_smem(const GemvArgs& a, int grid) {
+    const int niter = (a.K / 16 + 31) / 32;
+    const int nu_max = (a.n_units + grid - 1) / grid;
+    return (size_t)a.M * a.K * sizeof(float) + (size_t)nu_max * NR * niter * a.M * sizeof(float);
+}
+
 template <int WT, int EPI>
 cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
     const size_t smem = (size_t)a.M * a.K * sizeof(float);
@@ -349,6 +717,27 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
         int dev = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    if (a.M <= 2) {
+        // one or two rows: the streaming kernel, one CTA per SM
+        const int grid = a.n_units < sms ? a.n_units : sms;
+        const size_t ssm = stream_smem(a, grid);
+        if (grid > 0 && ssm <= S_SMEM_MAX) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(grid);
+            cfg.blockDim = dim3(S_THREADS);
+            cfg.dynamicSmemBytes = ssm;
+            cfg.stream = st;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            cudaError_t e = a.M == 1 ? cudaLaunchKernelEx(&cfg, k_gemv_stream<WT, EPI, 1>, a)
+                                     : cudaLaunchKernelEx(&cfg, k_gemv_stream<WT, EPI, 2>, a);
+            note_launch();
+            return e;
+        }
     }
     GemvArgs b = a;
     const int niter = (a.K / 16 + 31) / 32;
@@ -399,6 +788,15 @@ cudaError_t prepare_wt() {
                          (const void*)k_gemv<W_F16, EPI, GEMV_MAX_M>};
     for (const void* f : fns) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_SMEM_MAX);
+        if (e != cudaSuccess) return e;
+    }
+    const void* sfns[] = {(const void*)k_gemv_stream<W_Q8_0, EPI, 1>, (const void*)k_gemv_stream<W_Q8_0, EPI, 2>,
+                          (const void*)k_gemv_stream<W_Q5_K, EPI, 1>, (const void*)k_gemv_stream<W_Q5_K, EPI, 2>,
+                          (const void*)k_gemv_stream<W_Q6_K, EPI, 1>, (const void*)k_gemv_stream<W_Q6_K, EPI, 2>,
+                          (const void*)k_gemv_stream<W_F32, EPI, 1>, (const void*)k_gemv_stream<W_F32, EPI, 2>,
+                          (const void*)k_gemv_stream<W_F16, EPI, 1>, (const void*)k_gemv_stream<W_F16, EPI, 2>};
+    for (const void* f : sfns) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM_MAX);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

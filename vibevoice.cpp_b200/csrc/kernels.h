@@ -135,6 +135,7 @@ struct AttnDecodeArgs {
     int* err = nullptr;            // set to nonzero if a bounded wait gave up
     __half* out_h = nullptr;       // if set, write f16 output here instead of `out`
     float* lse = nullptr;          // optional [M][nq]: log-sum-exp of the scaled scores (-inf: no keys)
+    int defer_merge = 0;           // set by attn_decode_launch: partials only, a merge kernel follows
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st);
 cudaError_t attn_decode_prepare();
