@@ -169,6 +169,31 @@ def test_kquant_layer_c4_shape(vv):
     assert rel_err(got, ref) < TOL, rel_err(got, ref)
 
 
+@pytest.mark.parametrize("rows,kv_len", [(1, 6001), (2, 3100), (2, 130)])
+def test_long_context_decode_hd128(vv, rows, kv_len):
+    """Decode of one token against long contexts with head_dim 128 and a GQA
+    group of 7: many attention splits (the separate log-sum-exp merge), a
+    partial last page, one and two rows."""
+    rng = np.random.default_rng(7000 + kv_len)
+    hp = dict(hidden=1792, n_heads=14, n_kv_heads=2, head_dim=128, ffn=1024, n_layers=1, vocab=0,
+              rope_theta=1.0e6, rms_eps=1.0e-6)
+    t = random_layer(rng, hp, O.Q8_0)
+    eng, kv, ora = _pair(vv, hp, [t], rows, kv_len + 8, GPU_MODE)
+    w = hp["n_kv_heads"] * hp["head_dim"]
+    for s in range(rows):
+        k = rng.standard_normal((kv_len - 1, w)).astype(np.float32)
+        v = rng.standard_normal((kv_len - 1, w)).astype(np.float32)
+        kv.load_prefix(s, 0, k, v)
+        ora.kv_load(s, 0, k, v)
+        kv.set_past_len(s, kv_len - 1)
+        ora.set_past_len(s, kv_len - 1)
+    x = rng.standard_normal((rows, 1, hp["hidden"])).astype(np.float32)
+    seqs = list(range(rows))
+    got = eng.forward(kv, seqs, x, [kv_len - 1] * rows)
+    ref = ora.forward(seqs, x, [kv_len - 1] * rows)
+    assert rel_err(got, ref) < TOL, rel_err(got, ref)
+
+
 def test_ragged_sequences_and_last_only(vv):
     """Two sequences at different past lengths in one call; LAST_ONLY output."""
     import vvq2

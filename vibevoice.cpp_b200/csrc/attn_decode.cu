@@ -122,10 +122,293 @@ __global__ void __launch_bounds__(HD / 4 * MG_SG) k_attn_merge(const AttnDecodeA
     if (a.lse && d4 == 0) a.lse[(size_t)m * a.nq + h] = mx + logf(dt);
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core decode attention (head_dim 64 / 128, pool with a TMA map).
+//
+// Same work item (split, KV head, row) and the same partial format as above,
+// but the dot products run on mma.sync (m16n8k16, f16 in, f32 accumulate):
+// warp w owns keys [16w, 16w + 16) of every 64-key page and keeps its own
+// online softmax, so the page loop has no block barrier except the one that
+// frees a stage for the next TMA copy.
+//   S  = Q K^T     M = the GQA group's query heads (rows 8..15 zero), N = 8
+//                  keys, K = head_dim; Q fragments live in registers.
+//   O^T += V^T P^T M = 16 head-dim rows, N = the 8 query heads, K = the
+//                  warp's 16 keys; P^T is exactly the S accumulator layout
+//                  (rounded to f16), V^T comes from ldmatrix.trans.
+// K/V pages arrive by TMA (64 x 64 boxes, 128-byte swizzle: 16-byte chunk c
+// of key row r sits at chunk c ^ (r & 7)), double-buffered.  At the end the
+// four warps' (max, sum, O) combine through shared memory.
+constexpr int AM_THREADS = 128;
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// shared address of the 16-byte chunk holding columns col .. col+7 (col % 8 == 0)
+// of key row `row` in a swizzled [64][HD] tile
+template <int HD>
+__device__ __forceinline__ uint32_t swz(uint32_t tile, int row, int col) {
+    return tile + (uint32_t)((col >> 6) * 8192 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(AM_THREADS) k_attn_mma(const __grid_constant__ CUtensorMap mk,
+                                                          const __grid_constant__ CUtensorMap mv,
+                                                          const AttnDecodeArgs a) {
+    constexpr int TILE_BYTES = TILE * HD * 2;   // K (or V) of one page
+    constexpr int NB = HD / 64;                 // 64-column boxes per page
+    constexpr int KS = HD / 16;                 // k-steps of S, m-tiles of O^T
+    extern __shared__ __align__(1024) uint8_t dsm[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ float cm[4][8], cl[4][8];
+    const int s = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = a.nq / a.nkv;
+    const RowMeta rm = a.meta[m];
+    const int lim = min(rm.pos + 1, rm.kvlen);
+    if (lim <= 0) {
+        // no keys for this row here (another rank holds its part of the sequence)
+        if (s == 0) {
+            for (int t = tid; t < G * HD; t += AM_THREADS) {
+                const size_t off = (size_t)m * a.nq * HD + (size_t)g * G * HD + t;
+                if (a.out_h) a.out_h[off] = __float2half_rn(0.f);
+                else a.out[off] = 0.f;
+            }
+            if (a.lse && tid < G) a.lse[(size_t)m * a.nq + g * G + tid] = -INFINITY;
+        }
+        return;
+    }
+    const int nsplit = (lim + a.split - 1) / a.split;
+    if (s >= nsplit) return;
+    const int j0 = s * a.split, j1 = min(lim, j0 + a.split);
+    const int ntiles = (j1 - j0 + TILE - 1) / TILE;
+    const uint32_t sbase = tc::smem_u32(sm);   // stage b: K at b * 2 * TILE_BYTES, V after it
+
+    auto issue = [&](int t) {
+        const int b = t & 1;
+        const int page = __ldg(a.kv.block_table + (size_t)rm.seq * a.kv.max_pages + (j0 + t * TILE) / TILE);
+        const int y = (page * a.kv.n_kv + g) * TILE;
+        uint8_t* kd = sm + b * 2 * TILE_BYTES;
+        tc::mbar_arrive_expect_tx(&bar[b], 2 * TILE_BYTES);
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+            tc::tma_load_2d(kd + nb * 8192, &mk, nb * 64, y, &bar[b]);
+            tc::tma_load_2d(kd + TILE_BYTES + nb * 8192, &mv, nb * 64, y, &bar[b]);
+        }
+    };
+    if (tid == 0) {
+        tc::mbar_init(&bar[0], 1);
+        tc::mbar_init(&bar[1], 1);
+        tc::mbar_fence_init();
+        issue(0);
+        if (ntiles > 1) issue(1);
+    }
+
+    // Q fragments (A of S): row r = lane / 4 is query head g * G + r (zero
+    // beyond G), columns 16 kk + 2 (lane % 4) + {0, 1, 8, 9}; rounded to f16
+    // as ggml's flash attention converts Q to the K type
+    const int r = lane >> 2, q4 = lane & 3;
+    uint32_t qa[KS][2];
+    {
+        const float* qp = a.q + (size_t)m * a.nq * HD + (size_t)(g * G + r) * HD;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            const int c = kk * 16 + 2 * q4;
+            if (r < G) {
+                const float2 x0 = __ldcg(reinterpret_cast<const float2*>(qp + c));
+                const float2 x1 = __ldcg(reinterpret_cast<const float2*>(qp + c + 8));
+                qa[kk][0] = pack_h2(x0.x, x0.y);
+                qa[kk][1] = pack_h2(x1.x, x1.y);
+            } else {
+                qa[kk][0] = qa[kk][1] = 0u;
+            }
+        }
+    }
+    __syncthreads();   // barrier init visible
+
+    float mrun = -INFINITY, lrun = 0.f;          // softmax state of head r over this warp's keys
+    float oacc[KS][4];                            // O^T: rows = head dim, columns = heads 2 q4 + {0, 1}
+#pragma unroll
+    for (int i = 0; i < KS; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
+    // ldmatrix lane roles: matrix i = lane / 8, row lane % 8
+    const int li = lane >> 3, lr = lane & 7;
+    const int krow = warp * 16 + (li >> 1) * 8 + lr;   // key row this lane addresses
+    const int kcol = (li & 1) * 8;                      // + column offset of its matrix
+
+    int t = 0;
+    for (; t < ntiles; ++t) {
+        const int b = t & 1;
+        const bool ok = tc::mbar_wait(&bar[b], (t >> 1) & 1);
+        if (__syncthreads_or(!ok)) {   // uniform: every warp leaves the loop together
+            if (tid == 0 && a.err) atomicExch(a.err, 1);
+            break;
+        }
+        const uint32_t kt = sbase + b * 2 * TILE_BYTES, vt = kt + TILE_BYTES;
+        const int nk = min(TILE, j1 - (j0 + t * TILE));
+        if (nk < TILE) {
+            // rows past the sequence end: P is 0 there, but 0 * V must not see a
+            // non-finite stale value, so this warp zeroes its part of them
+            uint8_t* vp = sm + b * 2 * TILE_BYTES + TILE_BYTES;
+            for (int i = lane; i < 16 * (HD / 8); i += 32) {
+                const int key = warp * 16 + i / (HD / 8), c = (i % (HD / 8)) * 8;
+                if (key >= nk) *reinterpret_cast<uint4*>(vp + (swz<HD>(0u, key, c))) = make_uint4(0, 0, 0, 0);
+            }
+            __syncwarp();
+        }
+        // ---- S = Q K^T for keys warp*16 + [0, 16): two n-tiles of 8 keys
+        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            uint32_t b00, b01, b10, b11;
+            ldsm_x4(swz<HD>(kt, krow, kk * 16 + kcol), b00, b01, b10, b11);
+            const uint32_t af[4] = {qa[kk][0], 0u, qa[kk][1], 0u};
+            mma16816(sacc[0], af, b00, b01);
+            mma16816(sacc[1], af, b10, b11);
+        }
+        // ---- online softmax of row r over these 16 keys (lanes 4r .. 4r+3)
+        float sv[4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int key = warp * 16 + nt * 8 + 2 * q4 + e;
+                sv[nt * 2 + e] = key < nk ? sacc[nt][e] * a.scale : -INFINITY;
+            }
+        float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mnew = fmaxf(mrun, mx);
+        const float mref = mnew == -INFINITY ? 0.f : mnew;   // nothing seen yet: p = 0, alpha = 0
+        const float alpha = expf(mrun - mref);
+        uint32_t pb[2];
+        float ps = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            const __half2 h = __floats2half2_rn(expf(sv[nt * 2] - mref), expf(sv[nt * 2 + 1] - mref));
+            pb[nt] = *reinterpret_cast<const uint32_t*>(&h);
+            const float2 f = __half22float2(h);   // the sum uses the rounded P the MMA sees
+            ps += f.x + f.y;
+        }
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        lrun = fmaf(lrun, alpha, ps);
+        mrun = mnew;
+        // O^T columns of this lane are heads 2 q4 and 2 q4 + 1: their alphas
+        const float al0 = __shfl_sync(0xffffffffu, alpha, 8 * q4);
+        const float al1 = __shfl_sync(0xffffffffu, alpha, 8 * q4 + 4);
+        // ---- O^T += V^T P^T (one k-step of 16 keys per m-tile of 16 head dims)
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+            uint32_t af[4];
+            // matrices: (keys 0-7, dims 0-7), (keys 0-7, dims 8-15), (keys 8-15, dims 0-7), (keys 8-15, dims 8-15)
+            // transposed they are A = V^T's (rows 0-7, k 0-7), (rows 8-15, k 0-7), (rows 0-7, k 8-15), (rows 8-15, k 8-15)
+            ldsm_x4_t(swz<HD>(vt, krow, mt * 16 + kcol), af[0], af[1], af[2], af[3]);
+            oacc[mt][0] *= al0;
+            oacc[mt][1] *= al1;
+            oacc[mt][2] *= al0;
+            oacc[mt][3] *= al1;
+            mma16816(oacc[mt], af, pb[0], pb[1]);
+        }
+        __syncthreads();   // every warp is done with stage b
+        if (tid == 0 && t + 2 < ntiles) {
+            tc::fence_proxy_async_smem();
+            issue(t + 2);
+        }
+    }
+    if (t < ntiles) {
+        // a wait gave up: wait (bounded) for the copies still in flight, then leave
+        if (tid == 0)
+            for (int tt = t; tt < min(ntiles, t + 2); ++tt) tc::mbar_wait(&bar[tt & 1], (tt >> 1) & 1);
+        __syncthreads();
+        return;
+    }
+    __syncthreads();
+    // ---- combine the four warps: (max, sum) per head, O^T through shared memory (the stages are free)
+    float* co = reinterpret_cast<float*>(sm);     // [4][8][HD]
+    if (q4 == 0) {
+        cm[warp][r] = mrun;
+        cl[warp][r] = lrun;
+    }
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+        const int d = mt * 16 + r;
+        co[(warp * 8 + 2 * q4) * HD + d] = oacc[mt][0];
+        co[(warp * 8 + 2 * q4 + 1) * HD + d] = oacc[mt][1];
+        co[(warp * 8 + 2 * q4) * HD + d + 8] = oacc[mt][2];
+        co[(warp * 8 + 2 * q4 + 1) * HD + d + 8] = oacc[mt][3];
+    }
+    __syncthreads();
+    const size_t pbase = ((size_t)m * a.max_splits + s) * a.nq;
+    for (int i = tid; i < G * HD; i += AM_THREADS) {
+        const int h = i / HD, d = i % HD;
+        float M = cm[0][h];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) M = fmaxf(M, cm[w][h]);
+        float L = 0.f, o = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float e = cm[w][h] == -INFINITY ? 0.f : expf(cm[w][h] - M);
+            L = fmaf(e, cl[w][h], L);
+            o = fmaf(e, co[(w * 8 + h) * HD + d], o);
+        }
+        const int qh = g * G + h;
+        if (nsplit == 1) {
+            const size_t off = (size_t)m * a.nq * HD + (size_t)qh * HD + d;
+            const float v = o / L;
+            if (a.out_h) a.out_h[off] = __float2half_rn(v);
+            else a.out[off] = v;
+            if (a.lse && d == 0) a.lse[(size_t)m * a.nq + qh] = M + logf(L);
+        } else {
+            a.part[(pbase + qh) * HD + d] = o;
+            if (d == 0) {
+                a.part_ml[(pbase + qh) * 2 + 0] = M;
+                a.part_ml[(pbase + qh) * 2 + 1] = L;
+            }
+        }
+    }
+}
+
 template <int HD>
 cudaError_t launch_hd(const AttnDecodeArgs& a0, cudaStream_t st) {
     const size_t smem = ad::tile_smem_bytes(HD);   // attn_decode_prepare() opted in
     AttnDecodeArgs a = a0;
+    if constexpr (HD == 64 || HD == 128) {
+        CUtensorMap mk, mv;
+        const int64_t rows = (int64_t)a.kv.n_pages * a.kv.n_kv * TILE;
+        if (a.kv.n_pages > 0 && make_kv_map(&mk, a.kv.k, rows, HD) && make_kv_map(&mv, a.kv.v, rows, HD)) {
+            a.defer_merge = a.max_splits > 1;
+            dim3 grid(a.max_splits, a.nkv, a.M);
+            k_attn_mma<HD><<<grid, AM_THREADS, 4 * TILE * HD * 2 + 1024, st>>>(mk, mv, a);
+            note_launch();
+            if (a.defer_merge) {
+                k_attn_merge<HD><<<dim3(a.nq, a.M), HD / 4 * MG_SG, 0, st>>>(a);
+                note_launch();
+            }
+            return cudaGetLastError();
+        }
+    }
     a.defer_merge = a.max_splits > MERGE_INLINE;
     dim3 grid(a.max_splits, a.nkv, a.M);
     k_attn_decode<HD><<<grid, ad::THREADS, smem, st>>>(a);
@@ -143,7 +426,9 @@ cudaError_t attn_decode_prepare() {
     cudaError_t e;
     if ((e = cudaFuncSetAttribute(k_attn_decode<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ad::tile_smem_bytes(32))) != cudaSuccess) return e;
     if ((e = cudaFuncSetAttribute(k_attn_decode<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, ad::tile_smem_bytes(64))) != cudaSuccess) return e;
-    return cudaFuncSetAttribute(k_attn_decode<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, ad::tile_smem_bytes(128));
+    if ((e = cudaFuncSetAttribute(k_attn_decode<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, ad::tile_smem_bytes(128))) != cudaSuccess) return e;
+    if ((e = cudaFuncSetAttribute(k_attn_mma<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * TILE * 64 * 2 + 1024)) != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_attn_mma<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * TILE * 128 * 2 + 1024);
 }
 
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st) {

@@ -49,6 +49,7 @@ struct KvLayer {
     int max_pages = 0;
     int n_kv = 0;
     int hd = 0;
+    int n_pages = 0;                    // pages in the pool (0: unknown)
 };
 
 __device__ __forceinline__ size_t kv_offset(const KvLayer& kv, int seq, int cidx, int kvh) {

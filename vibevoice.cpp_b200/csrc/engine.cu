@@ -64,7 +64,7 @@ bool make_act_map(CUtensorMap* m, const __half* base, int rows, int cols) {
 
 // One layer's K or V pool as a 2-D f16 [rows][hd] TMA map: 64-key x 64-column
 // boxes, 128-byte swizzle (the prefill flash-attention operand layout).
-bool make_kv_map(CUtensorMap* m, const __half* base, int64_t rows, int hd) {
+bool kv_map_encode(CUtensorMap* m, const __half* base, int64_t rows, int hd) {
     EncodeTiledFn fn = encode_fn();
     if (!fn || hd % 64 || ((uintptr_t)base & 15)) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)rows};
@@ -143,6 +143,10 @@ struct Owned {
 };
 
 }  // namespace
+
+namespace vvq2 {
+bool make_kv_map(CUtensorMap* m, const __half* base, int64_t rows, int hd) { return kv_map_encode(m, base, rows, hd); }
+}  // namespace vvq2
 
 struct vvq2_ctx {
     vvq2_hparams hp{};
@@ -265,6 +269,7 @@ struct vvq2_kv {
         L.max_pages = max_pages;
         L.n_kv = ctx->pt.nkv;
         L.hd = ctx->hp.head_dim;
+        L.n_pages = (int)(layer_elems / ((size_t)L.n_kv * KV_PAGE * L.hd));
         return L;
     }
 };

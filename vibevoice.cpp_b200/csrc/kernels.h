@@ -138,6 +138,8 @@ struct AttnDecodeArgs {
     int defer_merge = 0;           // set by attn_decode_launch: partials only, a merge kernel follows
 };
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st);
+// f16 paged pool [rows][hd] as a TMA map: 64 x 64 boxes, 128-byte swizzle (engine.cu)
+bool make_kv_map(CUtensorMap* m, const __half* base, int64_t rows, int hd);
 cudaError_t attn_decode_prepare();
 
 // ------------------------------------------------------ prefill attention
