@@ -550,7 +550,11 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
     // Chunks of more than 256 rows first make an f16 copy of the weights
     // (read once), then the GEMM loads both operands with TMA; smaller
     // chunks dequantize weight tiles inside the GEMM.
-    const bool tma_b = M > 256;
+    static const int tmab_rows = [] {
+        const char* e = std::getenv("VVQ2_TMAB_ROWS");
+        return e ? std::atoi(e) : 256;
+    }();
+    const bool tma_b = M > tmab_rows;
     if (tma_b) {
         const vvq2_ctx::Layer& L0 = c->layers[first];
         const size_t need = std::max({(size_t)L0.qkv.rows * L0.qkv.cols, (size_t)L0.o.rows * L0.o.cols,

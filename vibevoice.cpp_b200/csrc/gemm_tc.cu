@@ -268,14 +268,82 @@ __global__ void __launch_bounds__(THREADS, 1)
             W = &a.w0;
             wrow = n0 + p;
         }
-        for (int kb = 0; !TMAB && kb < nk; ++kb) {   // local k-block index
-            const int s = kb % STAGES;
-            if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); break; }
-            if (*(volatile int*)&abort_flag) break;
-            uint8_t* bt = smem + s * STAGE_BYTES + 2 * TILE_BYTES;
-            produce_row<WT>(*W, wrow, (kb0 + kb) * BK, bt, p);
-            tc::fence_proxy_async_smem();
-            tc::mbar_arrive(&full[s]);
+        if constexpr (WT == W_Q8_0 && !TMAB) {
+            // Q8_0: the row's raw blocks are loaded PD k-blocks ahead of their
+            // conversion, so the global latency overlaps the MMAs instead of
+            // gating every k-block
+            constexpr int PD = 4;
+            const bool live = wrow >= 0 && wrow < W->rows;
+            const uint8_t* rp = W->q + (size_t)(live ? wrow : 0) * W->row_stride;
+            const unsigned short* dp = reinterpret_cast<const unsigned short*>(W->d) + (size_t)(live ? wrow : 0) * W->d_stride;
+            uint4 raw[PD][4];
+            uint32_t dd[PD];
+            auto fetch = [&](int kb, uint4 (&q)[4], uint32_t& d2) {
+                if (live && kb < nk) {
+                    const int k0 = (kb0 + kb) * BK;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) q[i] = __ldg(reinterpret_cast<const uint4*>(rp + k0) + i);
+                    d2 = __ldg(reinterpret_cast<const unsigned int*>(dp + k0 / 32));   // the two block scales
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) q[i] = make_uint4(0, 0, 0, 0);
+                    d2 = 0u;
+                }
+            };
+#pragma unroll
+            for (int d = 0; d < PD; ++d) fetch(d, raw[d], dd[d]);
+            bool stop = false;
+            for (int kb0l = 0; kb0l < nk && !stop; kb0l += PD) {
+#pragma unroll
+                for (int d = 0; d < PD; ++d) {
+                    const int kb = kb0l + d;
+                    if (kb >= nk) break;
+                    const int s = kb % STAGES;
+                    if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); stop = true; break; }
+                    if (*(volatile int*)&abort_flag) { stop = true; break; }
+                    uint8_t* bt = smem + s * STAGE_BYTES + 2 * TILE_BYTES;
+                    // int8 -> exact f16 (the byte q + 128 in the mantissa of 1024, minus 1152),
+                    // then one f16 multiply by the block scale: RN(q * d), the same value
+                    // as the exact f32 product rounded to f16
+                    const uint32_t dbits = dd[d];
+                    const __half2 s0 = __halves2half2(__ushort_as_half((unsigned short)(dbits & 0xffff)),
+                                                      __ushort_as_half((unsigned short)(dbits & 0xffff)));
+                    const __half2 s1 = __halves2half2(__ushort_as_half((unsigned short)(dbits >> 16)),
+                                                      __ushort_as_half((unsigned short)(dbits >> 16)));
+                    const __half2 off = __float2half2_rn(-1152.0f), one = __float2half2_rn(1.0f);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const __half2 sc = j < 4 ? s0 : s1;
+                        uint32_t o[4];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const uint32_t w = wsel(raw[d][j / 2], (j % 2) * 2 + h) ^ 0x80808080u;
+                            const uint32_t lo = __byte_perm(w, 0x64646464u, 0x5140);
+                            const uint32_t hi = __byte_perm(w, 0x64646464u, 0x7362);
+                            __half2 qlo = __hfma2(*reinterpret_cast<const __half2*>(&lo), one, off);
+                            __half2 qhi = __hfma2(*reinterpret_cast<const __half2*>(&hi), one, off);
+                            qlo = __hmul2(qlo, sc);
+                            qhi = __hmul2(qhi, sc);
+                            o[2 * h] = *reinterpret_cast<const uint32_t*>(&qlo);
+                            o[2 * h + 1] = *reinterpret_cast<const uint32_t*>(&qhi);
+                        }
+                        store_chunk(bt, p, j, make_uint4(o[0], o[1], o[2], o[3]));
+                    }
+                    fetch(kb + PD, raw[d], dd[d]);
+                    tc::fence_proxy_async_smem();
+                    tc::mbar_arrive(&full[s]);
+                }
+            }
+        } else {
+            for (int kb = 0; !TMAB && kb < nk; ++kb) {   // local k-block index
+                const int s = kb % STAGES;
+                if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); break; }
+                if (*(volatile int*)&abort_flag) break;
+                uint8_t* bt = smem + s * STAGE_BYTES + 2 * TILE_BYTES;
+                produce_row<WT>(*W, wrow, (kb0 + kb) * BK, bt, p);
+                tc::fence_proxy_async_smem();
+                tc::mbar_arrive(&full[s]);
+            }
         }
         (void)W;
         (void)wrow;
@@ -292,7 +360,69 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int t = t0 + acc * BM + r;
                 const bool valid = t < a.T;
                 const uint32_t tbase = tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-                if (a.kpart && EPI != EPI_ARGMAX && EPI != EPI_SWIGLU) {
+                if (EPI == EPI_RESID || EPI == EPI_STORE || EPI == EPI_SWIGLU || (EPI == EPI_QKV && a.kpart)) {
+                    // Staged through shared memory (the pipeline stages are free once
+                    // every MMA completed) so that global rows are written whole by a
+                    // warp: the warp's 32 rows x BN f32, 16-byte chunk j of row rr at
+                    // chunk (j & ~7) | ((j ^ rr) & 7) (conflict-free both ways).
+                    uint8_t* stg = smem + quarter * (32 * BN * 4);
+                    for (int c = 0; c < BN; c += 32) {
+                        float v[32];
+                        tc::tmem_ld32(tbase + c, v);
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const int j = c / 4 + k, pj = (j & ~7) | ((j ^ lane) & 7);
+                            *reinterpret_cast<float4*>(stg + lane * (BN * 4) + pj * 16) =
+                                make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+                        }
+                    }
+                    __syncwarp();
+                    for (int rr = 0; rr < 32; ++rr) {
+                        const int tr = t0 + acc * BM + quarter * 32 + rr;
+                        if (tr >= a.T) break;   // uniform in the warp
+                        if (EPI == EPI_SWIGLU) {
+                            // columns 0-63 gate, 64-127 up of features i0 .. i0+63; lane: 2 features
+                            const int i = blockIdx.x * 64 + 2 * lane;
+                            const int jg = lane >> 1, ju = 16 + (lane >> 1);
+                            const float4 g4 = *reinterpret_cast<const float4*>(
+                                stg + rr * (BN * 4) + ((jg & ~7) | ((jg ^ rr) & 7)) * 16);
+                            const float4 u4 = *reinterpret_cast<const float4*>(
+                                stg + rr * (BN * 4) + ((ju & ~7) | ((ju ^ rr) & 7)) * 16);
+                            const float g0 = (lane & 1) ? g4.z : g4.x, g1 = (lane & 1) ? g4.w : g4.y;
+                            const float u0 = (lane & 1) ? u4.z : u4.x, u1 = (lane & 1) ? u4.w : u4.y;
+                            __half* dst = a.yh + (size_t)tr * a.yh_stride + i;
+                            if (i + 1 < a.N)
+                                *reinterpret_cast<__half2*>(dst) =
+                                    __floats2half2_rn(__fmul_rn(silu_ref(g0), u0), __fmul_rn(silu_ref(g1), u1));
+                            else if (i < a.N)
+                                *dst = __float2half_rn(__fmul_rn(silu_ref(g0), u0));
+                        } else {
+                            const int pj = (lane & ~7) | ((lane ^ rr) & 7);
+                            float4 x = *reinterpret_cast<const float4*>(stg + rr * (BN * 4) + pj * 16);
+                            const int n = n0 + 4 * lane;
+                            float xv[4] = {x.x, x.y, x.z, x.w};
+                            if (a.kpart) {
+                                // split-K partial [z][T][N], summed by splitk_epilogue_launch
+                                float* dst = a.kpart + ((size_t)blockIdx.z * a.T + tr) * a.N + n;
+                                if (n + 3 < a.N && (a.N & 3) == 0) *reinterpret_cast<float4*>(dst) = x;
+                                else
+                                    for (int e = 0; e < 4; ++e)
+                                        if (n + e < a.N) dst[e] = xv[e];
+                            } else {
+                                float* dst = a.y + (size_t)tr * a.y_stride + n;
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    if (n + e < a.N) {
+                                        float v = xv[e];
+                                        if (a.bias) v = __fadd_rn(v, a.bias[n + e]);
+                                        dst[e] = (EPI == EPI_RESID) ? __fadd_rn(dst[e], v) : v;
+                                    }
+                                }
+                            }
+                        }
+                    }
+                    __syncwarp();   // the region is reused by the next accumulator
+                } else if (a.kpart && EPI != EPI_ARGMAX && EPI != EPI_SWIGLU) {
                     // split-K partial [z][T][N], summed by splitk_epilogue_launch
                     for (int c = 0; c < BN; c += 32) {
                         float v[32];
@@ -458,8 +588,19 @@ __global__ void k_splitk_epilogue(const GemmArgs a) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int t = (int)(i / per_row);
         auto sum = [&](int n) {
+            // in split order; eight independent loads in flight at a time
+            const float* kp = a.kpart + (size_t)t * a.N + n;
+            const size_t zs = (size_t)a.T * a.N;
             float v = 0.f;
-            for (int z = 0; z < ks; ++z) v += a.kpart[((size_t)z * a.T + t) * a.N + n];
+            int z = 0;
+            for (; z + 8 <= ks; z += 8) {
+                float p[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) p[i] = kp[(size_t)(z + i) * zs];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v += p[i];
+            }
+            for (; z < ks; ++z) v += kp[(size_t)z * zs];
             return v;
         };
         if (a.epi == EPI_QKV) {
