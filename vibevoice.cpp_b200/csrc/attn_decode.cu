@@ -58,6 +58,7 @@ __global__ void __launch_bounds__(HD / 4 * MG_SG) k_attn_merge(const AttnDecodeA
     constexpr int D4 = HD / 4;
     __shared__ float s_mx[MG_SG], s_den[MG_SG];
     __shared__ float4 s_num[MG_SG][D4];
+    asm volatile("griddepcontrol.launch_dependents;");   // see k_rmsnorm_f16
     const int h = blockIdx.x, m = blockIdx.y;
     const int tid = threadIdx.x, d4 = tid % D4, sg = tid / D4;
     const RowMeta rm = a.meta[m];

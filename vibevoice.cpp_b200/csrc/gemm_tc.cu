@@ -184,6 +184,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // a dependent GEMM may start its prologue and weight prefetch now (it waits
+    // for this grid before reading anything this grid writes)
+    asm volatile("griddepcontrol.launch_dependents;");
     const int n0 = blockIdx.x * BN, t0 = blockIdx.y * (2 * BM);
     const bool two = t0 + BM < a.T;
     // split-K: CTA z of gridDim.z takes k-blocks [kb0, kb0 + nk) and writes a
@@ -216,7 +219,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
 
     if (warp == 0 && lane == 0) {
-        // ---- TMA producer: activation tiles A0 (rows t0..) and A1 (rows t0+128..)
+        // ---- TMA producer: activation tiles A0 (rows t0..) and A1 (rows t0+128..).
+        // Launched as a programmatic dependent: everything above (barriers, TMEM,
+        // the weight producers' first fetches) overlapped the previous kernel;
+        // its outputs (A, a dequantized B copy) are read only after this wait.
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         for (int i = 0; i < nk; ++i) {
             const int s = i % STAGES, kx = (kb0 + i) * BK;
             if (i >= STAGES && !tc::mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) { fail(); break; }
@@ -377,9 +384,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                     }
                     __syncwarp();
+#pragma unroll 4
                     for (int rr = 0; rr < 32; ++rr) {
                         const int tr = t0 + acc * BM + quarter * 32 + rr;
-                        if (tr >= a.T) break;   // uniform in the warp
+                        if (tr >= a.T) continue;   // uniform in the warp
                         if (EPI == EPI_SWIGLU) {
                             // columns 0-63 gate, 64-127 up of features i0 .. i0+63; lane: 2 features
                             const int i = blockIdx.x * 64 + 2 * lane;
@@ -551,20 +559,33 @@ cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, const CUtensorM
                        cudaStream_t st) {
     dim3 grid((EPI == EPI_SWIGLU ? (a.N + 63) / 64 : (a.N + BN - 1) / BN), (a.T + 2 * BM - 1) / (2 * BM),
               a.kpart ? a.k_splits : 1);
+    // programmatic dependent launch: CTAs may start (prologue, weight
+    // prefetch) while the previous kernel drains; see griddepcontrol.wait
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
     if (b0) {
-        k_gemm_tc<W_F16, EPI, true><<<grid, THREADS, SMEM_BYTES, st>>>(tm, *b0, b1 ? *b1 : *b0, a);
+        e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F16, EPI, true>, tm, *b0, b1 ? *b1 : *b0, a);
     } else {
         switch (a.w0.type) {
-            case W_Q8_0: k_gemm_tc<W_Q8_0, EPI, false><<<grid, THREADS, SMEM_BYTES, st>>>(tm, tm, tm, a); break;
-            case W_Q5_K: k_gemm_tc<W_Q5_K, EPI, false><<<grid, THREADS, SMEM_BYTES, st>>>(tm, tm, tm, a); break;
-            case W_Q6_K: k_gemm_tc<W_Q6_K, EPI, false><<<grid, THREADS, SMEM_BYTES, st>>>(tm, tm, tm, a); break;
-            case W_F16: k_gemm_tc<W_F16, EPI, false><<<grid, THREADS, SMEM_BYTES, st>>>(tm, tm, tm, a); break;
-            case W_F32: k_gemm_tc<W_F32, EPI, false><<<grid, THREADS, SMEM_BYTES, st>>>(tm, tm, tm, a); break;
+            case W_Q8_0: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q8_0, EPI, false>, tm, tm, tm, a); break;
+            case W_Q5_K: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q5_K, EPI, false>, tm, tm, tm, a); break;
+            case W_Q6_K: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q6_K, EPI, false>, tm, tm, tm, a); break;
+            case W_F16: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F16, EPI, false>, tm, tm, tm, a); break;
+            case W_F32: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F32, EPI, false>, tm, tm, tm, a); break;
             default: return cudaErrorInvalidValue;
         }
     }
     note_launch();
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int EPI>

@@ -77,6 +77,9 @@ __global__ void k_rmsnorm(const float* x, const float* w, int n, float eps, floa
 __global__ void k_rmsnorm_f16(const float* x, const float* w, int n, float eps, __half* y) {
     __shared__ float red[32];
     __shared__ float scale_s;
+    // the next kernel (a GEMM launched as a programmatic dependent) may start its
+    // prologue now; it reads y only after griddepcontrol.wait
+    asm volatile("griddepcontrol.launch_dependents;");
     const float* xr = x + (size_t)blockIdx.x * n;
     float ss = 0.f;
     for (int k = threadIdx.x; k < n; k += blockDim.x) ss = fmaf(xr[k], xr[k], ss);
