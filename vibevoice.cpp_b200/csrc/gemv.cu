@@ -375,7 +375,7 @@ using SChunk = typename std::conditional<WT == W_Q8_0, Q8Raw, Chunk>::type;
 // register stages of weight loads per warp (by type and activation rows)
 template <int WT, int MB>
 struct SPipe {
-    static constexpr int P = WT == W_Q8_0 ? (MB == 1 ? 4 : 3) : WT == W_F32 ? 1 : 2;
+    static constexpr int P = WT == W_Q8_0 ? (MB == 1 ? 4 : 2) : WT == W_F32 ? 1 : 2;
 };
 
 template <int WT>
@@ -415,7 +415,9 @@ __device__ __forceinline__ void s_dot(const SChunk<WT>& ch, const float4 (&av)[M
         // Q8_0: signed quant, stored as q + 128; Q5_K: 0..31; Q6_K: q - 32 with q in 0..63
         constexpr float OFF = WT == W_Q8_0 ? -8388736.0f : WT == W_Q5_K ? -8388608.0f : -8388640.0f;
         const float2 off2 = make_float2(OFF, OFF);
-        float2 as[MB];
+        float2 as[MB], t[MB];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) t[m] = make_float2(0.f, 0.f);
 #pragma unroll
         for (int m = 0; m < MB; ++m) as[m] = make_float2(0.f, 0.f);
 #pragma unroll
@@ -439,8 +441,8 @@ __device__ __forceinline__ void s_dot(const SChunk<WT>& ch, const float4 (&av)[M
 #pragma unroll
             for (int m = 0; m < MB; ++m) {
                 const float2 a01 = make_float2(av[m][g].x, av[m][g].y), a23 = make_float2(av[m][g].z, av[m][g].w);
-                s[m] = __ffma2_rn(f01, a01, s[m]);
-                s[m] = __ffma2_rn(f23, a23, s[m]);
+                s[m] = __ffma2_rn(f01, a01, s[m]);    // two independent chains per row
+                t[m] = __ffma2_rn(f23, a23, t[m]);
                 if constexpr (WT == W_Q5_K) {
                     as[m] = __fadd2_rn(as[m], a01);
                     as[m] = __fadd2_rn(as[m], a23);
@@ -452,7 +454,7 @@ __device__ __forceinline__ void s_dot(const SChunk<WT>& ch, const float4 (&av)[M
         else d = ch.scale;
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
-            out[m] = __fmul_rn(d, s[m].x + s[m].y);
+            out[m] = __fmul_rn(d, (s[m].x + s[m].y) + (t[m].x + t[m].y));
             // Q5_K: w = d1 q - m1, so w.a = d1 (q.a) - m1 (sum a)
             if constexpr (WT == W_Q5_K) out[m] = fmaf(-ch.mscale, as[m].x + as[m].y, out[m]);
         }
@@ -519,8 +521,7 @@ __global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) 
     float4* act4 = reinterpret_cast<float4*>(sm_act);            // [(m * 4 + g) * NC + c]
     float* part = sm_act + (size_t)MB * K;                        // [(ul * NR + j) * niter + it][MB]
 
-    auto load_pair = [&](int p, SChunk<WT> (&dst)[NR]) {
-        const int ul = p / niter, it = p - ul * niter;
+    auto load_pair = [&](int ul, int it, SChunk<WT> (&dst)[NR]) {
         const int u = u0 + ul, c = it * 32 + lane;
         int r[NR], wh[NR];
         unit_rows<EPI>(a, u, r, wh);
@@ -533,9 +534,26 @@ __global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) 
 
     // weights do not depend on the previous kernel: start the stream first
     SChunk<WT> buf[P][NR];
+    // pairs as (unit, item): stage s of a round holds pair base + 16 s; a
+    // round advances the base by 16 P pairs (no divisions in the loop)
+    const int q16 = S_WARPS / niter, r16 = S_WARPS % niter;
+    auto step16 = [&](int& ul, int& it) {
+        ul += q16;
+        it += r16;
+        if (it >= niter) {
+            it -= niter;
+            ul += 1;
+        }
+    };
+    int bul = warp / niter, bit = warp % niter;   // this round's base pair
+    {
+        int ul = bul, it = bit;
 #pragma unroll
-    for (int s = 0; s < P; ++s)
-        if (warp + s * S_WARPS < npairs) load_pair(warp + s * S_WARPS, buf[s]);
+        for (int s = 0; s < P; ++s) {
+            if (ul < nu) load_pair(ul, it, buf[s]);
+            step16(ul, it);
+        }
+    }
     pdl_launch();
     pdl_wait();
     if (EPI == EPI_ARGMAX && tid < MB) best[tid] = 0ull;
@@ -585,12 +603,16 @@ __global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) 
     __syncthreads();
 
     // main loop: pair warp + (n + s) * 16 sits in register stage s
-    for (int n = 0; warp + n * S_WARPS < npairs; n += P) {
+    while (bul < nu) {
+        int ul = bul, it = bit;                 // pair of stage s
+        int nul = bul, nit = bit;               // pair of stage s in the next round
+#pragma unroll
+        for (int s = 0; s < P; ++s) step16(nul, nit);
+        bul = nul;
+        bit = nit;
 #pragma unroll
         for (int s = 0; s < P; ++s) {
-            const int p = warp + (n + s) * S_WARPS;
-            if (p < npairs) {
-                const int ul = p / niter, it = p - ul * niter;
+            if (ul < nu) {
                 const int c = it * 32 + lane;
                 float acc[NV];
                 if (c < NC) {
@@ -610,15 +632,16 @@ __global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) 
 #pragma unroll
                     for (int i = 0; i < NV; ++i) acc[i] = 0.f;
                 }
-                // the stage is free: request the pair P rounds ahead
-                const int pn = p + P * S_WARPS;
-                if (pn < npairs) load_pair(pn, buf[s]);
+                // the stage is free: request its pair of the next round
+                if (nul < nu) load_pair(nul, nit, buf[s]);
                 const float v = s_transpose_sum<NV>(acc, lane);
                 if ((lane & ((1 << SH) - 1)) == 0) {
                     const int idx = lane >> SH, j = idx / MB, m = idx % MB;
                     part[((size_t)(ul * NR + j) * niter + it) * MB + m] = v;
                 }
             }
+            step16(ul, it);
+            step16(nul, nit);
         }
     }
     __syncthreads();
