@@ -251,6 +251,103 @@ def run_c5(args, rank, local, world):
     return 0
 
 
+C4 = dict(hidden=1536, n_heads=12, n_kv_heads=2, head_dim=128, ffn=8960, n_layers=28, vocab=151936,
+          rope_theta=1.0e6, rms_eps=1.0e-6)
+
+
+def run_c4(args, rank, local, world):
+    """Config 4: the 1.5B-shaped stack (Q5_K attention, Q6_K FFN, Q8_0
+    lm_head), batch 2 (the CFG pair): causal prefill of args.c4_tokens prompt
+    embeddings per row, then greedy decode steps of both rows.  The prompt
+    embeddings stand for text-token embeddings plus projected acoustic
+    latents (the connector is not part of this path): N(0, 1) f32.  Each rank
+    runs its own replica (the config does not shard); times are CUDA events,
+    max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import synth
+    import vvq2
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+    hp = C4
+    eng = vvq2.Engine(hp, device=local)
+    rng = np.random.default_rng(SEED + 44)
+    wbytes = 0
+    for li in range(hp["n_layers"]):
+        L = synth.layer_c4_fast(rng, hp)
+        wbytes += sum(int(t[0].nbytes) for k, t in L.items() if t is not None and "norm" not in k and "bias" not in k)
+        eng.set_layer(li, L)
+    head = synth.q8_0_random_tensor(rng, hp["vocab"], hp["hidden"])
+    norm = synth.f32_tensor(1.0 + rng.standard_normal(hp["hidden"], dtype=np.float32) * 0.02)
+    eng.set_output(norm, head, head)
+    wbytes += int(head[0].nbytes)
+    T, steps = args.c4_tokens, args.c4_steps
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sh = stream.cuda_stream
+    kvw = eng.kv(2, 512)
+    eng.forward(kvw, [0, 1], np.zeros((2, 64, hp["hidden"]), np.float32), [0, 0], stream=sh)
+    kvw.close()
+    kv = eng.kv(2, T + steps + 16)
+    g = torch.Generator(device="cuda").manual_seed(SEED + 4)
+    x = torch.randn((2, T, hp["hidden"]), generator=g, device="cuda", dtype=torch.float32)
+    y = torch.empty((2, hp["hidden"]), device="cuda", dtype=torch.float32)
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    pre_ms = timed(lambda: eng.forward(kv, [0, 1], x, [0, 0], flags=vvq2.ADVANCE | vvq2.LAST_ONLY, y=y, stream=sh))
+    tok = torch.randint(0, hp["vocab"], (2,), dtype=torch.int32, device="cuda", generator=g)
+    for _ in range(3):
+        eng.decode_step(kv, [0, 1], tok, tok, stream=sh)
+    dec_ms = timed(lambda: [eng.decode_step(kv, [0, 1], tok, tok, stream=sh) for _ in range(steps)])
+    lin = 2.0 * 2 * T * hp["n_layers"] * hp["hidden"] * (
+        hp["n_heads"] * hp["head_dim"] + 2 * hp["n_kv_heads"] * hp["head_dim"] + hp["n_heads"] * hp["head_dim"]
+        + 3 * hp["ffn"])
+    att = 2 * 4.0 * hp["n_heads"] * hp["head_dim"] * T * (T + 1) / 2 * hp["n_layers"]
+    burst, _, kind = measured_tensor_peak()
+    hbm, hbm_kind = measured_peaks()
+    kv_len = T + 3 + steps / 2
+    step_bytes = wbytes + 2 * 4.0 * hp["n_layers"] * hp["n_kv_heads"] * hp["head_dim"] * kv_len
+    dec_s = dec_ms / 1000.0 / steps
+    line = {"impl": "ours", "metric": "qwen2_c4_prefill_decode", "workload":
+            f"config 4: 1.5B-shaped stack (28 layers, Q5_K attention, Q6_K FFN, Q8_0 lm_head), batch 2 (CFG pair), "
+            f"causal prefill of {T} prompt embeddings per row, then {steps} greedy decode steps", "n_gpus": world,
+            "parallelism": "replicas only (batch 2 does not shard)",
+            "prefill": {"tokens_per_s": round(2 * T / (pre_ms / 1000.0), 1), "ms": round(pre_ms, 2),
+                        "tflops": round((lin + att) / (pre_ms / 1000.0) / 1e12, 1),
+                        "frac_of_peak": round((lin + att) / (pre_ms / 1000.0) / 1e12 / burst, 4),
+                        "peak_tflops": burst, "peak_kind": kind},
+            "decode": {"tokens_per_s": round(2 * steps / (dec_ms / 1000.0), 1), "ms_per_step": round(dec_ms / steps, 3),
+                       "step_bytes": int(step_bytes), "step_hbm_gbs": round(step_bytes / dec_s / 1e9, 1),
+                       "frac_of_hbm": round(step_bytes / dec_s / 1e9 / hbm, 4), "peak_gbs": hbm, "peak_kind": hbm_kind},
+            "data": "synthetic (random Q5_K / Q6_K / Q8_0 blocks, N(0,1) prompt embeddings)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    kv.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -375,7 +472,9 @@ def main():
     ap.add_argument("--prefill-tokens", type=int, default=16384)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-c3", action="store_true")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5"])
+    ap.add_argument("--c4-tokens", type=int, default=1024)
+    ap.add_argument("--c4-steps", type=int, default=512)
     ap.add_argument("--c5-tokens", type=int, default=27000)
     ap.add_argument("--c5-steps", type=int, default=32)
     ap.add_argument("--c3-steps", type=int, default=10)
@@ -386,6 +485,8 @@ def main():
         return run_reference(args, rank)
     if args.workload == "c5":
         return run_c5(args, rank, local, world)
+    if args.workload == "c4":
+        return run_c4(args, rank, local, world)
 
     import torch
     import torch.distributed as dist

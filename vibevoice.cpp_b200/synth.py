@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import numpy as np
 
-F32, F16, Q8_0 = 0, 1, 8
+F32, F16, Q8_0, Q5_K, Q6_K = 0, 1, 8, 13, 14
 
 
 def _roundf(v: np.ndarray) -> np.ndarray:
@@ -95,6 +95,48 @@ def layer_q8_0_fast(rng, hp: dict) -> dict:
         "ffn_gate": q8_0_random_tensor(rng, F, H),
         "ffn_up": q8_0_random_tensor(rng, F, H),
         "ffn_down": q8_0_random_tensor(rng, H, F),
+    }
+
+
+def kquant_random_tensor(rng, qtype: int, rows: int, cols: int):
+    """Random Q5_K / Q6_K super-blocks for timing models: random quant and
+    scale bytes, f16 super-block scales chosen so that |w| stays below ~0.04
+    (the range of N(0, 0.02) weights).  Every byte pattern is a valid block."""
+    nb = rows * (cols // 256)
+    if qtype == Q5_K:
+        # block_q5_K: d, dmin (f16), scales[12] (6-bit sc/m), qh[32], qs[128]
+        raw = np.frombuffer(rng.bytes(nb * 176), np.uint8).reshape(nb, 176).copy()
+        d = (rng.uniform(0.8, 1.2, size=nb) * 2.0e-5).astype(np.float16)
+        dmin = (rng.uniform(0.8, 1.2, size=nb) * 1.0e-5).astype(np.float16)
+        raw[:, 0:2] = d.view(np.uint8).reshape(-1, 2)
+        raw[:, 2:4] = dmin.view(np.uint8).reshape(-1, 2)
+    elif qtype == Q6_K:
+        # block_q6_K: ql[128], qh[64], scales[16] (int8), d (f16)
+        raw = np.frombuffer(rng.bytes(nb * 210), np.uint8).reshape(nb, 210).copy()
+        d = (rng.uniform(0.8, 1.2, size=nb) * 1.0e-5).astype(np.float16)
+        raw[:, 208:210] = d.view(np.uint8).reshape(-1, 2)
+    else:
+        raise ValueError("qtype must be Q5_K or Q6_K")
+    return (raw.reshape(-1), qtype, cols, rows)
+
+
+def layer_c4_fast(rng, hp: dict) -> dict:
+    """Config-4 layer with random blocks: Q5_K attention, Q6_K FFN."""
+    H, nq, nkv, hd, F = hp["hidden"], hp["n_heads"], hp["n_kv_heads"], hp["head_dim"], hp["ffn"]
+    g = lambda *s: (rng.standard_normal(s, dtype=np.float32) * 0.02)
+    return {
+        "attn_norm": f32_tensor(1.0 + g(H)),
+        "attn_q": kquant_random_tensor(rng, Q5_K, nq * hd, H),
+        "attn_k": kquant_random_tensor(rng, Q5_K, nkv * hd, H),
+        "attn_v": kquant_random_tensor(rng, Q5_K, nkv * hd, H),
+        "attn_o": kquant_random_tensor(rng, Q5_K, H, nq * hd),
+        "attn_q_bias": f32_tensor(g(nq * hd)),
+        "attn_k_bias": f32_tensor(g(nkv * hd)),
+        "attn_v_bias": f32_tensor(g(nkv * hd)),
+        "ffn_norm": f32_tensor(1.0 + g(H)),
+        "ffn_gate": kquant_random_tensor(rng, Q6_K, F, H),
+        "ffn_up": kquant_random_tensor(rng, Q6_K, F, H),
+        "ffn_down": kquant_random_tensor(rng, Q6_K, H, F),
     }
 
 
