@@ -605,6 +605,24 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
     const int nq = c->pt.nq, nkv = c->pt.nkv;          // heads this rank holds (all, unpartitioned)
     const int F = c->pt.ffn, qw = hp.n_heads * hd, qw_l = nq * hd;   // F: this rank's FFN features
     const bool parted = c->pt.on();
+    // one-token rows of one or two sequences (a partitioned decode step): the
+    // linears are bandwidth-bound GEMVs, not 128-row tensor-core tiles
+    const bool gv = nt == 1 && M <= 2 && M <= c->max_rows;
+    GemvArgs gvb;
+    gvb.M = M;
+    gvb.meta = c->meta;
+    gvb.rope_meta = parted ? c->meta_rope : nullptr;
+    gvb.n_q_heads = nq;
+    gvb.n_kv_heads = nkv;
+    gvb.hd = hd;
+    gvb.rope_ts = c->rope_ts;
+    gvb.eps = hp.rms_norm_eps;
+    auto gemv = [&](const GemvArgs& g) -> int {
+        CU(R.begin());
+        CU(gemv_launch(g, st));
+        CU(R.end(0, (double)weight_bytes(g.w0) + (g.epi == EPI_SWIGLU ? (double)weight_bytes(g.w1) : 0.0)));
+        return 0;
+    };
     // RoPE from true positions (a later sequence part shifts meta.pos for its keys)
     CU(rope_table_launch(parted ? c->meta_rope : c->meta, M, hd, c->rope_ts, c->rope_cs, st));
     CUtensorMap mapX, mapA, mapF;
@@ -623,17 +641,32 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         g.rope_cs = c->rope_cs;
         g.err = c->err;
         // 1. RMSNorm -> f16, QKV GEMM (+bias, RoPE, K/V append; Q f32)
-        CU(rmsnorm_f16_launch(c->X, L.attn_norm, M, H, hp.rms_norm_eps, c->Xh, st));
-        GemmArgs q = g;
-        q.w0 = L.qkv;
-        q.N = L.qkv.rows;
-        q.K = H;
-        q.epi = EPI_QKV;
-        q.bias = L.qkv_bias;
-        q.y = c->Q;
-        q.y_stride = qw_l;
-        if (int rc = gemm(q, mapX)) return rc;
-        __half* att_out = parted ? c->ATTl : c->ATTh;        // this rank's heads
+        if (gv) {
+            GemvArgs q = gvb;
+            q.kv = kvl;
+            q.w0 = L.qkv;
+            q.K = H;
+            q.x = c->X;
+            q.x_stride = H;
+            q.norm_w = L.attn_norm;
+            q.bias = L.qkv_bias;
+            q.y = c->Q;
+            q.y_stride = qw_l;
+            q.epi = EPI_QKV;
+            if (int rc = gemv(q)) return rc;
+        } else {
+            CU(rmsnorm_f16_launch(c->X, L.attn_norm, M, H, hp.rms_norm_eps, c->Xh, st));
+            GemmArgs q = g;
+            q.w0 = L.qkv;
+            q.N = L.qkv.rows;
+            q.K = H;
+            q.epi = EPI_QKV;
+            q.bias = L.qkv_bias;
+            q.y = c->Q;
+            q.y_stride = qw_l;
+            if (int rc = gemm(q, mapX)) return rc;
+        }
+        __half* att_out = parted ? c->ATTl : (gv ? nullptr : c->ATTh);   // this rank's heads (gv: f32 c->ATT)
         float* att_lse = c->pt.seq_parts > 1 ? c->LSEl : nullptr;
         // 2. causal attention, f16 output: tcgen05 flash attention for prompt
         //    chunks (head_dim 64/128); rows of one token each (batched decode
@@ -665,6 +698,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         AttnDecodeArgs ad;
         ad.q = c->Q;
         ad.out_h = att_out;
+        ad.out = att_out ? nullptr : c->ATT;
         ad.lse = att_lse;
         ad.meta = c->meta;
         ad.kv = kvl;
@@ -717,6 +751,46 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
             } else {
                 CU(cudaMemcpyAsync(c->ATTh, c->ATTl, sizeof(__half) * M * qw, cudaMemcpyDeviceToDevice, st));
             }
+        }
+        if (gv) {
+            // 3-5 as GEMVs: O-proj + residual (replicated), RMSNorm + gate/up +
+            // SwiGLU over this rank's features, down (partial sums when partitioned)
+            if (parted) CU(half_to_float_launch(c->ATTh, c->ATT, (int64_t)M * qw, st));
+            GemvArgs o = gvb;
+            o.w0 = L.o;
+            o.K = qw;
+            o.x = c->ATT;
+            o.x_stride = qw;
+            o.y = c->X;
+            o.y_stride = H;
+            o.epi = EPI_RESID;
+            if (int rc = gemv(o)) return rc;
+            GemvArgs f = gvb;
+            f.w0 = L.gate;
+            f.w1 = L.up;
+            f.K = H;
+            f.x = c->X;
+            f.x_stride = H;
+            f.norm_w = L.ffn_norm;
+            f.y = c->FA;
+            f.y_stride = F;
+            f.epi = EPI_SWIGLU;
+            if (int rc = gemv(f)) return rc;
+            GemvArgs d = gvb;
+            d.w0 = L.down;
+            d.K = F;
+            d.x = c->FA;
+            d.x_stride = F;
+            d.y = parted ? c->Xp : c->X;
+            d.y_stride = H;
+            d.epi = parted ? EPI_STORE : EPI_RESID;
+            if (int rc = gemv(d)) return rc;
+            if (parted) {
+                if (ncclAllReduce(c->Xp, c->Xp, (size_t)M * H, ncclFloat, ncclSum, c->pt.comm, st) != ncclSuccess)
+                    return fail(VVQ2_ERR_CUDA, "NCCL all-reduce of the down projection failed");
+                CU(add_rows_launch(c->X, c->Xp, (int64_t)M * H, st));
+            }
+            continue;
         }
         // 3. O-proj + residual (replicated on partitioned ranks)
         GemmArgs o = g;
@@ -929,19 +1003,35 @@ int decode_step_batched(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, c
     if (int rc = run_layers_prefill(c, kv, M, M, 1, max_lim, 0, hp.n_layers, st, c->prof_on ? &recs : nullptr,
                                     attn_flops))
         return rc;
-    CU(rmsnorm_f16_launch(c->X, c->out_norm, M, H, hp.rms_norm_eps, c->Xh, st));
-    CUtensorMap mapX;
-    if (!make_act_map(&mapX, c->Xh, M, H)) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "hidden %d not a multiple of 64", H);
     CU(argmax_init_launch(c->amax, M, st));
-    GemmArgs g;
-    g.w0 = c->lm_head;
-    g.T = M;
-    g.N = c->lm_head.rows;
-    g.K = H;
-    g.epi = EPI_ARGMAX;
-    g.amax = c->amax;
-    g.err = c->err;
-    {
+    if (M <= 2 && M <= c->max_rows) {
+        // one or two rows: output norm + lm_head + argmax as one streaming GEMV
+        GemvArgs g;
+        g.w0 = c->lm_head;
+        g.M = M;
+        g.K = H;
+        g.x = c->X;
+        g.x_stride = H;
+        g.norm_w = c->out_norm;
+        g.eps = hp.rms_norm_eps;
+        g.argmax = c->amax;
+        g.epi = EPI_ARGMAX;
+        Recorder R{c, st, c->prof_on ? &recs : nullptr};
+        CU(R.begin());
+        CU(gemv_launch(g, st));
+        CU(R.end(0, (double)weight_bytes(c->lm_head)));
+    } else {
+        CU(rmsnorm_f16_launch(c->X, c->out_norm, M, H, hp.rms_norm_eps, c->Xh, st));
+        CUtensorMap mapX;
+        if (!make_act_map(&mapX, c->Xh, M, H)) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "hidden %d not a multiple of 64", H);
+        GemmArgs g;
+        g.w0 = c->lm_head;
+        g.T = M;
+        g.N = c->lm_head.rows;
+        g.K = H;
+        g.epi = EPI_ARGMAX;
+        g.amax = c->amax;
+        g.err = c->err;
         Recorder R{c, st, c->prof_on ? &recs : nullptr};
         CU(R.begin());
         CU(gemm_tc_launch(g, mapX, st));

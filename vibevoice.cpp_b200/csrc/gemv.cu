@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
         const int half = a.hd / 2;
         for (int t = threadIdx.x; t < M * half; t += GEMV_THREADS) {
             const int m = t / half, i = t % half;
-            float th = (float)a.meta[m].pos;
+            float th = (float)(a.rope_meta ? a.rope_meta : a.meta)[m].pos;   // true position (partitioned ranks shift meta.pos)
             for (int k = 0; k < i; ++k) th = __fmul_rn(th, a.rope_ts);
             rope_c[m][i] = cosf(th);
             rope_s[m][i] = sinf(th);
@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) 
         const int half = a.hd / 2;
         for (int t = tid; t < MB * half; t += S_THREADS) {
             const int m = t / half, i = t % half;
-            float th = (float)a.meta[m].pos;
+            float th = (float)(a.rope_meta ? a.rope_meta : a.meta)[m].pos;   // true position (partitioned ranks shift meta.pos)
             for (int k = 0; k < i; ++k) th = __fmul_rn(th, a.rope_ts);
             rope_c[m][i] = cosf(th);
             rope_s[m][i] = sinf(th);

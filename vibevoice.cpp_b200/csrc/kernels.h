@@ -36,6 +36,7 @@ struct GemvArgs {
     KvLayer kv;
     int n_q_heads = 0, n_kv_heads = 0, hd = 0;
     float rope_ts = 0.f;
+    const RowMeta* rope_meta = nullptr;   // RoPE positions if not meta's (a later sequence part)
     unsigned long long* argmax = nullptr;
     int wpu = 1;                   // warps per unit (set by gemv_launch)
 };
@@ -170,6 +171,7 @@ cudaError_t lse_merge_launch(const __half* o2, const float* l2, int64_t rows, in
                              cudaStream_t st);
 // x += y over n floats
 cudaError_t add_rows_launch(float* x, const float* y, int64_t n, cudaStream_t st);
+cudaError_t half_to_float_launch(const __half* x, float* y, int64_t n, cudaStream_t st);
 // [parts][rows][w] -> [rows][parts*w]
 cudaError_t gather_rows_launch(const __half* in, int64_t rows, int parts, int w, __half* out, cudaStream_t st);
 // ... to f16 [rows][cols] (exact dequantized value, rounded once)

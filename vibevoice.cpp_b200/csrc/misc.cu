@@ -221,6 +221,17 @@ __global__ void k_add_rows(float* x, const float* y, int64_t n) {
         x[i] = __fadd_rn(x[i], y[i]);
 }
 
+__global__ void k_half_to_float(const __half* x, float* y, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = __half2float(x[i]);
+}
+
+cudaError_t half_to_float_launch(const __half* x, float* y, int64_t n, cudaStream_t st) {
+    k_half_to_float<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
+    note_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t add_rows_launch(float* x, const float* y, int64_t n, cudaStream_t st) {
     k_add_rows<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
     note_launch();
