@@ -348,6 +348,68 @@ def run_c4(args, rank, local, world):
     return 0
 
 
+def run_case(args):
+    """Small single-GPU workloads for kernel profiles (a few GB on the device):
+    * decode7b: config-5 dims with args.case_layers layers and a small vocab,
+      args.kv keys of N(0,1) K/V per layer, then warm-up + timed greedy
+      decode steps of one row through vvq2_decode_step (GEMV graph path:
+      k_gemv_stream, k_attn_mma, k_attn_merge);
+    * c3: config 3's batched step (128 rows, ragged KV) -- tensor-core GEMMs
+      and the tensor-core decode attention.
+    Prints one JSON line with the mean step time (CUDA events)."""
+    import torch
+
+    import synth
+    import vvq2
+
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    if args.case == "c3":
+        hp = C2
+        model = synth.model_q8_0(SEED, hp)
+        eng = vvq2.Engine(hp, device=0)
+        for li, t in enumerate(model["layers"]):
+            eng.set_layer(li, t)
+        eng.set_output(model["output_norm"], model["lm_head"], model["tok_embd"])
+        r = c3_measure(eng, hp, torch, None, 0, 1, stream.cuda_stream, args.steps, warmup=args.warmup)
+        print(json.dumps({"case": "c3", "ms_per_step": r["ms_per_step"], "tokens_per_s": r["value"]}), flush=True)
+        return 0
+    hp = dict(C5)
+    hp["n_layers"] = args.case_layers
+    hp["vocab"] = 8192
+    eng = vvq2.Engine(hp, device=0)
+    rng = np.random.default_rng(SEED + 55)
+    for li in range(hp["n_layers"]):
+        eng.set_layer(li, synth.layer_q8_0_fast(rng, hp))
+    head = synth.q8_0_random_tensor(rng, hp["vocab"], hp["hidden"])
+    norm = synth.f32_tensor(1.0 + rng.standard_normal(hp["hidden"], dtype=np.float32) * 0.02)
+    eng.set_output(norm, head, head)
+    T = args.kv
+    kv = eng.kv(1, T + args.warmup + args.steps + 8)
+    w = hp["n_kv_heads"] * hp["head_dim"]
+    g = torch.Generator(device="cuda").manual_seed(SEED + 7)
+    for li in range(hp["n_layers"]):
+        kv.load_prefix(0, li, torch.randn((T, w), generator=g, device="cuda"),
+                       torch.randn((T, w), generator=g, device="cuda"))
+    kv.set_past_len(0, T)
+    tok = torch.randint(0, hp["vocab"], (1,), dtype=torch.int32, device="cuda", generator=g)
+    sh = stream.cuda_stream
+    for _ in range(args.warmup):
+        eng.decode_step(kv, [0], tok, tok, stream=sh)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        eng.decode_step(kv, [0], tok, tok, stream=sh)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    print(json.dumps({"case": "decode7b", "layers": hp["n_layers"], "kv": T,
+                      "ms_per_step": round(e0.elapsed_time(e1) / args.steps, 4)}), flush=True)
+    kv.close()
+    return 0
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -473,6 +535,9 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-c3", action="store_true")
     ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5"])
+    ap.add_argument("--case", default=None, choices=["decode7b", "c3"],
+                    help="small single-GPU workload for kernel profiles (see run_case)")
+    ap.add_argument("--case-layers", type=int, default=2)
     ap.add_argument("--c4-tokens", type=int, default=1024)
     ap.add_argument("--c4-steps", type=int, default=512)
     ap.add_argument("--c5-tokens", type=int, default=27000)
@@ -483,6 +548,8 @@ def main():
     rank, local, world = dist_env()
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.case:
+        return run_case(args)
     if args.workload == "c5":
         return run_c5(args, rank, local, world)
     if args.workload == "c4":
