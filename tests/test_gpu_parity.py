@@ -194,6 +194,30 @@ def test_long_context_decode_hd128(vv, rows, kv_len):
     assert rel_err(got, ref) < TOL, rel_err(got, ref)
 
 
+@pytest.mark.parametrize("rows", [1, 2])
+def test_kquant_decode_c4_shape(vv, rows):
+    """Config 4 decode: one token per row (the streaming GEMV for one or two
+    rows) over Q5_K attention and Q6_K FFN weights, hd 128, KV 300."""
+    rng = np.random.default_rng(4400 + rows)
+    hp = dict(hidden=1536, n_heads=12, n_kv_heads=2, head_dim=128, ffn=8960, n_layers=1, vocab=0,
+              rope_theta=1.0e6, rms_eps=1.0e-6)
+    t = random_layer(rng, hp, attn_type=O.Q5_K, ffn_type=O.Q6_K)
+    eng, kv, ora = _pair(vv, hp, [t], rows, 320, GPU_MODE)
+    w = hp["n_kv_heads"] * hp["head_dim"]
+    for s in range(rows):
+        k = rng.standard_normal((299, w)).astype(np.float32)
+        v = rng.standard_normal((299, w)).astype(np.float32)
+        kv.load_prefix(s, 0, k, v)
+        ora.kv_load(s, 0, k, v)
+        kv.set_past_len(s, 299)
+        ora.set_past_len(s, 299)
+    x = rng.standard_normal((rows, 1, hp["hidden"])).astype(np.float32)
+    seqs = list(range(rows))
+    got = eng.forward(kv, seqs, x, [299] * rows)
+    ref = ora.forward(seqs, x, [299] * rows)
+    assert rel_err(got, ref) < TOL, rel_err(got, ref)
+
+
 def test_ragged_sequences_and_last_only(vv):
     """Two sequences at different past lengths in one call; LAST_ONLY output."""
     import vvq2
