@@ -137,9 +137,10 @@ __global__ void __launch_bounds__(HD / 4 * MG_SG) k_attn_merge(const AttnDecodeA
 //                  warp's 16 keys; P^T is exactly the S accumulator layout
 //                  (rounded to f16), V^T comes from ldmatrix.trans.
 // K/V pages arrive by TMA (64 x 64 boxes, 128-byte swizzle: 16-byte chunk c
-// of key row r sits at chunk c ^ (r & 7)), double-buffered.  At the end the
+// of key row r sits at chunk c ^ (r & 7)), AM_STAGES pages in flight.  At the end the
 // four warps' (max, sum, O) combine through shared memory.
 constexpr int AM_THREADS = 128;
+constexpr int AM_STAGES = 3;          // pages of K and V in flight per CTA
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
@@ -182,7 +183,7 @@ __global__ void __launch_bounds__(AM_THREADS) k_attn_mma(const __grid_constant__
     constexpr int KS = HD / 16;                 // k-steps of S, m-tiles of O^T
     extern __shared__ __align__(1024) uint8_t dsm[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ __align__(8) uint64_t bar[AM_STAGES];
     __shared__ float cm[4][8], cl[4][8];
     const int s = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -208,7 +209,7 @@ __global__ void __launch_bounds__(AM_THREADS) k_attn_mma(const __grid_constant__
     const uint32_t sbase = tc::smem_u32(sm);   // stage b: K at b * 2 * TILE_BYTES, V after it
 
     auto issue = [&](int t) {
-        const int b = t & 1;
+        const int b = t % AM_STAGES;
         const int page = __ldg(a.kv.block_table + (size_t)rm.seq * a.kv.max_pages + (j0 + t * TILE) / TILE);
         const int y = (page * a.kv.n_kv + g) * TILE;
         uint8_t* kd = sm + b * 2 * TILE_BYTES;
@@ -220,11 +221,10 @@ __global__ void __launch_bounds__(AM_THREADS) k_attn_mma(const __grid_constant__
         }
     };
     if (tid == 0) {
-        tc::mbar_init(&bar[0], 1);
-        tc::mbar_init(&bar[1], 1);
+        for (int i = 0; i < AM_STAGES; ++i) tc::mbar_init(&bar[i], 1);
         tc::mbar_fence_init();
         issue(0);
-        if (ntiles > 1) issue(1);
+        for (int i = 1; i < AM_STAGES && i < ntiles; ++i) issue(i);
     }
 
     // Q fragments (A of S): row r = lane / 4 is query head g * G + r (zero
@@ -260,8 +260,8 @@ __global__ void __launch_bounds__(AM_THREADS) k_attn_mma(const __grid_constant__
 
     int t = 0;
     for (; t < ntiles; ++t) {
-        const int b = t & 1;
-        const bool ok = tc::mbar_wait(&bar[b], (t >> 1) & 1);
+        const int b = t % AM_STAGES;
+        const bool ok = tc::mbar_wait(&bar[b], (t / AM_STAGES) & 1);
         if (__syncthreads_or(!ok)) {   // uniform: every warp leaves the loop together
             if (tid == 0 && a.err) atomicExch(a.err, 1);
             break;
@@ -333,15 +333,16 @@ __global__ void __launch_bounds__(AM_THREADS) k_attn_mma(const __grid_constant__
             mma16816(oacc[mt], af, pb[0], pb[1]);
         }
         __syncthreads();   // every warp is done with stage b
-        if (tid == 0 && t + 2 < ntiles) {
+        if (tid == 0 && t + AM_STAGES < ntiles) {
             tc::fence_proxy_async_smem();
-            issue(t + 2);
+            issue(t + AM_STAGES);
         }
     }
     if (t < ntiles) {
         // a wait gave up: wait (bounded) for the copies still in flight, then leave
         if (tid == 0)
-            for (int tt = t; tt < min(ntiles, t + 2); ++tt) tc::mbar_wait(&bar[tt & 1], (tt >> 1) & 1);
+            for (int tt = t; tt < min(ntiles, t + AM_STAGES); ++tt)
+                tc::mbar_wait(&bar[tt % AM_STAGES], (tt / AM_STAGES) & 1);
         __syncthreads();
         return;
     }
@@ -401,7 +402,7 @@ cudaError_t launch_hd(const AttnDecodeArgs& a0, cudaStream_t st) {
         if (a.kv.n_pages > 0 && make_kv_map(&mk, a.kv.k, rows, HD) && make_kv_map(&mv, a.kv.v, rows, HD)) {
             a.defer_merge = a.max_splits > 1;
             dim3 grid(a.max_splits, a.nkv, a.M);
-            k_attn_mma<HD><<<grid, AM_THREADS, 4 * TILE * HD * 2 + 1024, st>>>(mk, mv, a);
+            k_attn_mma<HD><<<grid, AM_THREADS, 2 * AM_STAGES * TILE * HD * 2 + 1024, st>>>(mk, mv, a);
             note_launch();
             if (a.defer_merge) {
                 k_attn_merge<HD><<<dim3(a.nq, a.M), HD / 4 * MG_SG, 0, st>>>(a);
@@ -428,8 +429,8 @@ cudaError_t attn_decode_prepare() {
     if ((e = cudaFuncSetAttribute(k_attn_decode<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ad::tile_smem_bytes(32))) != cudaSuccess) return e;
     if ((e = cudaFuncSetAttribute(k_attn_decode<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, ad::tile_smem_bytes(64))) != cudaSuccess) return e;
     if ((e = cudaFuncSetAttribute(k_attn_decode<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, ad::tile_smem_bytes(128))) != cudaSuccess) return e;
-    if ((e = cudaFuncSetAttribute(k_attn_mma<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * TILE * 64 * 2 + 1024)) != cudaSuccess) return e;
-    return cudaFuncSetAttribute(k_attn_mma<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * TILE * 128 * 2 + 1024);
+    if ((e = cudaFuncSetAttribute(k_attn_mma<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * AM_STAGES * TILE * 64 * 2 + 1024)) != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_attn_mma<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * AM_STAGES * TILE * 128 * 2 + 1024);
 }
 
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st) {
