@@ -327,7 +327,7 @@ __device__ __forceinline__ void tile_dot(const uint8_t* tile, int rs, int K, con
             for (int m = 0; m < MB; ++m) s[m] = make_float2(0.f, 0.f);
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
-                const uint32_t w = word(q, g) ^ 0x80808080u;   // q + 128 as unsigned bytes
+                const uint32_t w = word(q, g);   // the device layout stores q + 128 as unsigned bytes
                 float2 f01 = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440)),
                                          __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441)));
                 float2 f23 = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7442)),
@@ -858,7 +858,7 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
             if (r >= 0 && r < E.rows) {
                 const uint8_t* rp = E.q + (size_t)r * E.row_stride;
                 const float d = __half2float(*reinterpret_cast<const __half*>(rp + H + (k / 32) * 2));
-                v = __fmul_rn((float)reinterpret_cast<const int8_t*>(rp)[k], d);
+                v = __fmul_rn((float)((int)rp[k] - 128), d);   // quants stored as q + 128
             }
             a.X[t] = v;
         }

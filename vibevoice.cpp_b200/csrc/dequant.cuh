@@ -15,7 +15,7 @@ namespace vvq2 {
 __device__ __forceinline__ float deq_elem(const DevW& w, int row, int e) {
     switch (w.type) {
         case W_Q8_0: {
-            const int8_t q = reinterpret_cast<const int8_t*>(w.q + (size_t)row * w.row_stride)[e];
+            const int q = (int)(w.q + (size_t)row * w.row_stride)[e] - 128;   // stored biased: q + 128
             const float d = __half2float(w.d[(size_t)row * w.d_stride + e / 32]);
             return __fmul_rn((float)q, d);
         }

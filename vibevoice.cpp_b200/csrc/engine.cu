@@ -305,7 +305,10 @@ int upload_tensor(vvq2_ctx* c, const vvq2_tensor& t, DevW* out, int expect_ne0, 
     switch (t.type) {
         case W_Q8_0:
             // one row = [cols quants][nb f16 scales, padded to 16 bytes]: a run of
-            // rows is one contiguous, 16-byte aligned range (one bulk copy)
+            // rows is one contiguous, 16-byte aligned range (one bulk copy).  Quants
+            // are stored biased, q + 128 as an unsigned byte: the kernels turn a
+            // byte b into the exact float 2^23 + b with one byte permute, so the
+            // bias saves them an XOR per word
             w.row_stride = cols + (nb * 2 + 15) / 16 * 16;
             w.d_stride = w.row_stride / 2;
             q.assign((size_t)rows * w.row_stride, 0);
@@ -313,7 +316,8 @@ int upload_tensor(vvq2_ctx* c, const vvq2_tensor& t, DevW* out, int expect_ne0, 
                 for (int64_t b = 0; b < nb; ++b) {
                     const uint8_t* blk = src + ((size_t)r * nb + b) * 34;
                     memcpy(&q[(size_t)r * w.row_stride + cols + b * 2], blk, 2);
-                    memcpy(&q[(size_t)r * w.row_stride + b * 32], blk + 2, 32);
+                    uint8_t* qd = &q[(size_t)r * w.row_stride + b * 32];
+                    for (int i = 0; i < 32; ++i) qd[i] = (uint8_t)(blk[2 + i] ^ 0x80u);   // int8 q -> q + 128
                 }
             break;
         case W_Q6_K:

@@ -79,10 +79,10 @@ __device__ __forceinline__ void produce_row(const DevW& W, int row, int k0, uint
             const float d = j < 4 ? d0 : d1;
             const uint32_t w0 = wsel(q[j / 2], (j % 2) * 2), w1 = wsel(q[j / 2], (j % 2) * 2 + 1);
             uint4 o;
-            o.x = pack_h2(__fmul_rn((float)(int8_t)(w0 & 0xff), d), __fmul_rn((float)(int8_t)((w0 >> 8) & 0xff), d));
-            o.y = pack_h2(__fmul_rn((float)(int8_t)((w0 >> 16) & 0xff), d), __fmul_rn((float)(int8_t)(w0 >> 24), d));
-            o.z = pack_h2(__fmul_rn((float)(int8_t)(w1 & 0xff), d), __fmul_rn((float)(int8_t)((w1 >> 8) & 0xff), d));
-            o.w = pack_h2(__fmul_rn((float)(int8_t)((w1 >> 16) & 0xff), d), __fmul_rn((float)(int8_t)(w1 >> 24), d));
+            o.x = pack_h2(__fmul_rn((float)((int)(w0 & 0xff) - 128), d), __fmul_rn((float)((int)((w0 >> 8) & 0xff) - 128), d));
+            o.y = pack_h2(__fmul_rn((float)((int)((w0 >> 16) & 0xff) - 128), d), __fmul_rn((float)((int)(w0 >> 24) - 128), d));
+            o.z = pack_h2(__fmul_rn((float)((int)(w1 & 0xff) - 128), d), __fmul_rn((float)((int)((w1 >> 8) & 0xff) - 128), d));
+            o.w = pack_h2(__fmul_rn((float)((int)((w1 >> 16) & 0xff) - 128), d), __fmul_rn((float)((int)(w1 >> 24) - 128), d));
             store_chunk(btile, p, j, o);
         }
     } else if constexpr (WT == W_Q5_K) {
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); stop = true; break; }
                     if (*(volatile int*)&abort_flag) { stop = true; break; }
                     uint8_t* bt = smem + s * STAGE_BYTES + 2 * TILE_BYTES;
-                    // int8 -> exact f16 (the byte q + 128 in the mantissa of 1024, minus 1152),
+                    // quant -> exact f16 (the stored byte q + 128 in the mantissa of 1024, minus 1152),
                     // then one f16 multiply by the block scale: RN(q * d), the same value
                     // as the exact f32 product rounded to f16
                     const uint32_t dbits = dd[d];
@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         uint32_t o[4];
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
-                            const uint32_t w = wsel(raw[d][j / 2], (j % 2) * 2 + h) ^ 0x80808080u;
+                            const uint32_t w = wsel(raw[d][j / 2], (j % 2) * 2 + h);   // q + 128 bytes
                             const uint32_t lo = __byte_perm(w, 0x64646464u, 0x5140);
                             const uint32_t hi = __byte_perm(w, 0x64646464u, 0x7362);
                             __half2 qlo = __hfma2(*reinterpret_cast<const __half2*>(&lo), one, off);

@@ -412,7 +412,7 @@ __device__ __forceinline__ void s_dot(const SChunk<WT>& ch, const float4 (&av)[M
 #pragma unroll
     for (int m = 0; m < MB; ++m) s[m] = make_float2(0.f, 0.f);
     if constexpr (WT == W_Q8_0 || WT == W_Q5_K || WT == W_Q6_K) {
-        // Q8_0: signed quant, stored as q + 128; Q5_K: 0..31; Q6_K: q - 32 with q in 0..63
+        // Q8_0: stored as the unsigned byte q + 128; Q5_K: 0..31; Q6_K: q - 32 with q in 0..63
         constexpr float OFF = WT == W_Q8_0 ? -8388736.0f : WT == W_Q5_K ? -8388608.0f : -8388640.0f;
         const float2 off2 = make_float2(OFF, OFF);
         float2 as[MB], t[MB];
@@ -424,7 +424,7 @@ __device__ __forceinline__ void s_dot(const SChunk<WT>& ch, const float4 (&av)[M
         for (int g = 0; g < 4; ++g) {
             uint32_t w;
             if constexpr (WT == W_Q8_0) {
-                w = gd::word(ch.q, g) ^ 0x80808080u;
+                w = gd::word(ch.q, g);   // bytes are q + 128 (device layout)
             } else if constexpr (WT == W_Q5_K) {
                 const int j = ch.shift;
                 w = ((gd::word(ch.r0, g) >> (4 * (j & 1))) & 0x0F0F0F0Fu) |

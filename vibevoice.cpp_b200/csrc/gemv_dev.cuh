@@ -75,7 +75,7 @@ __device__ __forceinline__ void expand4(const Chunk& ch, int g, float* w) {
     if constexpr (WT == W_Q8_0) {
         const uint32_t q = word(ch.r0, g);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) w[e] = __fmul_rn((float)(int8_t)((q >> (8 * e)) & 0xff), ch.scale);
+        for (int e = 0; e < 4; ++e) w[e] = __fmul_rn((float)((int)((q >> (8 * e)) & 0xff) - 128), ch.scale);   // q + 128 stored
     } else if constexpr (WT == W_Q5_K) {
         const int j = ch.shift;
         const uint32_t q = ((word(ch.r0, g) >> (4 * (j & 1))) & 0x0F0F0F0Fu) |
