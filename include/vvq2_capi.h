@@ -157,6 +157,23 @@ int  vvq2_forward(vvq2_ctx* ctx, vvq2_kv* kv, const int* seqs, int n_seqs, int n
 int  vvq2_lm_head(vvq2_ctx* ctx, int n, const float* h, float* logits, int32_t* argmax,
                   void* stream);
 
+/* ---- per-frame heads around the stack (src/vibevoice_tts.cpp:464-537) ----
+ * SpeechConnector: y = fc2(rms_norm(fc1(x) + b1) * norm) + b2, eps 1e-6
+ * (run_speech_connector): x f32 [batch][latent] -> y f32 [batch][hidden];
+ * fc1 has ne0 = latent, ne1 = hidden; fc2 ne0 = ne1 = hidden; biases are
+ * optional (data == NULL).  EOS classifier: p = sigmoid(fc2(relu(fc1(x) + b1))
+ * + b2) (run_eos_classifier): x f32 [batch][hidden] -> p f32 [batch]; fc1 has
+ * ne0 = hidden, ne1 = inner; fc2 ne0 = inner, ne1 = 1.  Weights in any type
+ * the layers take (F32, F16, Q8_0, Q5_K, Q6_K); input dims must be multiples
+ * of 16 (32 for Q8_0, 256 for K-quants); batch <= 8.  x, y and p may be host
+ * or device pointers; with a host output the call returns when it is written. */
+int  vvq2_set_connector(vvq2_ctx* ctx, const vvq2_tensor* fc1_w, const vvq2_tensor* fc1_b,
+                        const vvq2_tensor* norm_w, const vvq2_tensor* fc2_w, const vvq2_tensor* fc2_b);
+int  vvq2_connector(vvq2_ctx* ctx, const float* x, int batch, float* y, void* stream);
+int  vvq2_set_eos(vvq2_ctx* ctx, const vvq2_tensor* fc1_w, const vvq2_tensor* fc1_b,
+                  const vvq2_tensor* fc2_w, const vvq2_tensor* fc2_b);
+int  vvq2_eos(vvq2_ctx* ctx, const float* x, int batch, float* p, void* stream);
+
 /* Token-embedding rows (dequantized tok_embd rows), f32 [n][hidden]. */
 int  vvq2_embed(vvq2_ctx* ctx, int n, const int32_t* tokens, float* out, void* stream);
 

@@ -144,6 +144,51 @@ def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     return y
 
 
+def _vec(spec):
+    """f32 vector of an optional (raw, type, ne0, ne1) bias / norm spec."""
+    if spec is None or spec[0] is None:
+        return None
+    raw, qt, ne0, ne1 = spec
+    return dequantize(qt, raw, ne0 * max(ne1, 1))
+
+
+def connector(x: np.ndarray, fc1, fc1_b, norm, fc2, fc2_b, flags: int = 0) -> np.ndarray:
+    """SpeechConnector (src/vibevoice_tts.cpp:464-501, run_speech_connector):
+    y = fc2(rms_norm(fc1(x) + b1, eps 1e-6) * norm) + b2, per row of x [batch][latent];
+    fc* are (raw GGUF bytes, type, ne0, ne1) specs."""
+    x = np.atleast_2d(np.asarray(x, np.float32))
+    b1, g, b2 = _vec(fc1_b), _vec(norm), _vec(fc2_b)
+    out = []
+    for row in x:
+        h = matvec(fc1[0], fc1[1], fc1[2], fc1[3], row, flags)
+        if b1 is not None:
+            h = (h + b1).astype(np.float32)
+        h = rms_norm(h, g if g is not None else np.ones_like(h), 1e-6)
+        y = matvec(fc2[0], fc2[1], fc2[2], fc2[3], h, flags)
+        if b2 is not None:
+            y = (y + b2).astype(np.float32)
+        out.append(y)
+    return np.stack(out)
+
+
+def eos(x: np.ndarray, fc1, fc1_b, fc2, fc2_b, flags: int = 0) -> np.ndarray:
+    """EOS classifier (src/vibevoice_tts.cpp:503-537, run_eos_classifier):
+    p = sigmoid(fc2(relu(fc1(x) + b1)) + b2) per row of x [batch][hidden]."""
+    x = np.atleast_2d(np.asarray(x, np.float32))
+    b1, b2 = _vec(fc1_b), _vec(fc2_b)
+    out = []
+    for row in x:
+        h = matvec(fc1[0], fc1[1], fc1[2], fc1[3], row, flags)
+        if b1 is not None:
+            h = (h + b1).astype(np.float32)
+        h = np.maximum(h, np.float32(0))
+        z = matvec(fc2[0], fc2[1], fc2[2], fc2[3], h, flags)
+        if b2 is not None:
+            z = (z + b2).astype(np.float32)
+        out.append(np.float32(1) / (np.float32(1) + np.exp(-z.astype(np.float32))))
+    return np.concatenate(out).astype(np.float32)
+
+
 def rope_neox(x: np.ndarray, pos: int, theta: float, flags: int) -> np.ndarray:
     """x [n_heads, hd] at one position."""
     x = np.ascontiguousarray(x, np.float32)

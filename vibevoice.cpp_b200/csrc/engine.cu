@@ -177,6 +177,12 @@ struct vvq2_ctx {
     std::vector<Layer> layers;
     float* out_norm = nullptr;
     DevW lm_head, tok_embd;
+    // per-frame heads around the stack: speech connector and EOS classifier
+    struct Head {
+        DevW fc1, fc2;
+        float *b1 = nullptr, *norm = nullptr, *b2 = nullptr;
+        float *xin = nullptr, *mid = nullptr, *out = nullptr;   // [GEMV_MAX_M] rows of in / mid / out
+    } conn, eos;
     std::vector<void*> allocs;
     // scratch for up to GEMV_MAX_M activation rows
     float *X = nullptr, *Q = nullptr, *ATT = nullptr, *FA = nullptr, *LOGITS = nullptr;
@@ -1151,6 +1157,75 @@ int enqueue_decode_mega(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, cudaStream
 
 // ======================================================================= C ABI
 
+namespace {
+
+// Upload one per-frame head: fc1 [mid][in] (+ b1), optional norm [mid], fc2
+// [out][mid] (+ b2); scratch rows for GEMV_MAX_M frames.
+int set_head(vvq2_ctx* c, vvq2_ctx::Head* h, const vvq2_tensor* fc1, const vvq2_tensor* b1, const vvq2_tensor* norm,
+             const vvq2_tensor* fc2, const vvq2_tensor* b2, const char* name) {
+    if (int rc = check_ctx(c)) return rc;
+    if (!fc1 || !fc1->data || !fc2 || !fc2->data) return fail(VVQ2_ERR_INVALID_ARG, "%s: fc1 and fc2 required", name);
+    const int in = (int)fc1->ne0, mid = (int)fc1->ne1, out = (int)fc2->ne1;
+    if (fc2->ne0 != mid) return fail(VVQ2_ERR_INVALID_ARG, "%s: fc2 ne0 %lld != fc1 rows %d", name, (long long)fc2->ne0, mid);
+    vvq2_ctx::Head n;
+    if (int rc = upload_tensor(c, *fc1, &n.fc1, in, mid, name)) return rc;
+    if (int rc = upload_tensor(c, *fc2, &n.fc2, mid, out, name)) return rc;
+    if (b1 && b1->data)
+        if (int rc = upload_vec(c, *b1, mid, &n.b1, name)) return rc;
+    if (norm && norm->data)
+        if (int rc = upload_vec(c, *norm, mid, &n.norm, name)) return rc;
+    if (b2 && b2->data)
+        if (int rc = upload_vec(c, *b2, out, &n.b2, name)) return rc;
+    if (int rc = c->alloc(&n.xin, (size_t)GEMV_MAX_M * in)) return rc;
+    if (int rc = c->alloc(&n.mid, (size_t)GEMV_MAX_M * mid)) return rc;
+    if (int rc = c->alloc(&n.out, (size_t)GEMV_MAX_M * out)) return rc;
+    *h = n;
+    return 0;
+}
+
+// x [batch][in] -> fc1 (+b1) -> [relu] -> fc2 over [rms_norm * norm] (+b2) -> [sigmoid] -> y
+int run_head(vvq2_ctx* c, const vvq2_ctx::Head& h, const float* x, int batch, float* y, bool relu_mid,
+             bool sigmoid_out, void* stream, const char* name) {
+    if (int rc = check_ctx(c)) return rc;
+    if (h.fc1.type < 0) return fail(VVQ2_ERR_INVALID_ARG, "%s: weights not set", name);
+    if (!x || !y || batch <= 0 || batch > GEMV_MAX_M)
+        return fail(VVQ2_ERR_INVALID_ARG, "%s: batch %d (1..%d) or null buffers", name, batch, GEMV_MAX_M);
+    cudaStream_t st = pick_stream(c, stream);
+    const int in = h.fc1.cols, mid = h.fc1.rows, out = h.fc2.rows;
+    CU(cudaMemcpyAsync(h.xin, x, sizeof(float) * batch * in, cudaMemcpyDefault, st));
+    GemvArgs g;
+    g.M = batch;
+    g.w0 = h.fc1;
+    g.K = in;
+    g.x = h.xin;
+    g.x_stride = in;
+    g.bias = h.b1;
+    g.y = h.mid;
+    g.y_stride = mid;
+    g.epi = EPI_STORE;
+    if (gemv_launch(g, st) != cudaSuccess)
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "%s: fc1 [%d x %d] not supported by the GEMV", name, mid, in);
+    if (relu_mid) CU(act_launch(h.mid, (int64_t)batch * mid, ACT_RELU, st));
+    GemvArgs f = g;
+    f.w0 = h.fc2;
+    f.K = mid;
+    f.x = h.mid;
+    f.x_stride = mid;
+    f.norm_w = h.norm;   // ggml_rms_norm(eps 1e-6) * norm, fused into the GEMV's staging
+    f.eps = 1e-6f;
+    f.bias = h.b2;
+    f.y = h.out;
+    f.y_stride = out;
+    if (gemv_launch(f, st) != cudaSuccess)
+        return fail(VVQ2_ERR_NOT_IMPLEMENTED, "%s: fc2 [%d x %d] not supported by the GEMV", name, out, mid);
+    if (sigmoid_out) CU(act_launch(h.out, (int64_t)batch * out, ACT_SIGMOID, st));
+    CU(cudaMemcpyAsync(y, h.out, sizeof(float) * batch * out, cudaMemcpyDefault, st));
+    if (!is_device_ptr(y)) CU(cudaStreamSynchronize(st));
+    return 0;
+}
+
+}  // namespace
+
 extern "C" {
 
 int vvq2_device_count(void) {
@@ -1735,6 +1810,28 @@ int vvq2_lm_head(vvq2_ctx* c, int n, const float* h, float* logits, int32_t* arg
         CU(cudaStreamSynchronize(st));
     }
     return 0;
+}
+
+int vvq2_set_connector(vvq2_ctx* c, const vvq2_tensor* fc1_w, const vvq2_tensor* fc1_b, const vvq2_tensor* norm_w,
+                       const vvq2_tensor* fc2_w, const vvq2_tensor* fc2_b) {
+    if (fc1_w && c && fc2_w && fc2_w->ne1 != c->hp.hidden_size)
+        return fail(VVQ2_ERR_INVALID_ARG, "connector output %lld != hidden %d", (long long)fc2_w->ne1, c->hp.hidden_size);
+    return set_head(c, c ? &c->conn : nullptr, fc1_w, fc1_b, norm_w, fc2_w, fc2_b, "connector");
+}
+
+int vvq2_connector(vvq2_ctx* c, const float* x, int batch, float* y, void* stream) {
+    return c ? run_head(c, c->conn, x, batch, y, false, false, stream, "connector") : check_ctx(c);
+}
+
+int vvq2_set_eos(vvq2_ctx* c, const vvq2_tensor* fc1_w, const vvq2_tensor* fc1_b, const vvq2_tensor* fc2_w,
+                 const vvq2_tensor* fc2_b) {
+    if (fc1_w && c && fc1_w->ne0 != c->hp.hidden_size)
+        return fail(VVQ2_ERR_INVALID_ARG, "eos input %lld != hidden %d", (long long)fc1_w->ne0, c->hp.hidden_size);
+    return set_head(c, c ? &c->eos : nullptr, fc1_w, fc1_b, nullptr, fc2_w, fc2_b, "eos");
+}
+
+int vvq2_eos(vvq2_ctx* c, const float* x, int batch, float* p, void* stream) {
+    return c ? run_head(c, c->eos, x, batch, p, true, true, stream, "eos") : check_ctx(c);
 }
 
 int vvq2_embed(vvq2_ctx* c, int n, const int32_t* tokens, float* out, void* stream) {

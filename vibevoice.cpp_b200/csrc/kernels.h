@@ -172,6 +172,9 @@ cudaError_t lse_merge_launch(const __half* o2, const float* l2, int64_t rows, in
 // x += y over n floats
 cudaError_t add_rows_launch(float* x, const float* y, int64_t n, cudaStream_t st);
 cudaError_t half_to_float_launch(const __half* x, float* y, int64_t n, cudaStream_t st);
+// in place: ACT_RELU max(x, 0); ACT_SIGMOID 1 / (1 + expf(-x))
+enum { ACT_RELU = 0, ACT_SIGMOID = 1 };
+cudaError_t act_launch(float* x, int64_t n, int act, cudaStream_t st);
 // [parts][rows][w] -> [rows][parts*w]
 cudaError_t gather_rows_launch(const __half* in, int64_t rows, int parts, int w, __half* out, cudaStream_t st);
 // ... to f16 [rows][cols] (exact dequantized value, rounded once)

@@ -232,6 +232,20 @@ cudaError_t half_to_float_launch(const __half* x, float* y, int64_t n, cudaStrea
     return cudaGetLastError();
 }
 
+// ggml_relu and the classifier's sigmoid (src/vibevoice_tts.cpp:522,537)
+__global__ void k_act(float* x, int64_t n, int act) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        x[i] = act == ACT_RELU ? fmaxf(v, 0.f) : __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+    }
+}
+
+cudaError_t act_launch(float* x, int64_t n, int act, cudaStream_t st) {
+    k_act<<<grid_for(n, 256), 256, 0, st>>>(x, n, act);
+    note_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t add_rows_launch(float* x, const float* y, int64_t n, cudaStream_t st) {
     k_add_rows<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
     note_launch();

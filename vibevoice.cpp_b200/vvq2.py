@@ -78,6 +78,10 @@ def lib() -> C.CDLL:
             "vvq2_mega_trace": (I, [P, P, C.c_int64, P, P]),
             "vvq2_nccl_unique_id": (I, [P]),
             "vvq2_partition": (I, [P, I, I, I, P]),
+            "vvq2_set_connector": (I, [P, P, P, P, P, P]),
+            "vvq2_connector": (I, [P, P, I, P, P]),
+            "vvq2_set_eos": (I, [P, P, P, P, P]),
+            "vvq2_eos": (I, [P, P, I, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -156,6 +160,46 @@ class Engine:
             ts.append(t)
         # a tied table: same array object for lm_head and tok_embd -> same pointer
         _chk(lib().vvq2_set_output(self.ctx, *[C.byref(t) if t.data else None for t in ts]))
+
+    def _tensors(self, specs):
+        ts, keep = [], []
+        for spec in specs:
+            t = self._tensor(spec)
+            if isinstance(t, tuple):
+                keep.append(t[1])
+                t = t[0]
+            ts.append(t)
+        return [C.byref(t) if t.data else None for t in ts], keep
+
+    def set_connector(self, fc1_w, fc1_b, norm_w, fc2_w, fc2_b) -> None:
+        """SpeechConnector weights (src/vibevoice_tts.cpp:464-501)."""
+        args, keep = self._tensors((fc1_w, fc1_b, norm_w, fc2_w, fc2_b))
+        _chk(lib().vvq2_set_connector(self.ctx, *args))
+
+    def connector(self, x, y=None, stream=None):
+        """x [batch][latent] -> y [batch][hidden] = fc2(rms_norm(fc1 x + b1) * norm) + b2."""
+        if not hasattr(x, "data_ptr"):
+            x = np.ascontiguousarray(x, np.float32)
+        batch = x.shape[0]
+        if y is None:
+            y = np.empty((batch, self.hp["hidden"]), np.float32)
+        _chk(lib().vvq2_connector(self.ctx, _p(x), batch, _p(y), stream))
+        return y
+
+    def set_eos(self, fc1_w, fc1_b, fc2_w, fc2_b) -> None:
+        """EOS classifier weights (src/vibevoice_tts.cpp:503-537)."""
+        args, keep = self._tensors((fc1_w, fc1_b, fc2_w, fc2_b))
+        _chk(lib().vvq2_set_eos(self.ctx, *args))
+
+    def eos(self, x, p=None, stream=None):
+        """x [batch][hidden] -> p [batch] = sigmoid(fc2(relu(fc1 x + b1)) + b2)."""
+        if not hasattr(x, "data_ptr"):
+            x = np.ascontiguousarray(x, np.float32)
+        batch = x.shape[0]
+        if p is None:
+            p = np.empty(batch, np.float32)
+        _chk(lib().vvq2_eos(self.ctx, _p(x), batch, _p(p), stream))
+        return p
 
     def profile(self, enable: bool) -> None:
         _chk(lib().vvq2_profile(self.ctx, int(enable)))
