@@ -13,14 +13,19 @@ rows; tokens/s counts both rows.  The 550 MB of weights per step exceed the
           launching stream, max over ranks
   e2e   : the same steps through the C ABI with HOST token buffers
           (vvq2_decode_step: H2D ids, D2H argmax ids every step)
-  roofline : the dominant kernel (the fused dequant GEMV), algorithmic bytes
-          per launch / mean launch time from CUDA events, vs measured HBM peak
+  roofline : the dominant kernel (the persistent decode-step kernel),
+          algorithmic bytes per launch / mean launch time from CUDA events,
+          vs measured HBM peak; traffic from an ncu capture
   cpu_baseline : the CPU oracle (port of the reference's ggml CPU numerics)
           on this host's cores, bounded sample of decode steps
+  prefill, c3 : the 16k-token 7B-shaped prefill layer and config 3's
+          batched step (see prefill_measure, c3_measure)
 
---impl reference times that CPU implementation alone (the reference cannot be
-built here: its ggml submodule is absent).  Multi-GPU: C2 does not shard,
-so N GPUs run N independent replicas (weak scaling, no collectives)."""
+--impl reference times that CPU implementation alone for --warmup + --steps
+greedy steps (the reference cannot be built here: its ggml submodule is
+absent).  --workload c4 / c5 print the config-4 / config-5 lines; --case
+runs small profiling workloads.  Multi-GPU: C2 does not shard, so N GPUs run
+N independent replicas (weak scaling, no collectives)."""
 from __future__ import annotations
 
 import argparse
@@ -422,14 +427,16 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
 
 
-def cpu_decode_rate(model, hp, kv_len, budget_s=15.0, flags=None):
-    """CPU oracle (test infrastructure) decode steps/s on this host, bounded sample."""
+def cpu_decode_rate(model, hp, kv_len, budget_s=15.0, flags=None, steps=64, warmup=0):
+    """CPU oracle (test infrastructure) decode tokens/s on this host: `warmup`
+    untimed greedy steps of both rows, then up to `steps` timed ones (fewer if
+    the time budget runs out first).  Returns (tokens/s, timed steps, threads)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import vvq2_oracle as O
     flags = O.GGML_CPU if flags is None else flags
     rng = np.random.default_rng(SEED + 1)
-    max_steps = 64
-    ora = O.Model(hp, 2, kv_len + max_steps + 2, flags)
+    max_steps = steps
+    ora = O.Model(hp, 2, kv_len + warmup + max_steps + 2, flags)
     for li, t in enumerate(model["layers"]):
         ora.set_layer(li, t)
     ora.set_output(model["output_norm"], model["lm_head"], model["tok_embd"])
@@ -441,6 +448,10 @@ def cpu_decode_rate(model, hp, kv_len, budget_s=15.0, flags=None):
     for s in range(2):
         ora.set_past_len(s, kv_len)
     tok = rng.integers(0, hp["vocab"], size=2).astype(np.int32)
+    for _ in range(warmup):
+        pos = [ora.past_len(0), ora.past_len(1)]
+        h = ora.forward([0, 1], ora.embed(tok)[:, None, :], pos, output_norm=True)
+        tok = ora.lm_head(h[:, 0]).astype(np.int32)
     t0 = time.perf_counter()
     n = 0
     while n < max_steps:
@@ -500,10 +511,12 @@ def run_reference(args, rank):
         return 0
     import synth
     model = synth.model_q8_0(SEED, C2)
-    rate, n, cores = cpu_decode_rate(model, C2, args.kv, budget_s=max(5.0, 4.0 * args.steps / 10))
+    # the arm's own --steps/--warmup, each step one greedy decode step of both
+    # rows; a 150 s budget bounds the timed part on slow hosts
+    rate, n, cores = cpu_decode_rate(model, C2, args.kv, budget_s=150.0, steps=args.steps, warmup=args.warmup)
     line = {
         "impl": "reference", "metric": "qwen2_decode_tokens_per_s", "value": round(rate, 3), "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": n, "warmup": 0, "ms_per_step": round(2000.0 / rate, 3),
+        "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": round(2000.0 / rate, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->f32 (ggml q8_0 dot)",
         "data": "synthetic", "config": workload_config(args),
         "cpu_baseline": {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
