@@ -360,8 +360,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
 // summed in item order (deterministic), scaled by the row's RMSNorm factor
 // (the staged activations are x * w; W (x s o w) = s W (x o w)), and the
 // epilogue applied.
-constexpr int S_THREADS = 512;
-constexpr int S_WARPS = S_THREADS / 32;
+// K-quants use 32-weight lane tasks (gd::kq_*) with ~11-12 registers per row
+// and 3 register stages: 256-thread CTAs (255 registers); everything else 512
+template <int WT>
+struct SKq {
+    static constexpr bool v = WT == W_Q5_K || WT == W_Q6_K;
+};
+template <int WT>
+struct SThreads {
+    static constexpr int v = SKq<WT>::v ? 256 : 512;
+};
 constexpr size_t S_SMEM_MAX = 220 * 1024;
 
 struct Q8Raw {
@@ -369,18 +377,43 @@ struct Q8Raw {
     uint32_t d;     // f16 block scale bits
 };
 
+// one 32-weight K-quant lane task of one row, as loaded
+struct KqRaw {
+    uint4 lo, hi;   // low-bit run (Q6_K ql / Q5_K qs) and high-bit run (qh)
+    uint4 aux;      // Q5_K: the block header (d, dmin, 12 scale bytes); Q6_K: x, y = the
+                    // half's 8 int8 scales, z = f16 d bits
+};
+
 template <int WT>
-using SChunk = typename std::conditional<WT == W_Q8_0, Q8Raw, Chunk>::type;
+using SChunk = typename std::conditional<WT == W_Q8_0, Q8Raw,
+                                         typename std::conditional<SKq<WT>::v, KqRaw, Chunk>::type>::type;
 
 // register stages of weight loads per warp (by type and activation rows)
 template <int WT, int MB>
 struct SPipe {
-    static constexpr int P = WT == W_Q8_0 ? (MB == 1 ? 4 : 2) : WT == W_F32 ? 1 : 2;
+    static constexpr int P = WT == W_Q8_0 ? (MB == 1 ? 4 : 2) : WT == W_F32 ? 1 : SKq<WT>::v ? 3 : 2;
 };
 
 template <int WT>
 __device__ __forceinline__ void s_load(const DevW& W, int row, int c, bool ok, SChunk<WT>& ch) {
-    if constexpr (WT == W_Q8_0) {
+    if constexpr (SKq<WT>::v) {
+        // c is the lane task t: super-block t >> 3 (see gd::kq_*)
+        if (ok) {
+            const int sb = c >> 3;
+            const uint8_t* b = W.q + (size_t)row * W.row_stride + (size_t)sb * (WT == W_Q6_K ? Q6K_PACKED : Q5K_BYTES);
+            ch.lo = __ldg(reinterpret_cast<const uint4*>(b + gd::kq_lo_off<WT>(c)));
+            ch.hi = __ldg(reinterpret_cast<const uint4*>(b + gd::kq_hi_off<WT>(c)));
+            if constexpr (WT == W_Q6_K) {
+                const uint2 sc = __ldg(reinterpret_cast<const uint2*>(b + 192 + ((c & 7) >> 2) * 8));
+                ch.aux = make_uint4(sc.x, sc.y, __ldg(reinterpret_cast<const unsigned short*>(W.d) +
+                                                      (size_t)row * W.d_stride + sb), 0u);
+            } else {
+                ch.aux = __ldg(reinterpret_cast<const uint4*>(b));
+            }
+        } else {
+            ch.lo = ch.hi = ch.aux = make_uint4(0, 0, 0, 0);
+        }
+    } else if constexpr (WT == W_Q8_0) {
         if (ok) {
             const uint8_t* rp = W.q + (size_t)row * W.row_stride;
             ch.q = __ldg(reinterpret_cast<const uint4*>(rp) + c);
@@ -474,6 +507,64 @@ __device__ __forceinline__ void s_dot(const SChunk<WT>& ch, const float4 (&av)[M
     }
 }
 
+// byte k (runtime) of a 16-byte register quad
+__device__ __forceinline__ uint32_t qbyte(const uint4& v, int k) { return (gd::word(v, k >> 2) >> (8 * (k & 3))) & 0xffu; }
+
+// Dot of sub-chunk s (16 weights) of K-quant lane task t of one row with MB
+// activation chunks; scales as ggml: Q6_K (d * sc) * (q - 32), Q5_K
+// (d * sc) * q - dmin * m, factored out of the 16-weight sum.
+template <int WT, int MB>
+__device__ __forceinline__ void kq_dot(const KqRaw& ch, const float4 (&av)[MB][4], int t, int s, float (&out)[MB]) {
+    const float2 one2 = make_float2(1.0f, 1.0f);
+    constexpr float OFF = WT == W_Q5_K ? -8388608.0f : -8388640.0f;   // 2^23 (+ 32 for Q6_K)
+    const float2 off2 = make_float2(OFF, OFF);
+    float2 sa[MB], sb[MB], as[MB];
+#pragma unroll
+    for (int m = 0; m < MB; ++m) sa[m] = sb[m] = as[m] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const uint32_t w = gd::kq_word<WT>(gd::word(ch.lo, g), gd::word(ch.hi, g), t, s);
+        float2 f01, f23;
+        magic4(w, f01, f23);
+        f01 = __ffma2_rn(f01, one2, off2);
+        f23 = __ffma2_rn(f23, one2, off2);
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            const float2 a01 = make_float2(av[m][g].x, av[m][g].y), a23 = make_float2(av[m][g].z, av[m][g].w);
+            sa[m] = __ffma2_rn(f01, a01, sa[m]);
+            sb[m] = __ffma2_rn(f23, a23, sb[m]);
+            if constexpr (WT == W_Q5_K) {
+                as[m] = __fadd2_rn(as[m], a01);
+                as[m] = __fadd2_rn(as[m], a23);
+            }
+        }
+    }
+    float scale, mscale = 0.f;
+    if constexpr (WT == W_Q6_K) {
+        const int k = gd::q6_scale_idx(t, s);
+        const int sc = (int)(int8_t)(((k < 4 ? ch.aux.x : ch.aux.y) >> (8 * (k & 3))) & 0xffu);
+        scale = __fmul_rn(__half2float(__ushort_as_half((unsigned short)ch.aux.z)), (float)sc);
+    } else {
+        const int j = ((t & 7) >> 1) * 2 + s;
+        int sc, mn;
+        if (j < 4) {
+            sc = (int)(qbyte(ch.aux, 4 + j) & 63);
+            mn = (int)(qbyte(ch.aux, 8 + j) & 63);
+        } else {
+            sc = (int)((qbyte(ch.aux, 8 + j) & 0xF) | ((qbyte(ch.aux, j) >> 6) << 4));
+            mn = (int)((qbyte(ch.aux, 8 + j) >> 4) | ((qbyte(ch.aux, 4 + j) >> 6) << 4));
+        }
+        const __half2 dh = *reinterpret_cast<const __half2*>(&ch.aux.x);
+        scale = __fmul_rn(__low2float(dh), (float)sc);     // d1 = d * sc
+        mscale = __fmul_rn(__high2float(dh), (float)mn);   // m1 = dmin * m
+    }
+#pragma unroll
+    for (int m = 0; m < MB; ++m) {
+        out[m] = __fmul_rn(scale, (sa[m].x + sa[m].y) + (sb[m].x + sb[m].y));
+        if constexpr (WT == W_Q5_K) out[m] = fmaf(-mscale, as[m].x + as[m].y, out[m]);
+    }
+}
+
 template <int N>
 struct SLog2 {
     static constexpr int v = 1 + SLog2<N / 2>::v;
@@ -503,7 +594,10 @@ __device__ __forceinline__ float s_transpose_sum(float (&v)[NV], int lane) {
 }
 
 template <int WT, int EPI, int MB>
-__global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) {
+__global__ void __launch_bounds__(SThreads<WT>::v, 1) k_gemv_stream(const GemvArgs a) {
+    constexpr int S_THREADS = SThreads<WT>::v;
+    constexpr int S_WARPS = S_THREADS / 32;
+    constexpr bool KQ = SKq<WT>::v;
     constexpr int P = SPipe<WT, MB>::P;
     constexpr int NV = NR * MB;
     constexpr int SH = 5 - SLog2<NV>::v;
@@ -513,7 +607,9 @@ __global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) 
     __shared__ float rope_c[EPI == EPI_QKV ? MB : 1][EPI == EPI_QKV ? 64 : 1];
     __shared__ float rope_s[EPI == EPI_QKV ? MB : 1][EPI == EPI_QKV ? 64 : 1];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = a.K, NC = K / 16, niter = (NC + 31) / 32;
+    // an item is 32 lane tasks: 16-weight chunks (NC per row) or, for the
+    // K-quants, 32-weight lane tasks (NTK per row)
+    const int K = a.K, NC = K / 16, NTK = K / 32, niter = ((KQ ? NTK : NC) + 31) / 32;
     const int U = a.n_units;
     const int u0 = (int)((long long)U * blockIdx.x / gridDim.x);
     const int nu = (int)((long long)U * (blockIdx.x + 1) / gridDim.x) - u0;
@@ -528,7 +624,7 @@ __global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) 
 #pragma unroll
         for (int j = 0; j < NR; ++j) {
             const DevW& W = wh[j] ? a.w1 : a.w0;
-            s_load<WT>(W, r[j], c, c < NC && r[j] < W.rows, dst[j]);
+            s_load<WT>(W, r[j], c, c < (KQ ? NTK : NC) && r[j] < W.rows, dst[j]);
         }
     };
 
@@ -615,7 +711,29 @@ __global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) 
             if (ul < nu) {
                 const int c = it * 32 + lane;
                 float acc[NV];
-                if (c < NC) {
+#pragma unroll
+                for (int i = 0; i < NV; ++i) acc[i] = 0.f;
+                if constexpr (KQ) {
+                    if (c < NTK) {
+                        // lane task c: two 16-weight chunks (its two groups)
+#pragma unroll
+                        for (int sc2 = 0; sc2 < 2; ++sc2) {
+                            const int ch = (c >> 3) * 16 + gd::kq_chunk0<WT>(c) + sc2 * gd::kq_chunk_step<WT>();
+                            float4 av[MB][4];
+#pragma unroll
+                            for (int m = 0; m < MB; ++m)
+#pragma unroll
+                                for (int g = 0; g < 4; ++g) av[m][g] = act4[(m * 4 + g) * NC + ch];
+#pragma unroll
+                            for (int j = 0; j < NR; ++j) {
+                                float o[MB];
+                                kq_dot<WT, MB>(buf[s][j], av, c, sc2, o);
+#pragma unroll
+                                for (int m = 0; m < MB; ++m) acc[j * MB + m] += o[m];
+                            }
+                        }
+                    }
+                } else if (c < NC) {
                     float4 av[MB][4];
 #pragma unroll
                     for (int m = 0; m < MB; ++m)
@@ -628,9 +746,6 @@ __global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) 
 #pragma unroll
                         for (int m = 0; m < MB; ++m) acc[j * MB + m] = o[m];
                     }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < NV; ++i) acc[i] = 0.f;
                 }
                 // the stage is free: request its pair of the next round
                 if (nul < nu) load_pair(nul, nit, buf[s]);
@@ -725,7 +840,8 @@ __global__ void __launch_bounds__(S_THREADS, 1) k_gemv_stream(const GemvArgs a) 
 }
 
 size_t stream_smem(const GemvArgs& a, int grid) {
-    const int niter = (a.K / 16 + 31) / 32;
+    const bool kq = a.w0.type == W_Q5_K || a.w0.type == W_Q6_K;   // 32-weight lane tasks
+    const int niter = ((kq ? a.K / 32 : a.K / 16) + 31) / 32;
     const int nu_max = (a.n_units + grid - 1) / grid;
     return (size_t)a.M * a.K * sizeof(float) + (size_t)nu_max * NR * niter * a.M * sizeof(float);
 }
@@ -748,7 +864,7 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t st) {
         if (grid > 0 && ssm <= S_SMEM_MAX) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(grid);
-            cfg.blockDim = dim3(S_THREADS);
+            cfg.blockDim = dim3(SThreads<WT>::v);
             cfg.dynamicSmemBytes = ssm;
             cfg.stream = st;
             cudaLaunchAttribute attr[1];

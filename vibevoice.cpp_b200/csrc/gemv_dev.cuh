@@ -122,5 +122,78 @@ __device__ __forceinline__ void clear_chunk(Chunk& ch) {
     if constexpr (WT == W_Q5_K || WT == W_Q6_K) ch.shift = 0;
 }
 
+// ---------------------------------------------------------------------------
+// K-quant lane tasks of 32 weights (the streaming GEMV's K-quant mapping).
+// A lane task covers 16 consecutive positions l0 .. l0+15 of two 32-weight
+// groups of one super-block that share their low-bit bytes, so one 16-byte
+// run of low bits and one of high bits serve all 32 weights:
+//   Q6_K task t (8 per super-block): half hf = (t & 7) >> 2, quarter pair
+//     kk = ((t & 7) >> 1) & 1 (quarters kk and kk + 2: low / high nibbles of
+//     ql[hf*64 + kk*32 + l], high bits 2k..2k+1 of qh[hf*32 + l]),
+//     l0 = 16 * (t & 1); weights hf*128 + k*32 + l.
+//   Q5_K task t: sub-block pair q = (t & 7) >> 1 (sub-blocks 2q and 2q + 1:
+//     low / high nibbles of qs[32q + l], bit j of qh[l]), l0 = 16 * (t & 1);
+//     weights j*32 + l.
+// Sub-chunk s (0, 1) of a task is its first / second group; kq_word gives
+// its four quants of 32-bit word g (positions l0 + 4g .. l0 + 4g + 3) as
+// bytes: Q6_K q in 0..63 (value (q - 32) * d * sc), Q5_K q in 0..31 (value
+// d * sc * q - dmin * m).  These are the bit layouts of ggml's
+// dequantize_row_q6_K / dequantize_row_q5_K.
+
+// first 16-weight chunk (of 16) of task t within its super-block, and the
+// chunk distance to the task's second group
+template <int WT>
+__host__ __device__ __forceinline__ int kq_chunk0(int t) {
+    const int sub = t & 7, l16 = sub & 1;
+    if constexpr (WT == W_Q6_K) return (sub >> 2) * 8 + ((sub >> 1) & 1) * 2 + l16;
+    else return (sub >> 1) * 4 + l16;
+}
+template <int WT>
+__host__ __device__ __forceinline__ constexpr int kq_chunk_step() { return WT == W_Q6_K ? 4 : 2; }
+
+// byte offsets (within the super-block) of the task's low-bit and high-bit runs
+template <int WT>
+__host__ __device__ __forceinline__ int kq_lo_off(int t) {
+    const int sub = t & 7, l0 = (sub & 1) * 16;
+    if constexpr (WT == W_Q6_K) return (sub >> 2) * 64 + ((sub >> 1) & 1) * 32 + l0;
+    else return 48 + (sub >> 1) * 32 + l0;
+}
+template <int WT>
+__host__ __device__ __forceinline__ int kq_hi_off(int t) {
+    const int sub = t & 7, l0 = (sub & 1) * 16;
+    if constexpr (WT == W_Q6_K) return 128 + (sub >> 2) * 32 + l0;
+    else return 16 + l0;
+}
+
+// quants of sub-chunk s, word g: lo / hi are the task's low-bit / high-bit words g
+template <int WT>
+__host__ __device__ __forceinline__ uint32_t kq_word(uint32_t lo, uint32_t hi, int t, int s) {
+    const int sub = t & 7;
+    if constexpr (WT == W_Q6_K) {
+        const int k = ((sub >> 1) & 1) + 2 * s;          // quarter
+        return ((lo >> (4 * s)) & 0x0F0F0F0Fu) | (((hi >> (2 * k)) & 0x03030303u) << 4);
+    } else {
+        const int j = (sub >> 1) * 2 + s;                // sub-block
+        return ((lo >> (4 * s)) & 0x0F0F0F0Fu) | (((hi >> j) & 0x01010101u) << 4);
+    }
+}
+
+// Q6_K: index of the int8 scale of sub-chunk s within the half's 8 scales
+__host__ __device__ __forceinline__ int q6_scale_idx(int t, int s) {
+    const int sub = t & 7;
+    return (sub & 1) + 2 * (((sub >> 1) & 1) + 2 * s);
+}
+
+// Q5_K: 6-bit scale and min of sub-block j from the 12 packed bytes (ggml's get_scale_min_k4)
+__host__ __device__ __forceinline__ void q5_scale_min(const uint8_t* scb, int j, int& sc, int& m) {
+    if (j < 4) {
+        sc = scb[j] & 63;
+        m = scb[j + 4] & 63;
+    } else {
+        sc = (scb[j + 4] & 0xF) | ((scb[j - 4] >> 6) << 4);
+        m = (scb[j + 4] >> 4) | ((scb[j] >> 6) << 4);
+    }
+}
+
 }  // namespace gd
 }  // namespace vvq2
