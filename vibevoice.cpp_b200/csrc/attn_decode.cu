@@ -8,13 +8,17 @@
 // evaluated from the row's position; nothing is materialised.
 //
 // Grid (split, kv_head, row); a split is a whole number of 64-position pages.
-// Each page's K and V slices ([64][hd] f16, contiguous in the paged pool) are
-// staged into shared memory by the TMA bulk-copy engine (cp.async.bulk with an
-// mbarrier), double-buffered so the next page streams in while this one is
-// scored.  The whole GQA group (7 or 6 query heads) shares each K/V tile; Q is
-// rounded to f16 as ggml does.  Online softmax runs across the pages of the
-// split; the last CTA of a (row, kv_head) to finish -- a device-scope counter
-// -- merges the splits' partial (O, max, sum) with the log-sum-exp rule.
+// The whole GQA group (7 or 6 query heads) shares each K/V tile; Q is rounded
+// to f16 as ggml does; online softmax runs across the pages of the split.
+// Two kernels do the page math:
+//  * k_attn_mma (head_dim 64/128, the engine's paths): pages arrive by TMA
+//    tensor copies in the 128-byte swizzle, three in flight, and the dot
+//    products run on mma.sync tensor cores (S = Q K^T, O^T += V^T P^T); the
+//    splits' partial (O, max, sum) are merged afterwards by k_attn_merge with
+//    the log-sum-exp rule, one CTA per (query head, row).
+//  * k_attn_decode (head_dim 32, the allocation-free entry point): pages by
+//    cp.async.bulk, double-buffered, CUDA-core math; the last CTA of a (row,
+//    kv_head) to finish -- a device-scope counter -- merges the partials.
 //
 // Every mbarrier wait is bounded: on timeout the kernel records an error code
 // in args.err, stops, and returns (no trap, no endless spin).

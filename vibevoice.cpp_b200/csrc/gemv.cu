@@ -11,16 +11,18 @@
 // the activations to int8 blocks (its vec_dot_type), a step whose rounding
 // flips cascade through RMSNorm, so it is reproduced only by the CPU oracle.
 //
-// Structure: a persistent grid (one wave of resident CTAs).  Each CTA first stages the
-// M activation rows in shared memory -- applying the RMSNorm
-// (src/rms_norm.hpp:11-17) when the linear follows one -- then its warps walk
-// 4-row units of the weight matrix.  Lanes take 16-element chunks (one 16-byte
-// load per Q8_0 row, two for F16, ...), so every weight byte is read from HBM
-// once; the activation chunk is read from shared memory once per lane and
-// reused for the 4 rows.  Epilogues: QKV (+bias, NEOX RoPE on Q/K, Q to a
-// buffer, K/V appended to the f16 paged cache), residual add, SwiGLU, store,
-// and argmax.  Kernels are launched with programmatic dependent launch: each
-// warp starts pulling its first unit's weights into L2 before
+// Two kernels, both persistent grids (one wave of resident CTAs) that stage
+// the M activation rows in shared memory first -- with the RMSNorm
+// (src/rms_norm.hpp:11-17) when the linear follows one -- and read every
+// weight byte from HBM once, 4-row units at a time, the activation chunk
+// reused for the 4 rows:
+//  * k_gemv_stream (1-2 rows, the decode of one sequence or a CFG pair; see
+//    its own comment): register-pipelined weight loads, no block barrier in
+//    the main loop, I2F-free dequantization;
+//  * k_gemv (3-8 rows): warps split a unit's K, register ping-pong.
+// Epilogues: QKV (+bias, NEOX RoPE on Q/K, Q to a buffer, K/V appended to the
+// f16 paged cache), residual add, SwiGLU, store, and argmax.  Kernels are
+// launched with programmatic dependent launch: weight loads start before
 // griddepcontrol.wait, overlapping the previous kernel's tail.
 #include <type_traits>
 
