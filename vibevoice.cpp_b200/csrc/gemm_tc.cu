@@ -22,8 +22,14 @@
 // TMA as well (TMAB variant): the producer warps then only run the epilogue,
 // and no weight tile is dequantized once per 256-row block of tokens.
 // Pipeline: 4 stages of {A0, A1, B} 16 KB tiles (BK = 64), mbarriers full/empty.
-// Every wait is bounded; a timeout sets args.err and unwinds without leaving
-// TMEM allocated.
+// The Q8_0 weight producers fetch each row's raw blocks 4 k-blocks ahead of
+// their conversion.  Epilogues that write rows stage the accumulators
+// through the drained pipeline buffers so that a warp stores whole rows.  The
+// kernel is launched as a programmatic dependent: barrier setup, TMEM
+// allocation and the first weight fetches overlap the previous kernel; the
+// TMA warp waits (griddepcontrol.wait) before loading anything that kernel
+// wrote.  Every wait is bounded; a timeout sets args.err and unwinds without
+// leaving TMEM allocated.
 #include <algorithm>
 
 #include "common.cuh"
