@@ -615,7 +615,6 @@ __global__ void __launch_bounds__(SThreads<WT>::v, 1) k_gemv_stream(const GemvAr
     const int U = a.n_units;
     const int u0 = (int)((long long)U * blockIdx.x / gridDim.x);
     const int nu = (int)((long long)U * (blockIdx.x + 1) / gridDim.x) - u0;
-    const int npairs = nu * niter;
     float4* act4 = reinterpret_cast<float4*>(sm_act);            // [(m * 4 + g) * NC + c]
     float* part = sm_act + (size_t)MB * K;                        // [(ul * NR + j) * niter + it][MB]
 
