@@ -51,3 +51,20 @@ def test_backend_selection_env(monkeypatch):
 def test_version_string():
     import vvq2
     assert b"sm_100a" in vvq2.lib().vvq2_version()
+
+
+def test_null_context_is_an_argument_error():
+    """Every context entry point reports a null context as VVQ2_ERR_INVALID_ARG
+    (-2) instead of dereferencing it (checked for the per-frame heads, the
+    stack step and the lm_head)."""
+    import numpy as np
+
+    import vvq2
+    lib = vvq2.lib()
+    x = np.zeros((1, 896), np.float32)
+    y = np.zeros((1, 896), np.float32)
+    assert lib.vvq2_set_connector(None, None, None, None, None, None) == -2
+    assert lib.vvq2_connector(None, x.ctypes.data, 1, y.ctypes.data, None) == -2
+    assert lib.vvq2_set_eos(None, None, None, None, None) == -2
+    assert lib.vvq2_eos(None, x.ctypes.data, 1, y.ctypes.data, None) == -2
+    assert lib.vvq2_lm_head(None, 1, x.ctypes.data, None, None, None) == -2
