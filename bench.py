@@ -32,6 +32,7 @@ import argparse
 import json
 import os
 import subprocess
+import tempfile
 import sys
 import time
 from pathlib import Path
@@ -470,11 +471,11 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.out = ROOT / "gpurun_out" / f"clocks_rank{index}.csv"
+        # a private temporary file: the samples are summarised into the JSON line
+        self.out = Path(tempfile.gettempdir()) / f"vvq2_clocks_rank{index}_{os.getpid()}.csv"
 
     def __enter__(self):
         try:
-            self.out.parent.mkdir(exist_ok=True)
             self.f = open(self.out, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index),
@@ -491,11 +492,13 @@ class ClockSampler:
             self.proc.terminate()
             self.proc.wait(timeout=10)
             self.f.close()
+            self.text = self.out.read_text() if self.out.exists() else ""
+            self.out.unlink(missing_ok=True)
 
     def summary(self):
-        if not self.proc or not self.out.exists():
+        if not self.proc or not getattr(self, "text", ""):
             return None
-        rows = [r.split(", ") for r in self.out.read_text().strip().splitlines() if r.strip()]
+        rows = [r.split(", ") for r in self.text.strip().splitlines() if r.strip()]
         if not rows:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
@@ -608,6 +611,9 @@ def main():
         for _ in range(n):
             eng.decode_step(kv, [0, 1], tok, tok, stream=sh)
 
+    # clocks are sampled over the whole GPU part of the run (warm-up, timed
+    # steps, e2e, profiling pass, c3 and prefill fields)
+    clk = ClockSampler(local).__enter__()
     steps(args.warmup)
     torch.cuda.synchronize()
     if world > 1:
@@ -615,11 +621,10 @@ def main():
     torch.cuda.synchronize()
     l0 = vvq2.launches()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0.record(stream)
-        steps(args.steps)
-        e1.record(stream)
-        torch.cuda.synchronize()
+    e0.record(stream)
+    steps(args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
     launches = vvq2.launches() - l0
     ms = e0.elapsed_time(e1)
     if world > 1:
@@ -686,12 +691,13 @@ def main():
                      "attn_decode": {"achieved_gbs": round(a_bytes / (a_ms / 1000.0) / 1e9, 1) if a_n else None,
                                      "mean_launch_us": round(1000.0 * a_ms / a_n, 3) if a_n else None},
                      "step_hbm_gbs": round(synth.weight_bytes(model) * 1.0 / (ms / args.steps / 1000.0) / 1e9, 1)},
-        "clocks": clk.summary(),
     }
     if not args.no_c3:
         line["c3"] = c3_measure(eng, hp, torch, dist, rank, world, sh, args.c3_steps)
     if not args.no_prefill:
         line["prefill"] = prefill_measure(vvq2, synth, torch, local, sh, args.prefill_tokens)
+    clk.__exit__(None, None, None)
+    line["clocks"] = clk.summary()
     if rank == 0 and world == 1 and not args.no_cpu:
         rate, n, cores = cpu_decode_rate(model, hp, args.kv)
         line["cpu_baseline"] = {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",

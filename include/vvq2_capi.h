@@ -228,19 +228,27 @@ int  vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int 
  *   block_table int32 [seq][max_pages] logical -> physical page
  *   row_meta   int32 [n_rows][4] = {seq, pos, (unused), kv_len}; keys j < kv_len
  *              with j <= pos are attended
- *   max_kv     an upper bound of every row's kv_len (sizes the split grid)
+ *   max_kv     an upper bound of every row's kv_len (sizes the split grid); a
+ *              row with more keys than max_kv (or than its block-table row
+ *              holds) is clamped to the first keys and sets error word 5
  *   out        f32 [n_rows][n_heads*head_dim]
+ *   err_out    int the caller owns (device memory, or pinned / managed host
+ *              memory), or NULL: receives the kernels' error word in stream
+ *              order -- 0 ok, 1 a bounded wait gave up (out is not valid),
+ *              5 a row was clamped.  A return of 0 only says the work was
+ *              enqueued; read *err_out after the stream has finished.
  * Limits: n_rows <= 8, n_heads*head_dim <= 4096, n_heads <= 64, n_kv_heads
  * <= 16, head_dim 32/64/128, n_heads/n_kv_heads <= 8; beyond them it returns
  * VVQ2_ERR_INVALID_ARG.  The array (about 2.1 MB) stays allocated on every GPU
  * that loads the library until exit.  Calls share it: calls that overlap on
- * the GPU race and must be serialized by the caller.  The first call on a
- * device looks up the array's device address (cudaGetSymbolAddress); make that
- * first call before any stream capture.  Allocates nothing. */
+ * the GPU race and must be serialized by the caller.  Every call looks up the
+ * array's device address (cudaGetSymbolAddress) in the calling thread's
+ * current context; the first call in a context loads the library's module
+ * there, so make it before any stream capture.  Allocates nothing. */
 int  vvq2_attention_decode_noalloc(const float* q, const void* k_pages, const void* v_pages,
                                    const int* block_table, int max_pages, const int* row_meta,
                                    int n_rows, int max_kv, int n_heads, int n_kv_heads,
-                                   int head_dim, float* out, void* stream);
+                                   int head_dim, float* out, int* err_out, void* stream);
 
 /* ---- measurement (no counterpart in the reference, which has no profiler
  * hooks; used by bench.py for the roofline figures) ------------------------

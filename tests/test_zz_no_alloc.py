@@ -9,7 +9,15 @@ identity and whose FFN is zero makes vvq2_forward's output minus its input
 exactly the attention output; the allocation-free call, given the same Q and
 the K/V pages that forward left behind, must match it within the tolerance of
 the other parity tests, on two calls in a row (different lengths, so stale
-scratch from the first call would show in the second)."""
+scratch from the first call would show in the second).
+
+A second test covers each kernel path the entry point can take -- one split,
+the in-kernel merge by the last split (2-4 splits), the separate merge kernel
+(more splits) -- at head_dim 32, 64 and 128 with a shuffled block table,
+against a direct evaluation of the attention formula, and reads the error
+word back through `err_out`: 0 on valid calls, 5 when a row is longer than
+`max_kv` (its keys are then clamped, never read past the grid or the
+block-table row)."""
 import ctypes as C
 
 import numpy as np
@@ -81,10 +89,13 @@ def test_noalloc_attention_matches_forward(vv):
         meta = torch.tensor([[0, pos, pos, pos + 1], [1, pos, pos, pos + 1]], dtype=torch.int32, device=dev)
         q_d = torch.from_numpy(q).to(dev)
         out = torch.zeros((2, nq * hd), dtype=torch.float32, device=dev)
+        err = torch.full((1,), -1, dtype=torch.int32, device=dev)
         rc = lib.vvq2_attention_decode_noalloc(q_d.data_ptr(), k_d.data_ptr(), v_d.data_ptr(), bt.data_ptr(),
                                                max_pages, meta.data_ptr(), 2, pos + 1, nq, nkv, hd,
-                                               out.data_ptr(), None)
+                                               out.data_ptr(), err.data_ptr(), None)
         assert rc == 0, rc
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
         torch.cuda.synchronize()
         got = out.cpu().numpy()
         assert rel_err(got, ref) < TOL, (pos, rel_err(got, ref))
@@ -92,5 +103,86 @@ def test_noalloc_attention_matches_forward(vv):
     # sizes beyond the fixed scratch are refused, not truncated
     rc = lib.vvq2_attention_decode_noalloc(q_d.data_ptr(), k_d.data_ptr(), v_d.data_ptr(), bt.data_ptr(),
                                            max_pages, meta.data_ptr(), 9, pos + 1, nq, nkv, hd,
-                                           out.data_ptr(), None)
+                                           out.data_ptr(), None, None)
     assert rc == -2
+
+
+def _attention_ref(q, kp, vp, bt, meta, nq, nkv, hd):
+    """softmax(q_f16 . K^T / sqrt(hd)) V over keys j < min(pos + 1, kv_len), in f64
+    (ggml's flash attention rounds Q to the f16 type of K)."""
+    G = nq // nkv
+    out = np.zeros((len(meta), nq * hd), np.float64)
+    for r, (seq, pos, _, kvlen) in enumerate(meta):
+        n = min(pos + 1, kvlen)
+        for h in range(nq):
+            g = h // G
+            qh = q[r, h * hd:(h + 1) * hd].astype(np.float16).astype(np.float64)
+            ks = np.stack([kp[bt[seq, j // 64], g, j % 64] for j in range(n)]).astype(np.float64)
+            vs = np.stack([vp[bt[seq, j // 64], g, j % 64] for j in range(n)]).astype(np.float64)
+            s = ks @ qh / np.sqrt(hd)
+            p = np.exp(s - s.max())
+            out[r, h * hd:(h + 1) * hd] = (p / p.sum()) @ vs
+    return out
+
+
+# (head_dim, n_heads, n_kv_heads, max_kv, kv lengths of the two calls): one
+# split (<= 64 keys), 2-4 splits merged by the last split, and > 4 splits
+# merged by the separate kernel
+PATHS = [
+    (32, 8, 2, 60, ([60, 17, 33], [41, 60, 1])),
+    (64, 14, 2, 250, ([250, 130, 65], [190, 250, 64])),
+    (128, 12, 2, 700, ([700, 333], [512, 699])),
+]
+
+
+@pytest.mark.parametrize("hd,nq,nkv,max_kv,lens", PATHS, ids=["hd32-1split", "hd64-inline", "hd128-kernel"])
+def test_noalloc_attention_paths_vs_formula(vv, hd, nq, nkv, max_kv, lens):
+    import torch
+
+    rng = np.random.default_rng(hd * 7 + max_kv)
+    dev = torch.device("cuda:0")
+    lib = vv.lib()
+    n_seq = 3
+    max_pages = (max_kv + 63) // 64 + 1
+    n_pages = n_seq * max_pages
+    kp = rng.standard_normal((n_pages, nkv, 64, hd)).astype(np.float16)
+    vp = rng.standard_normal((n_pages, nkv, 64, hd)).astype(np.float16)
+    bt = rng.permutation(n_pages).astype(np.int32).reshape(n_seq, max_pages)
+    k_d = torch.from_numpy(kp).to(dev)
+    v_d = torch.from_numpy(vp).to(dev)
+    bt_d = torch.from_numpy(bt).to(dev)
+    for call, lengths in enumerate(lens):          # two calls in a row, different lengths
+        rows = len(lengths)
+        meta = np.array([[(r + call) % n_seq, L - 1, L - 1, L] for r, L in enumerate(lengths)], np.int32)
+        q = rng.standard_normal((rows, nq * hd)).astype(np.float32)
+        out = torch.zeros((rows, nq * hd), dtype=torch.float32, device=dev)
+        err = torch.full((1,), -1, dtype=torch.int32, device=dev)
+        meta_d = torch.from_numpy(meta).to(dev)
+        q_d = torch.from_numpy(q).to(dev)
+        rc = lib.vvq2_attention_decode_noalloc(q_d.data_ptr(), k_d.data_ptr(), v_d.data_ptr(), bt_d.data_ptr(),
+                                               max_pages, meta_d.data_ptr(), rows, max_kv, nq, nkv, hd,
+                                               out.data_ptr(), err.data_ptr(), None)
+        assert rc == 0, rc
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0, int(err.item())
+        ref = _attention_ref(q, kp, vp, bt, meta, nq, nkv, hd)
+        e = rel_err(out.cpu().numpy(), ref)
+        assert e < TOL, (call, e)
+
+    # a row longer than max_kv: clamped to the keys the launch covers, error word 5
+    L = max_kv + 64
+    meta = np.array([[0, L - 1, L - 1, L]], np.int32)
+    q = rng.standard_normal((1, nq * hd)).astype(np.float32)
+    out = torch.zeros((1, nq * hd), dtype=torch.float32, device=dev)
+    err = torch.full((1,), -1, dtype=torch.int32, device=dev)
+    rc = lib.vvq2_attention_decode_noalloc(torch.from_numpy(q).to(dev).data_ptr(), k_d.data_ptr(), v_d.data_ptr(),
+                                           bt_d.data_ptr(), max_pages, torch.from_numpy(meta).to(dev).data_ptr(),
+                                           1, max_kv, nq, nkv, hd, out.data_ptr(), err.data_ptr(), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 5
+    split = max(64, ((max_kv + 15) // 16 + 63) // 64 * 64)
+    covered = min((max_kv + split - 1) // split * split, max_pages * 64)
+    clamped = np.array([[0, covered - 1, covered - 1, covered]], np.int32)
+    e = rel_err(out.cpu().numpy(), _attention_ref(q, kp, vp, bt, clamped, nq, nkv, hd))
+    assert e < TOL, e

@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(HD / 4 * MG_SG) k_attn_merge(const AttnDecodeA
     const int h = blockIdx.x, m = blockIdx.y;
     const int tid = threadIdx.x, d4 = tid % D4, sg = tid / D4;
     const RowMeta rm = a.meta[m];
-    const int lim = min(rm.pos + 1, rm.kvlen);
+    const int lim = ad::key_limit(a, rm, false);   // the attention kernel flagged a clamped row
     const int ns = lim > 0 ? (lim + a.split - 1) / a.split : 0;
     if (ns <= 1) return;   // no keys, or one split: the attention kernel wrote the output
     float4 p[MG_PER];
@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(AM_THREADS) k_attn_mma(const __grid_constant__
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = a.nq / a.nkv;
     const RowMeta rm = a.meta[m];
-    const int lim = min(rm.pos + 1, rm.kvlen);
+    const int lim = ad::key_limit(a, rm, s == 0 && tid == 0);
     if (lim <= 0) {
         // no keys for this row here (another rank holds its part of the sequence)
         if (s == 0) {
@@ -465,10 +465,13 @@ cudaError_t attn_decode_launch(const AttnDecodeArgs& a, cudaStream_t st) {
 //
 // The array is shared by every call: calls that overlap on the GPU (two
 // streams, two threads) race on it and must be serialized by the caller.  Each
-// call clears the counters and the error word it relies on before launching.
-// The device address of the array is looked up once per device, on that
-// device's first call (cudaGetSymbolAddress); make that first call before any
-// stream capture.
+// call clears the counters and the error word it relies on before launching,
+// and copies the error word out to the caller's `err_out` after the kernels,
+// in stream order (a later call clears it again).  The array's device address
+// and the kernel's shared-memory opt-in are looked up on every call, in the
+// context current on the calling thread, so a call made in another
+// framework's context never uses an address or attribute of a different
+// context; neither lookup allocates.
 namespace {
 
 constexpr int NA_MAX_ROWS = 8;
@@ -483,8 +486,11 @@ constexpr size_t NA_BYTES = NA_PART + NA_ML + NA_COUNTERS + 256;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_BYTES];
 
-constexpr int NA_MAX_DEVICES = 64;
-unsigned char* g_noalloc_ptr[NA_MAX_DEVICES] = {};
+template <int HD>
+cudaError_t noalloc_opt_in() {
+    return cudaFuncSetAttribute(k_attn_decode<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                ad::tile_smem_bytes(HD));
+}
 
 }  // namespace
 
@@ -493,7 +499,7 @@ unsigned char* g_noalloc_ptr[NA_MAX_DEVICES] = {};
 extern "C" int vvq2_attention_decode_noalloc(const float* q, const void* k_pages, const void* v_pages,
                                              const int* block_table, int max_pages, const int* row_meta,
                                              int n_rows, int max_kv, int n_heads, int n_kv_heads,
-                                             int head_dim, float* out, void* stream) {
+                                             int head_dim, float* out, int* err_out, void* stream) {
     using namespace vvq2;
     if (!q || !k_pages || !v_pages || !block_table || !row_meta || !out || n_rows <= 0 || max_kv <= 0 ||
         max_pages <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
@@ -502,18 +508,19 @@ extern "C" int vvq2_attention_decode_noalloc(const float* q, const void* k_pages
         n_kv_heads > NA_MAX_KV || n_heads / n_kv_heads > AD_MAXG ||
         (head_dim != 32 && head_dim != 64 && head_dim != 128) || max_kv > max_pages * KV_PAGE)
         return -2;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= NA_MAX_DEVICES) return -10;
-    if (!g_noalloc_ptr[dev]) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
-            cudaGetLastError();
-            return -9;   // VVQ2_ERR_CUDA
-        }
-        if (attn_decode_prepare() != cudaSuccess) return -9;
-        g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+    // device address of the array in the calling thread's current context
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+        cudaGetLastError();
+        return -9;   // VVQ2_ERR_CUDA
     }
-    unsigned char* base = g_noalloc_ptr[dev];
+    const cudaError_t oe = head_dim == 32 ? noalloc_opt_in<32>() : head_dim == 64 ? noalloc_opt_in<64>()
+                                                                                  : noalloc_opt_in<128>();
+    if (oe != cudaSuccess) {
+        cudaGetLastError();
+        return -9;
+    }
+    unsigned char* base = static_cast<unsigned char*>(p);
     // whole pages per split, at most NA_MAX_SPLITS splits over max_kv keys
     int split = (max_kv + NA_MAX_SPLITS - 1) / NA_MAX_SPLITS;
     split = (split + KV_PAGE - 1) / KV_PAGE * KV_PAGE;
@@ -543,5 +550,8 @@ extern "C" int vvq2_attention_decode_noalloc(const float* q, const void* k_pages
     // counters and the error word must start at zero; partials are written before read
     if (cudaMemsetAsync(a.counters, 0, NA_COUNTERS + sizeof(int), st) != cudaSuccess) return -9;
     if (attn_decode_launch(a, st) != cudaSuccess) return -9;
+    // the kernels' error word (0, 1 = a bounded wait gave up, 5 = a row longer
+    // than max_kv or its block-table row) into the caller's memory, in stream order
+    if (err_out && cudaMemcpyAsync(err_out, a.err, sizeof(int), cudaMemcpyDefault, st) != cudaSuccess) return -9;
     return 0;
 }

@@ -28,6 +28,24 @@ struct __align__(16) Shared {   // qs is read as float4; arrays of Shared stay a
 // dynamic shared memory per group: K and V, two stages each
 __host__ __device__ constexpr int tile_smem_bytes(int hd) { return 4 * TILE * hd * 2; }
 
+// Error word value of a row whose key count exceeds what the launch covers.
+constexpr int ERR_ROW_TOO_LONG = 5;
+
+// Keys row `rm` attends: min(pos + 1, kv_len), clamped to what the launch
+// covers -- max_splits * split keys (the grid) and max_pages * 64 (the
+// block-table row).  A clamped row records ERR_ROW_TOO_LONG in a.err (when
+// `flag`), so the caller learns that its output covers only the first keys;
+// nothing is read past the block-table row or written past the split slots.
+__device__ __forceinline__ int key_limit(const AttnDecodeArgs& a, const RowMeta& rm, bool flag) {
+    int lim = min(rm.pos + 1, rm.kvlen);
+    const int cap = min(a.max_splits * a.split, a.kv.max_pages * TILE);
+    if (lim > cap) {
+        if (flag && a.err) atomicCAS(a.err, 0, ERR_ROW_TOO_LONG);
+        lim = cap;
+    }
+    return lim;
+}
+
 // Initialise the two stage barriers of a group (one thread, once).
 __device__ __forceinline__ void init_bars(Shared& sh) {
     tc::mbar_init(&sh.bar[0], 1);
@@ -47,7 +65,7 @@ __device__ bool item(const AttnDecodeArgs& a, int s, int g, int m, int tid, __ha
     const int lane = tid & 31, warp = tid >> 5;
     const int G = a.nq / a.nkv;
     const RowMeta rm = a.meta[m];
-    const int lim = min(rm.pos + 1, rm.kvlen);
+    const int lim = key_limit(a, rm, s == 0 && tid == 0);
     if (lim <= 0) {
         // no keys for this row here (another rank holds its part of the
         // sequence): zeros and LSE -inf, written once (split 0)

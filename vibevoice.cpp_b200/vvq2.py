@@ -73,7 +73,7 @@ def lib() -> C.CDLL:
             "vvq2_kernel_launches": (I64, []),
             "vvq2_profile": (I, [P, I]),
             "vvq2_debug_gemm": (I, [I, P, I, I, P, I, P]),
-            "vvq2_attention_decode_noalloc": (I, [P, P, P, P, I, P, I, I, I, I, I, P, P]),
+            "vvq2_attention_decode_noalloc": (I, [P, P, P, P, I, P, I, I, I, I, I, P, P, P]),
             "vvq2_profile_read": (I, [P, I, P, P, P]),
             "vvq2_mega_trace": (I, [P, P, C.c_int64, P, P]),
             "vvq2_nccl_unique_id": (I, [P]),
