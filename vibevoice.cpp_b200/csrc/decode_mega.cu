@@ -1,11 +1,10 @@
 // decode_mega.cu -- the whole greedy decode step of a Q8_0 Qwen2 stack as ONE
 // persistent kernel (sm_100a), for 1 or 2 rows (one sequence or the CFG pair).
 //
-// A decode step of the 0.5B model is ~120 dependent phases (per layer:
-// QKV -> attention -> O-proj -> gate/up -> down) over 0.9-9 MB matrices.  As
-// separate launches every phase pays launch and prologue latency and starts
-// its weight stream cold.  Here one CTA per SM walks the phase list,
-// separated by grid-wide barriers, and the weight stream does not stop:
+// A decode step of the 0.5B model is ~140 dependent stages (per layer:
+// QKV -> attention -> merge -> O-proj -> gate/up -> down) over 0.9-9 MB
+// matrices.  One CTA per SM walks the stage list and the weight stream does
+// not stop:
 //
 //  * weights: every warp owns D slots of a shared-memory ring (D = 1 or 2)
 //    and streams its own share of the CTA's weight tiles: the CTA's
@@ -14,25 +13,46 @@
 //    Right after computing a tile a warp bulk-copies (cp.async.bulk; a run
 //    of Q8_0 rows with their scales is one contiguous range) its next tile
 //    into the freed slot.  Weights do not depend on activations, so a warp's
-//    next tiles -- often of the next phase -- are in flight while it waits in
-//    a grid barrier or runs attention, and no warp waits for another's slot.
-//  * each warp stages nothing of its own: the CTA stages the phase's
-//    activation rows (RMSNorm'd where the layer norms) from L2 into shared
-//    memory, then each warp computes its tiles' T x M dot products over the
-//    full K (exact dequantized int8 weights x f32 activations, packed FFMA2),
+//    next tiles -- often of the next stage -- are in flight while it waits
+//    for its inputs or runs attention.
+//  * hand-over between stages: there is no grid barrier.  Every value one
+//    stage hands to the next (hidden rows, raw q|k|v, attention partials,
+//    attention output, SwiGLU output) is written as a FLAGGED WORD, one
+//    64-bit store of (tag << 32 | f32 bits).  A 64-bit aligned store is
+//    single-copy atomic, so a reader that sees the expected tag sees the
+//    value with it; the consumer polls exactly the words it needs until all
+//    carry the tag of the current launch and stage, which costs one L2 round
+//    trip after the last producer instead of a barrier (release fence, atomic
+//    round trip, poll) followed by a separate read.  Each buffer is reused by
+//    every layer: every stage consumes ALL words of its predecessor's buffer
+//    (or, for attention, all words of its KV head group), so a writer of
+//    layer l + 1 is causally after every reader of layer l and no word is
+//    overwritten while still unread.
+//  * each warp stages nothing of its own: the CTA stages the stage's
+//    activation rows (RMSNorm'd where the layer norms) into shared memory,
+//    then each warp computes its tiles' T x M dot products over the full K
+//    (exact dequantized int8 weights x f32 activations, packed FFMA2),
 //    reduces them with one transposing butterfly and applies the epilogue
-//    (bias, residual add, SwiGLU, running argmax) straight to global memory.
+//    (bias, residual add, SwiGLU, running argmax).
 //  * attention: one item per (row, KV head, split of whole 64-key pages) on
-//    128-thread groups.  The first page of each group's first item is
-//    requested by TMA BEFORE the QKV -> attention barrier (past keys do not
-//    depend on this step).  The item applies RoPE to this step's raw q/k,
-//    patches the new key/value row into its tile, appends it to the paged
-//    cache, and the last split to finish merges the partials (log-sum-exp).
+//    128-thread groups.  The first page of each group's item is requested by
+//    TMA as soon as the shared memory it lands in is free (past keys do not
+//    depend on this step), i.e. during the previous layer's down-projection
+//    hand-over.  The item applies RoPE to this step's raw q/k, patches the new
+//    key/value row into its tile, appends it to the paged cache and writes an
+//    (O, max, sum) partial; one CTA per (row, q head) merges the partials
+//    (log-sum-exp) into the attention output.
+//  * the end of the step: each CTA folds its lm_head rows into a running
+//    argmax key (atomicMax); the last CTA to arrive (an acquire-release
+//    counter) writes the token ids, advances the row positions and the launch
+//    epoch the tags derive from.
 //
 // Every wait is bounded.  A wait that gives up records an error code, raises
-// the global abort flag and this CTA's `fail` flag; all warps then skip the
-// remaining work (control flow only changes at grid barriers, where it is
-// uniform) and wait for their copies in flight before returning.
+// the global abort flag and this CTA's `fail` flag; every other poll checks
+// them, CTAs skip their remaining work at the next CTA-wide check (a
+// __syncthreads_or, so control flow stays uniform), wait for their bulk copies
+// in flight and still arrive at the end-of-step counter.  The host then clears
+// the flagged buffers and the abort flag before reporting the error.
 #include <algorithm>
 
 #include "common.cuh"
@@ -50,9 +70,15 @@ constexpr int MAX_STAGES = 32;          // ring slots: NCW x D
 constexpr int ATT_THREADS = 128;
 constexpr int MAXG = 8;                 // q heads per KV head
 constexpr int PAGE = KV_PAGE;           // keys per page / tile
-constexpr int MAX_MERGE = 64;
-constexpr uint32_t BAR_POLLS = 1u << 22;
-constexpr uint32_t WAIT_POLLS = 1u << 24;
+constexpr int MAX_MERGE = MEGA_MAX_SPLITS;
+constexpr uint32_t WAIT_POLLS = 1u << 24;   // mbarrier try_waits
+constexpr uint32_t LL_POLLS = 1u << 21;     // L2 polls of a flagged word (~0.5 us each)
+constexpr int SB = 1;                   // flagged float4 groups in flight per thread while staging
+                                        // (more spill the GEMV tile loop: the kernel sits at 128 registers)
+// pause between unsuccessful poll rounds: every waiting thread of every CTA
+// polls, and re-requesting at the L2 round-trip rate would flood L2 with
+// requests (starving the producers and the weight stream)
+constexpr unsigned POLL_PAUSE_NS = 128;
 
 enum { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DOWN = 3, PH_LM = 4 };
 
@@ -63,21 +89,33 @@ struct AttConst {
     static constexpr int GROUP_BYTES = 2 * TILE_BYTES;           // K and V of one page
 };
 
-// per-group attention state (in the phase-shared dynamic region)
+// per-group attention state (in the attention part of the shared region)
 template <int HD>
 struct __align__(16) AttSh {
     float qs[MAXG][HD];            // roped q, rounded to f16 (ggml FA converts Q to the K type)
     float sc[MAXG][PAGE];
     float run_max[MAXG], run_sum[MAXG], alpha[MAXG];
     __half kn[HD], vn[HD];         // this step's key (roped) and value row
-    int is_last, failed;
+    int failed;
 };
 
 struct Ctl {
-    unsigned long long target;
-    int aborted;                   // set only inside grid_sync: uniform control flow
-    int fail;                      // set by any warp whose wait gave up: ends other waits early
-    int nbar;
+    int fail;                      // a wait of this CTA gave up or the step is aborting
+};
+
+// Tags of the flagged words of one launch: 8 per layer plus the embedding.
+// Never 0 (the value buffers are cleared to), distinct for 2^32 - 1 stages.
+struct Tags {
+    unsigned long long base;
+    __device__ __forceinline__ uint32_t at(unsigned long long k) const {
+        return (uint32_t)((base + k) % 0xffffffffull) + 1u;
+    }
+    __device__ __forceinline__ uint32_t x_in(int l) const { return at(l == 0 ? 0 : 8ull * (l - 1) + 6); }
+    __device__ __forceinline__ uint32_t qkv(int l) const { return at(8ull * l + 1); }
+    __device__ __forceinline__ uint32_t part(int l) const { return at(8ull * l + 2); }
+    __device__ __forceinline__ uint32_t att(int l) const { return at(8ull * l + 3); }
+    __device__ __forceinline__ uint32_t x_o(int l) const { return at(8ull * l + 4); }
+    __device__ __forceinline__ uint32_t fa(int l) const { return at(8ull * l + 5); }
 };
 
 __device__ __forceinline__ unsigned long long gtimer() {
@@ -86,8 +124,15 @@ __device__ __forceinline__ unsigned long long gtimer() {
     return t;
 }
 
+// (The warp reconverges before going on: a warp left diverged by a one-thread
+// branch must not enter the out-of-line stage_ll, whose body assumes a
+// converged warp and is followed by aligned CTA barriers.)
 __device__ __forceinline__ void trace_mark(const MegaArgs& a, int slot) {
-    if (a.trace) a.trace[(size_t)slot * gridDim.x + blockIdx.x] = gtimer();
+    if (a.trace) {
+        const unsigned long long t = gtimer();
+        if (threadIdx.x == 0) a.trace[(size_t)slot * gridDim.x + blockIdx.x] = t;
+        __syncwarp();
+    }
 }
 
 __device__ __forceinline__ void cbar() { __syncthreads(); }
@@ -126,42 +171,169 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
-__device__ void raise_fail(const MegaArgs& a, Ctl& ctl, int code) {
-    atomicCAS(a.err, 0, code);
+// The first failure of a launch also records where: code, CTA, an index
+// (word offset for flagged-word waits, else 0), the expected tag and the last
+// word seen.
+__device__ void raise_fail(const MegaArgs& a, Ctl& ctl, int code, long long where = 0, uint32_t tag = 0,
+                           uint64_t seen = 0) {
+    if (atomicCAS(a.err, 0, code) == 0 && a.err_info) {
+        a.err_info[0] = ((unsigned long long)blockIdx.x << 32) | (uint32_t)code;
+        a.err_info[1] = (unsigned long long)where;
+        a.err_info[2] = ((unsigned long long)*(volatile unsigned int*)a.epoch << 32) | tag;
+        a.err_info[3] = seen;
+    }
     atomicExch(a.abort, 1);
     *(volatile int*)&ctl.fail = 1;
 }
 
-// Grid barrier over the consumer threads of every CTA.  The arrival is one
-// release reduction (orders this CTA's writes, observed through the CTA
-// barrier, before it); the wait polls with acquire loads.
-__device__ void grid_sync(const MegaArgs& a, Ctl& ctl) {
-    cbar();
-    if (threadIdx.x == 0) {
-        trace_mark(a, 1 + 2 * ctl.nbar);
-        ctl.target += gridDim.x;
-        asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(a.bar_count), "l"(1ull) : "memory");
-        uint32_t i = 0;
-        while (true) {
-            unsigned long long v;
-            asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a.bar_count) : "memory");
-            if (v >= ctl.target) break;
-            if (*(volatile int*)a.abort) break;
-            if (++i > BAR_POLLS) {
-                atomicCAS(a.err, 0, 3);
-                atomicExch(a.abort, 1);
-                break;
+// Uniform over the CTA (and a CTA barrier): true once any thread of the CTA
+// failed or another CTA raised the abort flag.
+// (A CTA learns of another CTA's failure when one of its polls sees the
+// abort flag; no global read is spent here.)
+__device__ __forceinline__ bool cta_failed(const MegaArgs&, Ctl& ctl) {
+    return __syncthreads_or(*(volatile int*)&ctl.fail) != 0;
+}
+
+// ------------------------------------------------------------ flagged words
+__device__ __forceinline__ uint64_t ll_word(float v, uint32_t tag) {
+    return ((uint64_t)tag << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ bool ll_ok(uint64_t w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
+__device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
+
+__device__ __forceinline__ void ll_put(uint64_t* p, float v, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(ll_word(v, tag)) : "memory");
+}
+// two flagged words at a 16-byte aligned address (each word is its own atomic unit)
+__device__ __forceinline__ void ll_put2(uint64_t* p, float v0, float v1, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(ll_word(v0, tag)),
+                 "l"(ll_word(v1, tag))
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t ll_get(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ void ll_get2(const uint64_t* p, uint64_t& w0, uint64_t& w1) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+}
+
+// Called every 32nd unsuccessful poll round: give up once the CTA is failing,
+// the step is aborting, or the poll budget is spent (then raise the failure).
+__device__ __forceinline__ bool poll_give_up(const MegaArgs& a, Ctl& ctl, uint32_t it, int code,
+                                             const uint64_t* p = nullptr, uint32_t tag = 0, uint64_t seen = 0) {
+    if (*(volatile int*)&ctl.fail || *(volatile int*)a.abort) {
+        *(volatile int*)&ctl.fail = 1;
+        return true;
+    }
+    if (it > LL_POLLS) {
+        raise_fail(a, ctl, code, p ? (long long)(p - a.xl) : 0, tag, seen);
+        return true;
+    }
+    return false;
+}
+
+// One flagged word, bounded.  Returns 0 after giving up (the CTA is failing).
+__device__ float ll_wait(const MegaArgs& a, Ctl& ctl, const uint64_t* p, uint32_t tag, int code) {
+    for (uint32_t it = 1;; ++it) {
+        const uint64_t w = ll_get(p);
+        if (ll_ok(w, tag)) return ll_val(w);
+        if ((it & 31) == 0 && poll_give_up(a, ctl, it, code, p, tag, w)) return 0.f;
+        __nanosleep(POLL_PAUSE_NS);
+    }
+}
+
+// ------------------------------------------------------------ activations
+// act layout: float4 index ((m * 4 + g) * NC + c) holds elements
+// 16c + 4g .. 16c + 4g + 3 of row m, so the lanes of a warp (consecutive
+// chunks c) read consecutive 16-byte words.
+//
+// The rows come from flagged words src[m][K] with tag `tag`: every thread
+// requests up to SB groups of 4 words at once and re-polls only the groups
+// not yet tagged, so a stage costs about one L2 round trip after its last
+// producer.  Where the stage RMSNorms its input, act = x * w (the norm
+// weight) and the per-warp partial sums of squares go to red[m][warp] (in a
+// fixed order, independent of arrival order); the row scale
+// 1/sqrt(mean(x^2) + eps) is applied to the dot products instead
+// (W (x s o w) = s W (x o w)), so no second pass over act is needed.
+// The caller follows with cta_failed() (the CTA barrier that publishes act).
+template <int MB>
+__device__ void stage_ll(const MegaArgs& a, Ctl& ctl, const uint64_t* src, int K, uint32_t tag, const float* norm_w,
+                         float* act, float* red) {
+    __syncwarp();   // entered by converged warps only (see trace_mark)
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int NC = K / 16, K4 = K / 4, NI = MB * K4;   // group i: words 4i..4i+3 = row i / K4, float4 i % K4
+    float4* act4 = reinterpret_cast<float4*>(act);
+    float ss0 = 0.f, ss1 = 0.f;
+    bool bad = false;
+    for (int b0 = tid; b0 < NI && !bad; b0 += SB * NCT) {
+        uint64_t w[SB][4];
+        uint32_t pend = 0;
+#pragma unroll
+        for (int j = 0; j < SB; ++j) {
+            const int i = b0 + j * NCT;
+            if (i < NI) {
+                ll_get2(src + 4 * (size_t)i, w[j][0], w[j][1]);
+                ll_get2(src + 4 * (size_t)i + 2, w[j][2], w[j][3]);
+                pend |= 1u << j;
             }
         }
-        __threadfence();
-        if (*(volatile int*)a.abort) {
-            ctl.aborted = 1;
-            *(volatile int*)&ctl.fail = 1;
+        // poll: re-request only the groups not yet tagged
+        for (uint32_t it = 1;; ++it) {
+#pragma unroll
+            for (int j = 0; j < SB; ++j)
+                if (ll_ok(w[j][0], tag) && ll_ok(w[j][1], tag) && ll_ok(w[j][2], tag) && ll_ok(w[j][3], tag))
+                    pend &= ~(1u << j);
+            if (!pend) break;
+            if ((it & 31) == 0 && poll_give_up(a, ctl, it, 6)) {
+                bad = true;
+                break;
+            }
+            __nanosleep(POLL_PAUSE_NS);
+#pragma unroll
+            for (int j = 0; j < SB; ++j) {
+                if ((pend >> j) & 1u) {
+                    const uint64_t* p = src + 4 * (size_t)(b0 + j * NCT);
+                    ll_get2(p, w[j][0], w[j][1]);
+                    ll_get2(p + 2, w[j][2], w[j][3]);
+                }
+            }
         }
-        trace_mark(a, 2 + 2 * ctl.nbar);
-        ctl.nbar += 1;
+        // values, in group order (the sums of squares do not depend on arrival order)
+#pragma unroll
+        for (int j = 0; j < SB; ++j) {
+            const int i = b0 + j * NCT;
+            if (i < NI) {
+                const int m = MB == 1 ? 0 : (i >= K4 ? 1 : 0);
+                const int k4 = i - m * K4;
+                float4 v = make_float4(ll_val(w[j][0]), ll_val(w[j][1]), ll_val(w[j][2]), ll_val(w[j][3]));
+                if (norm_w) {
+                    const float4 nw = __ldg(reinterpret_cast<const float4*>(norm_w) + k4);
+                    float q = m == 0 ? ss0 : ss1;
+                    q = fmaf(v.x, v.x, q);
+                    q = fmaf(v.y, v.y, q);
+                    q = fmaf(v.z, v.z, q);
+                    q = fmaf(v.w, v.w, q);
+                    if (m == 0) ss0 = q;
+                    else ss1 = q;
+                    v.x = __fmul_rn(v.x, nw.x);
+                    v.y = __fmul_rn(v.y, nw.y);
+                    v.z = __fmul_rn(v.z, nw.z);
+                    v.w = __fmul_rn(v.w, nw.w);
+                }
+                act4[(m * 4 + (k4 & 3)) * NC + (k4 >> 2)] = v;
+            }
+        }
     }
-    cbar();
+    if (norm_w) {
+        const float t0 = warp_sum(ss0);
+        if (lane == 0) red[warp] = t0;
+        if (MB > 1) {
+            const float t1 = warp_sum(ss1);
+            if (lane == 0) red[NCW + warp] = t1;
+        }
+    }
 }
 
 // ------------------------------------------------------------ tile schedule
@@ -237,53 +409,6 @@ __device__ __forceinline__ void ring_issue(WarpRing& w, const Geo* tab, int nph,
     w.issued += 1;
     w.ij += NCW;
     ring_normalize(w, tab, nph);
-}
-
-// ------------------------------------------------------------ activations
-// act layout: float4 index ((m * 4 + g) * NC + c) holds elements
-// 16c + 4g .. 16c + 4g + 3 of row m, so the lanes of a warp (consecutive
-// chunks c) read consecutive 16-byte words.
-//
-// Where the phase RMSNorms its input, act = x * w (the norm weight) and the
-// per-warp partial sums of squares go to red[m][warp]; the row scale
-// 1/sqrt(mean(x^2) + eps) is applied to the dot products instead
-// (W (x s o w) = s W (x o w)), so no second pass over act is needed.
-template <int MB>
-__device__ void stage(const float* x, const float* norm_w, int K, float* act, float* red) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int NC = K / 16, K4 = K / 4;
-    float4* act4 = reinterpret_cast<float4*>(act);
-    float ss[MB];
-#pragma unroll
-    for (int m = 0; m < MB; ++m) ss[m] = 0.f;
-#pragma unroll 4
-    for (int k4 = tid; k4 < K4; k4 += NCT) {
-        const int c = k4 >> 2, g = k4 & 3;
-        const float4 w = norm_w ? __ldg(reinterpret_cast<const float4*>(norm_w) + k4) : make_float4(1.f, 1.f, 1.f, 1.f);
-#pragma unroll
-        for (int m = 0; m < MB; ++m) {
-            float4 v = __ldcg(reinterpret_cast<const float4*>(x + (size_t)m * K) + k4);
-            if (norm_w) {
-                ss[m] = fmaf(v.x, v.x, ss[m]);
-                ss[m] = fmaf(v.y, v.y, ss[m]);
-                ss[m] = fmaf(v.z, v.z, ss[m]);
-                ss[m] = fmaf(v.w, v.w, ss[m]);
-                v.x = __fmul_rn(v.x, w.x);
-                v.y = __fmul_rn(v.y, w.y);
-                v.z = __fmul_rn(v.z, w.z);
-                v.w = __fmul_rn(v.w, w.w);
-            }
-            act4[(m * 4 + g) * NC + c] = v;
-        }
-    }
-    if (norm_w) {
-#pragma unroll
-        for (int m = 0; m < MB; ++m) {
-            const float t = warp_sum(ss[m]);
-            if (lane == 0) red[m * NCW + warp] = t;
-        }
-    }
-    cbar();
 }
 
 // RMSNorm row scale from the staged partial sums (ggml_rms_norm: 1/sqrt(mean + eps)).
@@ -374,13 +499,18 @@ __device__ __forceinline__ float warp_transpose_sum(float (&v)[NV], int lane) {
     return v[0];
 }
 
-// One tile of a GEMV phase: math + epilogue.  The epilogue's global
+// Tags a GEMV stage writes with (out) and reads its residual with (res).
+struct StageTags {
+    uint32_t out, res;
+};
+
+// One tile of a GEMV stage: math + epilogue.  The epilogue's global
 // operands (old residual, bias) are loaded before the math so their latency
 // overlaps it.  For lm_head the writer lanes keep a running argmax key.
 template <int PH, int T, int MB>
-__device__ __forceinline__ void tile_epilogue(const MegaArgs& a, const MegaLayer* L, const uint8_t* tile,
+__device__ __forceinline__ void tile_epilogue(const MegaArgs& a, Ctl& ctl, const MegaLayer* L, const uint8_t* tile,
                                               const Geo& g, int r, const float4* act4, int lane, float nsc,
-                                              unsigned long long& kbest) {
+                                              StageTags tg, unsigned long long& kbest) {
     constexpr int NR = PH == PH_GU ? 2 * T : T;
     constexpr int NV = NR * MB;
     constexpr int SH = 5 - Log2<NV>::v;
@@ -390,9 +520,12 @@ __device__ __forceinline__ void tile_epilogue(const MegaArgs& a, const MegaLayer
     const int nr = min(T, g.n - r);
     const int row = g.r0 + r + t;
     const bool w_ok = writer && t < nr;
+    uint64_t pre_w = 0;
     float pre = 0.f;
     if constexpr (PH == PH_O || PH == PH_DOWN) {
-        if (w_ok) pre = __ldcg(a.X + (size_t)m * a.H + row);
+        // this CTA wrote these rows in the previous hand-over (the O and down
+        // slices cover the same rows), or the embedding did: already tagged
+        if (w_ok) pre_w = ll_get(a.xl + (size_t)m * a.H + row);
     } else if constexpr (PH == PH_QKV) {
         if (w_ok && L->qkv_bias) pre = L->qkv_bias[row];
     }
@@ -402,23 +535,26 @@ __device__ __forceinline__ void tile_epilogue(const MegaArgs& a, const MegaLayer
     if constexpr (PH == PH_QKV || PH == PH_GU || PH == PH_LM) v = __fmul_rn(v, nsc);   // RMSNorm scale of row m
     if constexpr (PH == PH_GU) {
         const float u = __shfl_sync(0xffffffffu, v, (lane + ((T * MB) << SH)) & 31);
-        if (w_ok) a.FA[(size_t)m * a.F + row] = __fmul_rn(silu_ref(v), u);   // ggml_swiglu_split: silu(g) * u
+        if (w_ok) ll_put(a.fal + (size_t)m * a.F + row, __fmul_rn(silu_ref(v), u), tg.out);   // silu(g) * u
     } else if constexpr (PH == PH_QKV) {
-        if (w_ok) a.QKV[(size_t)m * a.qkv_rows + row] = L->qkv_bias ? __fadd_rn(v, pre) : v;
+        if (w_ok) ll_put(a.qkvl + (size_t)m * a.qkv_rows + row, L->qkv_bias ? __fadd_rn(v, pre) : v, tg.out);
     } else if constexpr (PH == PH_LM) {
         if (w_ok) {
             const unsigned long long k = argmax_key(v, row);
             kbest = k > kbest ? k : kbest;
         }
-    } else {   // O-proj / down: residual add into X (ggml_add(x, o))
-        if (w_ok) a.X[(size_t)m * a.H + row] = __fadd_rn(pre, v);
+    } else {   // O-proj / down: residual add (ggml_add(x, o))
+        if (w_ok) {
+            pre = ll_ok(pre_w, tg.res) ? ll_val(pre_w) : ll_wait(a, ctl, a.xl + (size_t)m * a.H + row, tg.res, 7);
+            ll_put(a.xl + (size_t)m * a.H + row, __fadd_rn(pre, v), tg.out);
+        }
     }
 }
 
 template <int PH, int MB>
-__device__ void gemv_tiles(const MegaArgs& a, int li, const Geo* tab, int nph, uint8_t* ring, uint64_t* full,
-                           const float* act, const float* red, uint32_t& seq, WarpRing& wr, int D, Ctl& ctl,
-                           unsigned long long* best) {
+__device__ void gemv_tiles(const MegaArgs& a, Ctl& ctl, int li, const Geo* tab, int nph, uint8_t* ring,
+                           uint64_t* full, const float* act, const float* red, uint32_t& seq, WarpRing& wr, int D,
+                           StageTags tg, unsigned long long* best) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const Geo& g = tab[PH == PH_LM ? 4 * a.n_layers : 4 * li + PH];
     const MegaLayer* L = PH == PH_LM ? nullptr : &a.layers[li];
@@ -426,7 +562,7 @@ __device__ void gemv_tiles(const MegaArgs& a, int li, const Geo* tab, int nph, u
     const int j0 = (warp - (int)(seq % NCW) + NCW) % NCW;
     const volatile int* fl = &ctl.fail;
     unsigned long long kbest = 0ull;
-    // this lane's row m is fixed by the lane and T; its RMSNorm scale where the phase norms
+    // this lane's row m is fixed by the lane and T; its RMSNorm scale where the stage norms
     float nsc = 1.f;
     if constexpr (PH == PH_QKV || PH == PH_GU || PH == PH_LM) {
         const int nv = (PH == PH_GU ? 2 : 1) * g.T * MB;
@@ -442,10 +578,10 @@ __device__ void gemv_tiles(const MegaArgs& a, int li, const Geo* tab, int nph, u
         const uint8_t* tile = ring + (size_t)slot * a.slot_bytes;
         const int r = j * g.T;
         switch (g.T) {
-            case 1: tile_epilogue<PH, 1, MB>(a, L, tile, g, r, act4, lane, nsc, kbest); break;
-            case 2: tile_epilogue<PH, 2, MB>(a, L, tile, g, r, act4, lane, nsc, kbest); break;
+            case 1: tile_epilogue<PH, 1, MB>(a, ctl, L, tile, g, r, act4, lane, nsc, tg, kbest); break;
+            case 2: tile_epilogue<PH, 2, MB>(a, ctl, L, tile, g, r, act4, lane, nsc, tg, kbest); break;
             default:
-                if constexpr (PH != PH_GU) tile_epilogue<PH, 4, MB>(a, L, tile, g, r, act4, lane, nsc, kbest);
+                if constexpr (PH != PH_GU) tile_epilogue<PH, 4, MB>(a, ctl, L, tile, g, r, act4, lane, nsc, tg, kbest);
                 break;
         }
         __syncwarp();
@@ -466,6 +602,12 @@ struct AttItem {
     int page0;             // physical page of the first tile
     RowMeta rm;
 };
+
+// Key splits of row m: whole pages of a.split keys over min(pos + 1, kvlen).
+__device__ __forceinline__ int row_splits(const MegaArgs& a, const RowMeta& rm) {
+    const int lim = min(rm.pos + 1, rm.kvlen);
+    return (lim + a.split - 1) / a.split;
+}
 
 __device__ __forceinline__ bool att_item_geo(const MegaArgs& a, int it, AttItem& x) {
     x.s = it % a.nsplit;
@@ -495,12 +637,20 @@ __device__ __forceinline__ void att_issue(const KvLayer& kv, const AttItem& x, i
     bulk_g2s(vt, kv.v + off, TB, bar);
 }
 
-// One attention item on a 128-thread group.  The first tile may already be
-// in flight (`prefetched`).  Returns false after a timed-out wait.
+// Flagged word of the partial (O, max, sum) buffer: [row][kv head][split][q head of the group][hd + 2].
 template <int HD>
-__device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x, int tid, __half* kt, __half* vt,
-                         AttSh<HD>& sh, const float2* cs_row, uint64_t* bar, uint32_t& uses, bool prefetched,
-                         GroupSync sync, int* merge_n, int4* merges) {
+__device__ __forceinline__ uint64_t* part_ptr(const MegaArgs& a, int m, int g, int s, int h) {
+    const int G = a.nq / a.nkv;
+    return a.pl + ((((size_t)m * a.nkv + g) * MAX_MERGE + s) * G + h) * (HD + 2);
+}
+
+// One attention item on a 128-thread group.  The first tile may already be
+// in flight (`prefetched`).  Returns false after a wait gave up (uniform in
+// the group).
+template <int HD>
+__device__ bool att_item(const MegaArgs& a, Ctl& ctl, const KvLayer& kv, const AttItem& x, int tid, __half* kt,
+                         __half* vt, AttSh<HD>& sh, const float2* cs_row, uint64_t* bar, uint32_t& uses,
+                         bool prefetched, GroupSync sync, uint32_t tag_qkv, uint32_t tag_out) {
     const int lane = tid & 31, warp = tid >> 5;
     const int G = a.nq / a.nkv;
     constexpr int half = HD / 2;
@@ -509,32 +659,60 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
     const int newj = rm.cidx;   // cache index of this step's key/value
     const bool has_new = newj >= x.j0 && newj < x.j1;
 
-    if (tid == 0) sh.failed = 0;
+    if (tid == 0) {
+        if (!prefetched) {
+            tc::fence_proxy_async_smem();
+            att_issue<HD>(kv, x, 0, kt, vt, bar);
+        }
+    }
     if (tid < MAXG) {
         sh.run_max[tid] = -INFINITY;
         sh.run_sum[tid] = 0.f;
     }
-    sync();
-    // this step's raw q (and new k, v) rows: all loads issued before any use
-    const float* qkv = a.QKV + (size_t)m * a.qkv_rows;
+    // this step's raw q (and new k, v) rows: flagged words of the QKV stage,
+    // all requested at once, then re-polled until tagged
+    const uint64_t* qkv = a.qkvl + (size_t)m * a.qkv_rows;
     constexpr int QI = (MAXG * half + ATT_THREADS - 1) / ATT_THREADS;
-    float qa[QI], qb[QI], ka = 0.f, kb = 0.f, vv = 0.f;
+    const uint64_t ready = (uint64_t)tag_qkv << 32;   // a word that needs no poll
+    uint64_t wa[QI], wb[QI], wk0 = ready, wk1 = ready, wv = ready;
+    const uint64_t* pa[QI];
 #pragma unroll
     for (int it = 0; it < QI; ++it) {
         const int t = tid + it * ATT_THREADS;
+        pa[it] = qkv + (size_t)(g * G + t / half) * HD + t % half;
+        wa[it] = wb[it] = ready;
         if (t < G * half) {
-            const float* q = qkv + (size_t)(g * G + t / half) * HD + t % half;
-            qa[it] = __ldcg(q);
-            qb[it] = __ldcg(q + half);
+            wa[it] = ll_get(pa[it]);
+            wb[it] = ll_get(pa[it] + half);
         }
     }
+    const uint64_t* pk = qkv + (size_t)(a.nq + g) * HD + tid;
+    const uint64_t* pv = qkv + (size_t)(a.nq + a.nkv + g) * HD + tid;
     if (has_new) {
         if (tid < half) {
-            const float* k = qkv + (size_t)(a.nq + g) * HD + tid;
-            ka = __ldcg(k);
-            kb = __ldcg(k + half);
+            wk0 = ll_get(pk);
+            wk1 = ll_get(pk + half);
         }
-        if (tid < HD) vv = __ldcg(qkv + (size_t)(a.nq + a.nkv + g) * HD + tid);
+        if (tid < HD) wv = ll_get(pv);
+    }
+    for (uint32_t it = 1;; ++it) {
+        bool ok = ll_ok(wk0, tag_qkv) && ll_ok(wk1, tag_qkv) && ll_ok(wv, tag_qkv);
+#pragma unroll
+        for (int i = 0; i < QI; ++i) ok = ok && ll_ok(wa[i], tag_qkv) && ll_ok(wb[i], tag_qkv);
+        if (ok) break;
+        if ((it & 31) == 0 && poll_give_up(a, ctl, it, 8)) {
+            sh.failed = 1;
+            break;
+        }
+        __nanosleep(POLL_PAUSE_NS);
+#pragma unroll
+        for (int i = 0; i < QI; ++i) {
+            if (!ll_ok(wa[i], tag_qkv)) wa[i] = ll_get(pa[i]);
+            if (!ll_ok(wb[i], tag_qkv)) wb[i] = ll_get(pa[i] + half);
+        }
+        if (!ll_ok(wk0, tag_qkv)) wk0 = ll_get(pk);
+        if (!ll_ok(wk1, tag_qkv)) wk1 = ll_get(pk + half);
+        if (!ll_ok(wv, tag_qkv)) wv = ll_get(pv);
     }
 #pragma unroll
     for (int it = 0; it < QI; ++it) {
@@ -542,8 +720,9 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
         if (t < G * half) {
             const int h = t / half, i = t % half;
             const float2 cs = cs_row[i];
-            const float y0 = __fsub_rn(__fmul_rn(qa[it], cs.x), __fmul_rn(qb[it], cs.y));
-            const float y1 = __fadd_rn(__fmul_rn(qa[it], cs.y), __fmul_rn(qb[it], cs.x));
+            const float qa = ll_val(wa[it]), qb = ll_val(wb[it]);
+            const float y0 = __fsub_rn(__fmul_rn(qa, cs.x), __fmul_rn(qb, cs.y));
+            const float y1 = __fadd_rn(__fmul_rn(qa, cs.y), __fmul_rn(qb, cs.x));
             sh.qs[h][i] = __half2float(__float2half_rn(y0));
             sh.qs[h][i + half] = __half2float(__float2half_rn(y1));
         }
@@ -551,14 +730,11 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
     if (has_new) {
         if (tid < half) {
             const float2 cs = cs_row[tid];
+            const float ka = ll_val(wk0), kb = ll_val(wk1);
             sh.kn[tid] = __float2half_rn(__fsub_rn(__fmul_rn(ka, cs.x), __fmul_rn(kb, cs.y)));
             sh.kn[tid + half] = __float2half_rn(__fadd_rn(__fmul_rn(ka, cs.y), __fmul_rn(kb, cs.x)));
         }
-        if (tid < HD) sh.vn[tid] = __float2half_rn(vv);
-    }
-    if (tid == 0 && !prefetched) {
-        tc::fence_proxy_async_smem();
-        att_issue<HD>(kv, x, 0, kt, vt, bar);
+        if (tid < HD) sh.vn[tid] = __float2half_rn(ll_val(wv));
     }
 
     constexpr int NCH = HD / 8;
@@ -573,6 +749,7 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
     const int rot = kk % NCH;
 
     for (int t = 0; t < x.ntiles; ++t) {
+        // the page copy was requested by this group: wait for it even when failing
         if (!tc::mbar_wait(bar, uses & 1)) {
             atomicCAS(a.err, 0, 1);
             sh.failed = 1;
@@ -685,118 +862,101 @@ __device__ bool att_item(const MegaArgs& a, const KvLayer& kv, const AttItem& x,
             kv.v[off + d] = sh.vn[d];
         }
     }
-
-    float* out = a.ATT + (size_t)m * a.nq * HD;
     if (x.nsplit == 1) {
+        // the only split: the normalized output, straight to the attention words
+        uint64_t* out = a.attl + (size_t)m * a.nq * HD;
 #pragma unroll
         for (int k = 0; k < HPER; ++k) {
             const int h = hs + k * HSUB;
             if (h < G) {
                 const float inv = 1.0f / sh.run_sum[h];
-                reinterpret_cast<float2*>(out + (size_t)(g * G + h) * HD)[dp] = make_float2(o[k].x * inv, o[k].y * inv);
+                ll_put2(out + (size_t)(g * G + h) * HD + 2 * dp, o[k].x * inv, o[k].y * inv, tag_out);
             }
         }
-        sync();   // sh is reused by the next item
-        return true;
-    }
-    // ---- partials, then the last arriving split merges (log-sum-exp)
-    const size_t pbase = ((size_t)m * MAX_MERGE + x.s) * a.nq;
+    } else {
+        // partial (O, max, sum) for the merge
 #pragma unroll
-    for (int k = 0; k < HPER; ++k) {
-        const int h = hs + k * HSUB;
-        if (h < G) reinterpret_cast<float2*>(a.part + (pbase + g * G + h) * HD)[dp] = o[k];
-    }
-    if (tid < G) {
-        a.part_ml[(pbase + g * G + tid) * 2 + 0] = sh.run_max[tid];
-        a.part_ml[(pbase + g * G + tid) * 2 + 1] = sh.run_sum[tid];
-    }
-    sync();
-    if (tid == 0) {
-        // release the partials (written by the group, ordered by the group
-        // barrier), count the split; the last one queues the merge for its CTA
-        int prev;
-        asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
-                     : "=r"(prev)
-                     : "l"(a.counters + m * a.nkv + g)
-                     : "memory");
-        if (prev == x.nsplit - 1) {
-            const int e = atomicAdd(merge_n, 1);
-            merges[e] = make_int4(m, g, x.nsplit, 0);
+        for (int k = 0; k < HPER; ++k) {
+            const int h = hs + k * HSUB;
+            if (h < G) ll_put2(part_ptr<HD>(a, m, g, x.s, h) + 2 * dp, o[k].x, o[k].y, tag_out);
         }
+        if (tid < G) ll_put2(part_ptr<HD>(a, m, g, x.s, tid) + HD, sh.run_max[tid], sh.run_sum[tid], tag_out);
     }
-    sync();
+    sync();   // sh is reused by the next item
     return true;
 }
 
-// Log-sum-exp merge of the ns partials of (row m, KV head g) by the whole
-// CTA (all partial loads in one round trip), then ATT[m][heads of g].
-// `scr`: shared scratch of at least mega_merge_scratch bytes.
+// Log-sum-exp merge of the ns partials of (row m, q head qh) by the whole CTA
+// into the attention words of the head.  `scr`: shared scratch of
+// ns * (HD + 2) + 2 * MAX_MERGE floats.  Returns false (uniform) after a
+// poll gave up.
 template <int HD>
-__device__ void cta_merge(const MegaArgs& a, int m, int g, int ns, float* scr) {
+__device__ bool cta_merge(const MegaArgs& a, Ctl& ctl, int m, int qh, int ns, uint32_t tag_part, uint32_t tag_out,
+                          float* scr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = a.nq / a.nkv;
-    constexpr int PAIRS = HD / 2;
-    float* ml = scr;                                  // [G][ns][2]
-    float* wts = ml + 2 * MAXG * MAX_MERGE;           // [G][ns]
-    float* inv = wts + MAXG * MAX_MERGE;              // [G]
-    float2* num = reinterpret_cast<float2*>(inv + 2 * MAXG);   // [Q][G * PAIRS]
-    const float2* pml = reinterpret_cast<const float2*>(a.part_ml);
-    for (int i = tid; i < G * ns; i += NCT) {
-        const int h = i / ns, ss = i % ns;
-        const float2 v = __ldcg(pml + ((size_t)m * MAX_MERGE + ss) * a.nq + g * G + h);
-        ml[2 * i] = v.x;
-        ml[2 * i + 1] = v.y;
+    const int g = qh / G, h = qh % G;
+    constexpr int W2 = (HD + 2) / 2;                  // word pairs per split
+    float* wts = scr + (size_t)MAX_MERGE * (HD + 2);  // [ns]
+    float* inv = wts + MAX_MERGE;                     // [1]
+    const size_t sstride = (size_t)G * (HD + 2);      // words between splits
+    const uint64_t* src = part_ptr<HD>(a, m, g, 0, h);
+    const int NP = ns * W2;
+    bool bad = false;
+    for (int b0 = 0; b0 < NP && !bad; b0 += SB * NCT) {
+        uint64_t w[SB][2];
+        uint32_t pend = 0;
+#pragma unroll
+        for (int j = 0; j < SB; ++j) {
+            const int p = b0 + j * NCT + tid;
+            if (p < NP) {
+                ll_get2(src + (p / W2) * sstride + 2 * (p % W2), w[j][0], w[j][1]);
+                pend |= 1u << j;
+            }
+        }
+        for (uint32_t it = 1; pend; ++it) {
+#pragma unroll
+            for (int j = 0; j < SB; ++j) {
+                if ((pend >> j) & 1u) {
+                    const int p = b0 + j * NCT + tid;
+                    if (ll_ok(w[j][0], tag_part) && ll_ok(w[j][1], tag_part)) {
+                        pend &= ~(1u << j);
+                        scr[(p / W2) * (HD + 2) + 2 * (p % W2)] = ll_val(w[j][0]);
+                        scr[(p / W2) * (HD + 2) + 2 * (p % W2) + 1] = ll_val(w[j][1]);
+                    } else {
+                        ll_get2(src + (p / W2) * sstride + 2 * (p % W2), w[j][0], w[j][1]);
+                    }
+                }
+            }
+            if (pend && (it & 31) == 0 && poll_give_up(a, ctl, it, 9)) {
+                bad = true;
+                break;
+            }
+            if (pend) __nanosleep(POLL_PAUSE_NS);
+        }
     }
-    cbar();
-    for (int h = warp; h < G; h += NCW) {
+    if (__syncthreads_or(bad ? 1 : 0)) return false;
+    if (warp == 0) {
         float mx = -INFINITY;
-        for (int ss = lane; ss < ns; ss += 32) mx = fmaxf(mx, ml[2 * (h * ns + ss)]);
+        for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, scr[s * (HD + 2) + HD]);
         mx = warp_max(mx);
         float den = 0.f;
-        for (int ss = lane; ss < ns; ss += 32) {
-            const float w = expf(ml[2 * (h * ns + ss)] - mx);
-            wts[h * ns + ss] = w;
-            den = fmaf(w, ml[2 * (h * ns + ss) + 1], den);
+        for (int s = lane; s < ns; s += 32) {
+            const float w = expf(scr[s * (HD + 2) + HD] - mx);
+            wts[s] = w;
+            den = fmaf(w, scr[s * (HD + 2) + HD + 1], den);
         }
         den = warp_sum(den);
-        if (lane == 0) inv[h] = 1.0f / den;
+        if (lane == 0) inv[0] = 1.0f / den;
     }
     cbar();
-    const int np = G * PAIRS, Q = NCT / np;          // Q threads share one (head, column pair)
-    if (tid < Q * np) {
-        const int pidx = tid % np, qi = tid / np;
-        const int h = pidx / PAIRS, d2 = pidx % PAIRS;
-        const float2* src = reinterpret_cast<const float2*>(a.part + (size_t)(g * G + h) * HD) + d2;
-        const size_t sstride = (size_t)a.nq * HD / 2;   // float2 per split
-        float2 acc = make_float2(0.f, 0.f);
-        for (int s0 = qi; s0 < ns; s0 += 8 * Q) {      // 8 independent loads in flight per batch
-            float2 p[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (s0 + i * Q < ns) p[i] = __ldcg(src + ((size_t)m * MAX_MERGE + s0 + i * Q) * sstride);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (s0 + i * Q < ns) {
-                    const float w = wts[h * ns + s0 + i * Q];
-                    acc.x = fmaf(w, p[i].x, acc.x);
-                    acc.y = fmaf(w, p[i].y, acc.y);
-                }
-        }
-        num[qi * np + pidx] = acc;
+    if (tid < HD) {
+        float num = 0.f;
+        for (int s = 0; s < ns; ++s) num = fmaf(wts[s], scr[s * (HD + 2) + tid], num);
+        ll_put(a.attl + (size_t)m * a.nq * HD + (size_t)qh * HD + tid, num * inv[0], tag_out);
     }
-    cbar();
-    float* out = a.ATT + (size_t)m * a.nq * HD;
-    for (int pidx = tid; pidx < np; pidx += NCT) {
-        float2 t = num[pidx];
-        for (int qi = 1; qi < Q; ++qi) {
-            t.x += num[qi * np + pidx].x;
-            t.y += num[qi * np + pidx].y;
-        }
-        const int h = pidx / PAIRS, d2 = pidx % PAIRS;
-        reinterpret_cast<float2*>(out + (size_t)(g * G + h) * HD)[d2] = make_float2(t.x * inv[h], t.y * inv[h]);
-    }
-    if (tid == 0) a.counters[m * a.nkv + g] = 0;   // ready for the next layer / launch
-    cbar();
+    cbar();   // scr is reused by the next merge
+    return true;
 }
 
 // ------------------------------------------------------------ kernel
@@ -809,37 +969,36 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
     __shared__ float red[2 * NCW];
     __shared__ unsigned long long best[2];
     __shared__ float2 rope_cs[2][64];              // RoPE (cos, sin) per row: positions are fixed for the launch
-    __shared__ int merge_n;                        // attention merges this CTA owes in the current layer
-    __shared__ int4 merges[16];                    // (m, g, nsplit)
     __shared__ Ctl ctl;
-    const int tid = threadIdx.x, warp = tid >> 5;
-    uint8_t* region = dyn;                         // activations | attention tiles + state
+    // state kept in shared memory rather than registers: the GEMV tile loop
+    // needs every register, and values live across it would spill there
+    __shared__ unsigned long long s_base;          // tag base of this launch
+    __shared__ AttItem s_x0[AttConst<HD>::NG];     // each group's first attention item
+    __shared__ int s_pre[AttConst<HD>::NG];        // ... exists
+    __shared__ int s_pending[AttConst<HD>::NG];    // ... page requested, not yet consumed
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint8_t* region = dyn;                         // activations / merge scratch | attention tiles + state
     uint8_t* ring = dyn + a.union_bytes;
     Geo* tab = reinterpret_cast<Geo*>(ring + (size_t)a.nstage * a.slot_bytes);   // [4 * n_layers + 1]
     const int nph = 4 * a.n_layers + 1;
     const int D = a.nstage / NCW;
     float* act = reinterpret_cast<float*>(region);
-
     if (tid == 0) {
-        const unsigned long long per_launch = (unsigned long long)(5 * a.n_layers + 2) * gridDim.x;
-        ctl.target = (unsigned long long)(*(volatile unsigned int*)a.epoch) * per_launch;
-        ctl.aborted = 0;
+        s_base = (unsigned long long)(*(volatile unsigned int*)a.epoch) * (8ull * a.n_layers + 8ull);
         ctl.fail = 0;
-        ctl.nbar = 0;
-        trace_mark(a, 0);
         for (int i = 0; i < a.nstage; ++i) tc::mbar_init(&full[i], 1);
         for (int i = 0; i < AC::NG; ++i) tc::mbar_init(&abar[i], 1);
         tc::mbar_fence_init();
     }
+    trace_mark(a, 0);
     if (tid < 2) best[tid] = 0ull;
-    if (blockIdx.x == 0 && tid < MB) a.amax[tid] = 0ull;
-    // this CTA's tile geometry of every phase of the step
+    if (tid < AttConst<HD>::NG) reinterpret_cast<AttSh<HD>*>(region + a.att_off + AttConst<HD>::NG * AttConst<HD>::GROUP_BYTES)[tid].failed = 0;
+    // this CTA's tile geometry of every stage of the step
     for (int p = tid; p < nph; p += NCT)
         tab[p] = phase_geo(a, p == nph - 1 ? 0 : p / 4, p == nph - 1 ? PH_LM : p % 4);
     __syncthreads();
 
     // every warp requests its first D tiles (layer 0's weights land during the embedding)
-    const int lane = tid & 31;
     WarpRing wr;
     wr.used = wr.issued = 0;
     wr.ip = 0;
@@ -847,10 +1006,34 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
     ring_normalize(wr, tab, nph);
     for (int d = 0; d < D; ++d) ring_issue(wr, tab, nph, ring, full, warp, lane, D, a.slot_bytes);
 
-    // ---- token embedding: X[m] = dequant(tok_embd[tok[m]])
+    // attention groups: the first item is the same in every layer of the launch
+    const int grp = tid / ATT_THREADS, gtid = tid % ATT_THREADS;
+    if (grp < AC::NG && gtid == 0) {
+        const int it0 = blockIdx.x + grp * gridDim.x;
+        AttItem x0;
+        s_pre[grp] = it0 < a.nsplit * a.nkv * MB && att_item_geo(a, it0, x0);
+        s_x0[grp] = x0;
+        s_pending[grp] = 0;
+    }
+    __syncthreads();
+    uint32_t uses = 0;                   // completed phases of this group's page barrier
+    // request the page of the group's first item for layer li (its tiles are free)
+    auto prefetch = [&](int li) {
+        if (grp < AC::NG && gtid == 0 && s_pre[grp]) {
+            __half* k0 = reinterpret_cast<__half*>(region + a.att_off + (size_t)grp * AC::GROUP_BYTES);
+            tc::fence_proxy_async_smem();
+            att_issue<HD>(a.layers[li].kv, s_x0[grp], 0, k0, k0 + PAGE * HD, &abar[grp]);
+            s_pending[grp] = 1;
+        }
+        __syncwarp();   // reconverge before stage_ll (see trace_mark)
+    };
+    prefetch(0);   // the attention region is free from the start
+
+    // ---- token embedding: X[m] = dequant(tok_embd[tok[m]]) as flagged words
     {
         const int H = a.H;
         const DevW& E = a.tok_embd;
+        const uint32_t t0 = Tags{s_base}.x_in(0);
         for (int t = blockIdx.x * NCT + tid; t < MB * H; t += gridDim.x * NCT) {
             const int m = t / H, k = t % H;
             const int r = a.tok[m];
@@ -860,7 +1043,7 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
                 const float d = __half2float(*reinterpret_cast<const __half*>(rp + H + (k / 32) * 2));
                 v = __fmul_rn((float)((int)rp[k] - 128), d);   // quants stored as q + 128
             }
-            a.X[t] = v;
+            ll_put(a.xl + t, v, t0);
         }
     }
 
@@ -873,98 +1056,120 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
     }
 
     uint32_t seq = 0;                    // ring tiles consumed so far
-    uint32_t uses = 0;                   // completed phases of this group's attention barrier
-    const int qw = a.nq * HD;
-    const int grp = tid / ATT_THREADS, gtid = tid % ATT_THREADS;
-    const int n_att = a.nsplit * a.nkv * MB;
-    AttSh<HD>* ash = reinterpret_cast<AttSh<HD>*>(region + AC::NG * AC::GROUP_BYTES);
-    __half* kt = reinterpret_cast<__half*>(region + (size_t)grp * AC::GROUP_BYTES);
-    __half* vt = kt + PAGE * HD;
-    // this group's first attention item: the same in every layer of the launch
-    const int it0 = blockIdx.x + grp * gridDim.x;
-    AttItem x0;
-    const bool pre = grp < AC::NG && it0 < n_att && att_item_geo(a, it0, x0);   // uniform in the group
-
+    bool failed = false;
     for (int li = 0; li < a.n_layers; ++li) {
         const MegaLayer& L = a.layers[li];
-        // 1. RMSNorm + QKV (+bias) -> raw q/k/v rows
-        grid_sync(a, ctl);
-        if (ctl.aborted) break;
-        stage<MB>(a.X, L.attn_norm, a.H, act, red);
-        gemv_tiles<PH_QKV, MB>(a, li, tab, nph, ring, full, act, red, seq, wr, D, ctl, best);
-        // 2. attention: the first page of each group's first item is requested
-        //    before the barrier (activations are dead: the region is free)
-        cbar();
-        if (tid == 0) merge_n = 0;
-        if (pre && gtid == 0) {
-            tc::fence_proxy_async_smem();
-            att_issue<HD>(L.kv, x0, 0, kt, vt, &abar[grp]);
+        const int tb = 1 + 10 * li;
+        const Tags tg{*(volatile unsigned long long*)&s_base};
+        if (li > 0) {
+            cbar();                      // the previous down tiles are done with act
+            prefetch(li);
         }
-        grid_sync(a, ctl);
+        trace_mark(a, tb);
+        // 1. RMSNorm + QKV (+bias) -> raw q|k|v words
+        // (a CTA with no rows in a stage stages nothing: nothing downstream
+        // waits for it, so the words it would read may already be renewed)
+        if (tab[4 * li + PH_QKV].ntiles) stage_ll<MB>(a, ctl, a.xl, a.H, tg.x_in(li), L.attn_norm, act, red);
+        if ((failed = cta_failed(a, ctl))) break;
+        trace_mark(a, tb + 1);
+        gemv_tiles<PH_QKV, MB>(a, ctl, li, tab, nph, ring, full, act, red, seq, wr, D, {tg.qkv(li), 0u}, best);
+        trace_mark(a, tb + 2);
+        // 2. attention items (groups 0..NG-1; the attention region is not act)
         if (grp < AC::NG) {
-            for (int it = it0; it < n_att; it += AC::NG * gridDim.x) {
+            const int it0 = blockIdx.x + grp * gridDim.x;
+            const int pre = s_pre[grp];
+            __half* kt = reinterpret_cast<__half*>(region + a.att_off + (size_t)grp * AC::GROUP_BYTES);
+            AttSh<HD>* ash = reinterpret_cast<AttSh<HD>*>(region + a.att_off + AC::NG * AC::GROUP_BYTES);
+            for (int it = it0; it < a.nsplit * a.nkv * MB; it += AC::NG * gridDim.x) {
                 const bool first = it == it0;
                 AttItem x;
-                if (first && pre) x = x0;
+                if (first && pre) x = s_x0[grp];
                 else if (!att_item_geo(a, it, x)) continue;
-                // a prefetched item runs even when aborting, so its copies are waited for
-                if (ctl.aborted && !(first && pre)) break;
-                if (!att_item<HD>(a, L.kv, x, gtid, kt, vt, ash[grp], rope_cs[x.m], &abar[grp], uses,
-                                  first && pre, GroupSync{1 + grp}, &merge_n, merges)) {
+                const bool pf = first && pre;
+                if (pf && gtid == 0) s_pending[grp] = 0;
+                if (!att_item<HD>(a, ctl, L.kv, x, gtid, kt, kt + PAGE * HD, ash[grp], rope_cs[x.m], &abar[grp],
+                                  uses, pf, GroupSync{1 + grp}, tg.qkv(li),
+                                  x.nsplit == 1 ? tg.att(li) : tg.part(li))) {
                     if (gtid == 0) raise_fail(a, ctl, 1);
                     break;
                 }
             }
         }
+        if ((failed = cta_failed(a, ctl))) break;
+        trace_mark(a, tb + 3);
+        // 3. merges: one (row, q head) per CTA from the top of the grid
+        for (int u = gridDim.x - 1 - blockIdx.x; u < MB * a.nq && !failed; u += gridDim.x) {
+            const int m = u / a.nq;
+            const int ns = row_splits(a, a.meta[m]);
+            if (ns > 1) failed = !cta_merge<HD>(a, ctl, m, u % a.nq, ns, tg.part(li), tg.att(li), act);
+        }
+        if (failed) break;
+        trace_mark(a, tb + 4);
+        // 4. O-proj + residual
+        if (tab[4 * li + PH_O].ntiles) stage_ll<MB>(a, ctl, a.attl, a.nq * HD, tg.att(li), nullptr, act, red);
+        if ((failed = cta_failed(a, ctl))) break;
+        trace_mark(a, tb + 5);
+        gemv_tiles<PH_O, MB>(a, ctl, li, tab, nph, ring, full, act, red, seq, wr, D, {tg.x_o(li), tg.x_in(li)},
+                             best);
+        // 5. RMSNorm + gate/up + SwiGLU
         cbar();
-        // splits that finished last merge with the whole CTA (the tiles are free now)
-        for (int e = 0; e < merge_n && !ctl.aborted; ++e)
-            cta_merge<HD>(a, merges[e].x, merges[e].y, merges[e].z, reinterpret_cast<float*>(region));
-        if (ctl.aborted) break;
-        // 3. O-proj + residual
-        grid_sync(a, ctl);
-        if (ctl.aborted) break;
-        stage<MB>(a.ATT, nullptr, qw, act, red);
-        gemv_tiles<PH_O, MB>(a, li, tab, nph, ring, full, act, red, seq, wr, D, ctl, best);
-        // 4. RMSNorm + gate/up + SwiGLU
-        grid_sync(a, ctl);
-        if (ctl.aborted) break;
-        stage<MB>(a.X, L.ffn_norm, a.H, act, red);
-        gemv_tiles<PH_GU, MB>(a, li, tab, nph, ring, full, act, red, seq, wr, D, ctl, best);
-        // 5. down + residual
-        grid_sync(a, ctl);
-        if (ctl.aborted) break;
-        stage<MB>(a.FA, nullptr, a.F, act, red);
-        gemv_tiles<PH_DOWN, MB>(a, li, tab, nph, ring, full, act, red, seq, wr, D, ctl, best);
+        trace_mark(a, tb + 6);
+        if (tab[4 * li + PH_GU].ntiles) stage_ll<MB>(a, ctl, a.xl, a.H, tg.x_o(li), L.ffn_norm, act, red);
+        if ((failed = cta_failed(a, ctl))) break;
+        trace_mark(a, tb + 7);
+        gemv_tiles<PH_GU, MB>(a, ctl, li, tab, nph, ring, full, act, red, seq, wr, D, {tg.fa(li), 0u}, best);
+        // 6. down + residual
+        cbar();
+        trace_mark(a, tb + 8);
+        if (tab[4 * li + PH_DOWN].ntiles) stage_ll<MB>(a, ctl, a.fal, a.F, tg.fa(li), nullptr, act, red);
+        if ((failed = cta_failed(a, ctl))) break;
+        trace_mark(a, tb + 9);
+        gemv_tiles<PH_DOWN, MB>(a, ctl, li, tab, nph, ring, full, act, red, seq, wr, D,
+                                {tg.x_in(li + 1), tg.x_o(li)}, best);
     }
     // output norm + lm_head + argmax
-    if (!ctl.aborted) {
-        grid_sync(a, ctl);
-        if (!ctl.aborted) {
-            stage<MB>(a.X, a.out_norm, a.H, act, red);
-            gemv_tiles<PH_LM, MB>(a, 0, tab, nph, ring, full, act, red, seq, wr, D, ctl, best);
+    if (!failed) {
+        const Tags tg{*(volatile unsigned long long*)&s_base};
+        cbar();
+        trace_mark(a, 1 + 10 * a.n_layers);
+        if (tab[4 * a.n_layers].ntiles) stage_ll<MB>(a, ctl, a.xl, a.H, tg.x_in(a.n_layers), a.out_norm, act, red);
+        failed = cta_failed(a, ctl);
+        if (!failed) {
+            trace_mark(a, 2 + 10 * a.n_layers);
+            gemv_tiles<PH_LM, MB>(a, ctl, 0, tab, nph, ring, full, act, red, seq, wr, D, {0u, 0u}, best);
             cbar();
             if (tid < MB && best[tid]) atomicMax(a.amax + tid, best[tid]);
-            grid_sync(a, ctl);
         }
     }
-    if (blockIdx.x == 0 && !ctl.aborted && tid < MB) {
-        a.tok[tid] = argmax_key_index(a.amax[tid]);
-        RowMeta r = a.meta[tid];
-        r.pos += 1;
-        r.cidx += 1;
-        r.kvlen += 1;
-        a.meta[tid] = r;
-    }
-    // copies still in flight (only after an abort): wait for them before exiting
+    // copies still in flight (only after a failure): wait for them before exiting
     for (uint32_t k = wr.used; k < wr.issued; ++k)
         tc::mbar_wait(&full[warp + NCW * (int)(k % D)], (k / D) & 1, 1u << 20);
+    if (grp < AC::NG && gtid == 0 && s_pending[grp]) tc::mbar_wait(&abar[grp], uses & 1, 1u << 20);
+    cbar();
+    trace_mark(a, 3 + 10 * a.n_layers);
     if (tid == 0) {
-        if (blockIdx.x == 0) {
+        // arrival (releases this CTA's argmax keys); the last CTA ends the step
+        unsigned int prev;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.done) : "memory");
+        if (prev == gridDim.x - 1) {
+            const bool ok = *(volatile int*)a.abort == 0;
+            for (int m = 0; m < MB; ++m) {
+                volatile unsigned long long* am = a.amax + m;
+                if (ok) {
+                    a.tok[m] = argmax_key_index(*am);
+                    RowMeta r = a.meta[m];
+                    r.pos += 1;
+                    r.cidx += 1;
+                    r.kvlen += 1;
+                    a.meta[m] = r;
+                }
+                *am = 0ull;   // ready for the next launch
+            }
+            *(volatile unsigned int*)a.done = 0u;
             __threadfence();
             atomicAdd(a.epoch, 1u);
         }
-        trace_mark(a, mega_trace_slots(a.n_layers) - 1);
+        trace_mark(a, 4 + 10 * a.n_layers);
     }
 }
 
@@ -974,16 +1179,23 @@ cudaError_t set_smem(int bytes) {
 }
 
 template <int HD>
-size_t att_union_bytes() {
+size_t att_region_bytes() {
     return (size_t)AttConst<HD>::NG * (AttConst<HD>::GROUP_BYTES + sizeof(AttSh<HD>));
 }
 
 }  // namespace
 
-int decode_mega_union_bytes(int hd, int M, int kmax) {
+// Shared region before the ring: the staged activation rows (up to M x kmax
+// f32), the merge scratch, and -- past the rows the QKV stage stages, so a
+// page prefetched during the previous layer survives that staging -- the
+// attention groups' page tiles and state.
+int decode_mega_att_offset(int M, int H) { return (M * H * 4 + 1023) / 1024 * 1024; }
+
+int decode_mega_union_bytes(int hd, int M, int kmax, int H) {
     const size_t act = (size_t)M * kmax * 4;
-    const size_t att = hd == 64 ? att_union_bytes<64>() : att_union_bytes<128>();
-    return (int)((std::max(act, att) + 1023) / 1024 * 1024);
+    const size_t att = (size_t)decode_mega_att_offset(M, H) + (hd == 64 ? att_region_bytes<64>() : att_region_bytes<128>());
+    const size_t merge = ((size_t)MAX_MERGE * (hd + 2) + 2 * MAX_MERGE) * 4;
+    return (int)((std::max({act, att, merge}) + 1023) / 1024 * 1024);
 }
 
 int decode_mega_max_stages() { return MAX_STAGES; }
@@ -1027,9 +1239,9 @@ cudaError_t decode_mega_launch(const MegaArgs& a, size_t smem, cudaStream_t st) 
     auto pow2_le4 = [](int t) { return t == 1 || t == 2 || t == 4; };
     const bool t_ok = a.t_gu == 1 || a.t_gu == 2;   // gate + up rows: at most 4 per tile
     if (a.M < 1 || a.M > 2 || a.nstage < NCW || a.nstage > MAX_STAGES || a.nstage % NCW || a.nsplit < 1 ||
-        a.nsplit > MAX_MERGE ||
-        !t_ok || !pow2_le4(a.t_qkv) || !pow2_le4(a.t_o) || !pow2_le4(a.t_down) || !pow2_le4(a.t_lm) ||
-        a.slot_bytes % 16 || a.union_bytes % 1024)
+        a.nsplit > MAX_MERGE || !t_ok || !pow2_le4(a.t_qkv) || !pow2_le4(a.t_o) || !pow2_le4(a.t_down) ||
+        !pow2_le4(a.t_lm) || a.slot_bytes % 16 || a.union_bytes % 1024 || a.att_off % 1024 ||
+        a.H % 16 || a.F % 16 || (a.nq * a.hd) % 16)
         return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.grid);
@@ -1037,7 +1249,8 @@ cudaError_t decode_mega_launch(const MegaArgs& a, size_t smem, cudaStream_t st) 
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;   // all CTAs co-resident: the grid barriers rely on it
+    // all CTAs co-resident: a CTA polls words that other CTAs of the same launch produce
+    attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;

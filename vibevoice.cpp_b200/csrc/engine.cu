@@ -186,7 +186,6 @@ struct vvq2_ctx {
     std::vector<void*> allocs;
     // scratch for up to GEMV_MAX_M activation rows
     float *X = nullptr, *Q = nullptr, *ATT = nullptr, *FA = nullptr, *LOGITS = nullptr;
-    float* QKVr = nullptr;         // persistent step: raw q|k|v rows [GEMV_MAX_M][qkv rows]
     // prefill (tensor-core) scratch for up to prefill_rows token rows
     int prefill_rows = PREFILL_ROWS_DEFAULT;
     __half *Xh = nullptr, *ATTh = nullptr, *Ah = nullptr;
@@ -206,9 +205,14 @@ struct vvq2_ctx {
     int* err = nullptr;            // device error word written by bounded waits
     std::vector<vvq2_kv*> kvs;   // caches created on this context (released with it)
 
-    // persistent decode-step kernel state: per-KV device layer tables, grid
-    // barrier counter / launch epoch / abort flag
-    unsigned long long* bar_count = nullptr;
+    // persistent decode-step kernel state: per-KV device layer tables, the
+    // flagged hand-over words (cleared to 0, a tag no launch uses), argmax keys
+    // and end-of-step counter (zero between launches), launch epoch, abort flag
+    uint64_t* mega_ll = nullptr;
+    size_t mega_ll_n = 0;
+    unsigned long long* mega_amax = nullptr;
+    unsigned long long* mega_err_info = nullptr;   // [4] where a persistent step's first failing wait gave up
+    unsigned int* mega_done = nullptr;
     unsigned int* epoch = nullptr;
     int* abort_flag = nullptr;
     unsigned long long* mega_trace = nullptr;   // VVQ2_MEGA_TRACE=1: phase timeline of the last step
@@ -389,13 +393,26 @@ int check_device_error(vvq2_ctx* c) {
     int e = 0;
     CU(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {
+        unsigned long long info[4] = {0, 0, 0, 0};
+        if (c->mega_err_info) {
+            cudaMemcpy(info, c->mega_err_info, sizeof(info), cudaMemcpyDeviceToHost);
+            cudaMemsetAsync(c->mega_err_info, 0, sizeof(info), c->stream);
+        }
         cudaMemsetAsync(c->err, 0, sizeof(int), c->stream);
-        // a persistent kernel that gave up leaves its barrier bookkeeping mid-launch
-        if (c->bar_count) cudaMemsetAsync(c->bar_count, 0, sizeof(unsigned long long), c->stream);
-        if (c->epoch) cudaMemsetAsync(c->epoch, 0, sizeof(unsigned int), c->stream);
+        // a persistent step that gave up leaves words of its launch behind:
+        // clear them (the next launch's tags differ, but a cleared buffer
+        // leaves nothing to mistake) and its argmax / arrival bookkeeping
+        if (c->mega_ll) cudaMemsetAsync(c->mega_ll, 0, c->mega_ll_n * sizeof(uint64_t), c->stream);
+        if (c->mega_amax) cudaMemsetAsync(c->mega_amax, 0, 2 * sizeof(unsigned long long), c->stream);
+        if (c->mega_done) cudaMemsetAsync(c->mega_done, 0, sizeof(unsigned int), c->stream);
         if (c->abort_flag) cudaMemsetAsync(c->abort_flag, 0, sizeof(int), c->stream);
         if (c->counters) cudaMemsetAsync(c->counters, 0, sizeof(int) * c->prefill_rows * c->hp.n_kv_heads, c->stream);
         cudaStreamSynchronize(c->stream);
+        if (info[0])
+            return fail(VVQ2_ERR_CUDA,
+                        "a device-side wait timed out (code %d; persistent step: CTA %u, word %lld, tag %u, epoch %u, seen %016llx)",
+                        e, (unsigned)(info[0] >> 32), (long long)info[1], (unsigned)info[2], (unsigned)(info[2] >> 32),
+                        info[3]);
         return fail(VVQ2_ERR_CUDA, "a device-side wait timed out (code %d)", e);
     }
     return 0;
@@ -883,7 +900,7 @@ MegaPlan mega_plan(const vvq2_ctx* c, int M) {
     if (grid <= 0 || M < 1 || M > 2 || c->layers.empty()) return p;
     const vvq2_ctx::Layer& L0 = c->layers[0];
     const int kmax = std::max({hp.hidden_size, hp.intermediate_size, hp.n_heads * hp.head_dim});
-    p.uni = decode_mega_union_bytes(hp.head_dim, M, kmax);
+    p.uni = decode_mega_union_bytes(hp.head_dim, M, kmax, hp.hidden_size);
     const int lim = decode_mega_smem_limit() - decode_mega_table_bytes(hp.n_layers);
     // The ring has D slots per warp (D = 2 preferred): tile i of a CTA goes
     // to warp i % ncw, which streams it into one of its own slots.
@@ -1118,18 +1135,23 @@ int enqueue_decode_mega(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, cudaStream
     a.lm_head = c->lm_head;
     a.tok_embd = c->tok_embd;
     a.out_norm = c->out_norm;
-    a.X = c->X;
-    a.ATT = c->ATT;
-    a.FA = c->FA;
-    a.QKV = c->QKVr;
     a.qkv_rows = c->layers[0].qkv.rows;
-    a.part = c->part;
-    a.part_ml = c->part_ml;
-    a.counters = c->counters;
+    {
+        uint64_t* w = c->mega_ll;
+        a.xl = w;
+        w += 2 * (size_t)hp.hidden_size;
+        a.qkvl = w;
+        w += 2 * (size_t)a.qkv_rows;
+        a.attl = w;
+        w += 2 * (size_t)hp.n_heads * hp.head_dim;
+        a.fal = w;
+        w += 2 * (size_t)hp.intermediate_size;
+        a.pl = w;   // 2 * nq * MEGA_MAX_SPLITS * (hd + 2) words; every offset above is even (16-byte aligned)
+    }
     a.meta = c->meta;
     a.tok = c->tok;
-    a.amax = c->amax;
-    a.bar_count = c->bar_count;
+    a.amax = c->mega_amax;
+    a.done = c->mega_done;
     a.epoch = c->epoch;
     a.abort = c->abort_flag;
     mega_split(c, M, max_lim, &a.split, &a.nsplit);
@@ -1137,10 +1159,12 @@ int enqueue_decode_mega(vvq2_ctx* c, vvq2_kv* kv, int M, int max_lim, cudaStream
     a.rope_ts = c->rope_ts;
     a.scale = 1.0f / sqrtf((float)hp.head_dim);
     a.err = c->err;
+    a.err_info = c->mega_err_info;
     a.trace = c->mega_trace;
     a.nstage = p.nstage;
     a.slot_bytes = p.slot;
     a.union_bytes = p.uni;
+    a.att_off = decode_mega_att_offset(M, hp.hidden_size);
     a.t_qkv = p.t_qkv;
     a.t_o = p.t_o;
     a.t_gu = p.t_gu;
@@ -1309,7 +1333,6 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     rc = rc ? rc : c->alloc(&c->rope_cs, (size_t)P * hp->head_dim / 2);
     rc = rc ? rc : c->alloc(&c->ATT, (size_t)M * qw);
     rc = rc ? rc : c->alloc(&c->FA, (size_t)M * F);
-    rc = rc ? rc : c->alloc(&c->QKVr, (size_t)M * (hp->n_heads + 2 * hp->n_kv_heads) * hp->head_dim);
     // attention partials: decode rows x splits, or batched-decode rows x splits (<= PART_SLOTS)
     rc = rc ? rc : c->alloc(&c->part, (size_t)PART_SLOTS * qw);
     rc = rc ? rc : c->alloc(&c->part_ml, (size_t)PART_SLOTS * hp->n_heads * 2);
@@ -1318,7 +1341,12 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
     rc = rc ? rc : c->alloc(&c->amax, (size_t)P);   // batched decode: one key / token per row
     rc = rc ? rc : c->alloc(&c->tok, (size_t)P);
     rc = rc ? rc : c->alloc(&c->err, (size_t)1);
-    rc = rc ? rc : c->alloc(&c->bar_count, (size_t)1);
+    c->mega_ll_n = mega_ll_words(hp->hidden_size, (hp->n_heads + 2 * hp->n_kv_heads) * hp->head_dim, hp->n_heads,
+                                 hp->head_dim, F);
+    rc = rc ? rc : c->alloc(&c->mega_ll, c->mega_ll_n);
+    rc = rc ? rc : c->alloc(&c->mega_amax, (size_t)2);
+    rc = rc ? rc : c->alloc(&c->mega_err_info, (size_t)4);
+    rc = rc ? rc : c->alloc(&c->mega_done, (size_t)1);
     rc = rc ? rc : c->alloc(&c->epoch, (size_t)1);
     rc = rc ? rc : c->alloc(&c->abort_flag, (size_t)1);
     c->mega_grid = decode_mega_grid();
@@ -1328,7 +1356,10 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
         rc = fail(VVQ2_ERR_OUT_OF_MEMORY, "pinned alloc failed");
     if (!rc && (cudaMemset(c->counters, 0, sizeof(int) * P * hp->n_kv_heads) != cudaSuccess ||
                 cudaMemset(c->err, 0, sizeof(int)) != cudaSuccess ||
-                cudaMemset(c->bar_count, 0, sizeof(unsigned long long)) != cudaSuccess ||
+                cudaMemset(c->mega_ll, 0, c->mega_ll_n * sizeof(uint64_t)) != cudaSuccess ||
+                cudaMemset(c->mega_amax, 0, 2 * sizeof(unsigned long long)) != cudaSuccess ||
+                cudaMemset(c->mega_err_info, 0, 4 * sizeof(unsigned long long)) != cudaSuccess ||
+                cudaMemset(c->mega_done, 0, sizeof(unsigned int)) != cudaSuccess ||
                 cudaMemset(c->epoch, 0, sizeof(unsigned int)) != cudaSuccess ||
                 cudaMemset(c->abort_flag, 0, sizeof(int)) != cudaSuccess ||
                 cudaDeviceSynchronize() != cudaSuccess))   // the engine stream does not wait for these

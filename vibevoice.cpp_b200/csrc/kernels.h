@@ -83,36 +83,53 @@ struct MegaLayer {
     KvLayer kv;
 };
 
+constexpr int MEGA_MAX_SPLITS = 64;   // attention splits per (row, KV head) of the persistent step
+
+// The persistent step hands values between its stages as flagged words:
+// uint64 (tag << 32) | f32 bits, one 64-bit store each (see decode_mega.cu).
 struct MegaArgs {
     const MegaLayer* layers = nullptr;   // device array
     int n_layers = 0, H = 0, F = 0, nq = 0, nkv = 0, hd = 0, M = 0, grid = 0;
     DevW lm_head, tok_embd;
     const float* out_norm = nullptr;
-    float *X = nullptr, *ATT = nullptr, *FA = nullptr;
-    float* QKV = nullptr;                // [M][qkv_rows] raw q|k|v (+bias), before RoPE
+    uint64_t* xl = nullptr;              // [M][H] hidden rows
+    uint64_t* qkvl = nullptr;            // [M][qkv_rows] raw q|k|v (+bias), before RoPE
+    uint64_t* pl = nullptr;              // [M][nkv][MEGA_MAX_SPLITS][nq/nkv][hd + 2] partial O, max, sum
+    uint64_t* attl = nullptr;            // [M][nq * hd] attention output
+    uint64_t* fal = nullptr;             // [M][F] SwiGLU output
     int qkv_rows = 0;
-    float *part = nullptr, *part_ml = nullptr;   // [M][64][nq][hd], [M][64][nq][2]
-    int* counters = nullptr;
     RowMeta* meta = nullptr;
     int32_t* tok = nullptr;
-    unsigned long long* amax = nullptr;
-    unsigned long long* bar_count = nullptr;
-    unsigned int* epoch = nullptr;
+    unsigned long long* amax = nullptr;  // [2] running argmax keys, zero between launches
+    unsigned int* done = nullptr;        // CTAs that finished the step, zero between launches
+    unsigned int* epoch = nullptr;       // launches so far (the tags derive from it)
     int* abort = nullptr;
     int split = 0, nsplit = 0;
     float eps = 0.f, rope_ts = 0.f, scale = 0.f;
     int* err = nullptr;
-    // shared-memory plan: [union_bytes: activations | attention][nstage x slot_bytes ring][phase table]
-    int nstage = 0, slot_bytes = 0, union_bytes = 0;
+    unsigned long long* err_info = nullptr;   // [4] where the first failing wait gave up
+    // shared-memory plan: [union_bytes: activations | merge scratch, attention
+    // at att_off][nstage x slot_bytes ring][stage table]
+    int nstage = 0, slot_bytes = 0, union_bytes = 0, att_off = 0;
     int t_qkv = 1, t_o = 1, t_gu = 1, t_down = 1, t_lm = 1;   // weight rows per ring tile
-    // optional phase timeline: [slot][grid] %globaltimer ns; slot 0 = start,
-    // 1 + 2b / 2 + 2b = arrival at / release from grid barrier b, last = end
+    // optional timeline: [slot][grid] %globaltimer ns of thread 0 of every CTA;
+    // slot 0 = start, per layer l slots 1 + 10l + {0: QKV stage begins, 1:
+    // QKV input staged, 2: thread 0's QKV tiles done, 3: attention items
+    // done (CTA), 4: merges done, 5: O input staged, 6: O tiles done (CTA),
+    // 7: gate/up input staged, 8: gate/up tiles done (CTA), 9: down input
+    // staged}, then lm_head stage begins, lm_head input staged, copies
+    // drained, end
     unsigned long long* trace = nullptr;
 };
-__host__ __device__ constexpr int mega_trace_slots(int n_layers) { return 2 * (5 * n_layers + 2) + 2; }
+__host__ __device__ constexpr int mega_trace_slots(int n_layers) { return 10 * n_layers + 5; }
+// flagged words of the persistent step for up to 2 rows
+__host__ __device__ constexpr size_t mega_ll_words(int H, int qkv_rows, int nq, int hd, int F) {
+    return 2 * ((size_t)H + qkv_rows + (size_t)nq * hd + F + (size_t)nq * MEGA_MAX_SPLITS * (hd + 2));
+}
 cudaError_t decode_mega_prepare();
 cudaError_t decode_mega_launch(const MegaArgs& a, size_t smem, cudaStream_t st);
-int decode_mega_union_bytes(int hd, int M, int kmax);
+int decode_mega_union_bytes(int hd, int M, int kmax, int H);
+int decode_mega_att_offset(int M, int H);
 int decode_mega_max_stages();
 int decode_mega_consumer_warps();
 int decode_mega_table_bytes(int n_layers);
