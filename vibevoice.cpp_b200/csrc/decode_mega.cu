@@ -73,8 +73,13 @@ constexpr int PAGE = KV_PAGE;           // keys per page / tile
 constexpr int MAX_MERGE = MEGA_MAX_SPLITS;
 constexpr uint32_t WAIT_POLLS = 1u << 24;   // mbarrier try_waits
 constexpr uint32_t LL_POLLS = 1u << 21;     // L2 polls of a flagged word (~0.5 us each)
-constexpr int SB = 1;                   // flagged float4 groups in flight per thread while staging
-                                        // (more spill the GEMV tile loop: the kernel sits at 128 registers)
+// flagged float4 groups each thread keeps in flight while staging: the
+// hidden-row and attention stages have fewer groups than threads; the
+// SwiGLU stage (M x F words) takes SB_FA groups (fewer round trips).
+// (Requests in flight hold registers, and at every other stage more of them
+// spill the GEMV tile loop: the kernel sits at the 128-register limit.)
+constexpr int SB_FA = 3;
+constexpr int SB_MERGE = 1;             // word pairs per thread in flight while a merge gathers partials
 // pause between unsuccessful poll rounds: every waiting thread of every CTA
 // polls, and re-requesting at the L2 round-trip rate would flood L2 with
 // requests (starving the producers and the weight stream)
@@ -82,22 +87,8 @@ constexpr unsigned POLL_PAUSE_NS = 128;
 
 enum { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DOWN = 3, PH_LM = 4 };
 
-template <int HD>
-struct AttConst {
-    static constexpr int NG = 2;                                 // attention groups per CTA
-    static constexpr int TILE_BYTES = PAGE * HD * 2;             // one page of K (or V) of one head
-    static constexpr int GROUP_BYTES = 2 * TILE_BYTES;           // K and V of one page
-};
-
-// per-group attention state (in the attention part of the shared region)
-template <int HD>
-struct __align__(16) AttSh {
-    float qs[MAXG][HD];            // roped q, rounded to f16 (ggml FA converts Q to the K type)
-    float sc[MAXG][PAGE];
-    float run_max[MAXG], run_sum[MAXG], alpha[MAXG];
-    __half kn[HD], vn[HD];         // this step's key (roped) and value row
-    int failed;
-};
+constexpr int AQ = 4;                   // quarters of the CTA in an attention item (4 x 128 threads)
+constexpr int AKEYS = PAGE / AQ;        // keys of a page per quarter
 
 struct Ctl {
     int fail;                      // a wait of this CTA gave up or the step is aborting
@@ -258,7 +249,7 @@ __device__ float ll_wait(const MegaArgs& a, Ctl& ctl, const uint64_t* p, uint32_
 // 1/sqrt(mean(x^2) + eps) is applied to the dot products instead
 // (W (x s o w) = s W (x o w)), so no second pass over act is needed.
 // The caller follows with cta_failed() (the CTA barrier that publishes act).
-template <int MB>
+template <int MB, int SB = 1>
 __device__ void stage_ll(const MegaArgs& a, Ctl& ctl, const uint64_t* src, int K, uint32_t tag, const float* norm_w,
                          float* act, float* red) {
     __syncwarp();   // entered by converged warps only (see trace_mark)
@@ -624,17 +615,19 @@ __device__ __forceinline__ bool att_item_geo(const MegaArgs& a, int it, AttItem&
     return true;
 }
 
-// K and V of page `tile` of the item into the group's single stage.
+// K and V of the first page of item x into the stage the CTA's page counter
+// selects (the same stage cta_att_item uses for it).
 template <int HD>
-__device__ __forceinline__ void att_issue(const KvLayer& kv, const AttItem& x, int tile, __half* kt, __half* vt,
-                                          uint64_t* bar) {
-    constexpr int TB = AttConst<HD>::TILE_BYTES;
-    const int page =
-        tile == 0 ? x.page0 : __ldg(kv.block_table + (size_t)x.rm.seq * kv.max_pages + (x.j0 + tile * PAGE) / PAGE);
-    const size_t off = ((size_t)page * kv.n_kv + x.g) * PAGE * HD;
+__device__ __forceinline__ void att_prefetch(const KvLayer& kv, const AttItem& x, uint8_t* att, uint64_t* abar,
+                                             uint32_t ptiles) {
+    constexpr int TB = PAGE * HD * 2;
+    const size_t off = ((size_t)x.page0 * kv.n_kv + x.g) * PAGE * HD;
+    uint64_t* bar = &abar[ptiles & 1];
+    __half* kd = reinterpret_cast<__half*>(att + (ptiles & 1) * 2 * TB);
+    tc::fence_proxy_async_smem();
     tc::mbar_arrive_expect_tx(bar, 2 * TB);
-    bulk_g2s(kt, kv.k + off, TB, bar);
-    bulk_g2s(vt, kv.v + off, TB, bar);
+    bulk_g2s(kd, kv.k + off, TB, bar);
+    bulk_g2s(kd + PAGE * HD, kv.v + off, TB, bar);
 }
 
 // Flagged word of the partial (O, max, sum) buffer: [row][kv head][split][q head of the group][hd + 2].
@@ -644,245 +637,271 @@ __device__ __forceinline__ uint64_t* part_ptr(const MegaArgs& a, int m, int g, i
     return a.pl + ((((size_t)m * a.nkv + g) * MAX_MERGE + s) * G + h) * (HD + 2);
 }
 
-// One attention item on a 128-thread group.  The first tile may already be
-// in flight (`prefetched`).  Returns false after a wait gave up (uniform in
-// the group).
+// Shared state of the CTA's attention item (in the attention part of the
+// shared region, after the two K|V page stages).
 template <int HD>
-__device__ bool att_item(const MegaArgs& a, Ctl& ctl, const KvLayer& kv, const AttItem& x, int tid, __half* kt,
-                         __half* vt, AttSh<HD>& sh, const float2* cs_row, uint64_t* bar, uint32_t& uses,
-                         bool prefetched, GroupSync sync, uint32_t tag_qkv, uint32_t tag_out) {
-    const int lane = tid & 31, warp = tid >> 5;
-    const int G = a.nq / a.nkv;
+struct __align__(16) AttSh {
+    float qs[MAXG][HD];                // roped q, rounded to f16 (ggml FA converts Q to the K type)
+    float sc[AQ][MAXG][AKEYS];         // per quarter: probabilities of its keys of the page
+    float alpha[AQ][MAXG];             // per quarter: rescale of O on a new running max
+    float og[AQ][MAXG][HD];            // per quarter: unnormalized O at the end of the item
+    float mg[AQ][MAXG], lg[AQ][MAXG];  // per quarter: running max and sum
+    __half kn[HD], vn[HD];             // this step's key (roped) and value row
+};
+
+// One attention item (row m, KV head g, split s: pages [j0, j1) of keys) by
+// the whole CTA.  The 16 warps form AQ = 4 quarters of 128 threads; quarter
+// q owns keys 16q .. 16q + 15 of every page, with its own online softmax:
+//  * scores: thread (key kk, head slot hh) computes one q.k dot product over
+//    HD (K read in a per-key rotated 16-byte order: no bank conflicts); the
+//    16 threads of a head are a half warp, so max and sum are shuffles;
+//  * P.V: thread (column pair dp, head slot hs) accumulates its heads'
+//    two columns over the quarter's 16 keys.
+// The quarters' (O, max, sum) are then merged (log-sum-exp) into the item's
+// partial, or -- when the row has a single split -- its output.
+// Pages live in two K|V stages (page t of the launch's page counter p uses
+// stage p & 1); the first page may have been requested already (`prefetched`).
+// Returns false (uniform over the CTA) after a wait gave up; pages it
+// requested are waited for before it returns.
+template <int HD>
+__device__ bool cta_att_item(const MegaArgs& a, Ctl& ctl, const KvLayer& kv, const AttItem& x, uint8_t* att,
+                             const float2* cs_row, uint64_t* abar, uint32_t& ptiles, bool prefetched,
+                             uint32_t tag_qkv, uint32_t tag_out) {
+    constexpr int TB = PAGE * HD * 2;           // bytes of K (or V) of one page of one head
     constexpr int half = HD / 2;
+    constexpr int NCH = HD / 8;                 // 16-byte chunks of a K row
+    constexpr int PAIRS = HD / 2;
+    constexpr int HSUB = 128 / PAIRS;           // head slots of P.V per quarter (4 at hd 64, 2 at hd 128)
+    constexpr int HPER = MAXG / HSUB;           // heads per P.V thread
+    AttSh<HD>& sh = *reinterpret_cast<AttSh<HD>*>(att + 4 * TB);
+    const int tid = threadIdx.x;
+    const int q = tid >> 7, gtid = tid & 127;   // quarter, thread in quarter
+    const int G = a.nq / a.nkv;
     const int m = x.m, g = x.g;
     const RowMeta& rm = x.rm;
-    const int newj = rm.cidx;   // cache index of this step's key/value
+    const int newj = rm.cidx;                   // cache index of this step's key/value
     const bool has_new = newj >= x.j0 && newj < x.j1;
-
+    const uint32_t base = ptiles;
+    auto stage_k = [&](uint32_t t) { return reinterpret_cast<__half*>(att + ((base + t) & 1) * 2 * TB); };
+    auto issue = [&](uint32_t t) {             // page t of the item into its stage (one thread)
+        const int page = __ldg(kv.block_table + (size_t)rm.seq * kv.max_pages + (x.j0 + (int)t * PAGE) / PAGE);
+        const size_t off = ((size_t)page * kv.n_kv + g) * PAGE * HD;
+        uint64_t* bar = &abar[(base + t) & 1];
+        __half* kd = stage_k(t);
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive_expect_tx(bar, 2 * TB);
+        bulk_g2s(kd, kv.k + off, TB, bar);
+        bulk_g2s(kd + PAGE * HD, kv.v + off, TB, bar);
+    };
     if (tid == 0) {
-        if (!prefetched) {
-            tc::fence_proxy_async_smem();
-            att_issue<HD>(kv, x, 0, kt, vt, bar);
-        }
+        if (!prefetched) issue(0);
+        if (x.ntiles > 1) issue(1);
     }
-    if (tid < MAXG) {
-        sh.run_max[tid] = -INFINITY;
-        sh.run_sum[tid] = 0.f;
-    }
-    // this step's raw q (and new k, v) rows: flagged words of the QKV stage,
-    // all requested at once, then re-polled until tagged
+    uint32_t issued = min(x.ntiles, 2);       // pages requested (identical in every thread)
+
+    // this step's raw q (and new k, v): flagged words of the QKV stage.  Task
+    // list: the G * hd/2 rotation pairs of q, the hd/2 pairs of k, the hd
+    // words of v; thread t takes tasks t, t + 512; all requested at once,
+    // then re-polled until tagged.
+    constexpr int NTASK = (MAXG * half + half + HD + MT - 1) / MT;
     const uint64_t* qkv = a.qkvl + (size_t)m * a.qkv_rows;
-    constexpr int QI = (MAXG * half + ATT_THREADS - 1) / ATT_THREADS;
     const uint64_t ready = (uint64_t)tag_qkv << 32;   // a word that needs no poll
-    uint64_t wa[QI], wb[QI], wk0 = ready, wk1 = ready, wv = ready;
-    const uint64_t* pa[QI];
+    const int nq_t = G * half, nk_t = has_new ? half : 0, nv_t = has_new ? HD : 0;
+    const uint64_t* pw[NTASK][2];
+    uint64_t w[NTASK][2];
 #pragma unroll
-    for (int it = 0; it < QI; ++it) {
-        const int t = tid + it * ATT_THREADS;
-        pa[it] = qkv + (size_t)(g * G + t / half) * HD + t % half;
-        wa[it] = wb[it] = ready;
-        if (t < G * half) {
-            wa[it] = ll_get(pa[it]);
-            wb[it] = ll_get(pa[it] + half);
+    for (int k = 0; k < NTASK; ++k) {
+        const int t = tid + k * MT;
+        pw[k][0] = pw[k][1] = nullptr;
+        if (t < nq_t) {
+            pw[k][0] = qkv + (size_t)(g * G + t / half) * HD + t % half;   // (q_h[i], q_h[i + hd/2])
+            pw[k][1] = pw[k][0] + half;
+        } else if (t < nq_t + nk_t) {
+            pw[k][0] = qkv + (size_t)(a.nq + g) * HD + (t - nq_t);         // (k[i], k[i + hd/2])
+            pw[k][1] = pw[k][0] + half;
+        } else if (t < nq_t + nk_t + nv_t) {
+            pw[k][0] = qkv + (size_t)(a.nq + a.nkv + g) * HD + (t - nq_t - nk_t);   // v[i]
         }
+        w[k][0] = pw[k][0] ? ll_get(pw[k][0]) : ready;
+        w[k][1] = pw[k][1] ? ll_get(pw[k][1]) : ready;
     }
-    const uint64_t* pk = qkv + (size_t)(a.nq + g) * HD + tid;
-    const uint64_t* pv = qkv + (size_t)(a.nq + a.nkv + g) * HD + tid;
-    if (has_new) {
-        if (tid < half) {
-            wk0 = ll_get(pk);
-            wk1 = ll_get(pk + half);
-        }
-        if (tid < HD) wv = ll_get(pv);
-    }
+    bool bad = false;
     for (uint32_t it = 1;; ++it) {
-        bool ok = ll_ok(wk0, tag_qkv) && ll_ok(wk1, tag_qkv) && ll_ok(wv, tag_qkv);
+        bool ok = true;
 #pragma unroll
-        for (int i = 0; i < QI; ++i) ok = ok && ll_ok(wa[i], tag_qkv) && ll_ok(wb[i], tag_qkv);
+        for (int k = 0; k < NTASK; ++k) ok = ok && ll_ok(w[k][0], tag_qkv) && ll_ok(w[k][1], tag_qkv);
         if (ok) break;
         if ((it & 31) == 0 && poll_give_up(a, ctl, it, 8)) {
-            sh.failed = 1;
+            bad = true;
             break;
         }
         __nanosleep(POLL_PAUSE_NS);
 #pragma unroll
-        for (int i = 0; i < QI; ++i) {
-            if (!ll_ok(wa[i], tag_qkv)) wa[i] = ll_get(pa[i]);
-            if (!ll_ok(wb[i], tag_qkv)) wb[i] = ll_get(pa[i] + half);
+        for (int k = 0; k < NTASK; ++k) {
+            if (!ll_ok(w[k][0], tag_qkv)) w[k][0] = ll_get(pw[k][0]);
+            if (!ll_ok(w[k][1], tag_qkv)) w[k][1] = ll_get(pw[k][1]);
         }
-        if (!ll_ok(wk0, tag_qkv)) wk0 = ll_get(pk);
-        if (!ll_ok(wk1, tag_qkv)) wk1 = ll_get(pk + half);
-        if (!ll_ok(wv, tag_qkv)) wv = ll_get(pv);
     }
 #pragma unroll
-    for (int it = 0; it < QI; ++it) {
-        const int t = tid + it * ATT_THREADS;
-        if (t < G * half) {
+    for (int k = 0; k < NTASK; ++k) {
+        const int t = tid + k * MT;
+        const float va = ll_val(w[k][0]), vb = ll_val(w[k][1]);
+        if (t < nq_t) {
             const int h = t / half, i = t % half;
             const float2 cs = cs_row[i];
-            const float qa = ll_val(wa[it]), qb = ll_val(wb[it]);
-            const float y0 = __fsub_rn(__fmul_rn(qa, cs.x), __fmul_rn(qb, cs.y));
-            const float y1 = __fadd_rn(__fmul_rn(qa, cs.y), __fmul_rn(qb, cs.x));
-            sh.qs[h][i] = __half2float(__float2half_rn(y0));
-            sh.qs[h][i + half] = __half2float(__float2half_rn(y1));
+            sh.qs[h][i] = __half2float(__float2half_rn(__fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y))));
+            sh.qs[h][i + half] = __half2float(__float2half_rn(__fadd_rn(__fmul_rn(va, cs.y), __fmul_rn(vb, cs.x))));
+        } else if (t < nq_t + nk_t) {
+            const int i = t - nq_t;
+            const float2 cs = cs_row[i];
+            sh.kn[i] = __float2half_rn(__fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y)));
+            sh.kn[i + half] = __float2half_rn(__fadd_rn(__fmul_rn(va, cs.y), __fmul_rn(vb, cs.x)));
+        } else if (t < nq_t + nk_t + nv_t) {
+            sh.vn[t - nq_t - nk_t] = __float2half_rn(va);
         }
-    }
-    if (has_new) {
-        if (tid < half) {
-            const float2 cs = cs_row[tid];
-            const float ka = ll_val(wk0), kb = ll_val(wk1);
-            sh.kn[tid] = __float2half_rn(__fsub_rn(__fmul_rn(ka, cs.x), __fmul_rn(kb, cs.y)));
-            sh.kn[tid + half] = __float2half_rn(__fadd_rn(__fmul_rn(ka, cs.y), __fmul_rn(kb, cs.x)));
-        }
-        if (tid < HD) sh.vn[tid] = __float2half_rn(ll_val(wv));
     }
 
-    constexpr int NCH = HD / 8;
-    constexpr int PAIRS = HD / 2;
-    constexpr int HSUB = ATT_THREADS / PAIRS;
-    constexpr int HPER = (MAXG + HSUB - 1) / HSUB;
-    const int dp = tid % PAIRS, hs = tid / PAIRS;
+    // scores ownership: key kk of the quarter, head slot hh (a half warp per head)
+    const int kk = gtid & (AKEYS - 1), hh = gtid >> 4;
+    const int key = q * AKEYS + kk;
+    const int rot = key % NCH;
+    const bool hrow = hh < G;
+    float rmax = -INFINITY, rsum = 0.f;         // running max / sum of head hh over this quarter's keys
+    // P.V ownership: column pair dp, heads hs, hs + HSUB, ...
+    const int dp = gtid % PAIRS, hs = gtid / PAIRS;
     float2 o[HPER];
 #pragma unroll
     for (int k = 0; k < HPER; ++k) o[k] = make_float2(0.f, 0.f);
-    const int kk = tid % PAGE, hh = tid / PAGE;
-    const int rot = kk % NCH;
+    GroupSync qsync{1 + q};
 
-    for (int t = 0; t < x.ntiles; ++t) {
-        // the page copy was requested by this group: wait for it even when failing
-        if (!tc::mbar_wait(bar, uses & 1)) {
-            atomicCAS(a.err, 0, 1);
-            sh.failed = 1;
+    for (uint32_t t = 0; t < (uint32_t)x.ntiles; ++t) {
+        if (!tc::mbar_wait(&abar[(base + t) & 1], ((base + t) >> 1) & 1)) {
+            if (!*(volatile int*)&ctl.fail) raise_fail(a, ctl, 1);
+            bad = true;
         }
-        uses += 1;
-        sync();
-        if (sh.failed) return false;   // uniform after the group barrier
-        __half* K = kt;
-        __half* V = vt;
-        const int tj0 = x.j0 + t * PAGE;
+        __half* K = stage_k(t);
+        __half* V = K + PAGE * HD;
+        const int tj0 = x.j0 + (int)t * PAGE;
         const int nk = min(PAGE, x.j1 - tj0);
         if (has_new && newj >= tj0 && newj < tj0 + PAGE) {
-            // the page copy predates this step's row: patch it in
-            for (int d = tid; d < HD; d += ATT_THREADS) {
+            // the page copy predates this step's row: patch it in (after the stage wait)
+            __syncthreads();
+            for (int d = tid; d < HD; d += MT) {
                 K[(newj - tj0) * HD + d] = sh.kn[d];
                 V[(newj - tj0) * HD + d] = sh.vn[d];
             }
-            sync();
         }
-        {
-            float acc[MAXG / 2];
-#pragma unroll
-            for (int i = 0; i < MAXG / 2; ++i) acc[i] = 0.f;
+        if (__syncthreads_or(bad ? 1 : 0)) break;   // also publishes qs / kn / vn / the patch
+        // ---- scores of the quarter's keys, running max / sum per head
+        float sres = -INFINITY;
+        if (hrow) {
+            float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
                 const int ch = (c + rot) % NCH;
-                const uint4 raw = reinterpret_cast<const uint4*>(K + kk * HD)[ch];
+                const uint4 raw = reinterpret_cast<const uint4*>(K + key * HD)[ch];
                 const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-                float kf[8];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(hp[e]);
-                    kf[2 * e] = f.x;
-                    kf[2 * e + 1] = f.y;
-                }
-#pragma unroll
-                for (int i = 0; i < MAXG / 2; ++i) {
-                    const int h = hh + 2 * i;
-                    if (h < G) {
-                        const float4* qp = reinterpret_cast<const float4*>(&sh.qs[h][ch * 8]);
-                        const float4 q0 = qp[0], q1 = qp[1];
-                        acc[i] = fmaf(q0.x, kf[0], acc[i]);
-                        acc[i] = fmaf(q0.y, kf[1], acc[i]);
-                        acc[i] = fmaf(q0.z, kf[2], acc[i]);
-                        acc[i] = fmaf(q0.w, kf[3], acc[i]);
-                        acc[i] = fmaf(q1.x, kf[4], acc[i]);
-                        acc[i] = fmaf(q1.y, kf[5], acc[i]);
-                        acc[i] = fmaf(q1.z, kf[6], acc[i]);
-                        acc[i] = fmaf(q1.w, kf[7], acc[i]);
-                    }
-                }
+                const float4* qp = reinterpret_cast<const float4*>(&sh.qs[hh][ch * 8]);
+                const float4 q0 = qp[0], q1 = qp[1];
+                const float2 k0 = __half22float2(hp[0]), k1 = __half22float2(hp[1]);
+                const float2 k2 = __half22float2(hp[2]), k3 = __half22float2(hp[3]);
+                acc0 = fmaf(q0.x, k0.x, acc0);
+                acc1 = fmaf(q0.y, k0.y, acc1);
+                acc0 = fmaf(q0.z, k1.x, acc0);
+                acc1 = fmaf(q0.w, k1.y, acc1);
+                acc0 = fmaf(q1.x, k2.x, acc0);
+                acc1 = fmaf(q1.y, k2.y, acc1);
+                acc0 = fmaf(q1.z, k3.x, acc0);
+                acc1 = fmaf(q1.w, k3.y, acc1);
             }
+            if (key < nk) sres = (acc0 + acc1) * a.scale;
+        }
+        float tmax = sres;
 #pragma unroll
-            for (int i = 0; i < MAXG / 2; ++i) {
-                const int h = hh + 2 * i;
-                if (h < G) sh.sc[h][kk] = kk < nk ? acc[i] * a.scale : -INFINITY;
-            }
+        for (int o2 = 8; o2 >= 1; o2 >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o2));
+        const float mnew = fmaxf(rmax, tmax);
+        // no key of this head seen yet in this quarter: nothing to rescale, p = 0
+        const float al = mnew == -INFINITY ? 1.f : expf(rmax - mnew);
+        const float p = sres == -INFINITY ? 0.f : expf(sres - mnew);
+        float psum = p;
+#pragma unroll
+        for (int o2 = 8; o2 >= 1; o2 >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o2);
+        rmax = mnew;
+        rsum = rsum * al + psum;
+        if (hrow) {
+            sh.sc[q][hh][kk] = p;
+            if (kk == 0) sh.alpha[q][hh] = al;
         }
-        sync();
-        for (int h = warp; h < G; h += 4) {
-            float mx = fmaxf(sh.sc[h][lane], sh.sc[h][lane + 32]);
-            mx = warp_max(mx);
-            if (lane == 0) {
-                const float mnew = fmaxf(sh.run_max[h], mx);
-                sh.alpha[h] = expf(sh.run_max[h] - mnew);   // exp(-inf) = 0 on the first tile
-                sh.run_max[h] = mnew;
-            }
-        }
-        sync();
-        for (int i = tid; i < G * PAGE; i += ATT_THREADS) {
-            const int h = i / PAGE, k = i % PAGE;
-            sh.sc[h][k] = expf(sh.sc[h][k] - sh.run_max[h]);   // masked keys: exp(-inf) = 0
-        }
-        sync();
-        for (int h = warp; h < G; h += 4) {
-            const float sm = warp_sum(sh.sc[h][lane] + sh.sc[h][lane + 32]);
-            if (lane == 0) sh.run_sum[h] = sh.run_sum[h] * sh.alpha[h] + sm;
-        }
+        qsync();
+        // ---- O = O * alpha + P.V over the quarter's keys
 #pragma unroll
         for (int k = 0; k < HPER; ++k) {
             const int h = hs + k * HSUB;
             if (h < G) {
-                o[k].x *= sh.alpha[h];
-                o[k].y *= sh.alpha[h];
-            }
-        }
-        for (int j = 0; j < nk; ++j) {
-            const float2 v = __half22float2(reinterpret_cast<const __half2*>(V + j * HD)[dp]);
+                const float al2 = sh.alpha[q][h];
+                float2 acc = make_float2(o[k].x * al2, o[k].y * al2);
 #pragma unroll
-            for (int k = 0; k < HPER; ++k) {
-                const int h = hs + k * HSUB;
-                if (h < G) {
-                    const float p = sh.sc[h][j];
-                    o[k].x = fmaf(p, v.x, o[k].x);
-                    o[k].y = fmaf(p, v.y, o[k].y);
+                for (int j = 0; j < AKEYS; ++j) {
+                    if (q * AKEYS + j >= nk) break;   // keys past the row: the stale page entries may hold any bits
+                    const float2 v = __half22float2(reinterpret_cast<const __half2*>(V + (q * AKEYS + j) * HD)[dp]);
+                    const float pj = sh.sc[q][h][j];
+                    acc.x = fmaf(pj, v.x, acc.x);
+                    acc.y = fmaf(pj, v.y, acc.y);
                 }
+                o[k] = acc;
             }
         }
-        sync();   // the stage and sc are free again
-        if (tid == 0 && t + 1 < x.ntiles) {
-            tc::fence_proxy_async_smem();
-            att_issue<HD>(kv, x, t + 1, kt, vt, bar);
-        }
+        __syncthreads();   // the stage and sc are free again
+        if (tid == 0 && issued < (uint32_t)x.ntiles) issue(issued);
+        issued = min((uint32_t)x.ntiles, issued + (t + 2 < (uint32_t)x.ntiles ? 1u : 0u));
     }
-    // append this step's K/V row to the paged cache (read by later steps)
+    ptiles = base + issued;
+    if (bad) {
+        // pages requested but not consumed: wait (bounded) before the stages are reused
+        for (uint32_t t = 0; t < issued; ++t) tc::mbar_wait(&abar[(base + t) & 1], ((base + t) >> 1) & 1, 1u << 20);
+        return false;
+    }
+    // ---- append this step's K/V row to the paged cache (read by later steps)
     if (has_new) {
         const size_t off = kv_offset(kv, rm.seq, newj, g);
-        for (int d = tid; d < HD; d += ATT_THREADS) {
+        for (int d = tid; d < HD; d += MT) {
             kv.k[off + d] = sh.kn[d];
             kv.v[off + d] = sh.vn[d];
         }
     }
-    if (x.nsplit == 1) {
-        // the only split: the normalized output, straight to the attention words
-        uint64_t* out = a.attl + (size_t)m * a.nq * HD;
-#pragma unroll
-        for (int k = 0; k < HPER; ++k) {
-            const int h = hs + k * HSUB;
-            if (h < G) {
-                const float inv = 1.0f / sh.run_sum[h];
-                ll_put2(out + (size_t)(g * G + h) * HD + 2 * dp, o[k].x * inv, o[k].y * inv, tag_out);
-            }
-        }
-    } else {
-        // partial (O, max, sum) for the merge
-#pragma unroll
-        for (int k = 0; k < HPER; ++k) {
-            const int h = hs + k * HSUB;
-            if (h < G) ll_put2(part_ptr<HD>(a, m, g, x.s, h) + 2 * dp, o[k].x, o[k].y, tag_out);
-        }
-        if (tid < G) ll_put2(part_ptr<HD>(a, m, g, x.s, tid) + HD, sh.run_max[tid], sh.run_sum[tid], tag_out);
+    // ---- merge the quarters
+    if (hrow && kk == 0) {
+        sh.mg[q][hh] = rmax;
+        sh.lg[q][hh] = rsum;
     }
-    sync();   // sh is reused by the next item
+#pragma unroll
+    for (int k = 0; k < HPER; ++k) {
+        const int h = hs + k * HSUB;
+        if (h < G) reinterpret_cast<float2*>(&sh.og[q][h][0])[dp] = o[k];
+    }
+    __syncthreads();
+    const bool single = x.nsplit == 1;
+    for (int i = tid; i < G * HD; i += MT) {
+        const int h = i / HD, d = i % HD;
+        float mx = sh.mg[0][h];
+#pragma unroll
+        for (int qq = 1; qq < AQ; ++qq) mx = fmaxf(mx, sh.mg[qq][h]);
+        float num = 0.f, den = 0.f;
+#pragma unroll
+        for (int qq = 0; qq < AQ; ++qq) {
+            const float w = sh.mg[qq][h] == -INFINITY ? 0.f : expf(sh.mg[qq][h] - mx);
+            num = fmaf(w, sh.og[qq][h][d], num);
+            den = fmaf(w, sh.lg[qq][h], den);
+        }
+        if (single) {
+            ll_put(a.attl + (size_t)m * a.nq * HD + (size_t)(g * G + h) * HD + d, num / den, tag_out);
+        } else {
+            uint64_t* pp = part_ptr<HD>(a, m, g, x.s, h);
+            ll_put(pp + d, num, tag_out);
+            if (d == 0) ll_put2(pp + HD, mx, den, tag_out);
+        }
+    }
+    __syncthreads();   // sh and the stages are reused by the next item
     return true;
 }
 
@@ -903,11 +922,11 @@ __device__ bool cta_merge(const MegaArgs& a, Ctl& ctl, int m, int qh, int ns, ui
     const uint64_t* src = part_ptr<HD>(a, m, g, 0, h);
     const int NP = ns * W2;
     bool bad = false;
-    for (int b0 = 0; b0 < NP && !bad; b0 += SB * NCT) {
-        uint64_t w[SB][2];
+    for (int b0 = 0; b0 < NP && !bad; b0 += SB_MERGE * NCT) {
+        uint64_t w[SB_MERGE][2];
         uint32_t pend = 0;
 #pragma unroll
-        for (int j = 0; j < SB; ++j) {
+        for (int j = 0; j < SB_MERGE; ++j) {
             const int p = b0 + j * NCT + tid;
             if (p < NP) {
                 ll_get2(src + (p / W2) * sstride + 2 * (p % W2), w[j][0], w[j][1]);
@@ -916,7 +935,7 @@ __device__ bool cta_merge(const MegaArgs& a, Ctl& ctl, int m, int qh, int ns, ui
         }
         for (uint32_t it = 1; pend; ++it) {
 #pragma unroll
-            for (int j = 0; j < SB; ++j) {
+            for (int j = 0; j < SB_MERGE; ++j) {
                 if ((pend >> j) & 1u) {
                     const int p = b0 + j * NCT + tid;
                     if (ll_ok(w[j][0], tag_part) && ll_ok(w[j][1], tag_part)) {
@@ -963,9 +982,8 @@ __device__ bool cta_merge(const MegaArgs& a, Ctl& ctl, int m, int qh, int ns, ui
 template <int HD, int MB>
 __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
     extern __shared__ __align__(1024) uint8_t dyn[];
-    using AC = AttConst<HD>;
     __shared__ __align__(8) uint64_t full[MAX_STAGES];
-    __shared__ __align__(8) uint64_t abar[AC::NG];
+    __shared__ __align__(8) uint64_t abar[2];     // the two K|V page stages of the attention items
     __shared__ float red[2 * NCW];
     __shared__ unsigned long long best[2];
     __shared__ float2 rope_cs[2][64];              // RoPE (cos, sin) per row: positions are fixed for the launch
@@ -973,9 +991,9 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
     // state kept in shared memory rather than registers: the GEMV tile loop
     // needs every register, and values live across it would spill there
     __shared__ unsigned long long s_base;          // tag base of this launch
-    __shared__ AttItem s_x0[AttConst<HD>::NG];     // each group's first attention item
-    __shared__ int s_pre[AttConst<HD>::NG];        // ... exists
-    __shared__ int s_pending[AttConst<HD>::NG];    // ... page requested, not yet consumed
+    __shared__ AttItem s_x0;                       // this CTA's first attention item
+    __shared__ int s_pre;                          // ... exists
+    __shared__ int s_pending;                      // ... its page is requested, not yet consumed
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint8_t* region = dyn;                         // activations / merge scratch | attention tiles + state
     uint8_t* ring = dyn + a.union_bytes;
@@ -987,12 +1005,11 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
         s_base = (unsigned long long)(*(volatile unsigned int*)a.epoch) * (8ull * a.n_layers + 8ull);
         ctl.fail = 0;
         for (int i = 0; i < a.nstage; ++i) tc::mbar_init(&full[i], 1);
-        for (int i = 0; i < AC::NG; ++i) tc::mbar_init(&abar[i], 1);
+        for (int i = 0; i < 2; ++i) tc::mbar_init(&abar[i], 1);
         tc::mbar_fence_init();
     }
     trace_mark(a, 0);
     if (tid < 2) best[tid] = 0ull;
-    if (tid < AttConst<HD>::NG) reinterpret_cast<AttSh<HD>*>(region + a.att_off + AttConst<HD>::NG * AttConst<HD>::GROUP_BYTES)[tid].failed = 0;
     // this CTA's tile geometry of every stage of the step
     for (int p = tid; p < nph; p += NCT)
         tab[p] = phase_geo(a, p == nph - 1 ? 0 : p / 4, p == nph - 1 ? PH_LM : p % 4);
@@ -1006,24 +1023,21 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
     ring_normalize(wr, tab, nph);
     for (int d = 0; d < D; ++d) ring_issue(wr, tab, nph, ring, full, warp, lane, D, a.slot_bytes);
 
-    // attention groups: the first item is the same in every layer of the launch
-    const int grp = tid / ATT_THREADS, gtid = tid % ATT_THREADS;
-    if (grp < AC::NG && gtid == 0) {
-        const int it0 = blockIdx.x + grp * gridDim.x;
+    // attention: this CTA's first item is the same in every layer of the launch
+    uint8_t* att = region + a.att_off;
+    if (tid == 0) {
         AttItem x0;
-        s_pre[grp] = it0 < a.nsplit * a.nkv * MB && att_item_geo(a, it0, x0);
-        s_x0[grp] = x0;
-        s_pending[grp] = 0;
+        s_pre = (int)blockIdx.x < a.nsplit * a.nkv * MB && att_item_geo(a, blockIdx.x, x0);
+        s_x0 = x0;
+        s_pending = 0;
     }
     __syncthreads();
-    uint32_t uses = 0;                   // completed phases of this group's page barrier
-    // request the page of the group's first item for layer li (its tiles are free)
+    uint32_t ptiles = 0;                 // K|V pages this CTA has requested in the launch
+    // request the first item's page for layer li (the stages are free)
     auto prefetch = [&](int li) {
-        if (grp < AC::NG && gtid == 0 && s_pre[grp]) {
-            __half* k0 = reinterpret_cast<__half*>(region + a.att_off + (size_t)grp * AC::GROUP_BYTES);
-            tc::fence_proxy_async_smem();
-            att_issue<HD>(a.layers[li].kv, s_x0[grp], 0, k0, k0 + PAGE * HD, &abar[grp]);
-            s_pending[grp] = 1;
+        if (tid == 0 && s_pre) {
+            att_prefetch<HD>(a.layers[li].kv, s_x0, att, abar, ptiles);
+            s_pending = 1;
         }
         __syncwarp();   // reconverge before stage_ll (see trace_mark)
     };
@@ -1074,25 +1088,19 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
         trace_mark(a, tb + 1);
         gemv_tiles<PH_QKV, MB>(a, ctl, li, tab, nph, ring, full, act, red, seq, wr, D, {tg.qkv(li), 0u}, best);
         trace_mark(a, tb + 2);
-        // 2. attention items (groups 0..NG-1; the attention region is not act)
-        if (grp < AC::NG) {
-            const int it0 = blockIdx.x + grp * gridDim.x;
-            const int pre = s_pre[grp];
-            __half* kt = reinterpret_cast<__half*>(region + a.att_off + (size_t)grp * AC::GROUP_BYTES);
-            AttSh<HD>* ash = reinterpret_cast<AttSh<HD>*>(region + a.att_off + AC::NG * AC::GROUP_BYTES);
-            for (int it = it0; it < a.nsplit * a.nkv * MB; it += AC::NG * gridDim.x) {
-                const bool first = it == it0;
+        // 2. attention items, one per CTA at a time (the attention region is not act)
+        {
+            const int pre = s_pre;
+            for (int it = blockIdx.x; it < a.nsplit * a.nkv * MB && !failed; it += gridDim.x) {
+                const bool first = it == (int)blockIdx.x;
                 AttItem x;
-                if (first && pre) x = s_x0[grp];
+                if (first && pre) x = s_x0;
                 else if (!att_item_geo(a, it, x)) continue;
                 const bool pf = first && pre;
-                if (pf && gtid == 0) s_pending[grp] = 0;
-                if (!att_item<HD>(a, ctl, L.kv, x, gtid, kt, kt + PAGE * HD, ash[grp], rope_cs[x.m], &abar[grp],
-                                  uses, pf, GroupSync{1 + grp}, tg.qkv(li),
-                                  x.nsplit == 1 ? tg.att(li) : tg.part(li))) {
-                    if (gtid == 0) raise_fail(a, ctl, 1);
-                    break;
-                }
+                __syncthreads();   // every warp is done with its QKV tiles' shared reads of s_x0 / sh
+                if (pf && tid == 0) s_pending = 0;
+                failed = !cta_att_item<HD>(a, ctl, L.kv, x, att, rope_cs[x.m], abar, ptiles, pf, tg.qkv(li),
+                                           x.nsplit == 1 ? tg.att(li) : tg.part(li));
             }
         }
         if ((failed = cta_failed(a, ctl))) break;
@@ -1121,7 +1129,7 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
         // 6. down + residual
         cbar();
         trace_mark(a, tb + 8);
-        if (tab[4 * li + PH_DOWN].ntiles) stage_ll<MB>(a, ctl, a.fal, a.F, tg.fa(li), nullptr, act, red);
+        if (tab[4 * li + PH_DOWN].ntiles) stage_ll<MB, SB_FA>(a, ctl, a.fal, a.F, tg.fa(li), nullptr, act, red);
         if ((failed = cta_failed(a, ctl))) break;
         trace_mark(a, tb + 9);
         gemv_tiles<PH_DOWN, MB>(a, ctl, li, tab, nph, ring, full, act, red, seq, wr, D,
@@ -1144,7 +1152,7 @@ __global__ void __launch_bounds__(MT, 1) k_decode_mega(const MegaArgs a) {
     // copies still in flight (only after a failure): wait for them before exiting
     for (uint32_t k = wr.used; k < wr.issued; ++k)
         tc::mbar_wait(&full[warp + NCW * (int)(k % D)], (k / D) & 1, 1u << 20);
-    if (grp < AC::NG && gtid == 0 && s_pending[grp]) tc::mbar_wait(&abar[grp], uses & 1, 1u << 20);
+    if (tid == 0 && s_pending) tc::mbar_wait(&abar[ptiles & 1], (ptiles >> 1) & 1, 1u << 20);
     cbar();
     trace_mark(a, 3 + 10 * a.n_layers);
     if (tid == 0) {
@@ -1180,7 +1188,7 @@ cudaError_t set_smem(int bytes) {
 
 template <int HD>
 size_t att_region_bytes() {
-    return (size_t)AttConst<HD>::NG * (AttConst<HD>::GROUP_BYTES + sizeof(AttSh<HD>));
+    return (size_t)4 * PAGE * HD * 2 + sizeof(AttSh<HD>);   // two K|V page stages + item state
 }
 
 }  // namespace
@@ -1202,7 +1210,7 @@ int decode_mega_max_stages() { return MAX_STAGES; }
 
 int decode_mega_consumer_warps() { return NCW; }
 
-int decode_mega_att_groups() { return AttConst<64>::NG; }
+int decode_mega_att_groups() { return 1; }
 
 int decode_mega_table_bytes(int n_layers) { return (int)((4 * n_layers + 1) * sizeof(Geo)); }
 
