@@ -116,6 +116,83 @@ def prefill_measure(vvq2, synth, torch, local, sh, n_tok, reps=3):
     }
 
 
+def c1_measure(vvq2, synth, torch, local, sh, n_copies=64, kv_len=512, steps=200, warmup=5):
+    """Config 1 -- one Qwen2.5-0.5B-shaped attention layer at batch 2 (CFG
+    pair), decode 1 token against an f16 KV cache of 512 positions -- timed
+    as the attention-layer step of the persistent decode kernel over
+    n_copies DISTINCT copies of the layer (own Q8_0 weights, own KV cache;
+    ~175 MB in all, above the 126 MB L2), so each copy's bytes come from HBM.
+    The copies carry a 64-wide FFN (the kernel always runs one; its bytes are
+    counted) and the stack a 1024-row lm_head (counted).  CUDA events over
+    `steps` steps.  The attention phase alone (q hand-over, split-K items,
+    merges) is timed from the kernel's own %globaltimer stamps and set
+    against the KV bytes it reads."""
+    hp = dict(C2, n_layers=n_copies, ffn=64, vocab=1024)
+    H, nq, nkv, hd, F = hp["hidden"], hp["n_heads"], hp["n_kv_heads"], hp["head_dim"], hp["ffn"]
+    rng = np.random.default_rng(SEED + 1)
+    eng = vvq2.Engine(hp, device=local)
+    wbytes = 0
+    for li in range(n_copies):
+        L = synth.layer_q8_0_fast(rng, hp)
+        wbytes += sum(int(t[0].nbytes) for k, t in L.items() if t is not None and "norm" not in k and "bias" not in k)
+        eng.set_layer(li, L)
+    head = synth.q8_0_random_tensor(rng, hp["vocab"], H)
+    norm = synth.f32_tensor(1.0 + rng.standard_normal(H, dtype=np.float32) * 0.02)
+    eng.set_output(norm, head, head)
+    kv = eng.kv(2, kv_len + warmup + steps + 8)
+    g = torch.Generator(device="cuda").manual_seed(SEED + 1)
+    for li in range(n_copies):
+        for s in range(2):
+            kv.load_prefix(s, li, torch.randn((kv_len, nkv * hd), generator=g, device="cuda"),
+                           torch.randn((kv_len, nkv * hd), generator=g, device="cuda"))
+    for s in range(2):
+        kv.set_past_len(s, kv_len)
+    tok = torch.randint(0, hp["vocab"], (2,), dtype=torch.int32, device="cuda", generator=g)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        # every step decodes position kv_len: the cache stays at 512 past keys (+ the new one)
+        for s in range(2):
+            kv.set_past_len(s, kv_len)
+        eng.decode_step(kv, [0, 1], tok, tok, stream=sh)
+
+    # the step's timeline buffer is set up with its CUDA graph (first step)
+    os.environ["VVQ2_MEGA_TRACE"] = "1"
+    try:
+        for _ in range(warmup):
+            step()
+    finally:
+        del os.environ["VVQ2_MEGA_TRACE"]
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    step_us = 1000.0 * e0.elapsed_time(e1) / steps
+    tr = eng.mega_trace().astype(np.float64) / 1000.0   # last step, us: [slot][cta]
+    kv_bytes = 2 * 2 * nkv * hd * 2 * (kv_len + 1)      # rows x (K, V) x heads x hd x f16 per layer
+    layer_bytes = wbytes / n_copies + kv_bytes + int(head[0].nbytes) / n_copies
+    hbm, hbm_kind = measured_peaks()
+    # attention phase per layer: from the last CTA's QKV tiles (mark 2) to the last CTA's merges (mark 4)
+    att_us = float(np.mean([tr[1 + 10 * l + 4].max() - tr[1 + 10 * l + 2].max() for l in range(n_copies)]))
+    att_kv = kv_bytes
+    del kv, eng
+    return {
+        "workload": f"config 1: 0.5B-shaped attention layer (hidden 896, 14/2 heads, hd 64, Q8_0 + bias), batch 2, "
+                    f"decode 1 token vs an f16 KV cache of {kv_len} positions; {n_copies} distinct layer copies "
+                    f"(weights + KV {n_copies * layer_bytes / 1e6:.0f} MB > L2) in one persistent step",
+        "layer_us": round(step_us / n_copies, 3), "layer_bytes": int(layer_bytes),
+        "achieved_gbs": round(layer_bytes / (step_us / n_copies / 1e6) / 1e9, 1),
+        "frac": round(layer_bytes / (step_us / n_copies / 1e6) / 1e9 / hbm, 4), "peak_gbs": hbm, "peak_kind": hbm_kind,
+        "attn_phase": {"us_per_layer": round(att_us, 3), "kv_bytes": int(att_kv),
+                       "achieved_gbs": round(att_kv / (att_us / 1e6) / 1e9, 1),
+                       "frac": round(att_kv / (att_us / 1e6) / 1e9 / hbm, 4),
+                       "timed_by": "kernel %globaltimer stamps (last step)"},
+    }
+
+
 def c3_measure(eng, hp, torch, dist, rank, world, sh, steps, warmup=2):
     """Config 3: 64 independent TTS streams (128 rows with their CFG pairs),
     ragged KV lengths uniform in [64, 2048] (a pair shares its length), one
@@ -171,22 +248,14 @@ C5 = dict(hidden=3584, n_heads=28, n_kv_heads=4, head_dim=128, ffn=18944, n_laye
           rope_theta=1.0e6, rms_eps=1.0e-6)
 
 
-def run_c5(args, rank, local, world):
-    """Config 5: the 7B-shaped Q8_0 ASR stack, causal prefill of
-    args.c5_tokens prompt embeddings, then greedy decode steps.  At N > 1 the
-    attention is partitioned (vvq2_partition): KV heads over 2/4 GPUs, KV heads
-    x sequence halves over 8, with NCCL (O, LSE) combines; each rank decodes
-    the same single stream.  Times are CUDA events, max over ranks."""
-    import torch
-    import torch.distributed as dist
-
-    import synth
-    import vvq2
-
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+def c5_measure(vvq2, synth, torch, dist, rank, local, world, sh, T, steps):
+    """Config 5: the 7B-shaped Q8_0 ASR stack, causal prefill of T prompt
+    embeddings (N(0,1)), then `steps` greedy decode steps of the stream.  At
+    N > 1 the attention is partitioned (vvq2_partition): KV heads over 2/4
+    GPUs, KV heads x sequence halves over 8, with NCCL (O, LSE) combines;
+    each rank decodes the same single stream.  Times are CUDA events on the
+    launching stream, max over ranks.  Decode bytes per step: the GGUF
+    weights plus the f16 K/V of every key (57,344 B per position)."""
     hp = C5
     eng = vvq2.Engine(hp, device=local)
     seq_parts = 2 if world == 8 else 1
@@ -195,12 +264,16 @@ def run_c5(args, rank, local, world):
         dist.broadcast_object_list(ids, src=0)
         eng.partition(rank, world, seq_parts, ids[0])
     rng = np.random.default_rng(SEED + 55)
+    wbytes = 0
     for li in range(hp["n_layers"]):
-        eng.set_layer(li, synth.layer_q8_0_fast(rng, hp))
+        L = synth.layer_q8_0_fast(rng, hp)
+        wbytes += sum(int(t[0].nbytes) for k, t in L.items() if t is not None and "norm" not in k and "bias" not in k)
+        eng.set_layer(li, L)
+        del L
     head = synth.q8_0_random_tensor(rng, hp["vocab"], hp["hidden"])
     norm = synth.f32_tensor(1.0 + rng.standard_normal(hp["hidden"], dtype=np.float32) * 0.02)
     eng.set_output(norm, head, head)
-    T, steps = args.c5_tokens, args.c5_steps
+    wbytes += int(head[0].nbytes)
     # warm-up on a separate cache (NCCL connections, lazily created scratch)
     kvw = eng.kv(1, 512)
     eng.forward(kvw, [0], np.zeros((1, 256, hp["hidden"]), np.float32), [0])
@@ -209,9 +282,7 @@ def run_c5(args, rank, local, world):
     g = torch.Generator(device="cuda").manual_seed(SEED + 5)
     x = torch.randn((1, T, hp["hidden"]), generator=g, device="cuda", dtype=torch.float32)
     y = torch.empty((1, hp["hidden"]), device="cuda", dtype=torch.float32)
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
-    sh = stream.cuda_stream
+    stream = torch.cuda.current_stream()
 
     def timed(fn):
         torch.cuda.synchronize()
@@ -230,25 +301,55 @@ def run_c5(args, rank, local, world):
         return ms
 
     pre_ms = timed(lambda: eng.forward(kv, [0], x, [0], flags=vvq2.ADVANCE | vvq2.LAST_ONLY, y=y, stream=sh))
+    del x
     tok = torch.randint(0, hp["vocab"], (1,), dtype=torch.int32, device="cuda", generator=g)
     for _ in range(2):
         eng.decode_step(kv, [0], tok, tok, stream=sh)
     dec_ms = timed(lambda: [eng.decode_step(kv, [0], tok, tok, stream=sh) for _ in range(steps)])
+    kv.close()
     lin = 2.0 * T * hp["n_layers"] * hp["hidden"] * (
         hp["n_heads"] * hp["head_dim"] + 2 * hp["n_kv_heads"] * hp["head_dim"] + hp["n_heads"] * hp["head_dim"]
         + 3 * hp["ffn"])
     att = 4.0 * hp["n_heads"] * hp["head_dim"] * T * (T + 1) / 2 * hp["n_layers"]
     burst, _, kind = measured_tensor_peak()
-    line = {"impl": "ours", "metric": "qwen2_c5_prefill_decode", "workload":
-            f"config 5: 7B-shaped Q8_0 stack (28 layers), causal prefill of {T} prompt embeddings, "
-            f"then {steps} greedy decode steps, batch 1", "n_gpus": world,
-            "partition": "none" if world == 1 else (f"KV heads over {world} GPUs" if seq_parts == 1 else
-                                                     f"KV heads x sequence halves over {world} GPUs"),
-            "prefill": {"tokens_per_s": round(T / (pre_ms / 1000.0), 1), "ms": round(pre_ms, 1),
-                        "tflops_per_gpu": round((lin + att) / (pre_ms / 1000.0) / 1e12 / world, 1),
-                        "peak_tflops": burst, "peak_kind": kind},
-            "decode": {"tokens_per_s": round(steps / (dec_ms / 1000.0), 2), "ms_per_step": round(dec_ms / steps, 3)},
-            "data": "synthetic (random Q8_0 blocks, N(0,1) embeddings)"}
+    hbm, hbm_kind = measured_peaks()
+    kv_mean = T + 2 + steps / 2
+    step_bytes = wbytes + 2.0 * 2 * hp["n_layers"] * hp["n_kv_heads"] * hp["head_dim"] * kv_mean
+    dec_s = dec_ms / 1000.0 / steps
+    return {
+        "workload": f"config 5: 7B-shaped Q8_0 stack (28 layers, hidden 3584, 28/4 heads, hd 128, ffn 18944, "
+                    f"vocab 152064), causal prefill of {T} prompt embeddings, then {steps} greedy decode steps, "
+                    f"batch 1", "n_gpus": world,
+        "partition": "none" if world == 1 else (f"KV heads over {world} GPUs" if seq_parts == 1 else
+                                                 f"KV heads x sequence halves over {world} GPUs"),
+        "prefill": {"tokens_per_s": round(T / (pre_ms / 1000.0), 1), "ms": round(pre_ms, 1),
+                    "tflops_per_gpu": round((lin + att) / (pre_ms / 1000.0) / 1e12 / world, 1),
+                    "frac_of_peak": round((lin + att) / (pre_ms / 1000.0) / 1e12 / world / burst, 4),
+                    "peak_tflops": burst, "peak_kind": kind},
+        "decode": {"tokens_per_s": round(steps / (dec_ms / 1000.0), 2), "ms_per_step": round(dec_ms / steps, 3),
+                   "step_bytes": int(step_bytes),
+                   "step_hbm_gbs_per_gpu": round(step_bytes / world / dec_s / 1e9, 1),
+                   "frac_of_hbm": round(step_bytes / world / dec_s / 1e9 / hbm, 4), "peak_gbs": hbm,
+                   "peak_kind": hbm_kind},
+        "data": "synthetic (random Q8_0 blocks, N(0,1) embeddings)"}
+
+
+def run_c5(args, rank, local, world):
+    """--workload c5: config 5's own JSON line (partitioned over the ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    import synth
+    import vvq2
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    r = c5_measure(vvq2, synth, torch, dist, rank, local, world, stream.cuda_stream, args.c5_tokens, args.c5_steps)
+    line = {"impl": "ours", "metric": "qwen2_c5_prefill_decode", **r}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -261,24 +362,14 @@ C4 = dict(hidden=1536, n_heads=12, n_kv_heads=2, head_dim=128, ffn=8960, n_layer
           rope_theta=1.0e6, rms_eps=1.0e-6)
 
 
-def run_c4(args, rank, local, world):
+def c4_measure(vvq2, synth, torch, dist, world, local, sh, T, steps):
     """Config 4: the 1.5B-shaped stack (Q5_K attention, Q6_K FFN, Q8_0
-    lm_head), batch 2 (the CFG pair): causal prefill of args.c4_tokens prompt
-    embeddings per row, then greedy decode steps of both rows.  The prompt
+    lm_head), batch 2 (the CFG pair): causal prefill of T prompt embeddings
+    per row, then `steps` greedy decode steps of both rows.  The prompt
     embeddings stand for text-token embeddings plus projected acoustic
     latents (the connector is not part of this path): N(0, 1) f32.  Each rank
     runs its own replica (the config does not shard); times are CUDA events,
     max over ranks."""
-    import torch
-    import torch.distributed as dist
-
-    import synth
-    import vvq2
-
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
     hp = C4
     eng = vvq2.Engine(hp, device=local)
     rng = np.random.default_rng(SEED + 44)
@@ -291,10 +382,7 @@ def run_c4(args, rank, local, world):
     norm = synth.f32_tensor(1.0 + rng.standard_normal(hp["hidden"], dtype=np.float32) * 0.02)
     eng.set_output(norm, head, head)
     wbytes += int(head[0].nbytes)
-    T, steps = args.c4_tokens, args.c4_steps
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
-    sh = stream.cuda_stream
+    stream = torch.cuda.current_stream()
     kvw = eng.kv(2, 512)
     eng.forward(kvw, [0, 1], np.zeros((2, 64, hp["hidden"]), np.float32), [0, 0], stream=sh)
     kvw.close()
@@ -333,7 +421,8 @@ def run_c4(args, rank, local, world):
     kv_len = T + 3 + steps / 2
     step_bytes = wbytes + 2 * 4.0 * hp["n_layers"] * hp["n_kv_heads"] * hp["head_dim"] * kv_len
     dec_s = dec_ms / 1000.0 / steps
-    line = {"impl": "ours", "metric": "qwen2_c4_prefill_decode", "workload":
+    kv.close()
+    return {"workload":
             f"config 4: 1.5B-shaped stack (28 layers, Q5_K attention, Q6_K FFN, Q8_0 lm_head), batch 2 (CFG pair), "
             f"causal prefill of {T} prompt embeddings per row, then {steps} greedy decode steps", "n_gpus": world,
             "parallelism": "replicas only (batch 2 does not shard)",
@@ -345,9 +434,26 @@ def run_c4(args, rank, local, world):
                        "step_bytes": int(step_bytes), "step_hbm_gbs": round(step_bytes / dec_s / 1e9, 1),
                        "frac_of_hbm": round(step_bytes / dec_s / 1e9 / hbm, 4), "peak_gbs": hbm, "peak_kind": hbm_kind},
             "data": "synthetic (random Q5_K / Q6_K / Q8_0 blocks, N(0,1) prompt embeddings)"}
+
+
+def run_c4(args, rank, local, world):
+    """--workload c4: config 4's own JSON line (replicas over the ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    import synth
+    import vvq2
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    r = c4_measure(vvq2, synth, torch, dist, world, local, stream.cuda_stream, args.c4_tokens, args.c4_steps)
+    line = {"impl": "ours", "metric": "qwen2_c4_prefill_decode", **r}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    kv.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -434,7 +540,7 @@ def cpu_decode_rate(model, hp, kv_len, budget_s=15.0, flags=None, steps=64, warm
     the time budget runs out first).  Returns (tokens/s, timed steps, threads)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import vvq2_oracle as O
-    flags = O.GGML_CPU if flags is None else flags
+    flags = (O.GGML_CPU | O.SIMD) if flags is None else flags
     rng = np.random.default_rng(SEED + 1)
     max_steps = steps
     ora = O.Model(hp, 2, kv_len + warmup + max_steps + 2, flags)
@@ -464,7 +570,7 @@ def cpu_decode_rate(model, hp, kv_len, budget_s=15.0, flags=None, steps=64, warm
             break
     dt = time.perf_counter() - t0
     cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return 2 * n / dt, n, cores
+    return 2 * n / dt, n, cores, (O.simd_isa() if flags & O.SIMD else "generic")
 
 
 class ClockSampler:
@@ -516,17 +622,19 @@ def run_reference(args, rank):
     model = synth.model_q8_0(SEED, C2)
     # the arm's own --steps/--warmup, each step one greedy decode step of both
     # rows; a 150 s budget bounds the timed part on slow hosts
-    rate, n, cores = cpu_decode_rate(model, C2, args.kv, budget_s=150.0, steps=args.steps, warmup=args.warmup)
+    rate, n, cores, isa = cpu_decode_rate(model, C2, args.kv, budget_s=150.0, steps=args.steps, warmup=args.warmup)
     line = {
         "impl": "reference", "metric": "qwen2_decode_tokens_per_s", "value": round(rate, 3), "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": round(2000.0 / rate, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->f32 (ggml q8_0 dot)",
         "data": "synthetic", "config": workload_config(args),
         "cpu_baseline": {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{n} greedy decode steps x 2 rows of the full C2 stack (ggml CPU numerics)"},
+                         "sample": f"{n} greedy decode steps x 2 rows of the full C2 stack (ggml CPU numerics, "
+                                   f"SIMD kernels: {isa} Q8_0 dot, AVX2/F16C f16 flash attention)"},
         "e2e": {"value": round(rate, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference's ggml CPU backend cannot be built here (ggml submodule absent); "
-                "this is the CPU restatement of its numerics (oracle/), all host threads",
+                "this is the CPU restatement of its numerics (oracle/) with SIMD integer dots and f16 "
+                "attention as ggml's x86 backend runs them, all host threads",
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -550,6 +658,9 @@ def main():
     ap.add_argument("--prefill-tokens", type=int, default=16384)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-c3", action="store_true")
+    ap.add_argument("--no-c1", action="store_true")
+    ap.add_argument("--no-c4", action="store_true")
+    ap.add_argument("--no-c5", action="store_true")
     ap.add_argument("--workload", default="c2", choices=["c2", "c4", "c5"])
     ap.add_argument("--case", default=None, choices=["decode7b", "c3"],
                     help="small single-GPU workload for kernel profiles (see run_case)")
@@ -557,7 +668,7 @@ def main():
     ap.add_argument("--c4-tokens", type=int, default=1024)
     ap.add_argument("--c4-steps", type=int, default=512)
     ap.add_argument("--c5-tokens", type=int, default=27000)
-    ap.add_argument("--c5-steps", type=int, default=32)
+    ap.add_argument("--c5-steps", type=int, default=2048)
     ap.add_argument("--c3-steps", type=int, default=10)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -694,15 +805,27 @@ def main():
     }
     if not args.no_c3:
         line["c3"] = c3_measure(eng, hp, torch, dist, rank, world, sh, args.c3_steps)
+    if not args.no_c1:
+        c1 = c1_measure(vvq2, synth, torch, local, sh)
+        line["c1"] = c1
+        line["roofline"]["attn_decode"] = {"achieved_gbs": c1["attn_phase"]["achieved_gbs"],
+                                           "frac": c1["attn_phase"]["frac"],
+                                           "us_per_layer": c1["attn_phase"]["us_per_layer"],
+                                           "source": "c1: attention phase of the persistent step, 64 layer copies"}
     if not args.no_prefill:
         line["prefill"] = prefill_measure(vvq2, synth, torch, local, sh, args.prefill_tokens)
     clk.__exit__(None, None, None)
     line["clocks"] = clk.summary()
+    if world == 1 and not args.no_c4:
+        line["c4"] = c4_measure(vvq2, synth, torch, dist, world, local, sh, args.c4_tokens, args.c4_steps)
+    if world == 1 and not args.no_c5:
+        line["c5"] = c5_measure(vvq2, synth, torch, dist, rank, local, world, sh, args.c5_tokens, args.c5_steps)
     if rank == 0 and world == 1 and not args.no_cpu:
-        rate, n, cores = cpu_decode_rate(model, hp, args.kv)
+        rate, n, cores, isa = cpu_decode_rate(model, hp, args.kv)
         line["cpu_baseline"] = {"value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
                                 "sample": f"{n} greedy decode steps x 2 rows of the full C2 stack, ggml CPU "
-                                          f"numerics (oracle/, OpenMP over {cores} threads)"}
+                                          f"numerics with SIMD kernels ({isa} Q8_0 dot, AVX2/F16C f16 flash "
+                                          f"attention; oracle/, OpenMP over {cores} threads)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -33,7 +33,11 @@ _Static_assert(sizeof(blk_q8_K) == 292, "q8_K size");
 
 /* ------------------------------------------------------------------ fp16 */
 
-uint16_t vvo_fp32_to_fp16(float f) {
+/* IEEE binary16 conversions, round to nearest even.  Where the build targets
+ * F16C (x86-64-v3 and up) the hardware instructions do them; the software
+ * routines below give the identical result for every non-NaN input (checked
+ * over all 2^32 floats and all 2^16 halves) and serve other hosts. */
+static uint16_t fp32_to_fp16_sw(float f) {
     uint32_t x;
     memcpy(&x, &f, 4);
     const uint32_t sign = (x >> 16) & 0x8000u;
@@ -58,7 +62,7 @@ uint16_t vvo_fp32_to_fp16(float f) {
     return (uint16_t)h;
 }
 
-float vvo_fp16_to_fp32(uint16_t h) {
+static float fp16_to_fp32_sw(uint16_t h) {
     const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
     const uint32_t exp = (h >> 10) & 0x1Fu;
     const uint32_t mant = h & 0x3FFu;
@@ -80,6 +84,15 @@ float vvo_fp16_to_fp32(uint16_t h) {
     memcpy(&f, &x, 4);
     return f;
 }
+
+#if defined(__F16C__)
+#include <immintrin.h>
+uint16_t vvo_fp32_to_fp16(float f) { return (uint16_t)_cvtss_sh(f, _MM_FROUND_TO_NEAREST_INT); }
+float vvo_fp16_to_fp32(uint16_t h) { return _cvtsh_ss(h); }
+#else
+uint16_t vvo_fp32_to_fp16(float f) { return fp32_to_fp16_sw(f); }
+float vvo_fp16_to_fp32(uint16_t h) { return fp16_to_fp32_sw(h); }
+#endif
 
 static float f16r(float x) { return vvo_fp16_to_fp32(vvo_fp32_to_fp16(x)); }
 
@@ -365,6 +378,72 @@ static float dot_q8_0(const blk_q8_0* w, const blk_q8_0* x, int nb) {
     return sumf;
 }
 
+/* SIMD Q8_0 x Q8_0 dots (VVO_SIMD): the same per-block integer sums as
+ * dot_q8_0, accumulated in vector lanes (the lane-wise float order of a SIMD
+ * backend).  The signed x signed byte product uses the unsigned x signed
+ * multiply-add: |w| * (x with the sign of w), exact since ggml's quantizer
+ * never emits -128.  Only the timed CPU baseline uses these. */
+#if defined(__x86_64__)
+#include <immintrin.h>
+
+__attribute__((target("avx2,fma,f16c"))) static float dot_q8_0_avx2(const blk_q8_0* w, const blk_q8_0* x, int nb) {
+    __m256 acc = _mm256_setzero_ps();
+    const __m256i ones = _mm256_set1_epi16(1);
+    for (int ib = 0; ib < nb; ib++) {
+        const __m256i a = _mm256_loadu_si256((const __m256i*)w[ib].qs);
+        const __m256i b = _mm256_loadu_si256((const __m256i*)x[ib].qs);
+        const __m256i p16 = _mm256_maddubs_epi16(_mm256_sign_epi8(a, a), _mm256_sign_epi8(b, a));
+        const __m256 s = _mm256_cvtepi32_ps(_mm256_madd_epi16(p16, ones));
+        const float d = _cvtsh_ss(w[ib].d) * _cvtsh_ss(x[ib].d);
+        acc = _mm256_fmadd_ps(_mm256_set1_ps(d), s, acc);
+    }
+    __m128 h = _mm_add_ps(_mm256_castps256_ps128(acc), _mm256_extractf128_ps(acc, 1));
+    h = _mm_add_ps(h, _mm_movehl_ps(h, h));
+    h = _mm_add_ss(h, _mm_movehdup_ps(h));
+    return _mm_cvtss_f32(h);
+}
+
+__attribute__((target("avx512f,avx512bw,avx512vnni,avx2,fma,f16c")))
+static float dot_q8_0_vnni(const blk_q8_0* w, const blk_q8_0* x, int nb) {
+    __m512 acc = _mm512_setzero_ps();
+    int ib = 0;
+    for (; ib + 1 < nb; ib += 2) {   /* two blocks per 512-bit register, one scale per half */
+        const __m512i a = _mm512_inserti64x4(_mm512_castsi256_si512(_mm256_loadu_si256((const __m256i*)w[ib].qs)),
+                                             _mm256_loadu_si256((const __m256i*)w[ib + 1].qs), 1);
+        const __m512i b = _mm512_inserti64x4(_mm512_castsi256_si512(_mm256_loadu_si256((const __m256i*)x[ib].qs)),
+                                             _mm256_loadu_si256((const __m256i*)x[ib + 1].qs), 1);
+        const __mmask64 neg = _mm512_movepi8_mask(a);
+        const __m512i sb = _mm512_mask_sub_epi8(b, neg, _mm512_setzero_si512(), b);
+        const __m512 s = _mm512_cvtepi32_ps(_mm512_dpbusd_epi32(_mm512_setzero_si512(), _mm512_abs_epi8(a), sb));
+        const float d0 = _cvtsh_ss(w[ib].d) * _cvtsh_ss(x[ib].d);
+        const float d1 = _cvtsh_ss(w[ib + 1].d) * _cvtsh_ss(x[ib + 1].d);
+        const __m512 dv = _mm512_mask_mov_ps(_mm512_set1_ps(d0), (__mmask16)0xFF00, _mm512_set1_ps(d1));
+        acc = _mm512_fmadd_ps(dv, s, acc);
+    }
+    float sum = _mm512_reduce_add_ps(acc);
+    if (ib < nb) sum += dot_q8_0_avx2(w + ib, x + ib, 1);
+    return sum;
+}
+
+typedef float (*dot_q8_0_fn)(const blk_q8_0*, const blk_q8_0*, int);
+
+static dot_q8_0_fn simd_dot(void) {
+    __builtin_cpu_init();
+    if (__builtin_cpu_supports("avx512vnni") && __builtin_cpu_supports("avx512bw")) return dot_q8_0_vnni;
+    if (__builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma")) return dot_q8_0_avx2;
+    return NULL;
+}
+
+const char* vvo_simd_isa(void) {
+    const dot_q8_0_fn f = simd_dot();
+    return f == dot_q8_0_vnni ? "avx512vnni" : f == dot_q8_0_avx2 ? "avx2" : "generic";
+}
+#else
+typedef float (*dot_q8_0_fn)(const blk_q8_0*, const blk_q8_0*, int);
+static dot_q8_0_fn simd_dot(void) { return NULL; }
+const char* vvo_simd_isa(void) { return "generic"; }
+#endif
+
 /* ggml_vec_dot_q6_K_q8_K (generic): per super-block isum = sum_j sc_j * dot_j,
  * sumf += (d_w * d_x) * isum */
 static float dot_q6_K(const blk_q6_K* w, const blk_q8_K* x, int nb) {
@@ -474,9 +553,11 @@ int vvo_matvec(const vvo_tensor* w, const float* x, float* y, int flags) {
         case VVO_Q8_0: {
             blk_q8_0* xq = (blk_q8_0*)malloc((size_t)(K / QK8_0) * sizeof(blk_q8_0));
             vvo_quantize_q8_0(x, K, xq);
+            dot_q8_0_fn dot = (flags & VVO_SIMD) ? simd_dot() : NULL;
+            if (!dot) dot = dot_q8_0;
 #pragma omp parallel for schedule(static)
             for (int64_t r = 0; r < R; r++)
-                y[r] = dot_q8_0((const blk_q8_0*)(base + (size_t)r * rb), xq, (int)(K / QK8_0));
+                y[r] = dot((const blk_q8_0*)(base + (size_t)r * rb), xq, (int)(K / QK8_0));
             free(xq);
             return 0;
         }
@@ -656,6 +737,59 @@ static const float* as_f32(const vvo_tensor* t, float* scratch, int n) {
     return scratch;
 }
 
+#if defined(__x86_64__)
+/* attend() in the VVO_FA_F16ACC mode with 8-lane AVX2 / F16C arithmetic (the
+ * VVO_SIMD timed baseline): the same per-key updates -- online max, the f16
+ * VKQ accumulator rounded after every scale and every add -- with the Q.K
+ * product summed in 8 float lanes instead of one double chain.  hd % 8 == 0. */
+__attribute__((target("avx2,fma,f16c"))) static void attend_f16acc_simd(const float* qv, const float* K,
+                                                                         const float* V, size_t stride,
+                                                                         int hd, int lim, float scale,
+                                                                         float* out) {
+    float M = -INFINITY, S = 0.0f;
+    __m256 acc[128];
+    __m256 q8[128];
+    const int nv = hd / 8;
+    for (int c = 0; c < nv; c++) {
+        acc[c] = _mm256_setzero_ps();
+        q8[c] = _mm256_cvtph_ps(_mm256_cvtps_ph(_mm256_loadu_ps(qv + 8 * c), _MM_FROUND_TO_NEAREST_INT));
+    }
+    for (int j = 0; j < lim; j++) {
+        const float* kj = K + (size_t)j * stride;
+        __m256 d8 = _mm256_setzero_ps();
+        for (int c = 0; c < nv; c++) d8 = _mm256_fmadd_ps(q8[c], _mm256_loadu_ps(kj + 8 * c), d8);
+        __m128 h = _mm_add_ps(_mm256_castps256_ps128(d8), _mm256_extractf128_ps(d8, 1));
+        h = _mm_add_ps(h, _mm_movehl_ps(h, h));
+        h = _mm_add_ss(h, _mm_movehdup_ps(h));
+        const float s = _mm_cvtss_f32(h) * scale;
+        const float Mold = M;
+        float ms = 1.0f, vs = 1.0f;
+        if (s > M) {
+            M = s;
+            ms = expf(Mold - M);
+            const __m256 m8 = _mm256_set1_ps(ms);
+            for (int c = 0; c < nv; c++)
+                acc[c] = _mm256_cvtph_ps(_mm256_cvtps_ph(_mm256_mul_ps(acc[c], m8), _MM_FROUND_TO_NEAREST_INT));
+        } else {
+            vs = expf(s - M);
+        }
+        const float* vj = V + (size_t)j * stride;
+        const __m256 v8s = _mm256_set1_ps(vs);
+        for (int c = 0; c < nv; c++)
+            acc[c] = _mm256_cvtph_ps(_mm256_cvtps_ph(_mm256_fmadd_ps(_mm256_loadu_ps(vj + 8 * c), v8s, acc[c]),
+                                                     _MM_FROUND_TO_NEAREST_INT));
+        S = S * ms + vs;
+    }
+    const __m256 inv = _mm256_set1_ps(1.0f / S);
+    for (int c = 0; c < nv; c++) _mm256_storeu_ps(out + 8 * c, _mm256_mul_ps(acc[c], inv));
+}
+
+static int have_avx2_f16c(void) {
+    __builtin_cpu_init();
+    return __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma") && __builtin_cpu_supports("f16c");
+}
+#endif
+
 /* one query head against keys [0, L) with key j visible iff j <= qpos */
 static void attend(const vvo_model* m, const float* q, int layer, int row, int kvh, int L,
                    int qpos, float* out) {
@@ -667,6 +801,12 @@ static void attend(const vvo_model* m, const float* q, int layer, int row, int k
     const float* K = m->kc + kv_off(m, layer, row, 0) + (size_t)kvh * hd;
     const float* V = m->vc + kv_off(m, layer, row, 0) + (size_t)kvh * hd;
     const size_t stride = (size_t)nkv * hd;
+#if defined(__x86_64__)
+    if ((m->flags & VVO_FA_F16ACC) && (m->flags & VVO_SIMD) && hd % 8 == 0 && hd <= 1024 && have_avx2_f16c()) {
+        attend_f16acc_simd(qv, K, V, stride, hd, lim, scale, out);
+        return;
+    }
+#endif
     if (m->flags & VVO_FA_F16ACC) {
         /* ggml_compute_forward_flash_attn_ext_f16_one_chunk with F16 V:
          * online softmax, VKQ16 accumulator rounded to f16 every update */
@@ -737,7 +877,7 @@ int vvo_forward(vvo_model* m, int n_sel, const int* rows, int n_tok, const float
     float* xn = (float*)malloc((size_t)H * sizeof(float));
     float* q = (float*)malloc(nrow * qw * sizeof(float));
     float* tmp = (float*)malloc((size_t)(qw > F ? qw : F) * sizeof(float));
-    float* att = (float*)malloc((size_t)qw * sizeof(float));
+    float* att = (float*)malloc(nrow * qw * sizeof(float));
     float* g = (float*)malloc((size_t)F * sizeof(float));
     float* u = (float*)malloc((size_t)F * sizeof(float));
     float* o = (float*)malloc((size_t)H * sizeof(float));
@@ -766,18 +906,18 @@ int vvo_forward(vvo_model* m, int n_sel, const int* rows, int n_tok, const float
                 for (int i = 0; i < kvw; i++) { kd[i] = kv_store(m, k[i]); vd[i] = kv_store(m, v[i]); }
             }
         }
-        /* 2. attention, O-proj, residual, FFN */
+        /* 2. attention of every (row, token, head) in one parallel region,
+         *    then O-proj, residual, FFN per row */
+#pragma omp parallel for schedule(dynamic)
+        for (int64_t i = 0; i < (int64_t)nrow * nq; i++) {
+            const int st = (int)(i / nq), hh = (int)(i % nq), s = st / n_tok, t = st % n_tok;
+            attend(m, q + (size_t)st * qw + (size_t)hh * hd, li, rows[s], hh / grp, m->past[rows[s]] + n_tok,
+                   pos_start[s] + t, att + (size_t)st * qw + (size_t)hh * hd);
+        }
         for (int s = 0; s < n_sel; s++) {
-            const int r = rows[s];
-            const int L = m->past[r] + n_tok;
             for (int t = 0; t < n_tok; t++) {
                 float* hx = h + ((size_t)s * n_tok + t) * H;
-                const float* qt = q + ((size_t)s * n_tok + t) * qw;
-#pragma omp parallel for schedule(static)
-                for (int hh = 0; hh < nq; hh++)
-                    attend(m, qt + (size_t)hh * hd, li, r, hh / grp, L, pos_start[s] + t,
-                           att + (size_t)hh * hd);
-                vvo_matvec(&w->attn_o, att, o, fl);
+                vvo_matvec(&w->attn_o, att + ((size_t)s * n_tok + t) * qw, o, fl);
                 for (int i = 0; i < H; i++) hx[i] = hx[i] + o[i];
                 if (fl & VVO_NO_FFN) continue;
                 vvo_rms_norm(hx, as_f32(&w->ffn_norm, nw, H), H, hp->rms_eps, xn);

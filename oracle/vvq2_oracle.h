@@ -53,8 +53,18 @@ enum {
     VVO_FA_F16ACC  = 1 << 3, /* ggml CPU FA: V accumulated in an f16 buffer      */
     VVO_ROPE_GGML  = 1 << 4, /* theta_i by iterated f32 product (ggml CPU cache)
                                 else exact double pos*theta^(-2i/d)              */
-    VVO_NO_FFN     = 1 << 5  /* attention half only (y = x + O(attn))            */
+    VVO_NO_FFN     = 1 << 5, /* attention half only (y = x + O(attn))            */
+    VVO_SIMD       = 1 << 6  /* with VVO_ACT_GGML: Q8_0 x Q8_0 dots by the SIMD
+                                integer kernel (AVX-512 VNNI when the CPU has
+                                it, else AVX2), as ggml's x86 backend runs them:
+                                same integer block sums, different float
+                                summation order than the generic dot.  For the
+                                timed CPU baseline; parity uses the generic one */
 };
+
+/* The SIMD instruction set VVO_SIMD uses on this CPU: "avx512vnni", "avx2"
+ * or "generic" (no SIMD kernel available: the generic dot runs). */
+const char* vvo_simd_isa(void);
 
 typedef struct vvo_hparams {
     int   hidden, n_heads, n_kv_heads, head_dim, ffn, n_layers, vocab;

@@ -17,7 +17,7 @@ HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "build" / "libvvq2_oracle.so"
 
 F32, F16, Q8_0, Q5_K, Q6_K = 0, 1, 8, 13, 14
-ACT_GGML, KV_F16, Q_F16, FA_F16ACC, ROPE_GGML, NO_FFN = 1, 2, 4, 8, 16, 32
+ACT_GGML, KV_F16, Q_F16, FA_F16ACC, ROPE_GGML, NO_FFN, SIMD = 1, 2, 4, 8, 16, 32, 64
 # what the reference's CPU backend computes (ggml semantics on every op)
 GGML_CPU = ACT_GGML | KV_F16 | Q_F16 | FA_F16ACC | ROPE_GGML
 BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q5_K: (256, 176), Q6_K: (256, 210)}
@@ -63,6 +63,7 @@ def lib() -> C.CDLL:
             "vvo_matvec": (I, [P, P, P, I]),
             "vvo_rms_norm": (None, [P, P, I, F, P]),
             "vvo_rope_neox": (None, [P, I, I, I, F, I, P]),
+            "vvo_simd_isa": (C.c_char_p, []),
             "vvo_fp32_to_fp16": (C.c_uint16, [F]),
             "vvo_fp16_to_fp32": (F, [C.c_uint16]),
             "vvo_model_new": (P, [P, I, I, I]),
@@ -195,6 +196,11 @@ def rope_neox(x: np.ndarray, pos: int, theta: float, flags: int) -> np.ndarray:
     y = np.empty_like(x)
     lib().vvo_rope_neox(_p(x), x.shape[0], x.shape[1], int(pos), theta, flags, _p(y))
     return y
+
+
+def simd_isa() -> str:
+    """Instruction set of the SIMD Q8_0 dot on this CPU (flag SIMD)."""
+    return lib().vvo_simd_isa().decode()
 
 
 def fp16_round(x: np.ndarray) -> np.ndarray:

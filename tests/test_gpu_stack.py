@@ -2,11 +2,13 @@
 0.5B-shaped Q8_0 stack, tied lm_head, batch 2 CFG, greedy decode from KV
 lengths 128 / 1024 / 4096).
 
-Greedy identity is checked with the oracle's token fed to both sides at every
-step (so one near-tie cannot derail the rest of the run); a GPU argmax that
-differs from the oracle's is only accepted when the two logits are within
-float-summation noise of each other, and the run reports how many steps were
-bit-identical."""
+Greedy identity is checked free-running: the GPU is fed its OWN previous token
+every step, exactly as a caller's decode loop runs, and the oracle follows the
+GPU's token sequence, computing its argmax at every step.  A GPU argmax that
+differs from the oracle's is only accepted when the two oracle logits are
+within float-summation noise of each other (a near-tie); the run reports how
+many tokens were identical and the first divergence.  A teacher-forced variant
+(the oracle's token fed to both sides) is kept as a diagnostic."""
 import numpy as np
 import pytest
 
@@ -48,9 +50,13 @@ def fill_prefix(rng, hp, kv, ora, n_rows, L):
         ora.set_past_len(s, L)
 
 
-def greedy_compare(eng, kv, ora, hp, tok0, steps):
+def greedy_compare(eng, kv, ora, hp, tok0, steps, follow="gpu"):
+    """Greedy decode of both rows for `steps` steps.  follow="gpu": each side
+    is fed the GPU's previous token (the GPU runs free); follow="oracle": the
+    oracle's (teacher forcing).  Returns (identical, near_ties, first
+    divergence (step, row) or None)."""
     tok = np.array(tok0, np.int32)
-    identical, ties = 0, 0
+    identical, ties, first = 0, 0, None
     for step in range(steps):
         got = eng.decode_step(kv, [0, 1], tok)
         pos = [ora.past_len(0), ora.past_len(1)]
@@ -63,8 +69,10 @@ def greedy_compare(eng, kv, ora, hp, tok0, steps):
                 gap = abs(lg[r, am[r]] - lg[r, got[r]]) / np.max(np.abs(lg[r]))
                 assert gap < 1e-5, (step, r, int(got[r]), int(am[r]), gap)
                 ties += 1
-        tok = am.astype(np.int32)
-    return identical, ties
+                if first is None:
+                    first = (step, r)
+        tok = (got if follow == "gpu" else am).astype(np.int32)
+    return identical, ties, first
 
 
 def test_small_stack_decode_step_equals_forward(vv):
@@ -89,6 +97,7 @@ def test_small_stack_decode_step_equals_forward(vv):
 
 @pytest.mark.parametrize("kv_len", [128, 1024, 4096])
 def test_c2_greedy_256_steps(vv, kv_len):
+    """Free-running: the GPU's own 256-token sequence, checked step by step."""
     hp = dict(C2)
     model = build(20261201, hp, hp["n_layers"])
     steps = 256
@@ -96,7 +105,24 @@ def test_c2_greedy_256_steps(vv, kv_len):
     rng = np.random.default_rng(kv_len)
     fill_prefix(rng, hp, kv, ora, 2, kv_len)
     tok0 = rng.integers(0, hp["vocab"], size=2).astype(np.int32)
-    identical, ties = greedy_compare(eng, kv, ora, hp, tok0, steps)
-    print(f"kv {kv_len}: {identical}/{2 * steps} argmax identical, {ties} near-ties")
+    identical, ties, first = greedy_compare(eng, kv, ora, hp, tok0, steps, follow="gpu")
+    print(f"kv {kv_len}: free-running, {identical}/{2 * steps} tokens identical, {ties} near-ties, "
+          f"first divergence {first}")
+    assert identical + ties == 2 * steps
+    assert ties <= 2
+
+
+def test_c2_greedy_teacher_forced_diagnostic(vv):
+    """Diagnostic: the oracle's token fed to both sides (a near-tie cannot
+    move the GPU onto another trajectory)."""
+    hp = dict(C2)
+    model = build(20261201, hp, hp["n_layers"])
+    steps, kv_len = 128, 1024
+    eng, kv, ora = make_pair(vv, hp, model, 2, kv_len + steps + 1)
+    rng = np.random.default_rng(7 * kv_len)
+    fill_prefix(rng, hp, kv, ora, 2, kv_len)
+    tok0 = rng.integers(0, hp["vocab"], size=2).astype(np.int32)
+    identical, ties, first = greedy_compare(eng, kv, ora, hp, tok0, steps, follow="oracle")
+    print(f"kv {kv_len}: teacher-forced, {identical}/{2 * steps} identical, {ties} near-ties, first {first}")
     assert identical + ties == 2 * steps
     assert ties <= 2

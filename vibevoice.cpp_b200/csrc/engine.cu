@@ -191,6 +191,8 @@ struct vvq2_ctx {
     __half *Xh = nullptr, *ATTh = nullptr, *Ah = nullptr;
     __half* Wh = nullptr;          // f16 copy of the weight matrix the current prefill GEMM uses
     size_t wh_elems = 0;
+    unsigned long long* tile_best = nullptr;   // many-row lm_head: best key per row and 128-column tile
+    size_t tile_best_n = 0;
     float* kpart = nullptr;        // split-K partials of the tensor-core GEMMs
     size_t kpart_elems = 0;
     float2* rope_cs = nullptr;
@@ -1051,6 +1053,13 @@ int decode_step_batched(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, c
         CU(rmsnorm_f16_launch(c->X, c->out_norm, M, H, hp.rms_norm_eps, c->Xh, st));
         CUtensorMap mapX;
         if (!make_act_map(&mapX, c->Xh, M, H)) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "hidden %d not a multiple of 64", H);
+        // f16 operands: each row's candidate tiles (within 3 % of its best
+        // approximate logit) are rescored in f32 for the exact argmax
+        const int ntiles = (c->lm_head.rows + 127) / 128;
+        if ((size_t)M * ntiles > c->tile_best_n) {
+            if (int rc = c->alloc(&c->tile_best, (size_t)M * ntiles)) return rc;
+            c->tile_best_n = (size_t)M * ntiles;
+        }
         GemmArgs g;
         g.w0 = c->lm_head;
         g.T = M;
@@ -1058,11 +1067,15 @@ int decode_step_batched(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, c
         g.K = H;
         g.epi = EPI_ARGMAX;
         g.amax = c->amax;
+        g.tile_best = c->tile_best;
+        g.tile_stride = ntiles;
         g.err = c->err;
         Recorder R{c, st, c->prof_on ? &recs : nullptr};
         CU(R.begin());
         CU(gemm_tc_launch(g, mapX, st));
         CU(R.end(3, 2.0 * M * (double)g.N * H));
+        CU(argmax_rescore_launch(c->X, c->out_norm, hp.rms_norm_eps, M, H, c->lm_head, c->tile_best, ntiles,
+                                 0.03f, c->amax, c->err, st));
     }
     CU(argmax_final_launch(c->amax, M, c->tok, st));
     CU(cudaMemcpyAsync(tokens_out, c->tok, sizeof(int32_t) * M, cudaMemcpyDefault, st));

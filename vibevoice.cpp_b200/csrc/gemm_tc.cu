@@ -463,6 +463,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                     }
                     if (valid && best) atomicMax(a.amax + t, best);
+                    if (valid && a.tile_best) a.tile_best[(size_t)t * a.tile_stride + blockIdx.x] = best;
                 } else if constexpr (EPI == EPI_RESID || EPI == EPI_STORE) {
                     for (int c = 0; c < BN; c += 32) {
                         float v[32];

@@ -61,6 +61,8 @@ struct GemmArgs {
     int nq = 0, nkv = 0, hd = 0;
     const float2* rope_cs = nullptr;   // [T][hd/2] (cos, sin)
     unsigned long long* amax = nullptr;   // ARGMAX: [T] running (logit, index) keys
+    unsigned long long* tile_best = nullptr;   // ARGMAX, optional: [T][tile_stride] best key per 128-column tile
+    int tile_stride = 0;
     float* kpart = nullptr;        // split-K: [k_splits][T][N] f32 partials (then splitk_epilogue_launch)
     int k_splits = 1;
     int* err = nullptr;
@@ -215,6 +217,13 @@ cudaError_t kv_upload_launch(const KvLayer& kv, int seq, const float* k, const f
 cudaError_t kv_download_launch(const KvLayer& kv, int seq, float* k, float* v, int n_pos,
                                cudaStream_t st);
 cudaError_t argmax_init_launch(unsigned long long* keys, int n, cudaStream_t st);
+// Exact argmax of rows whose lm_head ran on f16 operands: every 128-column
+// tile whose best approximate logit lies within `margin` (relative to the
+// row's approximate maximum) is rescored in f32 -- RMSNorm of X [rows][H]
+// with norm_w, exactly dequantized weights -- and keys[] gets the exact key.
+cudaError_t argmax_rescore_launch(const float* X, const float* norm_w, float eps, int rows, int H, const DevW& w,
+                                  const unsigned long long* tile_best, int ntiles, float margin,
+                                  unsigned long long* keys, int* err, cudaStream_t st);
 cudaError_t advance_meta_launch(RowMeta* meta, int n, cudaStream_t st);
 cudaError_t argmax_final_launch(const unsigned long long* keys, int n, int32_t* out,
                                 cudaStream_t st);

@@ -165,6 +165,77 @@ __global__ void k_argmax_final(const unsigned long long* keys, int n, int32_t* o
     if (i < n) out[i] = argmax_key_index(keys[i]);
 }
 
+// Float of an argmax key (inverse of argmax_key's order-preserving map).
+__device__ __forceinline__ float argmax_key_value(unsigned long long k) {
+    uint32_t u = (uint32_t)(k >> 32);
+    u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
+    return __uint_as_float(u);
+}
+
+constexpr int RS_THREADS = 256;
+constexpr int RS_MAX_CAND = 256;   // candidate tiles rescored per row
+
+// One CTA per row: x o w and the RMSNorm row scale into shared memory, the
+// candidate tiles (best approximate key within margin of the row's best),
+// then one warp per column computes the exact logit
+//   (sum_k deq(W[n][k]) * (x[k] * w[k])) * 1/sqrt(mean(x^2) + eps)
+// and the CTA keeps the first-maximum key.  More candidates than
+// RS_MAX_CAND: the excess tiles keep their approximate keys and err gets 6.
+__global__ void __launch_bounds__(RS_THREADS) k_argmax_rescore(const float* X, const float* norm_w, float eps,
+                                                                int H, const DevW w,
+                                                                const unsigned long long* tile_best, int ntiles,
+                                                                float margin, unsigned long long* keys, int* err) {
+    extern __shared__ float xs[];   // [H]
+    __shared__ int cand[RS_MAX_CAND];
+    __shared__ int ncand;
+    __shared__ float red[RS_THREADS / 32];
+    __shared__ unsigned long long best_w[RS_THREADS / 32];
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) ncand = 0;
+    float ss = 0.f;
+    for (int k = tid; k < H; k += RS_THREADS) {
+        const float v = X[(size_t)t * H + k];
+        ss = fmaf(v, v, ss);
+        xs[k] = norm_w ? __fmul_rn(v, norm_w[k]) : v;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < RS_THREADS / 32; ++i) tot += red[i];
+    const float nsc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)H), eps)));
+    const float M = argmax_key_value(keys[t]);
+    const float thr = M - margin * fabsf(M);
+    for (int j = tid; j < ntiles; j += RS_THREADS) {
+        const unsigned long long kb = tile_best[(size_t)t * ntiles + j];
+        if (kb && argmax_key_value(kb) >= thr) {
+            const int e = atomicAdd(&ncand, 1);
+            if (e < RS_MAX_CAND) cand[e] = j;
+            else if (err) atomicCAS(err, 0, 6);
+        }
+    }
+    __syncthreads();
+    const int nc = min(ncand, RS_MAX_CAND);
+    unsigned long long mine = 0ull;
+    for (int c = warp; c < nc * 128; c += RS_THREADS / 32) {
+        const int n = cand[c / 128] * 128 + (c % 128);
+        if (n >= w.rows) continue;   // uniform in the warp
+        float acc = 0.f;
+        for (int k = lane; k < H; k += 32) acc = fmaf(deq_elem(w, n, k), xs[k], acc);
+        acc = warp_sum(acc);
+        const unsigned long long key = argmax_key(__fmul_rn(acc, nsc), n);
+        mine = key > mine ? key : mine;
+    }
+    if (lane == 0) best_w[warp] = mine;
+    __syncthreads();
+    if (tid == 0) {
+        unsigned long long b = 0ull;
+        for (int i = 0; i < RS_THREADS / 32; ++i) b = best_w[i] > b ? best_w[i] : b;
+        if (b) keys[t] = b;
+    }
+}
+
 int grid_for(int64_t n, int threads) {
     const int64_t g = (n + threads - 1) / threads;
     return (int)(g < 148 * 16 ? (g < 1 ? 1 : g) : 148 * 16);
@@ -334,6 +405,16 @@ cudaError_t advance_meta_launch(RowMeta* meta, int n, cudaStream_t st) {
 
 cudaError_t argmax_init_launch(unsigned long long* keys, int n, cudaStream_t st) {
     k_argmax_init<<<(n + 127) / 128, 128, 0, st>>>(keys, n);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t argmax_rescore_launch(const float* X, const float* norm_w, float eps, int rows, int H, const DevW& w,
+                                  const unsigned long long* tile_best, int ntiles, float margin,
+                                  unsigned long long* keys, int* err, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    k_argmax_rescore<<<rows, RS_THREADS, (size_t)H * sizeof(float), st>>>(X, norm_w, eps, H, w, tile_best, ntiles,
+                                                                          margin, keys, err);
     note_launch();
     return cudaGetLastError();
 }
