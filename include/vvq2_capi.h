@@ -215,6 +215,12 @@ int64_t vvq2_kernel_launches(void);
  * dequantized exactly and rounded to f16, f32 accumulation.  k % 64 == 0. */
 int  vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int t, float* y);
 
+/* ---- test hook (no counterpart in the reference) ----------------------
+ * y f32 [m][n] = x [m][k] . W[n][k]^T for m <= 2 rows through the
+ * tensor-core decode GEMV math of the persistent step (Q8_0 weights exact,
+ * x split into three int8 pieces per 32-block, s32 block sums).  k % 32 == 0. */
+int  vvq2_debug_gemv_mma(const void* w, int n, int k, const float* x, int m, float* y);
+
 /* ---- allocation-free decode attention (no counterpart in the reference) --
  * For callers that cannot call cudaMalloc -- an engine whose pool owns all GPU
  * memory, code inside another framework's context or a graph capture, a

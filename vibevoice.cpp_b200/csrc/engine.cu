@@ -2152,4 +2152,28 @@ int vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int t
     return 0;
 }
 
+int vvq2_debug_gemv_mma(const void* w, int n, int k, const float* x, int m, float* y) {
+    if (!w || !x || !y || n <= 0 || k <= 0 || k % 32 || m < 1 || m > 2)
+        return fail(VVQ2_ERR_INVALID_ARG, "bad gemv args");
+    if (vvq2_device_count() == 0) return fail(VVQ2_ERR_NO_DEVICE, "no sm_100 device");
+    vvq2_ctx tmp;
+    vvq2_tensor tw{w, W_Q8_0, k, n};
+    DevW dw;
+    int rc = upload_tensor(&tmp, tw, &dw, 0, 0, "debug_gemv_mma");
+    float *dx = nullptr, *dy = nullptr;
+    if (!rc) rc = tmp.alloc(&dx, (size_t)m * k);
+    if (!rc) rc = tmp.alloc(&dy, (size_t)m * n);
+    cudaError_t e = cudaSuccess;
+    if (!rc) {
+        e = cudaMemcpy(dx, x, sizeof(float) * m * k, cudaMemcpyDefault);
+        if (e == cudaSuccess) e = debug_gemv_mma_launch(dw, dx, m, dy, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaMemcpy(y, dy, sizeof(float) * m * n, cudaMemcpyDefault);
+    }
+    for (void* p : tmp.allocs) cudaFree(p);
+    if (rc) return rc;
+    if (e != cudaSuccess) return fail(VVQ2_ERR_CUDA, "debug gemv: %s", cudaGetErrorString(e));
+    return 0;
+}
+
 }  // extern "C"

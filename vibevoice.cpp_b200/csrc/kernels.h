@@ -217,6 +217,9 @@ cudaError_t kv_upload_launch(const KvLayer& kv, int seq, const float* k, const f
 cudaError_t kv_download_launch(const KvLayer& kv, int seq, float* k, float* v, int n_pos,
                                cudaStream_t st);
 cudaError_t argmax_init_launch(unsigned long long* keys, int n, cudaStream_t st);
+// test hook: y [M][rows] = x [M][cols] . W^T on the tensor-core decode GEMV
+// math (gemv_mma.cuh), one CTA, M <= 2, Q8_0
+cudaError_t debug_gemv_mma_launch(const DevW& w, const float* x, int M, float* y, cudaStream_t st);
 // Exact argmax of rows whose lm_head ran on f16 operands: every 128-column
 // tile whose best approximate logit lies within `margin` (relative to the
 // row's approximate maximum) is rescored in f32 -- RMSNorm of X [rows][H]

@@ -73,6 +73,7 @@ def lib() -> C.CDLL:
             "vvq2_kernel_launches": (I64, []),
             "vvq2_profile": (I, [P, I]),
             "vvq2_debug_gemm": (I, [I, P, I, I, P, I, P]),
+            "vvq2_debug_gemv_mma": (I, [P, I, I, P, I, P]),
             "vvq2_attention_decode_noalloc": (I, [P, P, P, P, I, P, I, I, I, I, I, P, P, P]),
             "vvq2_profile_read": (I, [P, I, P, P, P]),
             "vvq2_mega_trace": (I, [P, P, C.c_int64, P, P]),
@@ -351,4 +352,13 @@ def debug_gemm(qtype: int, raw: np.ndarray, n: int, k: int, x: np.ndarray) -> np
     x = np.ascontiguousarray(x, np.float32)
     y = np.empty((x.shape[0], n), np.float32)
     _chk(lib().vvq2_debug_gemm(qtype, _p(raw), n, k, _p(x), x.shape[0], _p(y)))
+    return y
+
+
+def debug_gemv_mma(raw: np.ndarray, n: int, k: int, x: np.ndarray) -> np.ndarray:
+    """y = x . W^T (1-2 rows, Q8_0) through the tensor-core decode GEMV math (test hook)."""
+    raw = np.ascontiguousarray(raw)
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty((x.shape[0], n), np.float32)
+    _chk(lib().vvq2_debug_gemv_mma(_p(raw), n, k, _p(x), x.shape[0], _p(y)))
     return y
