@@ -1,7 +1,8 @@
 """One rank of the partitioned-attention GPU test (launched by torchrun from
 test_gpu_partition.py): a small 2-layer model partitioned over the ranks
-(KV heads x sequence parts) against an unpartitioned engine on the same GPU,
-through a prefill of 2 x 300 prompt tokens and 6 greedy decode steps."""
+(KV heads x sequence parts, 2 to 8 ranks) against an unpartitioned engine on
+the same GPU, through a prefill of 2 x 300 prompt tokens and 6 greedy decode
+steps."""
 import argparse
 import datetime
 import os
@@ -24,10 +25,12 @@ def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
-    hp = dict(hidden=512, n_heads=8, n_kv_heads=2 if args.seq_parts == 2 else world, head_dim=64, ffn=1024,
+    # one KV head per head group (at least 2), 4 q heads per KV head; the FFN
+    # splits over every rank
+    groups = world // args.seq_parts
+    nkv = max(2, groups)
+    hp = dict(hidden=512, n_heads=4 * nkv, n_kv_heads=nkv, head_dim=64, ffn=128 * world if world > 8 else 1024,
               n_layers=2, vocab=2048, rope_theta=1.0e6, rms_eps=1.0e-6)
-    if args.seq_parts == 1 and hp["n_kv_heads"] == 1:
-        hp["n_kv_heads"] = 2
     model = synth.model_q8_0(20261201, hp)
     ids = [vvq2.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(ids, src=0)
