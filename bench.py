@@ -108,8 +108,8 @@ def prefill_measure(vvq2, synth, torch, local, sh, n_tok, reps=3):
                  "tflops": round(attn_tf, 1) if attn_tf else None,
                  "frac": round(attn_tf / burst, 4) if attn_tf else None,
                  "ms": round(a_ms / max(a_n, 1), 3), "flops_per_launch": a_fl / max(a_n, 1)},
-        "gemm": {"kernel": "k_gemm_tc<TMA B> (tcgen05 GEMM: per-chunk f16 weight copy and activations via TMA, "
-                           "fused RoPE/KV/residual/SwiGLU epilogues)",
+        "gemm": {"kernel": "k_gemm_ws (persistent tcgen05 GEMM: Q8_0 blocks dequantized in shared memory, "
+                           "activations by TMA, 256 x nt tiles, fused RoPE/KV/residual/SwiGLU epilogues)",
                  "tflops": round(gemm_tf, 1) if gemm_tf else None,
                  "frac": round(gemm_tf / burst, 4) if gemm_tf else None},
         "peak_tflops": burst, "peak_kind": f"{kind} bf16 dense burst (sustained {sustained})",

@@ -28,10 +28,17 @@ def test_plan_covers_each_head_and_key_once():
         assert sorted(seen_q) == [(h, s) for h in range(nq) for s in range(seq_parts)]
         assert set(seen_q.values()) == {1} and set(seen_kv.values()) == {1}
     n = 27000
-    sp = PT.seq_split(n)
-    assert sp % 64 == 0 and abs(sp - n / 2) < 64
-    k0, k1 = PT.keys_of_part(0, 2, sp, n), PT.keys_of_part(1, 2, sp, n)
-    assert len(k0) + len(k1) == n and k0.stop == k1.start
+    k0, k1 = PT.keys_of_part(0, 2, n), PT.keys_of_part(1, 2, n)
+    assert len(k0) + len(k1) == n and not set(k0.tolist()) & set(k1.tolist())
+    for part, keys in ((0, k0), (1, k1)):
+        assert len(keys) == PT.part_count(part, n)
+        # cache index of each held position = the part's positions below it
+        for i in (0, 1, 63, 64, 200, len(keys) - 1):
+            assert PT.part_count(part, int(keys[i])) == i
+    # causal prefill work (queries at or after each key) is balanced across
+    # the parts, where a split at the middle gives 3:1
+    work = [int(np.sum(n - k)) for k in (k0, k1)]
+    assert abs(work[0] - work[1]) / sum(work) < 0.01, work
     with pytest.raises(ValueError):
         PT.plan(0, 3, 1, 28, 4)
     for world in (2, 4, 8):
@@ -49,8 +56,7 @@ def _worker(rank, world, port, seq_parts, q_all, k_all, v_all, q_pos, out):
         nq, T, hd = q_all.shape
         nkv, n, _ = k_all.shape
         p = PT.plan(rank, world, seq_parts, nq, nkv)
-        split = PT.seq_split(n)
-        keys = np.array(list(PT.keys_of_part(p["part"], seq_parts, split, n)), dtype=np.int64)
+        keys = PT.keys_of_part(p["part"], seq_parts, n)
         G = nq // nkv
         o = np.zeros((len(p["q_heads"]), T, hd))
         l = np.zeros((len(p["q_heads"]), T))

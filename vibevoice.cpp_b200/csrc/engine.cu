@@ -50,12 +50,12 @@ EncodeTiledFn encode_fn() {
 
 // 2-D f16 activation matrix [rows][cols] (row-major) as a TMA map with a
 // 64 x 128 box and the 128-byte swizzle the UMMA descriptors assume
-bool make_act_map(CUtensorMap* m, const __half* base, int rows, int cols) {
+bool make_act_map(CUtensorMap* m, const __half* base, int rows, int cols, int box_rows = 128) {
     EncodeTiledFn fn = encode_fn();
-    if (!fn || cols % 64 || ((uintptr_t)base & 15)) return false;
+    if (!fn || cols % 64 || ((uintptr_t)base & 15) || box_rows < 8 || box_rows > 256) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     const cuuint32_t es[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -189,8 +189,9 @@ struct vvq2_ctx {
     // prefill (tensor-core) scratch for up to prefill_rows token rows
     int prefill_rows = PREFILL_ROWS_DEFAULT;
     __half *Xh = nullptr, *ATTh = nullptr, *Ah = nullptr;
-    __half* Wh = nullptr;          // f16 copy of the weight matrix the current prefill GEMM uses
-    size_t wh_elems = 0;
+    // chunks of more than ws_rows token rows use the persistent GEMM when its
+    // tiles fill at least ws_min_tiles CTAs (0: one per SM)
+    int ws_rows = 256, ws_min_tiles = 0;
     unsigned long long* tile_best = nullptr;   // many-row lm_head: best key per row and 128-column tile
     size_t tile_best_n = 0;
     float* kpart = nullptr;        // split-K partials of the tensor-core GEMMs
@@ -271,7 +272,6 @@ struct vvq2_kv {
     std::vector<int> past;
     // partitioned contexts, 2 sequence parts: first position of part 1 per
     // sequence (-1: not yet fixed; set by the sequence's first write)
-    std::vector<int> split;
 
     KvLayer layer(int li) const {
         KvLayer L;
@@ -576,36 +576,20 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
                        cudaStream_t st, std::vector<vvq2_ctx::Rec>* recs, double attn_flops) {
     const vvq2_hparams& hp = c->hp;
     Recorder R{c, st, recs};
-    // Chunks of more than 256 rows first make an f16 copy of the weights
-    // (read once), then the GEMM loads both operands with TMA; smaller
-    // chunks dequantize weight tiles inside the GEMM.
-    static const int tmab_rows = [] {
-        const char* e = std::getenv("VVQ2_TMAB_ROWS");
-        return e ? std::atoi(e) : 256;
-    }();
-    const bool tma_b = M > tmab_rows;
-    if (tma_b) {
-        const vvq2_ctx::Layer& L0 = c->layers[first];
-        const size_t need = std::max({(size_t)L0.qkv.rows * L0.qkv.cols, (size_t)L0.o.rows * L0.o.cols,
-                                      (size_t)L0.gate.rows * L0.gate.cols + (size_t)L0.up.rows * L0.up.cols,
-                                      (size_t)L0.down.rows * L0.down.cols});
-        if (need > c->wh_elems) {
-            if (int rc = c->alloc(&c->Wh, need)) return rc;
-            c->wh_elems = need;
-        }
-    }
-    auto gemm = [&](const GemmArgs& g, const CUtensorMap& map) -> int {
-        CUtensorMap b0, b1;
-        if (tma_b) {
-            const bool sw = g.epi == EPI_SWIGLU;
-            CU(dequant_f16_launch(g.w0, c->Wh, st));
-            if (!make_w_map(&b0, c->Wh, g.w0.rows, g.w0.cols, sw ? 64 : 128))
-                return fail(VVQ2_ERR_CUDA, "weight tensor map");
-            if (sw) {
-                __half* up = c->Wh + (size_t)g.w0.rows * g.w0.cols;
-                CU(dequant_f16_launch(g.w1, up, st));
-                if (!make_w_map(&b1, up, g.w1.rows, g.w1.cols, 64)) return fail(VVQ2_ERR_CUDA, "weight tensor map");
-            }
+    // Chunks of more than ws_rows rows run the persistent GEMM (256 weight
+    // rows x up to 256 tokens per tile) when its tiles fill the SMs; smaller
+    // ones the few-row kernel, split along K when it has few tiles.  Both
+    // dequantize the weight blocks in shared memory.
+    auto gemm = [&](const GemmArgs& g, const CUtensorMap& map, const __half* act) -> int {
+        const double n = g.epi == EPI_SWIGLU ? 2.0 * g.N : (double)g.N;
+        const int nt = M > c->ws_rows ? gemm_ws_tile_rows(g, c->ws_min_tiles) : 0;
+        if (nt) {
+            CUtensorMap mt;
+            if (!make_act_map(&mt, act, M, g.K, nt)) return fail(VVQ2_ERR_CUDA, "activation tensor map");
+            CU(R.begin());
+            CU(gemm_ws_launch(g, mt, nt, st));
+            CU(R.end(3, 2.0 * g.T * n * g.K));
+            return 0;
         }
         // few output tiles (small N, few rows): split K over more CTAs, then an
         // in-order reduction applies the epilogue
@@ -624,9 +608,8 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
             }
         }
         CU(R.begin());
-        CU(gemm_tc_launch(gg, map, st, tma_b ? &b0 : nullptr, tma_b && g.epi == EPI_SWIGLU ? &b1 : nullptr));
+        CU(gemm_tc_launch(gg, map, st));
         if (gg.kpart) CU(splitk_epilogue_launch(gg, st));
-        const double n = g.epi == EPI_SWIGLU ? 2.0 * g.N : (double)g.N;
         CU(R.end(3, 2.0 * g.T * n * g.K));
         return 0;
     };
@@ -693,7 +676,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
             q.bias = L.qkv_bias;
             q.y = c->Q;
             q.y_stride = qw_l;
-            if (int rc = gemm(q, mapX)) return rc;
+            if (int rc = gemm(q, mapX, c->Xh)) return rc;
         }
         __half* att_out = parted ? c->ATTl : (gv ? nullptr : c->ATTh);   // this rank's heads (gv: f32 c->ATT)
         float* att_lse = c->pt.seq_parts > 1 ? c->LSEl : nullptr;
@@ -829,7 +812,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         o.epi = EPI_RESID;
         o.y = c->X;
         o.y_stride = H;
-        if (int rc = gemm(o, mapA)) return rc;
+        if (int rc = gemm(o, mapA, c->ATTh)) return rc;
         // 4. RMSNorm -> f16, gate/up GEMM with SwiGLU epilogue (f16 out)
         CU(rmsnorm_f16_launch(c->X, L.ffn_norm, M, H, hp.rms_norm_eps, c->Xh, st));
         GemmArgs f = g;
@@ -840,7 +823,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         f.epi = EPI_SWIGLU;
         f.yh = c->Ah;
         f.yh_stride = F;
-        if (int rc = gemm(f, mapX)) return rc;
+        if (int rc = gemm(f, mapX, c->Xh)) return rc;
         // 5. down + residual (partitioned: partial sums over this rank's features,
         //    NCCL all-reduce, then the residual add)
         GemmArgs d = g;
@@ -850,7 +833,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         d.epi = parted ? EPI_STORE : EPI_RESID;
         d.y = parted ? c->Xp : c->X;
         d.y_stride = H;
-        if (int rc = gemm(d, mapF)) return rc;
+        if (int rc = gemm(d, mapF, c->Ah)) return rc;
         if (parted) {
             if (ncclAllReduce(c->Xp, c->Xp, (size_t)M * H, ncclFloat, ncclSum, c->pt.comm, st) != ncclSuccess)
                 return fail(VVQ2_ERR_CUDA, "NCCL all-reduce of the down projection failed");
@@ -967,33 +950,38 @@ void mega_split(const vvq2_ctx* c, int M, int max_lim, int* split, int* nsplit) 
     *nsplit = (max_lim + s - 1) / s;
 }
 
+// Sequence parts of a partitioned context interleave whole pages: page p of
+// every sequence belongs to part ZZ[p % 4] (0, 1, 1, 0), so each part holds
+// half of every 256-position span and a causal prompt of any length (and any
+// chunking) gives both parts the same attention work -- keys early in the
+// sequence are seen by more queries, and each part holds as many early as
+// late keys.  A part stores its positions in order: position p sits at cache
+// index zz_count(part, p), the number of the part's positions below p.
+constexpr int ZZ_PERIOD = 4 * KV_PAGE;
+inline int zz_part(int p) { return ((p / KV_PAGE) % 4 == 1 || (p / KV_PAGE) % 4 == 2) ? 1 : 0; }
+inline int zz_count(int part, int n) {
+    const int full = n / ZZ_PERIOD, rem = n % ZZ_PERIOD;
+    int c = full * (ZZ_PERIOD / 2);
+    for (int j = 0; j < 4; ++j)
+        if (zz_part(j * KV_PAGE) == part) c += std::min(KV_PAGE, std::max(0, rem - j * KV_PAGE));
+    return c;
+}
+
 // A token row as this rank sees it.  `rope` gets the true position (RoPE
 // table); the returned row has the cache index and key limits of the rank's
-// sequence part: part 0 holds positions [0, split), part 1 [split, ...) at
-// cache index pos - split (pos is shifted the same way so the kernels'
-// causal limit min(pos + 1, kvlen) stays right); cidx < 0 when the other
-// part stores the row.
-RowMeta local_row(const vvq2_ctx* c, const vvq2_kv* kv, int seq, int pos, int cidx, int kvlen, RowMeta* rope) {
+// sequence part: pos becomes the cache index of the part's last position <=
+// pos (-1 if none), so the kernels' causal limit min(pos + 1, kvlen) counts
+// exactly the part's keys at positions <= pos; kvlen the part's positions
+// below kvlen; cidx < 0 when the other part stores the row.
+RowMeta local_row(const vvq2_ctx* c, int seq, int pos, int cidx, int kvlen, RowMeta* rope) {
     RowMeta r{seq, pos, cidx, kvlen};
     if (rope) *rope = r;
     if (c->pt.seq_parts < 2) return r;
-    const int S0 = kv->split[seq];
-    if (c->pt.s == 0) {
-        r.cidx = cidx < S0 ? cidx : -1;
-        r.kvlen = std::min(kvlen, S0);
-    } else {
-        r.pos = pos - S0;
-        r.cidx = cidx >= S0 ? cidx - S0 : -1;
-        r.kvlen = std::max(0, kvlen - S0);
-    }
+    const int s = c->pt.s;
+    r.pos = zz_count(s, pos + 1) - 1;
+    r.cidx = zz_part(cidx) == s ? zz_count(s, cidx) : -1;
+    r.kvlen = zz_count(s, kvlen);
     return r;
-}
-
-// Fix a sequence's part split at its first write of n positions (half of it,
-// page aligned); later writes keep it.
-void fix_split(const vvq2_ctx* c, vvq2_kv* kv, int seq, int n) {
-    if (c->pt.seq_parts > 1 && kv->split[seq] < 0)
-        kv->split[seq] = std::max(KV_PAGE, ((n + 1) / 2 + KV_PAGE - 1) / KV_PAGE * KV_PAGE);
 }
 
 // Greedy decode step for more rows than the GEMV paths take (many streams at
@@ -1010,8 +998,7 @@ int decode_step_batched(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, c
     std::vector<RowMeta> rope(c->pt.on() ? M : 0);
     for (int s = 0; s < M; ++s) {
         const int past = kv->past[seqs[s]];
-        fix_split(c, kv, seqs[s], 1);
-        const RowMeta r = local_row(c, kv, seqs[s], past, past, past + 1, c->pt.on() ? &rope[s] : nullptr);
+        const RowMeta r = local_row(c, seqs[s], past, past, past + 1, c->pt.on() ? &rope[s] : nullptr);
         c->meta_host[s] = r;
         max_lim = std::max(max_lim, std::min(r.pos + 1, r.kvlen));
         attn_flops += 4.0 * c->pt.nq * hp.head_dim * std::max(0, std::min(r.pos + 1, r.kvlen));
@@ -1331,11 +1318,14 @@ int vvq2_init(const vvq2_hparams* hp, int device, vvq2_ctx** out) {
         const int v = atoi(pr);
         if (v >= 256 && v <= 65536) c->prefill_rows = v / 128 * 128;
     }
+    if (const char* e = std::getenv("VVQ2_WS_ROWS")) c->ws_rows = std::max(0, atoi(e));
+    if (const char* e = std::getenv("VVQ2_WS_MIN_TILES")) c->ws_min_tiles = std::max(1, atoi(e));
     const int P = c->prefill_rows;
     const int qw = hp->n_heads * hp->head_dim;
     const int F = std::max(hp->intermediate_size, 1);
     int rc = 0;
-    if (cudaSuccess != gemm_tc_prepare()) rc = fail(VVQ2_ERR_CUDA, "gemm prepare failed");
+    if (cudaSuccess != gemm_tc_prepare() || cudaSuccess != gemm_ws_prepare())
+        rc = fail(VVQ2_ERR_CUDA, "gemm prepare failed");
     if (!rc && cudaSuccess != fa_prefill_prepare()) rc = fail(VVQ2_ERR_CUDA, "flash attention prepare failed");
     if (!encode_fn()) rc = rc ? rc : fail(VVQ2_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     rc = rc ? rc : c->alloc(&c->X, (size_t)P * hp->hidden_size);
@@ -1604,7 +1594,6 @@ int vvq2_kv_init(vvq2_ctx* c, int n_seqs, int max_seq, vvq2_kv** out) {
         return fail(VVQ2_ERR_CUDA, "kv init copy failed");
     }
     kv->past.assign(n_seqs, 0);
-    kv->split.assign(n_seqs, c->pt.seq_parts > 1 ? -1 : INT32_MAX);
     c->kvs.push_back(kv);
     *out = kv;
     return 0;
@@ -1657,25 +1646,24 @@ static int kv_xfer(vvq2_kv* kv, int seq, int layer, float* k, float* v, const fl
     std::vector<float> lk, lv;   // partitioned upload: this rank's heads and sequence part
     if (c->pt.on()) {
         if (!upload) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "kv read on a partitioned context");
-        fix_split(c, kv, seq, n_pos);
         const int W = c->hp.n_kv_heads * c->hp.head_dim, wl = c->pt.nkv * c->hp.head_dim, c0 = c->pt.g * wl;
-        int p0 = 0, p1 = n_pos;
-        if (c->pt.seq_parts > 1) {
-            if (c->pt.s == 0) p1 = std::min(n_pos, kv->split[seq]);
-            else p0 = std::min(n_pos, kv->split[seq]);
-        }
         std::vector<float> hk((size_t)n_pos * W), hv((size_t)n_pos * W);
         if (is_device_ptr(kc) || is_device_ptr(vc)) CU(cudaDeviceSynchronize());
         CU(copy_on(hk.data(), kc, hk.size() * 4, c->stream));
         CU(copy_on(hv.data(), vc, hv.size() * 4, c->stream));
-        lk.resize((size_t)(p1 - p0) * wl);
+        // this rank's KV heads at the positions of its sequence part, in order
+        const int own = c->pt.seq_parts > 1 ? zz_count(c->pt.s, n_pos) : n_pos;
+        lk.resize((size_t)own * wl);
         lv.resize(lk.size());
-        for (int p = p0; p < p1; ++p)
+        for (int p = 0, i = 0; p < n_pos; ++p) {
+            if (c->pt.seq_parts > 1 && zz_part(p) != c->pt.s) continue;
             for (int j = 0; j < wl; ++j) {
-                lk[(size_t)(p - p0) * wl + j] = hk[(size_t)p * W + c0 + j];
-                lv[(size_t)(p - p0) * wl + j] = hv[(size_t)p * W + c0 + j];
+                lk[(size_t)i * wl + j] = hk[(size_t)p * W + c0 + j];
+                lv[(size_t)i * wl + j] = hv[(size_t)p * W + c0 + j];
             }
-        n_pos = p1 - p0;
+            ++i;
+        }
+        n_pos = own;
         kc = lk.data();
         vc = lv.data();
         if (n_pos == 0) return 0;
@@ -1756,10 +1744,9 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
         int max_lim = 1;
         std::vector<RowMeta> rope(c->pt.on() ? M : 0);
         for (int s = 0; s < n_seqs; ++s) {
-            fix_split(c, kv, seqs[s], kv->past[seqs[s]] + n_tok);
             for (int t = 0; t < nt; ++t) {
                 RowMeta& r = c->meta_host[s * nt + t];
-                r = local_row(c, kv, seqs[s], pos_start[s] + t0 + t, kv->past[seqs[s]] + t0 + t,
+                r = local_row(c, seqs[s], pos_start[s] + t0 + t, kv->past[seqs[s]] + t0 + t,
                               kv->past[seqs[s]] + t0 + nt, c->pt.on() ? &rope[s * nt + t] : nullptr);
                 max_lim = std::max(max_lim, std::min(r.pos + 1, r.kvlen));
             }
@@ -2100,7 +2087,8 @@ int vvq2_rms_norm(const float* x, const float* w, int rows, int n, float eps, fl
 int vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int t, float* y) {
     if (!w || !x || !y || n <= 0 || k <= 0 || t <= 0 || k % 64) return fail(VVQ2_ERR_INVALID_ARG, "bad gemm args");
     if (vvq2_device_count() == 0) return fail(VVQ2_ERR_NO_DEVICE, "no sm_100 device");
-    if (gemm_tc_prepare() != cudaSuccess) return fail(VVQ2_ERR_CUDA, "gemm prepare failed");
+    if (gemm_tc_prepare() != cudaSuccess || gemm_ws_prepare() != cudaSuccess)
+        return fail(VVQ2_ERR_CUDA, "gemm prepare failed");
     vvq2_ctx tmp;
     vvq2_tensor tw{w, type, k, n};
     DevW dw;
@@ -2129,16 +2117,12 @@ int vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int t
             g.y = dy;
             g.y_stride = n;
             g.err = derr;
-            if (t > 256) {   // the prefill engine's path for large chunks: f16 weight copy + TMA
-                __half* wh = nullptr;
-                rc = tmp.alloc(&wh, (size_t)n * k);
-                CUtensorMap bmap;
-                if (!rc) e = dequant_f16_launch(dw, wh, 0);
-                if (!rc && e == cudaSuccess && !make_w_map(&bmap, wh, n, k, 128)) rc = fail(VVQ2_ERR_CUDA, "tensor map");
-                if (!rc && e == cudaSuccess) e = gemm_tc_launch(g, map, 0, &bmap, nullptr);
-            } else {
-                e = gemm_tc_launch(g, map, 0);
-            }
+            // the prefill engine's kernel for chunks of more than 256 rows (here at
+            // any tile count), else the few-row kernel
+            const int nt = t > 256 ? gemm_ws_tile_rows(g, 1) : 0;
+            CUtensorMap mt;
+            if (nt && !make_act_map(&mt, dxh, t, k, nt)) rc = fail(VVQ2_ERR_CUDA, "tensor map");
+            if (!rc) e = nt ? gemm_ws_launch(g, mt, nt, 0) : gemm_tc_launch(g, map, 0);
         }
         if (!rc && e == cudaSuccess) e = cudaDeviceSynchronize();
         int herr = 0;

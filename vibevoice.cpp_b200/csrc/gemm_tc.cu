@@ -17,10 +17,9 @@
 // CTA: 6 warps.  warp 0: TMEM allocation + TMA producer (lane 0);
 // warp 1: MMA issuer (lane 0); warps 2-5: weight producers, then epilogue.
 //
-// Large prefill chunks instead take the weight operand from an f16 copy made
-// once per chunk (dequant_f16_launch: the same exact-then-f16 values) through
-// TMA as well (TMAB variant): the producer warps then only run the epilogue,
-// and no weight tile is dequantized once per 256-row block of tokens.
+// Chunks with enough rows to fill the SMs with 256 x 256 tiles run the
+// persistent kernel of gemm_ws.cu instead; this one serves the few-row
+// GEMMs (batched decode of many streams, short prompt chunks, split-K).
 // Pipeline: 4 stages of {A0, A1, B} 16 KB tiles (BK = 64), mbarriers full/empty.
 // The Q8_0 weight producers fetch each row's raw blocks 4 k-blocks ahead of
 // their conversion.  Epilogues that write rows stage the accumulators
@@ -33,6 +32,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "dequant_tile.cuh"
 #include "kernels.h"
 #include "tc.cuh"
 
@@ -50,140 +50,10 @@ constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 256;
 
-__device__ __forceinline__ void store_chunk(uint8_t* btile, int p, int j, uint4 v) {
-    *reinterpret_cast<uint4*>(btile + p * 128 + ((j ^ (p & 7)) * 16)) = v;
-}
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-__device__ __forceinline__ uint32_t wsel(const uint4& v, int t) {
-    return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w;
-}
-
-// Dequantize elements [k0, k0 + 64) of weight row `row` into 8 swizzled
-// 16-byte chunks of row p of the B tile (exact ggml values, then f16 RNE).
-template <int WT>
-__device__ __forceinline__ void produce_row(const DevW& W, int row, int k0, uint8_t* btile, int p) {
-    if (row < 0 || row >= W.rows) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) store_chunk(btile, p, j, make_uint4(0, 0, 0, 0));
-        return;
-    }
-    const uint8_t* rp = W.q + (size_t)row * W.row_stride;
-    if constexpr (WT == W_Q8_0) {
-        const uint4* qp = reinterpret_cast<const uint4*>(rp + k0);
-        uint4 q[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) q[i] = __ldg(qp + i);
-        const __half2 dd = *reinterpret_cast<const __half2*>(W.d + (size_t)row * W.d_stride + k0 / 32);
-        const float d0 = __low2float(dd), d1 = __high2float(dd);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float d = j < 4 ? d0 : d1;
-            const uint32_t w0 = wsel(q[j / 2], (j % 2) * 2), w1 = wsel(q[j / 2], (j % 2) * 2 + 1);
-            uint4 o;
-            o.x = pack_h2(__fmul_rn((float)((int)(w0 & 0xff) - 128), d), __fmul_rn((float)((int)((w0 >> 8) & 0xff) - 128), d));
-            o.y = pack_h2(__fmul_rn((float)((int)((w0 >> 16) & 0xff) - 128), d), __fmul_rn((float)((int)(w0 >> 24) - 128), d));
-            o.z = pack_h2(__fmul_rn((float)((int)(w1 & 0xff) - 128), d), __fmul_rn((float)((int)((w1 >> 8) & 0xff) - 128), d));
-            o.w = pack_h2(__fmul_rn((float)((int)((w1 >> 16) & 0xff) - 128), d), __fmul_rn((float)((int)(w1 >> 24) - 128), d));
-            store_chunk(btile, p, j, o);
-        }
-    } else if constexpr (WT == W_Q5_K) {
-        const int sb = k0 / 256, qq = (k0 % 256) / 64;    // 64-element chunk qq of the super-block
-        const uint8_t* b = rp + (size_t)sb * Q5K_BYTES;
-        const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(b));
-        uint4 qs[2], qh[2];
-        qs[0] = __ldg(reinterpret_cast<const uint4*>(b + 48 + 32 * qq));
-        qs[1] = __ldg(reinterpret_cast<const uint4*>(b + 48 + 32 * qq) + 1);
-        qh[0] = __ldg(reinterpret_cast<const uint4*>(b + 16));
-        qh[1] = __ldg(reinterpret_cast<const uint4*>(b + 16) + 1);
-        const uint8_t* scb = reinterpret_cast<const uint8_t*>(&hdr) + 4;
-        const __half2 dh = *reinterpret_cast<const __half2*>(&hdr.x);
-        float d1[2], m1[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int j = 2 * qq + h;
-            int s, m;
-            if (j < 4) {
-                s = scb[j] & 63;
-                m = scb[j + 4] & 63;
-            } else {
-                s = (scb[j + 4] & 0xF) | ((scb[j - 4] >> 6) << 4);
-                m = (scb[j + 4] >> 4) | ((scb[j] >> 6) << 4);
-            }
-            d1[h] = __fmul_rn(__low2float(dh), (float)s);
-            m1[h] = __fmul_rn(__high2float(dh), (float)m);
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int h = j / 4;                 // first or second 32 elements
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int l = (j % 4) * 8 + e;   // 0..31 within the sub-block
-                const uint32_t qsw = wsel(qs[l / 16], (l % 16) / 4), qhw = wsel(qh[l / 16], (l % 16) / 4);
-                const int qb = (qsw >> (8 * (l % 4))) & 0xff, hb = (qhw >> (8 * (l % 4))) & 0xff;
-                const int q = ((qb >> (4 * h)) & 0xF) + (((hb >> (2 * qq + h)) & 1) ? 16 : 0);
-                f[e] = __fsub_rn(__fmul_rn(d1[h], (float)q), m1[h]);
-            }
-            store_chunk(btile, p, j, make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
-                                                pack_h2(f[6], f[7])));
-        }
-    } else if constexpr (WT == W_Q6_K) {
-        const int sb = k0 / 256, qq = (k0 % 256) / 64, hf = qq >> 1, k0q = (qq & 1) * 2;
-        const uint8_t* b = rp + (size_t)sb * Q6K_PACKED;
-        uint4 ql[4], qh[2];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) ql[i] = __ldg(reinterpret_cast<const uint4*>(b + hf * 64) + i);
-        qh[0] = __ldg(reinterpret_cast<const uint4*>(b + 128 + hf * 32));
-        qh[1] = __ldg(reinterpret_cast<const uint4*>(b + 128 + hf * 32) + 1);
-        const int8_t* scl = reinterpret_cast<const int8_t*>(b + 192);
-        const float dsb = __half2float(W.d[(size_t)row * W.d_stride + sb]);
-        float ds[4];   // (k - k0q) * 2 + l/16
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk)
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) ds[kk * 2 + hh] = __fmul_rn(dsb, (float)scl[hf * 8 + hh + 2 * (k0q + kk)]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int kk = j / 4;                // quarter k = k0q + kk
-            const int k = k0q + kk;
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int l = (j % 4) * 8 + e;   // 0..31
-                const int qlbyte_idx = (k & 1) * 32 + l;   // within the 64 ql bytes of this half
-                const uint32_t lw = wsel(ql[qlbyte_idx / 16], (qlbyte_idx % 16) / 4);
-                const uint32_t hw = wsel(qh[l / 16], (l % 16) / 4);
-                const int lb = (lw >> (8 * (qlbyte_idx % 4))) & 0xff, hb = (hw >> (8 * (l % 4))) & 0xff;
-                const int q = (int)(((lb >> (4 * (k >> 1))) & 0xF) | (((hb >> (2 * k)) & 3) << 4)) - 32;
-                f[e] = __fmul_rn(ds[kk * 2 + l / 16], (float)q);
-            }
-            store_chunk(btile, p, j, make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]),
-                                                pack_h2(f[6], f[7])));
-        }
-    } else if constexpr (WT == W_F16) {
-        const uint4* hp = reinterpret_cast<const uint4*>(rp + (size_t)k0 * 2);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) store_chunk(btile, p, j, __ldg(hp + j));
-    } else {
-        const float4* fp = reinterpret_cast<const float4*>(rp + (size_t)k0 * 4);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float4 a = __ldg(fp + 2 * j), c = __ldg(fp + 2 * j + 1);
-            store_chunk(btile, p, j, make_uint4(pack_h2(a.x, a.y), pack_h2(a.z, a.w), pack_h2(c.x, c.y),
-                                                pack_h2(c.z, c.w)));
-        }
-    }
-}
-
-template <int WT, int EPI, bool TMAB>
+template <int WT, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
-              const __grid_constant__ CUtensorMap tmB1, const GemmArgs a) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const GemmArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], done;
@@ -203,7 +73,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            tc::mbar_init(&full[s], TMAB ? 1 : 1 + 128);
+            tc::mbar_init(&full[s], 1 + 128);
             tc::mbar_init(&empty[s], 1);
         }
         tc::mbar_init(&done, 1);
@@ -228,24 +98,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---- TMA producer: activation tiles A0 (rows t0..) and A1 (rows t0+128..).
         // Launched as a programmatic dependent: everything above (barriers, TMEM,
         // the weight producers' first fetches) overlapped the previous kernel;
-        // its outputs (A, a dequantized B copy) are read only after this wait.
+        // its outputs (the activations A) are read only after this wait.
         asm volatile("griddepcontrol.wait;" ::: "memory");
         for (int i = 0; i < nk; ++i) {
             const int s = i % STAGES, kx = (kb0 + i) * BK;
             if (i >= STAGES && !tc::mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) { fail(); break; }
             if (*(volatile int*)&abort_flag) break;
             uint8_t* st = smem + s * STAGE_BYTES;
-            tc::mbar_arrive_expect_tx(&full[s], ((two ? 2 : 1) + (TMAB ? 1 : 0)) * TILE_BYTES);
+            tc::mbar_arrive_expect_tx(&full[s], (two ? 2 : 1) * TILE_BYTES);
             tc::tma_load_2d(st, &tmA, kx, t0, &full[s]);
             if (two) tc::tma_load_2d(st + TILE_BYTES, &tmA, kx, t0 + BM, &full[s]);
-            if constexpr (TMAB) {
-                if constexpr (EPI == EPI_SWIGLU) {   // 64 gate rows, then the same 64 up rows
-                    tc::tma_load_2d(st + 2 * TILE_BYTES, &tmB0, kx, blockIdx.x * 64, &full[s]);
-                    tc::tma_load_2d(st + 2 * TILE_BYTES + 64 * 128, &tmB1, kx, blockIdx.x * 64, &full[s]);
-                } else {
-                    tc::tma_load_2d(st + 2 * TILE_BYTES, &tmB0, kx, n0, &full[s]);
-                }
-            }
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer
@@ -281,7 +143,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             W = &a.w0;
             wrow = n0 + p;
         }
-        if constexpr (WT == W_Q8_0 && !TMAB) {
+        if constexpr (WT == W_Q8_0) {
             // Q8_0: the row's raw blocks are loaded PD k-blocks ahead of their
             // conversion, so the global latency overlaps the MMAs instead of
             // gating every k-block
@@ -315,40 +177,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); stop = true; break; }
                     if (*(volatile int*)&abort_flag) { stop = true; break; }
                     uint8_t* bt = smem + s * STAGE_BYTES + 2 * TILE_BYTES;
-                    // quant -> exact f16 (the stored byte q + 128 in the mantissa of 1024, minus 1152),
-                    // then one f16 multiply by the block scale: RN(q * d), the same value
-                    // as the exact f32 product rounded to f16
-                    const uint32_t dbits = dd[d];
-                    const __half2 s0 = __halves2half2(__ushort_as_half((unsigned short)(dbits & 0xffff)),
-                                                      __ushort_as_half((unsigned short)(dbits & 0xffff)));
-                    const __half2 s1 = __halves2half2(__ushort_as_half((unsigned short)(dbits >> 16)),
-                                                      __ushort_as_half((unsigned short)(dbits >> 16)));
-                    const __half2 off = __float2half2_rn(-1152.0f), one = __float2half2_rn(1.0f);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const __half2 sc = j < 4 ? s0 : s1;
-                        uint32_t o[4];
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const uint32_t w = wsel(raw[d][j / 2], (j % 2) * 2 + h);   // q + 128 bytes
-                            const uint32_t lo = __byte_perm(w, 0x64646464u, 0x5140);
-                            const uint32_t hi = __byte_perm(w, 0x64646464u, 0x7362);
-                            __half2 qlo = __hfma2(*reinterpret_cast<const __half2*>(&lo), one, off);
-                            __half2 qhi = __hfma2(*reinterpret_cast<const __half2*>(&hi), one, off);
-                            qlo = __hmul2(qlo, sc);
-                            qhi = __hmul2(qhi, sc);
-                            o[2 * h] = *reinterpret_cast<const uint32_t*>(&qlo);
-                            o[2 * h + 1] = *reinterpret_cast<const uint32_t*>(&qhi);
-                        }
-                        store_chunk(bt, p, j, make_uint4(o[0], o[1], o[2], o[3]));
-                    }
+                    q8_0_tile_row(raw[d], dd[d], bt, p);
                     fetch(kb + PD, raw[d], dd[d]);
                     tc::fence_proxy_async_smem();
                     tc::mbar_arrive(&full[s]);
                 }
             }
         } else {
-            for (int kb = 0; !TMAB && kb < nk; ++kb) {   // local k-block index
+            for (int kb = 0; kb < nk; ++kb) {   // local k-block index
                 const int s = kb % STAGES;
                 if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); break; }
                 if (*(volatile int*)&abort_flag) break;
@@ -562,8 +398,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 template <int EPI>
-cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, const CUtensorMap* b0, const CUtensorMap* b1,
-                       cudaStream_t st) {
+cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, cudaStream_t st) {
     dim3 grid((EPI == EPI_SWIGLU ? (a.N + 63) / 64 : (a.N + BN - 1) / BN), (a.T + 2 * BM - 1) / (2 * BM),
               a.kpart ? a.k_splits : 1);
     // programmatic dependent launch: CTAs may start (prologue, weight
@@ -579,17 +414,13 @@ cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, const CUtensorM
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e;
-    if (b0) {
-        e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F16, EPI, true>, tm, *b0, b1 ? *b1 : *b0, a);
-    } else {
-        switch (a.w0.type) {
-            case W_Q8_0: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q8_0, EPI, false>, tm, tm, tm, a); break;
-            case W_Q5_K: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q5_K, EPI, false>, tm, tm, tm, a); break;
-            case W_Q6_K: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q6_K, EPI, false>, tm, tm, tm, a); break;
-            case W_F16: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F16, EPI, false>, tm, tm, tm, a); break;
-            case W_F32: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F32, EPI, false>, tm, tm, tm, a); break;
-            default: return cudaErrorInvalidValue;
-        }
+    switch (a.w0.type) {
+        case W_Q8_0: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q8_0, EPI>, tm, a); break;
+        case W_Q5_K: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q5_K, EPI>, tm, a); break;
+        case W_Q6_K: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q6_K, EPI>, tm, a); break;
+        case W_F16: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F16, EPI>, tm, a); break;
+        case W_F32: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F32, EPI>, tm, a); break;
+        default: return cudaErrorInvalidValue;
     }
     note_launch();
     return e != cudaSuccess ? e : cudaGetLastError();
@@ -597,9 +428,9 @@ cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, const CUtensorM
 
 template <int EPI>
 cudaError_t prepare_epi() {
-    const void* fns[] = {(const void*)k_gemm_tc<W_Q8_0, EPI, false>, (const void*)k_gemm_tc<W_Q5_K, EPI, false>,
-                         (const void*)k_gemm_tc<W_Q6_K, EPI, false>, (const void*)k_gemm_tc<W_F16, EPI, false>,
-                         (const void*)k_gemm_tc<W_F32, EPI, false>, (const void*)k_gemm_tc<W_F16, EPI, true>};
+    const void* fns[] = {(const void*)k_gemm_tc<W_Q8_0, EPI>, (const void*)k_gemm_tc<W_Q5_K, EPI>,
+                         (const void*)k_gemm_tc<W_Q6_K, EPI>, (const void*)k_gemm_tc<W_F16, EPI>,
+                         (const void*)k_gemm_tc<W_F32, EPI>};
     for (const void* f : fns) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
@@ -689,19 +520,17 @@ cudaError_t gemm_tc_prepare() {
     return prepare_epi<EPI_STORE>();
 }
 
-cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st, const CUtensorMap* tmB0,
-                           const CUtensorMap* tmB1) {
+cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st) {
     if (a.K % BK || a.T <= 0 || a.N <= 0) return cudaErrorInvalidValue;
     if (a.epi == EPI_QKV && (BN % a.hd || (a.hd != 32 && a.hd != 64 && a.hd != 128))) return cudaErrorInvalidValue;
-    if (a.epi == EPI_SWIGLU && tmB0 && !tmB1) return cudaErrorInvalidValue;
     if (a.kpart && (a.k_splits < 1 || a.k_splits > a.K / BK || a.epi == EPI_SWIGLU || a.epi == EPI_ARGMAX))
         return cudaErrorInvalidValue;
     switch (a.epi) {
-        case EPI_QKV: return launch_epi<EPI_QKV>(a, tmA, tmB0, tmB1, st);
-        case EPI_RESID: return launch_epi<EPI_RESID>(a, tmA, tmB0, tmB1, st);
-        case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(a, tmA, tmB0, tmB1, st);
-        case EPI_STORE: return launch_epi<EPI_STORE>(a, tmA, tmB0, tmB1, st);
-        case EPI_ARGMAX: return a.amax ? launch_epi<EPI_ARGMAX>(a, tmA, tmB0, tmB1, st) : cudaErrorInvalidValue;
+        case EPI_QKV: return launch_epi<EPI_QKV>(a, tmA, st);
+        case EPI_RESID: return launch_epi<EPI_RESID>(a, tmA, st);
+        case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(a, tmA, st);
+        case EPI_STORE: return launch_epi<EPI_STORE>(a, tmA, st);
+        case EPI_ARGMAX: return a.amax ? launch_epi<EPI_ARGMAX>(a, tmA, st) : cudaErrorInvalidValue;
         default: return cudaErrorInvalidValue;
     }
 }

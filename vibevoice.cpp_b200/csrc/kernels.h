@@ -67,14 +67,19 @@ struct GemmArgs {
     int k_splits = 1;
     int* err = nullptr;
 };
-// tmB0/tmB1 (optional): f16 weight maps [N][K], box 64 x 128 (SwiGLU: gate and
-// up, box 64 x 64); when given, weights are loaded by TMA instead of being
-// dequantized in the kernel
-cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st,
-                           const CUtensorMap* tmB0 = nullptr, const CUtensorMap* tmB1 = nullptr);
+// tmA: f16 activations [T][K], box 64 x 128; weight tiles are dequantized in the kernel
+cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st);
 cudaError_t gemm_tc_prepare();
 // sum split-K partials in order and apply a.epi (QKV / RESID / STORE)
 cudaError_t splitk_epilogue_launch(const GemmArgs& a, cudaStream_t st);
+
+// Persistent many-row GEMM with the weight dequantization fused (gemm_ws.cu):
+// QKV / RESID / SWIGLU / STORE epilogues, no split-K.  tmX: f16 activations
+// [T][K], box 64 x nt.  gemm_ws_tile_rows picks nt for a launch (0: fewer
+// than min_tiles tiles, <= 0 meaning one per SM; use gemm_tc_launch).
+int gemm_ws_tile_rows(const GemmArgs& a, int min_tiles);
+cudaError_t gemm_ws_launch(const GemmArgs& a, const CUtensorMap& tmX, int nt, cudaStream_t st);
+cudaError_t gemm_ws_prepare();
 
 // ------------------------------------------------------ persistent decode step
 struct MegaLayer {
@@ -196,8 +201,6 @@ enum { ACT_RELU = 0, ACT_SIGMOID = 1 };
 cudaError_t act_launch(float* x, int64_t n, int act, cudaStream_t st);
 // [parts][rows][w] -> [rows][parts*w]
 cudaError_t gather_rows_launch(const __half* in, int64_t rows, int parts, int w, __half* out, cudaStream_t st);
-// ... to f16 [rows][cols] (exact dequantized value, rounded once)
-cudaError_t dequant_f16_launch(const DevW& w, __half* dst, cudaStream_t st);
 cudaError_t rope_launch(const float* x, int n_tok, int n_heads, int hd, const int32_t* pos,
                         float ts, float* y, cudaStream_t st);
 cudaError_t rmsnorm_launch(const float* x, const float* w, int rows, int n, float eps, float* y,

@@ -23,18 +23,6 @@ __global__ void k_dequant(DevW w, int64_t n, float* out) {
         out[i] = deq_elem(w, (int)(i / w.cols), (int)(i % w.cols));
 }
 
-// 8 consecutive elements per thread, one 16-byte store
-__global__ void k_dequant_f16(DevW w, int64_t n8, __half* out) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t e0 = i * 8;
-        const int row = (int)(e0 / w.cols), col = (int)(e0 % w.cols);
-        __align__(16) __half h[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) h[k] = __float2half_rn(deq_elem(w, row, col + k));
-        reinterpret_cast<uint4*>(out)[i] = *reinterpret_cast<const uint4*>(h);
-    }
-}
-
 // ggml_rope_ext NEOX on [n_tok][n_heads][hd]; one thread per rotation pair
 __global__ void k_rope(const float* x, int n_tok, int n_heads, int hd, const int32_t* pos, float ts,
                        float* y) {
@@ -246,14 +234,6 @@ int grid_for(int64_t n, int threads) {
 cudaError_t dequant_rows_launch(const DevW& w, float* dst, cudaStream_t st) {
     const int64_t n = (int64_t)w.rows * w.cols;
     k_dequant<<<grid_for(n, 256), 256, 0, st>>>(w, n, dst);
-    note_launch();
-    return cudaGetLastError();
-}
-
-cudaError_t dequant_f16_launch(const DevW& w, __half* dst, cudaStream_t st) {
-    if (w.cols % 8) return cudaErrorInvalidValue;
-    const int64_t n8 = (int64_t)w.rows * w.cols / 8;
-    k_dequant_f16<<<grid_for(n8, 256), 256, 0, st>>>(w, n8, dst);
     note_launch();
     return cudaGetLastError();
 }

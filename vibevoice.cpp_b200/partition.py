@@ -3,8 +3,10 @@
 The same ownership rules the engine applies (vvq2_partition): `world` ranks
 = head_groups x seq_parts; rank r holds KV-head group r // seq_parts (its q
 heads, their QKV rows and attention) and sequence part r % seq_parts of
-every sequence's keys.  Part 1 starts at a page-aligned split fixed by the
-sequence's first write of n positions: max(64, roundup((n + 1) // 2, 64)).
+every sequence's keys.  The two parts interleave whole 64-position pages:
+page p belongs to part (0, 1, 1, 0)[p % 4], so each part holds half of every
+256-position span and a causal prompt of any length or chunking gives both
+the same attention work; a part stores its positions in order.
 Each rank's attention output is normalized over its own keys and carries its
 log-sum-exp; two parts merge as o = sum_i e^(l_i - l) o_i / sum_i e^(l_i - l).
 The FFN is split over all ranks: rank r holds intermediate features
@@ -20,9 +22,18 @@ import numpy as np
 KV_PAGE = 64
 
 
-def seq_split(n_first_write: int) -> int:
-    """First position of sequence part 1."""
-    return max(KV_PAGE, ((n_first_write + 1) // 2 + KV_PAGE - 1) // KV_PAGE * KV_PAGE)
+ZZ = (0, 1, 1, 0)
+
+
+def part_of(pos: int) -> int:
+    """Sequence part that stores position pos."""
+    return ZZ[(pos // KV_PAGE) % 4]
+
+
+def part_count(part: int, n: int) -> int:
+    """Positions below n that a part stores (= cache index of position n if it is the part's)."""
+    full, rem = divmod(n, 4 * KV_PAGE)
+    return full * 2 * KV_PAGE + sum(min(KV_PAGE, max(0, rem - j * KV_PAGE)) for j in range(4) if ZZ[j] == part)
 
 
 def plan(rank: int, world: int, seq_parts: int, n_heads: int, n_kv_heads: int) -> dict:
@@ -47,11 +58,12 @@ def ffn_range(rank: int, world: int, ffn: int) -> range:
     return range(rank * f, (rank + 1) * f)
 
 
-def keys_of_part(part: int, seq_parts: int, split: int, n_keys: int) -> range:
-    """Absolute key positions a sequence part holds."""
+def keys_of_part(part: int, seq_parts: int, n_keys: int) -> np.ndarray:
+    """Absolute key positions a sequence part holds, in cache order."""
+    pos = np.arange(n_keys, dtype=np.int64)
     if seq_parts == 1:
-        return range(0, n_keys)
-    return range(0, min(split, n_keys)) if part == 0 else range(min(split, n_keys), n_keys)
+        return pos
+    return pos[np.array([part_of(int(p)) == part for p in pos], dtype=bool)] if n_keys else pos
 
 
 def lse_merge(o: np.ndarray, lse: np.ndarray) -> np.ndarray:
