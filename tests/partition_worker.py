@@ -2,7 +2,9 @@
 test_gpu_partition.py): a small 2-layer model partitioned over the ranks
 (KV heads x sequence parts, 2 to 8 ranks) against an unpartitioned engine on
 the same GPU, through a prefill of 2 x 300 prompt tokens and 6 greedy decode
-steps."""
+steps.  With --skip-step-rank=r, rank r sits out one decode step (it stays
+alive, between steps, with nothing in flight) and every other rank must get
+the bounded peer wait's error back from that step."""
 import argparse
 import datetime
 import os
@@ -21,6 +23,7 @@ import vvq2  # noqa: E402
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--seq-parts", type=int, default=1)
+    ap.add_argument("--skip-step-rank", type=int, default=-1)
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
@@ -49,6 +52,23 @@ def main():
     hr = ref.forward(kvr, [0, 1], x, [0, 0])
     err = float(np.max(np.abs(hp_ - hr)) / np.max(np.abs(hr)))
     tok = rng.integers(0, hp["vocab"], size=2).astype(np.int32)
+    if args.skip_step_rank >= 0:
+        got = None
+        if rank != args.skip_step_rank:
+            try:
+                part.decode_step(kvp, [0, 1], tok)
+                got = "returned"
+            except Exception as e:  # the engine's error for a wait that ran out
+                got = str(e)
+        errs = [None] * world
+        dist.all_gather_object(errs, got)
+        if rank == 0:
+            print("errors:", errs, flush=True)
+            ok = all(e is not None and "timed out" in e for r, e in enumerate(errs) if r != args.skip_step_rank)
+            print("PEER_TIMEOUT_OK" if ok else "PEER_TIMEOUT_FAIL", flush=True)
+        dist.barrier()   # no rank frees its exchange buffer while another may still store into it
+        dist.destroy_process_group()
+        return
     same = 0
     for _ in range(steps):
         tp = part.decode_step(kvp, [0, 1], tok)

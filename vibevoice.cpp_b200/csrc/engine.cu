@@ -76,18 +76,27 @@ bool kv_map_encode(CUtensorMap* m, const __half* base, int64_t rows, int hd) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// f16 weight matrix [rows][cols] (dequantized copy) as a TMA map: 64 x box_rows
-// boxes, 128-byte swizzle (the GEMM's B operand layout)
-bool make_w_map(CUtensorMap* m, const __half* base, int rows, int cols, int box_rows) {
+// Repacked Q8_0 rows ([cols quants][block scales, padded to 16 bytes]) as a
+// byte map for the persistent GEMM's raw-weight TMA: box {box_x, box_rows},
+// no swizzle; rows past the matrix read as zeros.
+bool make_q8_map(CUtensorMap* m, const DevW& w, int box_x, int box_rows) {
     EncodeTiledFn fn = encode_fn();
-    if (!fn || cols % 64 || ((uintptr_t)base & 15)) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    if (!fn || w.type != W_Q8_0 || w.row_stride % 16 || ((uintptr_t)w.q & 15) || w.cols % 64) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)w.row_stride, (cuuint64_t)w.rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)w.row_stride};
+    const cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_rows};
     const cuuint32_t es[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w.q), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The four weight maps gemm_ws_launch takes for Q8_0 (w1 = w0 unless SwiGLU).
+bool make_ws_weight_maps(CUtensorMap* wq, const GemmArgs& g) {
+    const int r = gemm_ws_weight_box_rows(g);
+    const DevW& w1 = g.epi == EPI_SWIGLU ? g.w1 : g.w0;
+    return make_q8_map(&wq[0], g.w0, 64, r) && make_q8_map(&wq[1], w1, 64, r) && make_q8_map(&wq[2], g.w0, 16, r) &&
+           make_q8_map(&wq[3], w1, 16, r);
 }
 
 thread_local std::string g_err;
@@ -159,6 +168,10 @@ struct vvq2_ctx {
         int nq = 0, nkv = 0;                // heads held locally
         int ffn = 0;                        // FFN intermediate features held locally (split over all ranks)
         ncclComm_t comm = nullptr, pair = nullptr, heads = nullptr;
+        // decode-step exchanges over peer memory (peer.cu) instead of NCCL
+        PeerArgs px;
+        bool peer = false;
+        std::vector<void*> ipc;             // other ranks' exchange buffers, opened here
         bool on() const { return world > 1; }
     } pt;
     __half *ATTl = nullptr, *ATTg = nullptr;   // local / gathered attention output (partitioned)
@@ -584,10 +597,11 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         const double n = g.epi == EPI_SWIGLU ? 2.0 * g.N : (double)g.N;
         const int nt = M > c->ws_rows ? gemm_ws_tile_rows(g, c->ws_min_tiles) : 0;
         if (nt) {
-            CUtensorMap mt;
+            CUtensorMap mt, wq[4];
             if (!make_act_map(&mt, act, M, g.K, nt)) return fail(VVQ2_ERR_CUDA, "activation tensor map");
+            if (g.w0.type == W_Q8_0 && !make_ws_weight_maps(wq, g)) return fail(VVQ2_ERR_CUDA, "weight tensor map");
             CU(R.begin());
-            CU(gemm_ws_launch(g, mt, nt, st));
+            CU(gemm_ws_launch(g, mt, wq, nt, st));
             CU(R.end(3, 2.0 * g.T * n * g.K));
             return 0;
         }
@@ -745,7 +759,11 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         // f16 K and V read: 4 bytes per key and head dimension of each KV head
         CU(R.end(1, attn_flops * nkv / nq));
         }
-        if (parted) {
+        const bool px = parted && gv && c->pt.peer;   // decode-step exchanges over peer memory
+        if (px) {
+            // every rank's heads (both sequence parts merged) -> c->ATT, f32
+            CU(peer_attn_gather_launch(c->pt.px, c->ATTl, att_lse, M, nq, hd, c->pt.seq_parts, c->ATT, st));
+        } else if (parted) {
             // the two sequence parts of this head group: (O, LSE) all-gather, merge
             if (c->pt.seq_parts > 1) {
                 if (ncclGroupStart() != ncclSuccess ||
@@ -767,7 +785,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         if (gv) {
             // 3-5 as GEMVs: O-proj + residual (replicated), RMSNorm + gate/up +
             // SwiGLU over this rank's features, down (partial sums when partitioned)
-            if (parted) CU(half_to_float_launch(c->ATTh, c->ATT, (int64_t)M * qw, st));
+            if (parted && !px) CU(half_to_float_launch(c->ATTh, c->ATT, (int64_t)M * qw, st));
             GemvArgs o = gvb;
             o.w0 = L.o;
             o.K = qw;
@@ -797,7 +815,9 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
             d.y_stride = H;
             d.epi = parted ? EPI_STORE : EPI_RESID;
             if (int rc = gemv(d)) return rc;
-            if (parted) {
+            if (px) {
+                CU(peer_reduce_add_launch(c->pt.px, c->Xp, M * H, c->X, st));
+            } else if (parted) {
                 if (ncclAllReduce(c->Xp, c->Xp, (size_t)M * H, ncclFloat, ncclSum, c->pt.comm, st) != ncclSuccess)
                     return fail(VVQ2_ERR_CUDA, "NCCL all-reduce of the down projection failed");
                 CU(add_rows_launch(c->X, c->Xp, (int64_t)M * H, st));
@@ -1381,6 +1401,7 @@ void vvq2_free(vvq2_ctx* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (auto& g : c->graphs) cudaGraphExecDestroy(g.exec);
     for (cudaEvent_t e : c->events) cudaEventDestroy(e);
+    for (void* p : c->pt.ipc) cudaIpcCloseMemHandle(p);
     for (void* p : c->allocs) cudaFree(p);
     // caches outlive nothing: their device memory goes with the context and the
     // handles stay valid only for vvq2_kv_free
@@ -1405,6 +1426,60 @@ int vvq2_nccl_unique_id(void* out) {
     ncclUniqueId id;
     if (ncclGetUniqueId(&id) != ncclSuccess) return fail(VVQ2_ERR_CUDA, "ncclGetUniqueId failed");
     memcpy(out, &id, sizeof id);
+    return 0;
+}
+
+// Map every rank's exchange buffer into this process (CUDA IPC handles
+// all-gathered over the NCCL communicator) for the decode-step exchanges.
+// Returns 1 if the driver refuses (the context then keeps NCCL), a negative
+// error code if CUDA or NCCL fails.
+static int setup_peer(vvq2_ctx* c) {
+    const vvq2_hparams& hp = c->hp;
+    vvq2_ctx::Part& P = c->pt;
+    if (P.world > PEER_MAX) return 1;
+    // a decode step's rows: the partial down projection, or the attention block
+    const int rows = 2;
+    const int need = std::max(rows * hp.hidden_size * 4, peer_attn_block_bytes(rows, P.nq, hp.head_dim, P.seq_parts));
+    PeerArgs& X = P.px;
+    X.world = P.world;
+    X.rank = P.rank;
+    X.slot_bytes = (need + 255) / 256 * 256;
+    X.err = c->err;
+    uint8_t* buf = nullptr;
+    if (int rc = c->alloc(&buf, peer_buffer_bytes(X.slot_bytes))) return rc;
+    if (int rc = c->alloc(&X.epoch, 1)) return rc;
+    char* hs = nullptr;   // [world][handle]
+    if (int rc = c->alloc(&hs, (size_t)P.world * sizeof(cudaIpcMemHandle_t))) return rc;
+    cudaIpcMemHandle_t h;
+    CU(cudaMemsetAsync(buf, 0, peer_buffer_bytes(X.slot_bytes), c->stream));
+    CU(cudaMemsetAsync(X.epoch, 0, sizeof(unsigned int), c->stream));
+    if (cudaIpcGetMemHandle(&h, buf) != cudaSuccess) {
+        cudaGetLastError();
+        return 1;
+    }
+    CU(cudaMemcpyAsync(hs + (size_t)P.rank * sizeof h, &h, sizeof h, cudaMemcpyHostToDevice, c->stream));
+    if (ncclAllGather(hs + (size_t)P.rank * sizeof h, hs, sizeof h, ncclChar, P.comm, c->stream) != ncclSuccess)
+        return fail(VVQ2_ERR_CUDA, "NCCL all-gather of the exchange buffer handles failed");
+    std::vector<cudaIpcMemHandle_t> all(P.world);
+    CU(cudaMemcpyAsync(all.data(), hs, P.world * sizeof h, cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    X.base[P.rank] = buf;
+    for (int r = 0; r < P.world; ++r) {
+        if (r == P.rank) continue;
+        void* q = nullptr;
+        if (cudaIpcOpenMemHandle(&q, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            return 1;
+        }
+        P.ipc.push_back(q);
+        X.base[r] = static_cast<uint8_t*>(q);
+    }
+    // no rank's first exchange may reach a buffer before its owner cleared it:
+    // every rank cleared its own before the all-gather above; one more
+    // collective orders the mappings before any exchange
+    if (ncclAllGather(hs + (size_t)P.rank * sizeof h, hs, sizeof h, ncclChar, P.comm, c->stream) != ncclSuccess)
+        return fail(VVQ2_ERR_CUDA, "NCCL all-gather failed");
+    CU(cudaStreamSynchronize(c->stream));
     return 0;
 }
 
@@ -1453,6 +1528,14 @@ int vvq2_partition(vvq2_ctx* c, int rank, int world, int seq_parts, const void* 
     if (int rc = c->alloc(&c->LSEg, 2 * rows * hp.n_heads)) return rc;
     if (int rc = c->alloc(&c->meta_rope, rows)) return rc;
     if (int rc = c->alloc(&c->Xp, rows * hp.hidden_size)) return rc;
+    const char* pe = std::getenv("VVQ2_PEER");
+    if (!(pe && pe[0] == '0')) {
+        const int rc = setup_peer(c);
+        if (rc < 0) return rc;        // an error code: CUDA or NCCL failed
+        c->pt.peer = rc == 0;
+        if (rc == 1)                  // the driver refused the mapping: NCCL carries the exchanges
+            fprintf(stderr, "vvq2: peer exchange buffers unavailable, decode exchanges use NCCL\n");
+    }
     return 0;
 }
 
@@ -2120,9 +2203,10 @@ int vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int t
             // the prefill engine's kernel for chunks of more than 256 rows (here at
             // any tile count), else the few-row kernel
             const int nt = t > 256 ? gemm_ws_tile_rows(g, 1) : 0;
-            CUtensorMap mt;
+            CUtensorMap mt, wq[4];
             if (nt && !make_act_map(&mt, dxh, t, k, nt)) rc = fail(VVQ2_ERR_CUDA, "tensor map");
-            if (!rc) e = nt ? gemm_ws_launch(g, mt, nt, 0) : gemm_tc_launch(g, map, 0);
+            if (nt && !rc && dw.type == W_Q8_0 && !make_ws_weight_maps(wq, g)) rc = fail(VVQ2_ERR_CUDA, "tensor map");
+            if (!rc) e = nt ? gemm_ws_launch(g, mt, wq, nt, 0) : gemm_tc_launch(g, map, 0);
         }
         if (!rc && e == cudaSuccess) e = cudaDeviceSynchronize();
         int herr = 0;

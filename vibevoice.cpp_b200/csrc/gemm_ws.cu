@@ -20,9 +20,11 @@
 //
 // Persistent: one CTA per SM walks the tile list (grouped raster: 16 token
 // tiles at a time against every weight tile, so those token tiles stay in
-// L2 while the weights stream once per group).  The producers run ahead
-// across tile boundaries, so the next tile's first stages are ready while
-// the epilogue drains the accumulators.
+// L2 while the weights stream once per group).  Three rings run ahead of
+// the MMA, across tile boundaries: raw Q8_0 bytes (quants and block scales
+// of 256 rows, by TMA), the dequantized f16 A tiles, the f16 token tiles.
+// The producers read the raw ring from shared memory 512 contiguous bytes
+// per warp instruction, so no weight byte passes the L1 load path.
 //
 // Accumulator layouts per epilogue:
 //   RESID / STORE  acc0 = features n0..n0+127, acc1 = n0+128..n0+255
@@ -32,11 +34,11 @@
 //                  i + hd/2) of 256/hd heads, so the NEOX pair of a thread's
 //                  lane sits in its own two accumulators
 //
-// CTA: 18 warps.  warp 0: TMEM allocation + TMA producer (lane 0); warp 1:
-// MMA issuer (lane 0); warps 2-9: weight producers (one A row per thread);
-// warps 10-17: epilogue (two per TMEM lane quarter, alternating 32-column
-// chunks).  Every wait is bounded; a timeout sets args.err and unwinds
-// without leaving TMEM allocated.
+// CTA: 19 warps.  warp 0: TMEM allocation + token TMA (lane 0); warp 1: MMA
+// issuer (lane 0); warp 2: raw-weight TMA (lane 0, Q8_0); warps 3-10:
+// weight producers; warps 11-18: epilogue (two per TMEM lane quarter,
+// alternating 32-column chunks).  Every wait is bounded; a timeout sets
+// args.err and unwinds without leaving TMEM allocated.
 #include <algorithm>
 
 #include "common.cuh"
@@ -52,16 +54,19 @@ constexpr int WM = 128;                          // weight rows per accumulator 
 constexpr int BK = 64;                           // K per stage: 128 bytes of f16, one swizzle row
 constexpr int MAX_NT = 256;                      // token rows per tile (MMA N)
 constexpr int A_BYTES = WM * BK * 2;             // 16 KB per accumulator's weight tile
-constexpr int B_BYTES = MAX_NT * BK * 2;         // 32 KB token tile
-constexpr int STAGE_BYTES = 2 * A_BYTES + B_BYTES;
-constexpr int STAGES = 3;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;   // + alignment slack
-constexpr int N_PROD = 8;                        // producer warps: 256 threads, one A row each
+constexpr int A_STAGE = 2 * A_BYTES;             // both accumulators' A operands
+constexpr int B_STAGE = MAX_NT * BK * 2;         // 32 KB token tile
+constexpr int RQ_BYTES = 2 * WM * BK;            // raw Q8_0 quants of 256 rows x 64
+constexpr int R_STAGE = RQ_BYTES + 2 * WM * 16;  // + 16 bytes of block scales per row (4 k-blocks)
+constexpr int A_STAGES = 2, B_STAGES = 3, R_STAGES = 3;
+constexpr int B_OFF = A_STAGES * A_STAGE, R_OFF = B_OFF + B_STAGES * B_STAGE;
+constexpr int SMEM_BYTES = R_OFF + R_STAGES * R_STAGE + 1024;   // + alignment slack
+constexpr int N_PROD = 8;                        // producer warps: 256 threads
 constexpr int N_EPI = 8;                         // epilogue warps
-constexpr int THREADS = 32 * (2 + N_PROD + N_EPI);
+constexpr int PROD0 = 3, EPI0 = PROD0 + N_PROD;  // first producer / epilogue warp
+constexpr int THREADS = 32 * (EPI0 + N_EPI);
 constexpr int TMEM_COLS = 512;                   // acc0 at column 0, acc1 at column 256
 constexpr int TGROUP = 16;                       // token tiles per raster group
-constexpr int PD = 3;                            // Q8_0 k-blocks fetched ahead of their conversion
 
 struct Sched {
     int wt, tt, nt, nk, n_tiles;
@@ -93,21 +98,44 @@ __device__ __forceinline__ int a_row(const GemmArgs& a, int wi, int p, const Dev
     }
 }
 
+// A row (0..255) fed by row rho of the tile's raw weight rows (the tile's
+// 256 matrix rows in order; SwiGLU: 128 gate rows, then the same 128 up rows)
+template <int EPI>
+__device__ __forceinline__ int a_of_raw(const GemmArgs& a, int rho) {
+    if constexpr (EPI == EPI_QKV) {
+        const int half = a.hd >> 1, hh = rho / a.hd, rem = rho % a.hd;
+        return (rem / half) * WM + hh * half + rem % half;
+    } else {
+        return rho;
+    }
+}
+
 template <int WT, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
-    k_gemm_ws(const __grid_constant__ CUtensorMap tmX, const GemmArgs a, const Sched sc) {
+    k_gemm_ws(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmQ0,
+              const __grid_constant__ CUtensorMap tmQ1, const __grid_constant__ CUtensorMap tmS0,
+              const __grid_constant__ CUtensorMap tmS1, const GemmArgs a, const Sched sc) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull, tempty, drain;
+    __shared__ __align__(8) uint64_t a_full[A_STAGES], a_empty[A_STAGES], b_full[B_STAGES], b_empty[B_STAGES];
+    __shared__ __align__(8) uint64_t r_full[R_STAGES], r_empty[R_STAGES], tfull, tempty, drain;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     asm volatile("griddepcontrol.launch_dependents;");
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            tc::mbar_init(&full[s], 1 + 32 * N_PROD);
-            tc::mbar_init(&empty[s], 1);
+        for (int s = 0; s < A_STAGES; ++s) {
+            tc::mbar_init(&a_full[s], 32 * N_PROD);
+            tc::mbar_init(&a_empty[s], 1);
+        }
+        for (int s = 0; s < B_STAGES; ++s) {
+            tc::mbar_init(&b_full[s], 1);
+            tc::mbar_init(&b_empty[s], 1);
+        }
+        for (int s = 0; s < R_STAGES; ++s) {
+            tc::mbar_init(&r_full[s], 1);
+            tc::mbar_init(&r_empty[s], 32 * N_PROD);
         }
         tc::mbar_init(&tfull, 1);
         tc::mbar_init(&tempty, N_EPI);
@@ -132,20 +160,20 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---- TMA producer: the token tile of every stage
+            // ---- token TMA: the B operand of every k-block
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            uint32_t kbg = 0;
+            uint32_t g = 0;
             const uint32_t bytes = (uint32_t)sc.nt * BK * 2;
             for (int id = blockIdx.x; id < sc.n_tiles && !aborted(); id += gridDim.x) {
                 int wi, ti;
                 sc.tile(id, wi, ti);
                 const int t0 = ti * sc.nt;
-                for (int kb = 0; kb < nk; ++kb, ++kbg) {
-                    const int s = kbg % STAGES;
-                    if (kbg >= STAGES && !tc::mbar_wait(&empty[s], ((kbg / STAGES) - 1) & 1)) { fail(); break; }
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % B_STAGES;
+                    if (g >= B_STAGES && !tc::mbar_wait(&b_empty[s], ((g / B_STAGES) - 1) & 1)) { fail(); break; }
                     if (aborted()) break;
-                    tc::mbar_arrive_expect_tx(&full[s], bytes);
-                    tc::tma_load_2d(smem + s * STAGE_BYTES + 2 * A_BYTES, &tmX, kb * BK, t0, &full[s]);
+                    tc::mbar_arrive_expect_tx(&b_full[s], bytes);
+                    tc::tma_load_2d(smem + B_OFF + s * B_STAGE, &tmX, kb * BK, t0, &b_full[s]);
                 }
             }
         }
@@ -153,28 +181,33 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             // ---- MMA issuer: per stage 4 K-steps x 2 accumulators of 128 x nt
             const uint32_t idesc = tc::idesc_f16(WM, sc.nt);
-            uint32_t kbg = 0;
+            uint32_t g = 0;
             int it = 0;
             for (int id = blockIdx.x; id < sc.n_tiles; id += gridDim.x, ++it) {
                 if (it > 0 && !tc::mbar_wait(&tempty, (it - 1) & 1)) { fail(); break; }
                 if (aborted()) break;
                 tc::tc_fence_after();
                 bool ok = true;
-                for (int kb = 0; kb < nk; ++kb, ++kbg) {
-                    const int s = kbg % STAGES;
-                    if (!tc::mbar_wait(&full[s], (kbg / STAGES) & 1)) { fail(); ok = false; break; }
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int sa = g % A_STAGES, sb = g % B_STAGES;
+                    if (!tc::mbar_wait(&a_full[sa], (g / A_STAGES) & 1) || !tc::mbar_wait(&b_full[sb], (g / B_STAGES) & 1)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
                     if (aborted()) { ok = false; break; }
                     tc::tc_fence_after();
-                    uint8_t* st = smem + s * STAGE_BYTES;
-                    const uint64_t da0 = tc::desc_sw128(st), da1 = tc::desc_sw128(st + A_BYTES);
-                    const uint64_t db = tc::desc_sw128(st + 2 * A_BYTES);
+                    uint8_t* sta = smem + sa * A_STAGE;
+                    const uint64_t da0 = tc::desc_sw128(sta), da1 = tc::desc_sw128(sta + A_BYTES);
+                    const uint64_t db = tc::desc_sw128(smem + B_OFF + sb * B_STAGE);
 #pragma unroll
                     for (int k16 = 0; k16 < BK / 16; ++k16) {
                         const uint32_t acc = (kb | k16) != 0;
                         tc::mma_f16(tmem, da0 + 2 * k16, db + 2 * k16, idesc, acc);
                         tc::mma_f16(tmem + 256, da1 + 2 * k16, db + 2 * k16, idesc, acc);
                     }
-                    tc::mma_commit(&empty[s]);
+                    tc::mma_commit(&a_empty[sa]);
+                    tc::mma_commit(&b_empty[sb]);
                 }
                 if (!ok) break;
                 tc::mma_commit(&tfull);
@@ -182,82 +215,95 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc::mma_commit(&drain);   // every issued MMA complete (also after an abort)
             if (!tc::mbar_wait(&drain, 0)) fail();
         }
-    } else if (warp < 2 + N_PROD) {
-        // ---- weight producers: thread p writes A row p (acc p / 128, lane p % 128)
-        const int p = threadIdx.x - 64;
-        uint8_t* const abase = smem + (p >> 7) * A_BYTES;
-        const int r = p & 127;
-        if constexpr (WT == W_Q8_0) {
-            // raw blocks fetched PD k-blocks ahead, across tile boundaries
-            int f_id = blockIdx.x, f_kb = 0;       // the next (tile, k-block) to fetch
-            const uint8_t* f_rp = nullptr;
-            const unsigned short* f_dp = nullptr;
-            auto seek = [&]() {                     // row pointers of tile f_id
-                f_rp = nullptr;
-                if (f_id < sc.n_tiles) {
-                    int wi, ti;
-                    sc.tile(f_id, wi, ti);
-                    const DevW* W;
-                    const int row = a_row<EPI>(a, wi, p, W);
-                    if (row < W->rows) {
-                        f_rp = W->q + (size_t)row * W->row_stride;
-                        f_dp = reinterpret_cast<const unsigned short*>(W->d) + (size_t)row * W->d_stride;
+    } else if (warp == 2) {
+        if (WT == W_Q8_0 && lane == 0) {
+            // ---- raw-weight TMA: quants of the k-block and the block scales
+            // of its group of 4 k-blocks (16 bytes per row, the row's scale
+            // area starts at byte K of the row) for the tile's 256 rows
+            uint32_t g = 0;
+            const int rows_box = EPI == EPI_SWIGLU ? WM : 2 * WM;
+            for (int id = blockIdx.x; id < sc.n_tiles && !aborted(); id += gridDim.x) {
+                int wi, ti;
+                sc.tile(id, wi, ti);
+                const int y = wi * rows_box;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % R_STAGES;
+                    if (g >= R_STAGES && !tc::mbar_wait(&r_empty[s], ((g / R_STAGES) - 1) & 1)) { fail(); break; }
+                    if (aborted()) break;
+                    uint8_t* rs = smem + R_OFF + s * R_STAGE;
+                    const int xs = a.K + 16 * (kb >> 2);
+                    tc::mbar_arrive_expect_tx(&r_full[s], R_STAGE);
+                    tc::tma_load_2d(rs, &tmQ0, kb * BK, y, &r_full[s]);
+                    tc::tma_load_2d(rs + RQ_BYTES, &tmS0, xs, y, &r_full[s]);
+                    if (EPI == EPI_SWIGLU) {
+                        tc::tma_load_2d(rs + WM * BK, &tmQ1, kb * BK, y, &r_full[s]);
+                        tc::tma_load_2d(rs + RQ_BYTES + WM * 16, &tmS1, xs, y, &r_full[s]);
                     }
                 }
-            };
-            auto fetch = [&](uint4 (&q)[4], uint32_t& d2) {
-                if (f_rp) {
-                    const int k0 = f_kb * BK;
+            }
+        }
+    } else if (warp < EPI0) {
+        // ---- weight producers
+        const int t = threadIdx.x - 32 * PROD0;
+        if constexpr (WT == W_Q8_0) {
+            // thread (w, l) converts 16-byte chunk c = l % 4 of raw rows
+            // 8w + l/4 + 64i (i = 0..3): a warp reads 8 whole 64-byte rows,
+            // 512 contiguous bytes, per shared load
+            const int w = t >> 5, l = t & 31, c = l & 3;
+            int rho[4], aoff[4];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) q[i] = __ldg(reinterpret_cast<const uint4*>(f_rp + k0) + i);
-                    d2 = __ldg(reinterpret_cast<const unsigned int*>(f_dp + k0 / 32));
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) q[i] = make_uint4(0, 0, 0, 0);
-                    d2 = 0u;
-                }
-                if (++f_kb == nk) {
-                    f_kb = 0;
-                    f_id += gridDim.x;
-                    seek();
-                }
-            };
-            seek();
-            uint4 raw[PD][4];
-            uint32_t dd[PD];
-#pragma unroll
-            for (int d = 0; d < PD; ++d) fetch(raw[d], dd[d]);
-            const uint32_t total = (uint32_t)((sc.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * nk;
+            for (int i = 0; i < 4; ++i) {
+                rho[i] = 8 * w + (l >> 2) + 64 * i;
+                const int p = a_of_raw<EPI>(a, rho[i]);
+                aoff[i] = (p >> 7) * A_BYTES + (p & 127) * 128;
+            }
+            uint32_t g = 0;
             bool stop = false;
-            for (uint32_t kbg = 0; kbg < total && !stop; kbg += PD) {
-#pragma unroll
-                for (int d = 0; d < PD; ++d) {
-                    const uint32_t g = kbg + d;
-                    if (g >= total) break;
-                    const int s = g % STAGES;
-                    if (g >= STAGES && !tc::mbar_wait(&empty[s], ((g / STAGES) - 1) & 1)) { fail(); stop = true; break; }
+            for (int id = blockIdx.x; id < sc.n_tiles && !stop; id += gridDim.x) {
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int sr = g % R_STAGES, sa = g % A_STAGES;
+                    if (!tc::mbar_wait(&r_full[sr], (g / R_STAGES) & 1) ||
+                        (g >= A_STAGES && !tc::mbar_wait(&a_empty[sa], ((g / A_STAGES) - 1) & 1))) {
+                        fail();
+                        stop = true;
+                        break;
+                    }
                     if (aborted()) { stop = true; break; }
-                    q8_0_tile_row(raw[d], dd[d], abase + s * STAGE_BYTES, r);
-                    fetch(raw[d], dd[d]);
+                    const uint8_t* rs = smem + R_OFF + sr * R_STAGE;
+                    uint4 v[4];
+                    unsigned short d[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        v[i] = *reinterpret_cast<const uint4*>(rs + rho[i] * BK + c * 16);
+                        d[i] = *reinterpret_cast<const unsigned short*>(rs + RQ_BYTES + rho[i] * 16 + (kb & 3) * 4 +
+                                                                        (c >> 1) * 2);
+                    }
+                    tc::mbar_arrive(&r_empty[sr]);   // this thread's raw bytes are in registers
+                    uint8_t* st = smem + sa * A_STAGE;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) q8_0_chunk_pair(v[i], d[i], st + aoff[i], (aoff[i] >> 7) & 7, 2 * c);
                     tc::fence_proxy_async_smem();
-                    tc::mbar_arrive(&full[s]);
+                    tc::mbar_arrive(&a_full[sa]);
                 }
             }
         } else {
-            uint32_t kbg = 0;
+            // other types: thread t produces A row t from global memory
+            uint8_t* const aacc = smem + (t >> 7) * A_BYTES;
+            const int r = t & 127;
+            uint32_t g = 0;
             bool stop = false;
             for (int id = blockIdx.x; id < sc.n_tiles && !stop; id += gridDim.x) {
                 int wi, ti;
                 sc.tile(id, wi, ti);
                 const DevW* W;
-                const int row = a_row<EPI>(a, wi, p, W);
-                for (int kb = 0; kb < nk; ++kb, ++kbg) {
-                    const int s = kbg % STAGES;
-                    if (kbg >= STAGES && !tc::mbar_wait(&empty[s], ((kbg / STAGES) - 1) & 1)) { fail(); stop = true; break; }
+                const int row = a_row<EPI>(a, wi, t, W);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int sa = g % A_STAGES;
+                    if (g >= A_STAGES && !tc::mbar_wait(&a_empty[sa], ((g / A_STAGES) - 1) & 1)) { fail(); stop = true; break; }
                     if (aborted()) { stop = true; break; }
-                    produce_row<WT>(*W, row, kb * BK, abase + s * STAGE_BYTES, r);
+                    produce_row<WT>(*W, row, kb * BK, aacc + sa * A_STAGE, r);
                     tc::fence_proxy_async_smem();
-                    tc::mbar_arrive(&full[s]);
+                    tc::mbar_arrive(&a_full[sa]);
                 }
             }
         }
@@ -265,7 +311,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---- epilogue: warp w reads TMEM lanes 32*(w%4)..+31 of both
         // accumulators, 32-column chunks e, e+2, e+4, ... (e = its set)
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        const int q = warp & 3, e = (warp - 2 - N_PROD) >> 2;
+        const int q = warp & 3, e = (warp - EPI0) >> 2;
         const int r = q * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
         int it = 0;
@@ -349,25 +395,34 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const bool is_q = h < a.nq, is_k = !is_q && rot;
                         const int kvh = is_q ? 0 : (is_k ? h - a.nq : h - a.nq - a.nkv);
                         if (ok0) {
+                            // 4 tokens at a time: their RoPE table loads go out
+                            // before the stores
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) {
-                                if (j < ne) {
-                                    const int t = tb + j;
+                            for (int j0 = 0; j0 < 32; j0 += 4) {
+                                if (j0 >= ne) break;
+                                float2 cs[4];
+#pragma unroll
+                                for (int jj = 0; jj < 4; ++jj)
+                                    cs[jj] = (rot && j0 + jj < ne) ? __ldg(&a.rope_cs[(size_t)(tb + j0 + jj) * half + i])
+                                                                   : make_float2(1.f, 0.f);
+#pragma unroll
+                                for (int jj = 0; jj < 4; ++jj) {
+                                    const int j = j0 + jj;
+                                    if (j >= ne) break;
                                     float v0 = __fadd_rn(__uint_as_float(u0[j]), b0);
                                     float v1 = __fadd_rn(__uint_as_float(u1[j]), b1);
                                     if (rot) {
-                                        const float2 cs = a.rope_cs[(size_t)t * half + i];
-                                        const float y0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
-                                        const float y1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+                                        const float y0 = __fsub_rn(__fmul_rn(v0, cs[jj].x), __fmul_rn(v1, cs[jj].y));
+                                        const float y1 = __fadd_rn(__fmul_rn(v0, cs[jj].y), __fmul_rn(v1, cs[jj].x));
                                         v0 = y0;
                                         v1 = y1;
                                     }
                                     if (is_q) {
-                                        float* qd = a.y + (size_t)t * a.y_stride + h * hd;
+                                        float* qd = a.y + (size_t)(tb + j) * a.y_stride + h * hd;
                                         qd[i] = v0;
                                         qd[i + half] = v1;
                                     } else {
-                                        const RowMeta rm = a.meta[t];
+                                        const RowMeta rm = a.meta[tb + j];
                                         if (rm.cidx >= 0) {   // cidx < 0: another rank stores this position
                                             __half* dst = (is_k ? a.kv.k : a.kv.v) + kv_offset(a.kv, rm.seq, rm.cidx, kvh);
                                             dst[i] = __float2half_rn(v0);
@@ -405,7 +460,7 @@ int weight_tiles(const GemmArgs& a) {
 }
 
 template <int EPI>
-cudaError_t launch_ws(const GemmArgs& a, const CUtensorMap& tm, int nt, cudaStream_t st) {
+cudaError_t launch_ws(const GemmArgs& a, const CUtensorMap& tm, const CUtensorMap* wq, int nt, cudaStream_t st) {
     Sched sc;
     sc.wt = weight_tiles(a);
     sc.nt = nt;
@@ -424,11 +479,11 @@ cudaError_t launch_ws(const GemmArgs& a, const CUtensorMap& tm, int nt, cudaStre
     cfg.numAttrs = 1;
     cudaError_t e;
     switch (a.w0.type) {
-        case W_Q8_0: e = cudaLaunchKernelEx(&cfg, k_gemm_ws<W_Q8_0, EPI>, tm, a, sc); break;
-        case W_Q5_K: e = cudaLaunchKernelEx(&cfg, k_gemm_ws<W_Q5_K, EPI>, tm, a, sc); break;
-        case W_Q6_K: e = cudaLaunchKernelEx(&cfg, k_gemm_ws<W_Q6_K, EPI>, tm, a, sc); break;
-        case W_F16: e = cudaLaunchKernelEx(&cfg, k_gemm_ws<W_F16, EPI>, tm, a, sc); break;
-        case W_F32: e = cudaLaunchKernelEx(&cfg, k_gemm_ws<W_F32, EPI>, tm, a, sc); break;
+        case W_Q8_0: e = cudaLaunchKernelEx(&cfg, k_gemm_ws<W_Q8_0, EPI>, tm, wq[0], wq[1], wq[2], wq[3], a, sc); break;
+        case W_Q5_K: e = cudaLaunchKernelEx(&cfg, k_gemm_ws<W_Q5_K, EPI>, tm, tm, tm, tm, tm, a, sc); break;
+        case W_Q6_K: e = cudaLaunchKernelEx(&cfg, k_gemm_ws<W_Q6_K, EPI>, tm, tm, tm, tm, tm, a, sc); break;
+        case W_F16: e = cudaLaunchKernelEx(&cfg, k_gemm_ws<W_F16, EPI>, tm, tm, tm, tm, tm, a, sc); break;
+        case W_F32: e = cudaLaunchKernelEx(&cfg, k_gemm_ws<W_F32, EPI>, tm, tm, tm, tm, tm, a, sc); break;
         default: return cudaErrorInvalidValue;
     }
     note_launch();
@@ -478,17 +533,21 @@ cudaError_t gemm_ws_prepare() {
     return prepare_ws<EPI_STORE>();
 }
 
-cudaError_t gemm_ws_launch(const GemmArgs& a, const CUtensorMap& tmX, int nt, cudaStream_t st) {
+int gemm_ws_weight_box_rows(const GemmArgs& a) { return a.epi == EPI_SWIGLU ? WM : 2 * WM; }
+
+cudaError_t gemm_ws_launch(const GemmArgs& a, const CUtensorMap& tmX, const CUtensorMap* wq, int nt,
+                           cudaStream_t st) {
     if (a.K % BK || a.T <= 0 || a.N <= 0 || nt < 128 || nt > MAX_NT || nt % 32) return cudaErrorInvalidValue;
     if (a.kpart || a.epi == EPI_ARGMAX) return cudaErrorInvalidValue;
     if (a.epi == EPI_QKV && ((2 * WM) % a.hd || (a.hd != 32 && a.hd != 64 && a.hd != 128)))
         return cudaErrorInvalidValue;
     if (a.epi == EPI_SWIGLU && (a.w1.type != a.w0.type || a.w1.rows != a.w0.rows)) return cudaErrorInvalidValue;
+    if (a.w0.type == W_Q8_0 && (!wq || a.w0.cols != a.K)) return cudaErrorInvalidValue;
     switch (a.epi) {
-        case EPI_QKV: return launch_ws<EPI_QKV>(a, tmX, nt, st);
-        case EPI_RESID: return launch_ws<EPI_RESID>(a, tmX, nt, st);
-        case EPI_SWIGLU: return launch_ws<EPI_SWIGLU>(a, tmX, nt, st);
-        case EPI_STORE: return launch_ws<EPI_STORE>(a, tmX, nt, st);
+        case EPI_QKV: return launch_ws<EPI_QKV>(a, tmX, wq, nt, st);
+        case EPI_RESID: return launch_ws<EPI_RESID>(a, tmX, wq, nt, st);
+        case EPI_SWIGLU: return launch_ws<EPI_SWIGLU>(a, tmX, wq, nt, st);
+        case EPI_STORE: return launch_ws<EPI_STORE>(a, tmX, wq, nt, st);
         default: return cudaErrorInvalidValue;
     }
 }

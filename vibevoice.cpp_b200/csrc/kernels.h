@@ -75,11 +75,39 @@ cudaError_t splitk_epilogue_launch(const GemmArgs& a, cudaStream_t st);
 
 // Persistent many-row GEMM with the weight dequantization fused (gemm_ws.cu):
 // QKV / RESID / SWIGLU / STORE epilogues, no split-K.  tmX: f16 activations
-// [T][K], box 64 x nt.  gemm_ws_tile_rows picks nt for a launch (0: fewer
-// than min_tiles tiles, <= 0 meaning one per SM; use gemm_tc_launch).
+// [T][K], box 64 x nt.  Q8_0 weights also take wq[4]: byte maps of the
+// repacked rows of w0 and w1 (dims {row_stride, rows}, no swizzle), box
+// {64, r} for the quants (wq[0], wq[1]) and {16, r} for the block scales
+// (wq[2], wq[3]), r = gemm_ws_weight_box_rows.  gemm_ws_tile_rows picks nt
+// for a launch (0: fewer than min_tiles tiles, <= 0 meaning one per SM; use
+// gemm_tc_launch).
 int gemm_ws_tile_rows(const GemmArgs& a, int min_tiles);
-cudaError_t gemm_ws_launch(const GemmArgs& a, const CUtensorMap& tmX, int nt, cudaStream_t st);
+int gemm_ws_weight_box_rows(const GemmArgs& a);
+cudaError_t gemm_ws_launch(const GemmArgs& a, const CUtensorMap& tmX, const CUtensorMap* wq, int nt,
+                           cudaStream_t st);
 cudaError_t gemm_ws_prepare();
+
+// ------------------------------------------------------ peer exchanges (peer.cu)
+// Every rank of a partitioned context owns one exchange buffer mapped into
+// all ranks: [PEER_HDR bytes: flag (last epoch) per sender][2 parities]
+// [PEER_MAX senders][slot_bytes].
+constexpr int PEER_MAX = 8;
+constexpr int PEER_HDR = 256;
+struct PeerArgs {
+    int world = 0, rank = 0;
+    uint8_t* base[PEER_MAX] = {};        // rank r's buffer as mapped in this process
+    int slot_bytes = 0;
+    unsigned int* epoch = nullptr;       // exchanges so far (this rank's device counter)
+    int* err = nullptr;                  // set to 6 when a wait for a peer runs out
+};
+inline size_t peer_buffer_bytes(int slot_bytes) { return PEER_HDR + 2 * (size_t)PEER_MAX * slot_bytes; }
+// x[0..n) += sum over ranks of part[0..n) (n a multiple of 4)
+cudaError_t peer_reduce_add_launch(const PeerArgs& p, const float* part, int n, float* x, cudaStream_t st);
+// attention outputs o [M][nq_l*hd] f16 (+ lse [M][nq_l] with two sequence
+// parts) of all ranks -> out [M][nq*hd] f32, parts merged by log-sum-exp
+int peer_attn_block_bytes(int M, int nq_l, int hd, int seq_parts);
+cudaError_t peer_attn_gather_launch(const PeerArgs& p, const __half* o, const float* lse, int M, int nq_l, int hd,
+                                    int seq_parts, float* out, cudaStream_t st);
 
 // ------------------------------------------------------ persistent decode step
 struct MegaLayer {
