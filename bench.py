@@ -199,15 +199,19 @@ def c3_measure(eng, hp, torch, dist, rank, world, sh, steps, warmup=2):
     greedy decode step per stream per iteration.  The streams are split over
     the ranks (data parallel, no collective on the data path); each rank
     decodes its rows as one batched step (tensor-core path, split-K attention
-    over each row's own length).  Value: all ranks' rows per second, timed as
-    the max over ranks."""
+    over each row's own length).  The cache is paged: the rows share a pool
+    of exactly the 64-position pages their lengths need (an identity-mapped
+    cache would reserve the longest row's pages for every row).  Value: all
+    ranks' rows per second, timed as the max over ranks."""
     streams = 64
     mine = [s for s in range(streams) if s % world == rank]
     rows = 2 * len(mine)
     rng = np.random.default_rng(SEED + 3)
     lens_all = rng.integers(64, 2049, size=streams)
     lens = np.repeat(lens_all[mine], 2)
-    kv = eng.kv(rows, int(lens.max()) + warmup + steps + 8)
+    max_seq = int(lens.max()) + warmup + steps + 8
+    pool = int(sum((int(L) + warmup + steps + 63) // 64 for L in lens))
+    kv = eng.kv(rows, max_seq, pool_pages=pool)
     w = hp["n_kv_heads"] * hp["head_dim"]
     g = torch.Generator(device="cuda").manual_seed(SEED + 3 + rank)
     for r in range(rows):
@@ -241,6 +245,7 @@ def c3_measure(eng, hp, torch, dist, rank, world, sh, steps, warmup=2):
                         "64..2048, one greedy step per stream per iteration",
             "value": round(2 * streams * steps / (ms / 1000.0), 1), "unit": "tokens/s",
             "ms_per_step": round(ms / steps, 3), "rows_per_gpu": rows, "n_gpus": world, "steps": steps,
+            "kv_pages": {"pool": pool, "identity_would_reserve": rows * ((max_seq + 63) // 64)},
             "scaling": "strong", "parallelism": f"data parallel over {world} GPU(s), no collectives"}
 
 
@@ -252,7 +257,8 @@ def c5_measure(vvq2, synth, torch, dist, rank, local, world, sh, T, steps):
     """Config 5: the 7B-shaped Q8_0 ASR stack, causal prefill of T prompt
     embeddings (N(0,1)), then `steps` greedy decode steps of the stream.  At
     N > 1 the attention is partitioned (vvq2_partition): KV heads over 2/4
-    GPUs, KV heads x sequence halves over 8, with NCCL (O, LSE) combines;
+    GPUs, KV heads x interleaved sequence parts over 8; prefill exchanges
+    run on NCCL, the decode step's on peer memory (VVQ2_PEER=0: NCCL);
     each rank decodes the same single stream.  Times are CUDA events on the
     launching stream, max over ranks.  Decode bytes per step: the GGUF
     weights plus the f16 K/V of every key (57,344 B per position)."""
@@ -321,7 +327,9 @@ def c5_measure(vvq2, synth, torch, dist, rank, local, world, sh, T, steps):
                     f"vocab 152064), causal prefill of {T} prompt embeddings, then {steps} greedy decode steps, "
                     f"batch 1", "n_gpus": world,
         "partition": "none" if world == 1 else (f"KV heads over {world} GPUs" if seq_parts == 1 else
-                                                 f"KV heads x sequence halves over {world} GPUs"),
+                                                 f"KV heads x interleaved sequence parts over {world} GPUs"),
+        "decode_exchange": None if world == 1 else
+        ("nccl" if os.environ.get("VVQ2_PEER", "1").startswith("0") else "peer memory (CUDA IPC), one kernel each"),
         "prefill": {"tokens_per_s": round(T / (pre_ms / 1000.0), 1), "ms": round(pre_ms, 1),
                     "tflops_per_gpu": round((lin + att) / (pre_ms / 1000.0) / 1e12 / world, 1),
                     "frac_of_peak": round((lin + att) / (pre_ms / 1000.0) / 1e12 / world / burst, 4),

@@ -118,6 +118,17 @@ int  vvq2_set_output(vvq2_ctx* ctx, const vvq2_tensor* output_norm,
  * cond/uncond pair is n_seqs = 2) of up to max_seq positions, every layer.
  * Storage is an f16 paged cache (64-position pages) on the context's device. */
 int  vvq2_kv_init(vvq2_ctx* ctx, int n_seqs, int max_seq, vvq2_kv** out);
+/* The same cache backed by a shared pool of pool_pages 64-position pages
+ * (per layer) instead of n_seqs * ceil(max_seq / 64): a sequence takes pages
+ * as its writes need them (vvq2_forward, vvq2_decode_step, load_prefix,
+ * set_past_len to a longer length) and gives back the pages past a shorter
+ * vvq2_kv_set_past_len.  A write that finds too few free pages fails with
+ * VVQ2_ERR_OUT_OF_MEMORY and changes nothing.  This sizes memory by the
+ * tokens actually held, as the reference's per-sequence ResidentKV
+ * allocation does (src/qwen2.cpp:207-246), for many ragged streams. */
+int  vvq2_kv_init_paged(vvq2_ctx* ctx, int n_seqs, int max_seq, int pool_pages, vvq2_kv** out);
+/* Free pages of a paged cache (0 for an unpaged one). */
+int  vvq2_kv_free_pages(const vvq2_kv* kv);
 void vvq2_kv_free(vvq2_kv* kv);
 
 /* Uploads a K/V prefix for one sequence and layer in the voice-GGUF layout

@@ -35,8 +35,8 @@ struct DevW {
 struct RowMeta {
     int seq;    // KV sequence id
     int pos;    // absolute position (RoPE, causal limit: keys j <= pos).  A rank that
-                // holds a later part of a sequence's keys sees pos - part_start here
-                // (its cache indices start at the part) and gets RoPE from its own table
+                // holds one sequence part sees the cache index of its last key at or
+                // before the position here (zz_local_row) and gets RoPE from its own table
     int cidx;   // cache index the new K/V row is written to (< 0: another rank stores it)
     int kvlen;  // keys present after the step's writes (past_len + n_tok)
 };
@@ -51,6 +51,36 @@ struct KvLayer {
     int hd = 0;
     int n_pages = 0;                    // pages in the pool (0: unknown)
 };
+
+// Sequence parts of a partitioned context interleave whole pages: page p of
+// every sequence belongs to part (0, 1, 1, 0)[p % 4], so each part holds
+// half of every 256-position span and a causal prompt of any length (and any
+// chunking) gives both parts the same attention work -- keys early in the
+// sequence are seen by more queries, and each part holds as many early as
+// late keys.  A part stores its positions in order: position p sits at cache
+// index zz_count(part, p), the number of the part's positions below p.
+__host__ __device__ inline int zz_part(int p) { return ((p / KV_PAGE) % 4 == 1 || (p / KV_PAGE) % 4 == 2) ? 1 : 0; }
+__host__ __device__ inline int zz_count(int part, int n) {
+    const int period = 4 * KV_PAGE, full = n / period, rem = n % period;
+    int c = full * (period / 2);
+    for (int j = 0; j < 4; ++j) {
+        const int inpage = rem - j * KV_PAGE;
+        if (zz_part(j * KV_PAGE) == part) c += inpage < 0 ? 0 : (inpage > KV_PAGE ? KV_PAGE : inpage);
+    }
+    return c;
+}
+// A row (true position, cache index, key count) as part `part` sees it: pos
+// becomes the cache index of the part's last position <= pos (-1 if none),
+// so the kernels' causal limit min(pos + 1, kvlen) counts exactly the part's
+// keys at positions <= pos; kvlen the part's positions below kvlen; cidx < 0
+// when the other part stores the row.
+__host__ __device__ inline RowMeta zz_local_row(RowMeta r, int part) {
+    RowMeta l = r;
+    l.pos = zz_count(part, r.pos + 1) - 1;
+    l.cidx = zz_part(r.cidx) == part ? zz_count(part, r.cidx) : -1;
+    l.kvlen = zz_count(part, r.kvlen);
+    return l;
+}
 
 __device__ __forceinline__ size_t kv_offset(const KvLayer& kv, int seq, int cidx, int kvh) {
     const int page = __ldg(kv.block_table + (size_t)seq * kv.max_pages + cidx / KV_PAGE);

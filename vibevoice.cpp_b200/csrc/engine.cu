@@ -8,6 +8,7 @@
 // pool, positions and the causal mask are computed by the kernels, and a step
 // is a fixed sequence of launches on one stream.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <algorithm>
@@ -18,6 +19,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/vvq2_capi.h"
@@ -46,6 +48,45 @@ EncodeTiledFn encode_fn() {
             fn = reinterpret_cast<EncodeTiledFn>(p);
     }
     return fn;
+}
+
+// NCCL, resolved on first use (partitioned contexts only) instead of at
+// load time: a process that loads this library before another user of NCCL
+// (torch, for one) would otherwise bind its soname first and hand that user
+// an older copy.  An NCCL already in the process is reused.
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*);
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int);
+    ncclResult_t (*CommSplit)(ncclComm_t, int, int, ncclComm_t*, ncclConfig_t*);
+    ncclResult_t (*CommDestroy)(ncclComm_t);
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*GroupStart)();
+    ncclResult_t (*GroupEnd)();
+};
+
+const NcclApi* nccl() {
+    static NcclApi api;
+    static const bool ok = [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW);
+        if (!h) return false;
+        bool all = true;
+        auto sym = [&](auto& f, const char* name) {
+            f = reinterpret_cast<std::remove_reference_t<decltype(f)>>(dlsym(h, name));
+            all = all && f;
+        };
+        sym(api.GetUniqueId, "ncclGetUniqueId");
+        sym(api.CommInitRank, "ncclCommInitRank");
+        sym(api.CommSplit, "ncclCommSplit");
+        sym(api.CommDestroy, "ncclCommDestroy");
+        sym(api.AllGather, "ncclAllGather");
+        sym(api.AllReduce, "ncclAllReduce");
+        sym(api.GroupStart, "ncclGroupStart");
+        sym(api.GroupEnd, "ncclGroupEnd");
+        return all;
+    }();
+    return ok ? &api : nullptr;
 }
 
 // 2-D f16 activation matrix [rows][cols] (row-major) as a TMA map with a
@@ -283,9 +324,14 @@ struct vvq2_kv {
     __half* v = nullptr;
     int* block_table = nullptr;
     std::vector<int> past;
-    // partitioned contexts, 2 sequence parts: first position of part 1 per
-    // sequence (-1: not yet fixed; set by the sequence's first write)
-
+    // Paged caches (vvq2_kv_init_paged): pool_pages pages per layer pool are
+    // handed to sequences as they grow and returned when they shrink; every
+    // unmapped block-table entry points at page null_page (one more page,
+    // zero, never handed out), so a kernel reading past a sequence's pages
+    // stays inside the pool.  bt mirrors the device block table.
+    bool paged = false;
+    int pool_pages = 0, null_page = 0;
+    std::vector<int> bt, free_pages;
     KvLayer layer(int li) const {
         KvLayer L;
         L.k = k + (size_t)li * layer_elems;
@@ -698,7 +744,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         //    chunks (head_dim 64/128); rows of one token each (batched decode
         //    of many streams) and other head sizes use the split-K decode kernel
         if ((hd == 64 || hd == 128) && nt > 1) {
-            const int64_t kv_rows = (int64_t)kv->n_seqs * kv->max_pages * nkv * KV_PAGE;
+            const int64_t kv_rows = (int64_t)(kv->layer_elems / hd);   // every page of the pool
             CUtensorMap mk, mv;
             if (!make_kv_map(&mk, kvl.k, kv_rows, hd) || !make_kv_map(&mv, kvl.v, kv_rows, hd))
                 return fail(VVQ2_ERR_CUDA, "kv tensor map");
@@ -766,16 +812,16 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         } else if (parted) {
             // the two sequence parts of this head group: (O, LSE) all-gather, merge
             if (c->pt.seq_parts > 1) {
-                if (ncclGroupStart() != ncclSuccess ||
-                    ncclAllGather(c->ATTl, c->ATTg, (size_t)M * qw_l, ncclHalf, c->pt.pair, st) != ncclSuccess ||
-                    ncclAllGather(c->LSEl, c->LSEg, (size_t)M * nq, ncclFloat, c->pt.pair, st) != ncclSuccess ||
-                    ncclGroupEnd() != ncclSuccess)
+                if (nccl()->GroupStart() != ncclSuccess ||
+                    nccl()->AllGather(c->ATTl, c->ATTg, (size_t)M * qw_l, ncclHalf, c->pt.pair, st) != ncclSuccess ||
+                    nccl()->AllGather(c->LSEl, c->LSEg, (size_t)M * nq, ncclFloat, c->pt.pair, st) != ncclSuccess ||
+                    nccl()->GroupEnd() != ncclSuccess)
                     return fail(VVQ2_ERR_CUDA, "NCCL all-gather of (O, LSE) failed");
                 CU(lse_merge_launch(c->ATTg, c->LSEg, M, nq, hd, c->ATTl, st));
             }
             // head groups: all-gather the output rows, then [group][row][w] -> [row][all heads]
             if (c->pt.head_parts > 1) {
-                if (ncclAllGather(c->ATTl, c->ATTg, (size_t)M * qw_l, ncclHalf, c->pt.heads, st) != ncclSuccess)
+                if (nccl()->AllGather(c->ATTl, c->ATTg, (size_t)M * qw_l, ncclHalf, c->pt.heads, st) != ncclSuccess)
                     return fail(VVQ2_ERR_CUDA, "NCCL all-gather of attention rows failed");
                 CU(gather_rows_launch(c->ATTg, M, c->pt.head_parts, qw_l, c->ATTh, st));
             } else {
@@ -818,7 +864,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
             if (px) {
                 CU(peer_reduce_add_launch(c->pt.px, c->Xp, M * H, c->X, st));
             } else if (parted) {
-                if (ncclAllReduce(c->Xp, c->Xp, (size_t)M * H, ncclFloat, ncclSum, c->pt.comm, st) != ncclSuccess)
+                if (nccl()->AllReduce(c->Xp, c->Xp, (size_t)M * H, ncclFloat, ncclSum, c->pt.comm, st) != ncclSuccess)
                     return fail(VVQ2_ERR_CUDA, "NCCL all-reduce of the down projection failed");
                 CU(add_rows_launch(c->X, c->Xp, (int64_t)M * H, st));
             }
@@ -855,7 +901,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         d.y_stride = H;
         if (int rc = gemm(d, mapF, c->Ah)) return rc;
         if (parted) {
-            if (ncclAllReduce(c->Xp, c->Xp, (size_t)M * H, ncclFloat, ncclSum, c->pt.comm, st) != ncclSuccess)
+            if (nccl()->AllReduce(c->Xp, c->Xp, (size_t)M * H, ncclFloat, ncclSum, c->pt.comm, st) != ncclSuccess)
                 return fail(VVQ2_ERR_CUDA, "NCCL all-reduce of the down projection failed");
             CU(add_rows_launch(c->X, c->Xp, (int64_t)M * H, st));
         }
@@ -970,23 +1016,6 @@ void mega_split(const vvq2_ctx* c, int M, int max_lim, int* split, int* nsplit) 
     *nsplit = (max_lim + s - 1) / s;
 }
 
-// Sequence parts of a partitioned context interleave whole pages: page p of
-// every sequence belongs to part ZZ[p % 4] (0, 1, 1, 0), so each part holds
-// half of every 256-position span and a causal prompt of any length (and any
-// chunking) gives both parts the same attention work -- keys early in the
-// sequence are seen by more queries, and each part holds as many early as
-// late keys.  A part stores its positions in order: position p sits at cache
-// index zz_count(part, p), the number of the part's positions below p.
-constexpr int ZZ_PERIOD = 4 * KV_PAGE;
-inline int zz_part(int p) { return ((p / KV_PAGE) % 4 == 1 || (p / KV_PAGE) % 4 == 2) ? 1 : 0; }
-inline int zz_count(int part, int n) {
-    const int full = n / ZZ_PERIOD, rem = n % ZZ_PERIOD;
-    int c = full * (ZZ_PERIOD / 2);
-    for (int j = 0; j < 4; ++j)
-        if (zz_part(j * KV_PAGE) == part) c += std::min(KV_PAGE, std::max(0, rem - j * KV_PAGE));
-    return c;
-}
-
 // A token row as this rank sees it.  `rope` gets the true position (RoPE
 // table); the returned row has the cache index and key limits of the rank's
 // sequence part: pos becomes the cache index of the part's last position <=
@@ -996,12 +1025,7 @@ inline int zz_count(int part, int n) {
 RowMeta local_row(const vvq2_ctx* c, int seq, int pos, int cidx, int kvlen, RowMeta* rope) {
     RowMeta r{seq, pos, cidx, kvlen};
     if (rope) *rope = r;
-    if (c->pt.seq_parts < 2) return r;
-    const int s = c->pt.s;
-    r.pos = zz_count(s, pos + 1) - 1;
-    r.cidx = zz_part(cidx) == s ? zz_count(s, cidx) : -1;
-    r.kvlen = zz_count(s, kvlen);
-    return r;
+    return c->pt.seq_parts < 2 ? r : zz_local_row(r, c->pt.s);
 }
 
 // Greedy decode step for more rows than the GEMV paths take (many streams at
@@ -1415,7 +1439,7 @@ void vvq2_free(vvq2_ctx* c) {
     }
     if (c->meta_host) cudaFreeHost(c->meta_host);
     for (ncclComm_t m : {c->pt.heads, c->pt.pair, c->pt.comm})
-        if (m) ncclCommDestroy(m);
+        if (m) nccl()->CommDestroy(m);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -1424,7 +1448,8 @@ int vvq2_nccl_unique_id(void* out) {
     if (!out) return fail(VVQ2_ERR_INVALID_ARG, "null id buffer");
     static_assert(sizeof(ncclUniqueId) == VVQ2_NCCL_ID_BYTES, "NCCL unique id size");
     ncclUniqueId id;
-    if (ncclGetUniqueId(&id) != ncclSuccess) return fail(VVQ2_ERR_CUDA, "ncclGetUniqueId failed");
+    if (!nccl()) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "libnccl.so.2 not found");
+    if (nccl()->GetUniqueId(&id) != ncclSuccess) return fail(VVQ2_ERR_CUDA, "ncclGetUniqueId failed");
     memcpy(out, &id, sizeof id);
     return 0;
 }
@@ -1458,7 +1483,7 @@ static int setup_peer(vvq2_ctx* c) {
         return 1;
     }
     CU(cudaMemcpyAsync(hs + (size_t)P.rank * sizeof h, &h, sizeof h, cudaMemcpyHostToDevice, c->stream));
-    if (ncclAllGather(hs + (size_t)P.rank * sizeof h, hs, sizeof h, ncclChar, P.comm, c->stream) != ncclSuccess)
+    if (nccl()->AllGather(hs + (size_t)P.rank * sizeof h, hs, sizeof h, ncclChar, P.comm, c->stream) != ncclSuccess)
         return fail(VVQ2_ERR_CUDA, "NCCL all-gather of the exchange buffer handles failed");
     std::vector<cudaIpcMemHandle_t> all(P.world);
     CU(cudaMemcpyAsync(all.data(), hs, P.world * sizeof h, cudaMemcpyDeviceToHost, c->stream));
@@ -1477,7 +1502,7 @@ static int setup_peer(vvq2_ctx* c) {
     // no rank's first exchange may reach a buffer before its owner cleared it:
     // every rank cleared its own before the all-gather above; one more
     // collective orders the mappings before any exchange
-    if (ncclAllGather(hs + (size_t)P.rank * sizeof h, hs, sizeof h, ncclChar, P.comm, c->stream) != ncclSuccess)
+    if (nccl()->AllGather(hs + (size_t)P.rank * sizeof h, hs, sizeof h, ncclChar, P.comm, c->stream) != ncclSuccess)
         return fail(VVQ2_ERR_CUDA, "NCCL all-gather failed");
     CU(cudaStreamSynchronize(c->stream));
     return 0;
@@ -1513,11 +1538,12 @@ int vvq2_partition(vvq2_ctx* c, int rank, int world, int seq_parts, const void* 
     CU(cudaSetDevice(c->device));
     ncclUniqueId id;
     memcpy(&id, nccl_id, sizeof id);
-    if (ncclCommInitRank(&P.comm, world, id, rank) != ncclSuccess) return fail(VVQ2_ERR_CUDA, "ncclCommInitRank failed");
+    if (!nccl()) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "libnccl.so.2 not found");
+    if (nccl()->CommInitRank(&P.comm, world, id, rank) != ncclSuccess) return fail(VVQ2_ERR_CUDA, "ncclCommInitRank failed");
     // the two ranks of a head group (sequence parts), and the ranks of one part across head groups
-    if (seq_parts > 1 && ncclCommSplit(P.comm, P.g, P.s, &P.pair, nullptr) != ncclSuccess)
+    if (seq_parts > 1 && nccl()->CommSplit(P.comm, P.g, P.s, &P.pair, nullptr) != ncclSuccess)
         return fail(VVQ2_ERR_CUDA, "ncclCommSplit (pair) failed");
-    if (hp_parts > 1 && ncclCommSplit(P.comm, P.s, P.g, &P.heads, nullptr) != ncclSuccess)
+    if (hp_parts > 1 && nccl()->CommSplit(P.comm, P.s, P.g, &P.heads, nullptr) != ncclSuccess)
         return fail(VVQ2_ERR_CUDA, "ncclCommSplit (heads) failed");
     c->pt = P;
     const size_t rows = (size_t)c->prefill_rows;
@@ -1647,31 +1673,38 @@ int vvq2_set_output(vvq2_ctx* c, const vvq2_tensor* on, const vvq2_tensor* lm, c
     return 0;
 }
 
-int vvq2_kv_init(vvq2_ctx* c, int n_seqs, int max_seq, vvq2_kv** out) {
+static int kv_create(vvq2_ctx* c, int n_seqs, int max_seq, int pool_pages, vvq2_kv** out) {
     if (int rc = check_ctx(c)) return rc;
-    if (!out || n_seqs <= 0 || max_seq <= 0) return fail(VVQ2_ERR_INVALID_ARG, "bad kv size");
+    if (!out || n_seqs <= 0 || max_seq <= 0 || pool_pages < 0) return fail(VVQ2_ERR_INVALID_ARG, "bad kv size");
     *out = nullptr;
     vvq2_kv* kv = new vvq2_kv();
     kv->ctx = c;
     kv->n_seqs = n_seqs;
     kv->max_seq = max_seq;
     kv->max_pages = (max_seq + KV_PAGE - 1) / KV_PAGE;
-    const size_t pages = (size_t)n_seqs * kv->max_pages;
+    const size_t slots = (size_t)n_seqs * kv->max_pages;   // block-table entries
+    kv->paged = pool_pages > 0;
+    // identity: page s*max_pages + p of the pool is page p of sequence s
+    const size_t pages = kv->paged ? (size_t)pool_pages + 1 : slots;
+    kv->pool_pages = kv->paged ? pool_pages : (int)slots;
+    kv->null_page = pool_pages;
     kv->layer_elems = pages * c->pt.nkv * KV_PAGE * c->hp.head_dim;   // this rank's KV heads
     const size_t bytes = kv->layer_elems * c->hp.n_layers * sizeof(__half);
     if (cudaMalloc(&kv->k, bytes) != cudaSuccess || cudaMalloc(&kv->v, bytes) != cudaSuccess ||
-        cudaMalloc(&kv->block_table, pages * sizeof(int)) != cudaSuccess) {
+        cudaMalloc(&kv->block_table, slots * sizeof(int)) != cudaSuccess) {
         cudaGetLastError();
         vvq2_kv_free(kv);
         return fail(VVQ2_ERR_OUT_OF_MEMORY, "kv cache of %zu bytes", 2 * bytes);
     }
-    // pages of sequence s are [s*max_pages, (s+1)*max_pages): the block table keeps
-    // the indirection so pages can later be shared or reassigned
-    std::vector<int> bt(pages);
-    for (size_t i = 0; i < pages; ++i) bt[i] = (int)i;
+    kv->bt.resize(slots);
+    for (size_t i = 0; i < slots; ++i) kv->bt[i] = kv->paged ? kv->null_page : (int)i;
+    if (kv->paged) {   // handed out lowest first
+        kv->free_pages.resize(pool_pages);
+        for (int i = 0; i < pool_pages; ++i) kv->free_pages[i] = pool_pages - 1 - i;
+    }
     cudaError_t e = cudaMemsetAsync(kv->k, 0, bytes, c->stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(kv->v, 0, bytes, c->stream);
-    if (e == cudaSuccess) e = copy_on(kv->block_table, bt.data(), pages * sizeof(int), c->stream);
+    if (e == cudaSuccess) e = copy_on(kv->block_table, kv->bt.data(), slots * sizeof(int), c->stream);
     if (e != cudaSuccess || cudaGetLastError() != cudaSuccess) {
         vvq2_kv_free(kv);
         return fail(VVQ2_ERR_CUDA, "kv init copy failed");
@@ -1680,6 +1713,68 @@ int vvq2_kv_init(vvq2_ctx* c, int n_seqs, int max_seq, vvq2_kv** out) {
     c->kvs.push_back(kv);
     *out = kv;
     return 0;
+}
+
+int vvq2_kv_init(vvq2_ctx* c, int n_seqs, int max_seq, vvq2_kv** out) {
+    return kv_create(c, n_seqs, max_seq, 0, out);
+}
+
+int vvq2_kv_init_paged(vvq2_ctx* c, int n_seqs, int max_seq, int pool_pages, vvq2_kv** out) {
+    if (pool_pages <= 0) return fail(VVQ2_ERR_INVALID_ARG, "pool_pages must be positive");
+    return kv_create(c, n_seqs, max_seq, pool_pages, out);
+}
+
+int vvq2_kv_free_pages(const vvq2_kv* kv) {
+    if (!kv) return fail(VVQ2_ERR_INVALID_ARG, "null kv");
+    return kv->paged ? (int)kv->free_pages.size() : 0;
+}
+
+// Positions of a sequence this rank stores among its first n (all of them
+// unless a partitioned context splits sequences into parts).
+static int kv_own(const vvq2_kv* kv, int n) {
+    const vvq2_ctx* c = kv->ctx;
+    return c->pt.seq_parts > 1 ? zz_count(c->pt.s, n) : n;
+}
+
+static int kv_push_row(vvq2_kv* kv, int seq, cudaStream_t st) {
+    const size_t o = (size_t)seq * kv->max_pages;
+    CU(cudaMemcpyAsync(kv->block_table + o, kv->bt.data() + o, kv->max_pages * sizeof(int), cudaMemcpyHostToDevice, st));
+    return 0;
+}
+
+// Paged cache: give sequence seq pages for its first n positions.  Fails
+// (nothing changed) when the pool has too few free pages.
+int kv_reserve(vvq2_kv* kv, int seq, int n, cudaStream_t st) {
+    if (!kv->paged) return 0;
+    const int need = (kv_own(kv, std::min(n, kv->max_seq)) + KV_PAGE - 1) / KV_PAGE;
+    int* row = kv->bt.data() + (size_t)seq * kv->max_pages;
+    int missing = 0;
+    for (int p = 0; p < need; ++p) missing += row[p] == kv->null_page;
+    if (!missing) return 0;
+    if (missing > (int)kv->free_pages.size())
+        return fail(VVQ2_ERR_OUT_OF_MEMORY, "KV page pool exhausted: sequence %d needs %d more pages, %zu free of %d",
+                    seq, missing, kv->free_pages.size(), kv->pool_pages);
+    for (int p = 0; p < need; ++p)
+        if (row[p] == kv->null_page) {
+            row[p] = kv->free_pages.back();
+            kv->free_pages.pop_back();
+        }
+    return kv_push_row(kv, seq, st);
+}
+
+// Paged cache: return the pages of sequence seq past its first n positions.
+static int kv_release(vvq2_kv* kv, int seq, int n, cudaStream_t st) {
+    if (!kv->paged) return 0;
+    const int keep = (kv_own(kv, n) + KV_PAGE - 1) / KV_PAGE;
+    int* row = kv->bt.data() + (size_t)seq * kv->max_pages;
+    bool changed = false;
+    for (int p = keep; p < kv->max_pages; ++p)
+        if (row[p] != kv->null_page) {
+            kv->free_pages.push_back(row[p]);
+            row[p] = kv->null_page;
+            changed = true;
+        }
+    return changed ? kv_push_row(kv, seq, st) : 0;
 }
 
 void vvq2_kv_free(vvq2_kv* kv) {
@@ -1708,6 +1803,12 @@ void vvq2_kv_free(vvq2_kv* kv) {
 int vvq2_kv_set_past_len(vvq2_kv* kv, int seq, int past) {
     if (!kv || !kv->ctx || seq < 0 || seq >= kv->n_seqs || past < 0 || past > kv->max_seq)
         return fail(VVQ2_ERR_INVALID_ARG, "bad seq/past_len");
+    if (kv->paged) {   // a shorter sequence gives its later pages back; a longer one needs pages
+        if (int rc = past < kv->past[seq] ? kv_release(kv, seq, past, kv->ctx->stream)
+                                          : kv_reserve(kv, seq, past, kv->ctx->stream))
+            return rc;
+        CU(cudaStreamSynchronize(kv->ctx->stream));   // the table is current for work on any stream
+    }
     kv->past[seq] = past;
     if (kv->ctx && kv->ctx->meta_kv == kv) kv->ctx->meta_kv = nullptr;
     return 0;
@@ -1726,6 +1827,9 @@ static int kv_xfer(vvq2_kv* kv, int seq, int layer, float* k, float* v, const fl
     if (seq < 0 || seq >= kv->n_seqs || layer < 0 || layer >= c->hp.n_layers || n_pos < 0 || n_pos > kv->max_seq)
         return fail(VVQ2_ERR_INVALID_ARG, "bad kv transfer");
     if (n_pos == 0) return 0;
+    if (upload) {
+        if (int rc = kv_reserve(kv, seq, n_pos, c->stream)) return rc;
+    }
     std::vector<float> lk, lv;   // partitioned upload: this rank's heads and sequence part
     if (c->pt.on()) {
         if (!upload) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "kv read on a partitioned context");
@@ -1809,6 +1913,8 @@ int vvq2_forward(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, int n_to
         if (pos_start[s] < 0) return fail(VVQ2_ERR_INVALID_ARG, "negative position");
     }
     cudaStream_t st = pick_stream(c, stream);
+    for (int s = 0; s < n_seqs; ++s)   // paged cache: pages for the positions this call writes
+        if (int rc = kv_reserve(kv, seqs[s], kv->past[seqs[s]] + n_tok, st)) return rc;
     const int H = c->hp.hidden_size;
     const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
     const bool last_only = (flags & VVQ2_LAST_ONLY) != 0;
@@ -1970,6 +2076,31 @@ int vvq2_embed(vvq2_ctx* c, int n, const int32_t* tokens, float* out, void* stre
     return 0;
 }
 
+// Decode step of a partitioned context for one or two rows, captured as one
+// graph: embedding, the layers on the streaming-GEMV path with the
+// peer-memory exchanges (no NCCL call inside), the lm_head GEMV + argmax,
+// and the device-side advance of the true and the rank's own row tables.
+int enqueue_decode_parted(vvq2_ctx* c, vvq2_kv* kv, int M, int bucket, cudaStream_t st) {
+    const int H = c->hp.hidden_size;
+    CU(embed_launch(c->tok_embd, c->tok, M, c->X, st));
+    if (int rc = run_layers_prefill(c, kv, M, M, 1, bucket, 0, c->hp.n_layers, st, nullptr, 0.0)) return rc;
+    GemvArgs g;
+    g.w0 = c->lm_head;
+    g.M = M;
+    g.K = H;
+    g.x = c->X;
+    g.x_stride = H;
+    g.norm_w = c->out_norm;
+    g.eps = c->hp.rms_norm_eps;
+    g.argmax = c->amax;
+    g.epi = EPI_ARGMAX;
+    CU(argmax_init_launch(c->amax, M, st));
+    CU(gemv_launch(g, st));
+    CU(argmax_final_launch(c->amax, M, c->tok, st));
+    CU(advance_meta_part_launch(c->meta_rope, c->meta, M, c->pt.seq_parts, c->pt.s, st));
+    return 0;
+}
+
 int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, const int32_t* tokens_in,
                      int32_t* tokens_out, void* stream) {
     if (int rc = check_ctx(c)) return rc;
@@ -1987,8 +2118,13 @@ int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, cons
         if (kv->past[seqs[s]] + 1 > kv->max_seq) return fail(VVQ2_ERR_INVALID_ARG, "KV overflow");
     }
     cudaStream_t st = pick_stream(c, stream);
-    // partitioned contexts exchange attention through NCCL on the tensor-core path
-    if (n_seqs > c->max_rows || c->pt.on()) return decode_step_batched(c, kv, seqs, n_seqs, tokens_in, tokens_out, st);
+    for (int s = 0; s < n_seqs; ++s)   // paged cache: a page for the position this step writes
+        if (int rc = kv_reserve(kv, seqs[s], kv->past[seqs[s]] + 1, st)) return rc;
+    // partitioned contexts: one or two rows with the peer-memory exchanges run
+    // as a captured graph; otherwise the host-driven batched step (NCCL)
+    const bool parted = c->pt.on() && c->pt.peer && n_seqs <= 2 && n_seqs <= c->max_rows;
+    if (!parted && (n_seqs > c->max_rows || c->pt.on()))
+        return decode_step_batched(c, kv, seqs, n_seqs, tokens_in, tokens_out, st);
     const int M = n_seqs;
     std::vector<int> sv(seqs, seqs + n_seqs);
     int max_lim = 1;
@@ -2002,14 +2138,13 @@ int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, cons
     // attention grid covers the bucket and CTAs past a row's length exit
     const int bucket = (max_lim + 511) / 512 * 512;
     if (c->meta_kv != kv || c->meta_seqs != sv) {
+        std::vector<RowMeta> rope(M);
         for (int s = 0; s < n_seqs; ++s) {
-            RowMeta& r = c->meta_host[s];
-            r.seq = seqs[s];
-            r.pos = kv->past[seqs[s]];
-            r.cidx = kv->past[seqs[s]];
-            r.kvlen = kv->past[seqs[s]] + 1;
+            const int past = kv->past[seqs[s]];
+            c->meta_host[s] = local_row(c, seqs[s], past, past, past + 1, &rope[s]);
         }
         CU(cudaMemcpyAsync(c->meta, c->meta_host, sizeof(RowMeta) * M, cudaMemcpyHostToDevice, st));
+        if (parted) CU(cudaMemcpyAsync(c->meta_rope, rope.data(), sizeof(RowMeta) * M, cudaMemcpyHostToDevice, st));
         c->meta_kv = kv;
         c->meta_seqs = sv;
     }
@@ -2022,13 +2157,15 @@ int vvq2_decode_step(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, cons
         vvq2_ctx::Graph g{kv, sv, bucket, c->prof_on, nullptr, 0, {}};
         const long long k0 = launch_count();
         cudaGraph_t graph = nullptr;
-        if (mega_eligible(c, M)) {
+        if (!parted && mega_eligible(c, M)) {
             MegaLayer* dl = nullptr;
             if (int rc = ensure_mega_table(c, kv, &dl)) return rc;
         }
         CU(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         int rc;
-        if (mega_eligible(c, M)) {
+        if (parted) {
+            rc = enqueue_decode_parted(c, kv, M, bucket, st);
+        } else if (mega_eligible(c, M)) {
             double step_bytes = attn_bytes + (double)weight_bytes(c->lm_head);
             for (const auto& L : c->layers)
                 step_bytes += (double)(weight_bytes(L.qkv) + weight_bytes(L.o) + weight_bytes(L.gate) +

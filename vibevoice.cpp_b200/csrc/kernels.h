@@ -259,6 +259,9 @@ cudaError_t argmax_rescore_launch(const float* X, const float* norm_w, float eps
                                   const unsigned long long* tile_best, int ntiles, float margin,
                                   unsigned long long* keys, int* err, cudaStream_t st);
 cudaError_t advance_meta_launch(RowMeta* meta, int n, cudaStream_t st);
+// partitioned rows: true rows + 1, this rank's rows derived from them
+cudaError_t advance_meta_part_launch(RowMeta* meta_true, RowMeta* meta_local, int n, int seq_parts, int part,
+                                     cudaStream_t st);
 cudaError_t argmax_final_launch(const unsigned long long* keys, int n, int32_t* out,
                                 cudaStream_t st);
 

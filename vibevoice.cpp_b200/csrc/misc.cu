@@ -143,6 +143,19 @@ __global__ void k_advance_meta(RowMeta* meta, int n) {
     }
 }
 
+// The next decode position of a partitioned context's rows: the true rows
+// advance by one, this rank's rows are derived from them (its sequence part).
+__global__ void k_advance_meta_part(RowMeta* meta_true, RowMeta* meta_local, int n, int seq_parts, int part) {
+    if (threadIdx.x < n) {
+        RowMeta r = meta_true[threadIdx.x];
+        r.pos += 1;
+        r.cidx += 1;
+        r.kvlen += 1;
+        meta_true[threadIdx.x] = r;
+        meta_local[threadIdx.x] = seq_parts > 1 ? zz_local_row(r, part) : r;
+    }
+}
+
 __global__ void k_argmax_init(unsigned long long* keys, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) keys[i] = 0ull;
@@ -373,6 +386,13 @@ cudaError_t kv_download_launch(const KvLayer& kv, int seq, float* k, float* v, i
     const int64_t n = (int64_t)n_pos * kv.n_kv * kv.hd;
     if (n == 0) return cudaSuccess;
     k_kv_download<<<grid_for(n, 256), 256, 0, st>>>(kv, seq, k, v, n_pos);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t advance_meta_part_launch(RowMeta* meta_true, RowMeta* meta_local, int n, int seq_parts, int part,
+                                     cudaStream_t st) {
+    k_advance_meta_part<<<1, 32, 0, st>>>(meta_true, meta_local, n, seq_parts, part);
     note_launch();
     return cudaGetLastError();
 }

@@ -54,6 +54,8 @@ def lib() -> C.CDLL:
             "vvq2_set_layer": (I, [P, I, P]),
             "vvq2_set_output": (I, [P, P, P, P]),
             "vvq2_kv_init": (I, [P, I, I, P]),
+            "vvq2_kv_init_paged": (I, [P, I, I, I, P]),
+            "vvq2_kv_free_pages": (I, [P]),
             "vvq2_kv_free": (None, [P]),
             "vvq2_kv_load_prefix": (I, [P, I, I, P, P, I]),
             "vvq2_kv_read": (I, [P, I, I, P, P, I]),
@@ -225,8 +227,9 @@ class Engine:
         _chk(lib().vvq2_mega_trace(self.ctx, _p(out), out.size, None, None))
         return out
 
-    def kv(self, n_seqs: int, max_seq: int) -> "KV":
-        return KV(self, n_seqs, max_seq)
+    def kv(self, n_seqs: int, max_seq: int, pool_pages: int = 0) -> "KV":
+        """pool_pages > 0: a paged cache whose sequences share that many pages."""
+        return KV(self, n_seqs, max_seq, pool_pages)
 
     def forward(self, kv: "KV", seqs, x, pos_start, first_layer=0, n_layers=None, flags=ADVANCE,
                 y=None, stream=None):
@@ -274,13 +277,20 @@ class Engine:
 
 
 class KV:
-    """vvq2_kv: f16 paged resident KV cache for n_seqs sequences."""
+    """vvq2_kv: f16 paged resident KV cache for n_seqs sequences (pool_pages >
+    0: the sequences take pages from a shared pool as they grow)."""
 
-    def __init__(self, eng: Engine, n_seqs: int, max_seq: int):
+    def __init__(self, eng: Engine, n_seqs: int, max_seq: int, pool_pages: int = 0):
         self.eng = eng
         ptr = C.c_void_p()
-        _chk(lib().vvq2_kv_init(eng.ctx, n_seqs, max_seq, C.byref(ptr)))
+        if pool_pages > 0:
+            _chk(lib().vvq2_kv_init_paged(eng.ctx, n_seqs, max_seq, pool_pages, C.byref(ptr)))
+        else:
+            _chk(lib().vvq2_kv_init(eng.ctx, n_seqs, max_seq, C.byref(ptr)))
         self.kv = ptr.value
+
+    def free_pages(self) -> int:
+        return lib().vvq2_kv_free_pages(self.kv)
 
     def close(self):
         if getattr(self, "kv", None):
