@@ -1084,8 +1084,11 @@ int decode_step_batched(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, c
         CU(rmsnorm_f16_launch(c->X, c->out_norm, M, H, hp.rms_norm_eps, c->Xh, st));
         CUtensorMap mapX;
         if (!make_act_map(&mapX, c->Xh, M, H)) return fail(VVQ2_ERR_NOT_IMPLEMENTED, "hidden %d not a multiple of 64", H);
-        // f16 operands: each row's candidate tiles (within 3 % of its best
-        // approximate logit) are rescored in f32 for the exact argmax
+        // f16 operands: each row's candidate tiles (best approximate logit
+        // within 1 % of the row's best) are rescored in f32 for the exact
+        // argmax.  The f16 logits' error is ~2e-4 of the largest (f16
+        // rounding of x and w, 2^-11 each, over K random-sign terms), so the
+        // window is some 50 of those errors wide.
         const int ntiles = (c->lm_head.rows + 127) / 128;
         if ((size_t)M * ntiles > c->tile_best_n) {
             if (int rc = c->alloc(&c->tile_best, (size_t)M * ntiles)) return rc;
@@ -1106,7 +1109,7 @@ int decode_step_batched(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, c
         CU(gemm_tc_launch(g, mapX, st));
         CU(R.end(3, 2.0 * M * (double)g.N * H));
         CU(argmax_rescore_launch(c->X, c->out_norm, hp.rms_norm_eps, M, H, c->lm_head, c->tile_best, ntiles,
-                                 0.03f, c->amax, c->err, st));
+                                 0.01f, c->amax, c->err, st));
     }
     CU(argmax_final_launch(c->amax, M, c->tok, st));
     CU(cudaMemcpyAsync(tokens_out, c->tok, sizeof(int32_t) * M, cudaMemcpyDefault, st));

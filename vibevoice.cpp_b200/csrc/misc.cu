@@ -223,7 +223,24 @@ __global__ void __launch_bounds__(RS_THREADS) k_argmax_rescore(const float* X, c
         const int n = cand[c / 128] * 128 + (c % 128);
         if (n >= w.rows) continue;   // uniform in the warp
         float acc = 0.f;
-        for (int k = lane; k < H; k += 32) acc = fmaf(deq_elem(w, n, k), xs[k], acc);
+        if (w.type == W_Q8_0) {
+            // 16 stored bytes (q + 128) and their block scale per lane step;
+            // q * d is exact in f32 (8 x 11 significant bits), as deq_elem's
+            const uint8_t* rp = w.q + (size_t)n * w.row_stride;
+            const __half* dp = w.d + (size_t)n * w.d_stride;
+            for (int c = lane; c < H / 16; c += 32) {
+                const uint4 q4 = __ldg(reinterpret_cast<const uint4*>(rp) + c);
+                const float d = __half2float(dp[c >> 1]);
+                const uint32_t wd[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int q = (int)((wd[i >> 2] >> (8 * (i & 3))) & 0xffu) - 128;
+                    acc = fmaf(__fmul_rn((float)q, d), xs[c * 16 + i], acc);
+                }
+            }
+        } else {
+            for (int k = lane; k < H; k += 32) acc = fmaf(deq_elem(w, n, k), xs[k], acc);
+        }
         acc = warp_sum(acc);
         const unsigned long long key = argmax_key(__fmul_rn(acc, nsc), n);
         mine = key > mine ? key : mine;
