@@ -639,7 +639,12 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
     // rows x up to 256 tokens per tile) when its tiles fill the SMs; smaller
     // ones the few-row kernel, split along K when it has few tiles.  Both
     // dequantize the weight blocks in shared memory.
-    auto gemm = [&](const GemmArgs& g, const CUtensorMap& map, const __half* act) -> int {
+    // norm_w (residual GEMMs only): the RMSNorm -> f16 (c->Xh) that follows;
+    // a split-K residual GEMM then folds its reduction into that norm (one
+    // pass over the rows) and sets *normed
+    auto gemm = [&](const GemmArgs& g, const CUtensorMap& map, const __half* act, const float* norm_w = nullptr,
+                    bool* normed = nullptr) -> int {
+        if (normed) *normed = false;
         const double n = g.epi == EPI_SWIGLU ? 2.0 * g.N : (double)g.N;
         const int nt = M > c->ws_rows ? gemm_ws_tile_rows(g, c->ws_min_tiles) : 0;
         if (nt) {
@@ -669,7 +674,13 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         }
         CU(R.begin());
         CU(gemm_tc_launch(gg, map, st));
-        if (gg.kpart) CU(splitk_epilogue_launch(gg, st));
+        if (gg.kpart && gg.epi == EPI_RESID && norm_w && normed) {
+            CU(splitk_resid_rmsnorm_f16_launch(gg.kpart, gg.k_splits, gg.bias, c->X, norm_w, M, g.N,
+                                               hp.rms_norm_eps, c->Xh, st));
+            *normed = true;
+        } else if (gg.kpart) {
+            CU(splitk_epilogue_launch(gg, st));
+        }
         CU(R.end(3, 2.0 * g.T * n * g.K));
         return 0;
     };
@@ -700,6 +711,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
     CUtensorMap mapX, mapA, mapF;
     if (!make_act_map(&mapX, c->Xh, M, H) || !make_act_map(&mapA, c->ATTh, M, qw) || !make_act_map(&mapF, c->Ah, M, F))
         return fail(VVQ2_ERR_NOT_IMPLEMENTED, "activation tensor map (dims %d/%d/%d must be multiples of 64)", H, qw, F);
+    bool pre_normed = false;   // the next attention norm was done by the previous down projection
     for (int li = first; li < first + n_layers; ++li) {
         const vvq2_ctx::Layer& L = c->layers[li];
         const KvLayer kvl = kv->layer(li);
@@ -727,7 +739,7 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
             q.epi = EPI_QKV;
             if (int rc = gemv(q)) return rc;
         } else {
-            CU(rmsnorm_f16_launch(c->X, L.attn_norm, M, H, hp.rms_norm_eps, c->Xh, st));
+            if (!pre_normed) CU(rmsnorm_f16_launch(c->X, L.attn_norm, M, H, hp.rms_norm_eps, c->Xh, st));
             GemmArgs q = g;
             q.w0 = L.qkv;
             q.N = L.qkv.rows;
@@ -878,9 +890,10 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         o.epi = EPI_RESID;
         o.y = c->X;
         o.y_stride = H;
-        if (int rc = gemm(o, mapA, c->ATTh)) return rc;
+        bool o_normed = false;
+        if (int rc = gemm(o, mapA, c->ATTh, L.ffn_norm, &o_normed)) return rc;
         // 4. RMSNorm -> f16, gate/up GEMM with SwiGLU epilogue (f16 out)
-        CU(rmsnorm_f16_launch(c->X, L.ffn_norm, M, H, hp.rms_norm_eps, c->Xh, st));
+        if (!o_normed) CU(rmsnorm_f16_launch(c->X, L.ffn_norm, M, H, hp.rms_norm_eps, c->Xh, st));
         GemmArgs f = g;
         f.w0 = L.gate;
         f.w1 = L.up;
@@ -899,7 +912,10 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
         d.epi = parted ? EPI_STORE : EPI_RESID;
         d.y = parted ? c->Xp : c->X;
         d.y_stride = H;
-        if (int rc = gemm(d, mapF, c->Ah)) return rc;
+        // unpartitioned and not the last layer here: the next layer's attention
+        // norm can take the down projection's split-K reduction
+        const bool fold = !parted && li + 1 < first + n_layers;
+        if (int rc = gemm(d, mapF, c->Ah, fold ? c->layers[li + 1].attn_norm : nullptr, &pre_normed)) return rc;
         if (parted) {
             if (nccl()->AllReduce(c->Xp, c->Xp, (size_t)M * H, ncclFloat, ncclSum, c->pt.comm, st) != ncclSuccess)
                 return fail(VVQ2_ERR_CUDA, "NCCL all-reduce of the down projection failed");

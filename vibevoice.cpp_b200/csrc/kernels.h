@@ -234,6 +234,11 @@ cudaError_t rope_launch(const float* x, int n_tok, int n_heads, int hd, const in
 cudaError_t rmsnorm_launch(const float* x, const float* w, int rows, int n, float eps, float* y,
                            cudaStream_t st);
 // RMSNorm to f16 (the tensor-core GEMM's activation operand)
+// x[rows][n] += (bias +) the in-order sum of split-K partials part[ks][rows][n],
+// then y = f16(RMSNorm(x) * w): a residual GEMM's split-K epilogue fused with
+// the RMSNorm that follows it
+cudaError_t splitk_resid_rmsnorm_f16_launch(const float* part, int ks, const float* bias, float* x, const float* w,
+                                            int rows, int n, float eps, __half* y, cudaStream_t st);
 cudaError_t rmsnorm_f16_launch(const float* x, const float* w, int rows, int n, float eps, __half* y,
                                cudaStream_t st);
 // NEOX (cos, sin) per (row, pair) with ggml's CPU theta recurrence: [rows][hd/2]

@@ -85,6 +85,49 @@ __global__ void k_rmsnorm_f16(const float* x, const float* w, int n, float eps, 
         y[(size_t)blockIdx.x * n + k] = __float2half_rn(__fmul_rn(__fmul_rn(xr[k], sc), w[k]));
 }
 
+// A residual projection split along K, finished together with the RMSNorm
+// that reads its rows next: x[r][k] += (bias[k] +) sum over splits z, in
+// order, of part[z][r][k] -- the split-K epilogue's sum -- then y[r] =
+// f16(x[r] * rms_scale * w), the same arithmetic as k_rmsnorm_f16 on the
+// updated row.  One launch and one pass over the rows instead of two.
+__global__ void k_splitk_resid_rmsnorm_f16(const float* part, int ks, int64_t zs, const float* bias, float* x,
+                                           const float* w, int n, float eps, __half* y) {
+    __shared__ float red[32];
+    __shared__ float scale_s;
+    asm volatile("griddepcontrol.launch_dependents;");
+    float* xr = x + (size_t)blockIdx.x * n;
+    const float* pr = part + (size_t)blockIdx.x * n;
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        float v = 0.f;
+        int z = 0;
+        for (; z + 8 <= ks; z += 8) {
+            float p[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) p[i] = pr[(size_t)(z + i) * zs + k];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v += p[i];
+        }
+        for (; z < ks; ++z) v += pr[(size_t)z * zs + k];
+        if (bias) v = __fadd_rn(v, bias[k]);
+        const float xv = __fadd_rn(xr[k], v);
+        xr[k] = xv;
+        ss = fmaf(xv, xv, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+        scale_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)n), eps)));
+    }
+    __syncthreads();
+    const float sc = scale_s;
+    for (int k = threadIdx.x; k < n; k += blockDim.x)
+        y[(size_t)blockIdx.x * n + k] = __float2half_rn(__fmul_rn(__fmul_rn(xr[k], sc), w[k]));
+}
+
 __global__ void k_rope_table(const RowMeta* meta, int rows, int half, float ts, float2* cs) {
     const int64_t n = (int64_t)rows * half;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
@@ -366,6 +409,13 @@ cudaError_t rmsnorm_launch(const float* x, const float* w, int rows, int n, floa
 cudaError_t rmsnorm_f16_launch(const float* x, const float* w, int rows, int n, float eps, __half* y,
                                cudaStream_t st) {
     k_rmsnorm_f16<<<rows, 256, 0, st>>>(x, w, n, eps, y);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t splitk_resid_rmsnorm_f16_launch(const float* part, int ks, const float* bias, float* x, const float* w,
+                                            int rows, int n, float eps, __half* y, cudaStream_t st) {
+    k_splitk_resid_rmsnorm_f16<<<rows, 256, 0, st>>>(part, ks, (int64_t)rows * n, bias, x, w, n, eps, y);
     note_launch();
     return cudaGetLastError();
 }
