@@ -80,10 +80,13 @@ constexpr uint32_t LL_POLLS = 1u << 21;     // L2 polls of a flagged word (~0.5 
 // spill the GEMV tile loop: the kernel sits at the 128-register limit.)
 constexpr int SB_FA = 3;
 constexpr int SB_MERGE = 1;             // word pairs per thread in flight while a merge gathers partials
-// pause between unsuccessful poll rounds: every waiting thread of every CTA
-// polls, and re-requesting at the L2 round-trip rate would flood L2 with
-// requests (starving the producers and the weight stream)
-constexpr unsigned POLL_PAUSE_NS = 128;
+// pause between unsuccessful poll rounds.  Every waiting thread of every CTA
+// polls, but a poll round is already one L2 round trip per thread, and on
+// the config-2 step no pause measured best (0.571 ms against 0.576 at 32 ns
+// and 0.588 at 128 ns); a stage with little work between hand-overs (64
+// copies of one layer with a 64-wide FFN) prefers 128 ns (17.6 against
+// 19.0 us per layer)
+constexpr unsigned POLL_PAUSE_NS = 0;
 
 enum { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DOWN = 3, PH_LM = 4 };
 
