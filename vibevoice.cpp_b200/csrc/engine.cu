@@ -132,9 +132,10 @@ bool make_q8_map(CUtensorMap* m, const DevW& w, int box_x, int box_rows) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// The four weight maps gemm_ws_launch takes for Q8_0 (w1 = w0 unless SwiGLU).
-bool make_ws_weight_maps(CUtensorMap* wq, const GemmArgs& g) {
-    const int r = gemm_ws_weight_box_rows(g);
+// The four weight maps gemm_ws_launch (or, few_rows, gemm_tc_launch) takes
+// for Q8_0 (w1 = w0 unless SwiGLU).
+bool make_ws_weight_maps(CUtensorMap* wq, const GemmArgs& g, bool few_rows = false) {
+    const int r = few_rows ? (g.epi == EPI_SWIGLU ? 64 : 128) : gemm_ws_weight_box_rows(g);
     const DevW& w1 = g.epi == EPI_SWIGLU ? g.w1 : g.w0;
     return make_q8_map(&wq[0], g.w0, 64, r) && make_q8_map(&wq[1], w1, 64, r) && make_q8_map(&wq[2], g.w0, 16, r) &&
            make_q8_map(&wq[3], w1, 16, r);
@@ -672,8 +673,10 @@ int run_layers_prefill(vvq2_ctx* c, vvq2_kv* kv, int M, int n_seqs, int nt, int 
                 gg.k_splits = ks;
             }
         }
+        CUtensorMap wq[4];
+        if (g.w0.type == W_Q8_0 && !make_ws_weight_maps(wq, g, true)) return fail(VVQ2_ERR_CUDA, "weight tensor map");
         CU(R.begin());
-        CU(gemm_tc_launch(gg, map, st));
+        CU(gemm_tc_launch(gg, map, wq, st));
         if (gg.kpart && gg.epi == EPI_RESID && norm_w && normed) {
             CU(splitk_resid_rmsnorm_f16_launch(gg.kpart, gg.k_splits, gg.bias, c->X, norm_w, M, g.N,
                                                hp.rms_norm_eps, c->Xh, st));
@@ -1122,7 +1125,9 @@ int decode_step_batched(vvq2_ctx* c, vvq2_kv* kv, const int* seqs, int n_seqs, c
         g.err = c->err;
         Recorder R{c, st, c->prof_on ? &recs : nullptr};
         CU(R.begin());
-        CU(gemm_tc_launch(g, mapX, st));
+        CUtensorMap wq[4];
+        if (g.w0.type == W_Q8_0 && !make_ws_weight_maps(wq, g, true)) return fail(VVQ2_ERR_CUDA, "weight tensor map");
+        CU(gemm_tc_launch(g, mapX, wq, st));
         CU(R.end(3, 2.0 * M * (double)g.N * H));
         CU(argmax_rescore_launch(c->X, c->out_norm, hp.rms_norm_eps, M, H, c->lm_head, c->tile_best, ntiles,
                                  0.01f, c->amax, c->err, st));
@@ -2361,8 +2366,8 @@ int vvq2_debug_gemm(int type, const void* w, int n, int k, const float* x, int t
             const int nt = t > 256 ? gemm_ws_tile_rows(g, 1) : 0;
             CUtensorMap mt, wq[4];
             if (nt && !make_act_map(&mt, dxh, t, k, nt)) rc = fail(VVQ2_ERR_CUDA, "tensor map");
-            if (nt && !rc && dw.type == W_Q8_0 && !make_ws_weight_maps(wq, g)) rc = fail(VVQ2_ERR_CUDA, "tensor map");
-            if (!rc) e = nt ? gemm_ws_launch(g, mt, wq, nt, 0) : gemm_tc_launch(g, map, 0);
+            if (!rc && dw.type == W_Q8_0 && !make_ws_weight_maps(wq, g, nt == 0)) rc = fail(VVQ2_ERR_CUDA, "tensor map");
+            if (!rc) e = nt ? gemm_ws_launch(g, mt, wq, nt, 0) : gemm_tc_launch(g, map, wq, 0);
         }
         if (!rc && e == cudaSuccess) e = cudaDeviceSynchronize();
         int herr = 0;

@@ -47,16 +47,27 @@ constexpr int STAGES = 4;
 constexpr int TILE_BYTES = BM * BK * 2;                 // 16 KB
 constexpr int STAGE_BYTES = 3 * TILE_BYTES;             // A0, A1, B
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+// Q8_0: the raw weight bytes of a k-block (quants of the tile's 128 rows,
+// then the rows' block scales of its group of 4 k-blocks) arrive by TMA into
+// an R_STAGES-deep ring that runs ahead of the f16 stages; 3 f16 stages
+// leave it room
+constexpr int Q8_STAGES = 3, R_STAGES = 8;
+constexpr int RQ_BYTES = BN * BK, R_STAGE = RQ_BYTES + BN * 16;
+constexpr int Q8_SMEM_BYTES = Q8_STAGES * STAGE_BYTES + R_STAGES * R_STAGE + 1024;
+__host__ __device__ constexpr int smem_bytes(int wt) { return wt == W_Q8_0 ? Q8_SMEM_BYTES : SMEM_BYTES; }
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 256;
 
 
 template <int WT, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const GemmArgs a) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ0,
+              const __grid_constant__ CUtensorMap tmQ1, const __grid_constant__ CUtensorMap tmS0,
+              const __grid_constant__ CUtensorMap tmS1, const GemmArgs a) {
+    constexpr int ST = WT == W_Q8_0 ? Q8_STAGES : STAGES;   // f16 pipeline stages
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], done;
+    __shared__ __align__(8) uint64_t full[ST], empty[ST], done, r_full[R_STAGES], r_empty[R_STAGES];
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -72,10 +83,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb0;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < ST; ++s) {
             tc::mbar_init(&full[s], 1 + 128);
             tc::mbar_init(&empty[s], 1);
         }
+        if (WT == W_Q8_0)
+            for (int s = 0; s < R_STAGES; ++s) {
+                tc::mbar_init(&r_full[s], 1);
+                tc::mbar_init(&r_empty[s], 128);
+            }
         tc::mbar_init(&done, 1);
         abort_flag = 0;
         tc::mbar_fence_init();
@@ -95,27 +111,53 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
 
     if (warp == 0 && lane == 0) {
-        // ---- TMA producer: activation tiles A0 (rows t0..) and A1 (rows t0+128..).
-        // Launched as a programmatic dependent: everything above (barriers, TMEM,
-        // the weight producers' first fetches) overlapped the previous kernel;
-        // its outputs (the activations A) are read only after this wait.
+        // ---- TMA producer: activation tiles A0 (rows t0..) and A1 (rows
+        // t0+128..) and, for Q8_0, the raw weight ring (k-block j's quants and
+        // its scale group), R_STAGES k-blocks ahead of the producers.
+        // Launched as a programmatic dependent: everything before the wait
+        // (barriers, TMEM, the first raw weight loads) overlapped the previous
+        // kernel; its outputs (the activations A) are read only after it.
+        uint8_t* const rawb = smem + ST * STAGE_BYTES;
+        const int y = EPI == EPI_SWIGLU ? (int)blockIdx.x * 64 : n0;
+        auto issue_raw = [&](int j) {   // j: local k-block
+            uint8_t* rs = rawb + (j % R_STAGES) * R_STAGE;
+            const int kx = (kb0 + j) * BK, xs = a.K + 16 * ((kb0 + j) >> 2);
+            uint64_t* bar = &r_full[j % R_STAGES];
+            tc::mbar_arrive_expect_tx(bar, R_STAGE);
+            tc::tma_load_2d(rs, &tmQ0, kx, y, bar);
+            tc::tma_load_2d(rs + RQ_BYTES, &tmS0, xs, y, bar);
+            if (EPI == EPI_SWIGLU) {   // gate rows, then the same up rows
+                tc::tma_load_2d(rs + 64 * BK, &tmQ1, kx, y, bar);
+                tc::tma_load_2d(rs + RQ_BYTES + 64 * 16, &tmS1, xs, y, bar);
+            }
+        };
+        if constexpr (WT == W_Q8_0)
+            for (int j = 0; j < min(nk, R_STAGES); ++j) issue_raw(j);
         asm volatile("griddepcontrol.wait;" ::: "memory");
         for (int i = 0; i < nk; ++i) {
-            const int s = i % STAGES, kx = (kb0 + i) * BK;
-            if (i >= STAGES && !tc::mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) { fail(); break; }
+            const int s = i % ST, kx = (kb0 + i) * BK;
+            if (i >= ST && !tc::mbar_wait(&empty[s], ((i / ST) - 1) & 1)) { fail(); break; }
             if (*(volatile int*)&abort_flag) break;
             uint8_t* st = smem + s * STAGE_BYTES;
             tc::mbar_arrive_expect_tx(&full[s], (two ? 2 : 1) * TILE_BYTES);
             tc::tma_load_2d(st, &tmA, kx, t0, &full[s]);
             if (two) tc::tma_load_2d(st + TILE_BYTES, &tmA, kx, t0 + BM, &full[s]);
+            if constexpr (WT == W_Q8_0) {
+                // raw k-block i + R_STAGES into the slot the producers finish with k-block i
+                const int j = i + R_STAGES;
+                if (j < nk) {
+                    if (!tc::mbar_wait(&r_empty[i % R_STAGES], (i / R_STAGES) & 1)) { fail(); break; }
+                    issue_raw(j);
+                }
+            }
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer
         constexpr uint32_t idesc = tc::idesc_f16(BM, BN);
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {   // local k-block index
-            const int s = kb % STAGES;
-            if (!tc::mbar_wait(&full[s], (kb / STAGES) & 1)) { fail(); ok = false; break; }
+            const int s = kb % ST;
+            if (!tc::mbar_wait(&full[s], (kb / ST) & 1)) { fail(); ok = false; break; }
             if (*(volatile int*)&abort_flag) { ok = false; break; }
             tc::tc_fence_after();
             uint8_t* st = smem + s * STAGE_BYTES;
@@ -144,49 +186,45 @@ __global__ void __launch_bounds__(THREADS, 1)
             wrow = n0 + p;
         }
         if constexpr (WT == W_Q8_0) {
-            // Q8_0: the row's raw blocks are loaded PD k-blocks ahead of their
-            // conversion, so the global latency overlaps the MMAs instead of
-            // gating every k-block
-            constexpr int PD = 4;
-            const bool live = wrow >= 0 && wrow < W->rows;
-            const uint8_t* rp = W->q + (size_t)(live ? wrow : 0) * W->row_stride;
-            const unsigned short* dp = reinterpret_cast<const unsigned short*>(W->d) + (size_t)(live ? wrow : 0) * W->d_stride;
-            uint4 raw[PD][4];
-            uint32_t dd[PD];
-            auto fetch = [&](int kb, uint4 (&q)[4], uint32_t& d2) {
-                if (live && kb < nk) {
-                    const int k0 = (kb0 + kb) * BK;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) q[i] = __ldg(reinterpret_cast<const uint4*>(rp + k0) + i);
-                    d2 = __ldg(reinterpret_cast<const unsigned int*>(dp + k0 / 32));   // the two block scales
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) q[i] = make_uint4(0, 0, 0, 0);
-                    d2 = 0u;
-                }
-            };
-#pragma unroll
-            for (int d = 0; d < PD; ++d) fetch(d, raw[d], dd[d]);
+            // Q8_0 from the raw ring: thread (w, l) converts 16-byte chunk
+            // c = l % 4 of tile rows 8w + l/4 + 32i (i = 0..3): a warp reads 8
+            // whole 64-byte rows, 512 contiguous bytes, per shared load
+            const int w = p >> 5, l = p & 31, c = l & 3;
+            const uint8_t* rawb = smem + ST * STAGE_BYTES;
             bool stop = false;
-            for (int kb0l = 0; kb0l < nk && !stop; kb0l += PD) {
-#pragma unroll
-                for (int d = 0; d < PD; ++d) {
-                    const int kb = kb0l + d;
-                    if (kb >= nk) break;
-                    const int s = kb % STAGES;
-                    if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); stop = true; break; }
-                    if (*(volatile int*)&abort_flag) { stop = true; break; }
-                    uint8_t* bt = smem + s * STAGE_BYTES + 2 * TILE_BYTES;
-                    q8_0_tile_row(raw[d], dd[d], bt, p);
-                    fetch(kb + PD, raw[d], dd[d]);
-                    tc::fence_proxy_async_smem();
-                    tc::mbar_arrive(&full[s]);
+            for (int kb = 0; kb < nk && !stop; ++kb) {   // local k-block index
+                const int s = kb % ST, rsl = kb % R_STAGES;
+                if (!tc::mbar_wait(&r_full[rsl], (kb / R_STAGES) & 1) ||
+                    (kb >= ST && !tc::mbar_wait(&empty[s], ((kb / ST) - 1) & 1))) {
+                    fail();
+                    break;
                 }
+                if (*(volatile int*)&abort_flag) break;
+                const uint8_t* rs = rawb + rsl * R_STAGE;
+                uint4 v[4];
+                unsigned short d[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int rho = 8 * w + (l >> 2) + 32 * i;
+                    v[i] = *reinterpret_cast<const uint4*>(rs + rho * BK + c * 16);
+                    d[i] = *reinterpret_cast<const unsigned short*>(rs + RQ_BYTES + rho * 16 +
+                                                                    ((kb0 + kb) & 3) * 4 + (c >> 1) * 2);
+                }
+                tc::mbar_arrive(&r_empty[rsl]);   // this thread's raw bytes are in registers
+                uint8_t* bt = smem + s * STAGE_BYTES + 2 * TILE_BYTES;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int rho = 8 * w + (l >> 2) + 32 * i;
+                    q8_0_chunk_pair(v[i], d[i], bt + rho * 128, rho & 7, 2 * c);
+                }
+                tc::fence_proxy_async_smem();
+                tc::mbar_arrive(&full[s]);
             }
+            (void)stop;
         } else {
             for (int kb = 0; kb < nk; ++kb) {   // local k-block index
-                const int s = kb % STAGES;
-                if (kb >= STAGES && !tc::mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { fail(); break; }
+                const int s = kb % ST;
+                if (kb >= ST && !tc::mbar_wait(&empty[s], ((kb / ST) - 1) & 1)) { fail(); break; }
                 if (*(volatile int*)&abort_flag) break;
                 uint8_t* bt = smem + s * STAGE_BYTES + 2 * TILE_BYTES;
                 produce_row<WT>(*W, wrow, (kb0 + kb) * BK, bt, p);
@@ -398,7 +436,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 template <int EPI>
-cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, cudaStream_t st) {
+cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, const CUtensorMap* wq, cudaStream_t st) {
     dim3 grid((EPI == EPI_SWIGLU ? (a.N + 63) / 64 : (a.N + BN - 1) / BN), (a.T + 2 * BM - 1) / (2 * BM),
               a.kpart ? a.k_splits : 1);
     // programmatic dependent launch: CTAs may start (prologue, weight
@@ -406,7 +444,7 @@ cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, cudaStream_t st
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.dynamicSmemBytes = smem_bytes(a.w0.type);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -415,11 +453,11 @@ cudaError_t launch_epi(const GemmArgs& a, const CUtensorMap& tm, cudaStream_t st
     cfg.numAttrs = 1;
     cudaError_t e;
     switch (a.w0.type) {
-        case W_Q8_0: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q8_0, EPI>, tm, a); break;
-        case W_Q5_K: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q5_K, EPI>, tm, a); break;
-        case W_Q6_K: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q6_K, EPI>, tm, a); break;
-        case W_F16: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F16, EPI>, tm, a); break;
-        case W_F32: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F32, EPI>, tm, a); break;
+        case W_Q8_0: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q8_0, EPI>, tm, wq[0], wq[1], wq[2], wq[3], a); break;
+        case W_Q5_K: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q5_K, EPI>, tm, tm, tm, tm, tm, a); break;
+        case W_Q6_K: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_Q6_K, EPI>, tm, tm, tm, tm, tm, a); break;
+        case W_F16: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F16, EPI>, tm, tm, tm, tm, tm, a); break;
+        case W_F32: e = cudaLaunchKernelEx(&cfg, k_gemm_tc<W_F32, EPI>, tm, tm, tm, tm, tm, a); break;
         default: return cudaErrorInvalidValue;
     }
     note_launch();
@@ -431,8 +469,9 @@ cudaError_t prepare_epi() {
     const void* fns[] = {(const void*)k_gemm_tc<W_Q8_0, EPI>, (const void*)k_gemm_tc<W_Q5_K, EPI>,
                          (const void*)k_gemm_tc<W_Q6_K, EPI>, (const void*)k_gemm_tc<W_F16, EPI>,
                          (const void*)k_gemm_tc<W_F32, EPI>};
-    for (const void* f : fns) {
-        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    const int types[] = {W_Q8_0, W_Q5_K, W_Q6_K, W_F16, W_F32};
+    for (int i = 0; i < 5; ++i) {
+        cudaError_t e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(types[i]));
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
@@ -520,17 +559,18 @@ cudaError_t gemm_tc_prepare() {
     return prepare_epi<EPI_STORE>();
 }
 
-cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st) {
+cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap* wq, cudaStream_t st) {
     if (a.K % BK || a.T <= 0 || a.N <= 0) return cudaErrorInvalidValue;
     if (a.epi == EPI_QKV && (BN % a.hd || (a.hd != 32 && a.hd != 64 && a.hd != 128))) return cudaErrorInvalidValue;
     if (a.kpart && (a.k_splits < 1 || a.k_splits > a.K / BK || a.epi == EPI_SWIGLU || a.epi == EPI_ARGMAX))
         return cudaErrorInvalidValue;
+    if (a.w0.type == W_Q8_0 && (!wq || a.w0.cols != a.K)) return cudaErrorInvalidValue;
     switch (a.epi) {
-        case EPI_QKV: return launch_epi<EPI_QKV>(a, tmA, st);
-        case EPI_RESID: return launch_epi<EPI_RESID>(a, tmA, st);
-        case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(a, tmA, st);
-        case EPI_STORE: return launch_epi<EPI_STORE>(a, tmA, st);
-        case EPI_ARGMAX: return a.amax ? launch_epi<EPI_ARGMAX>(a, tmA, st) : cudaErrorInvalidValue;
+        case EPI_QKV: return launch_epi<EPI_QKV>(a, tmA, wq, st);
+        case EPI_RESID: return launch_epi<EPI_RESID>(a, tmA, wq, st);
+        case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(a, tmA, wq, st);
+        case EPI_STORE: return launch_epi<EPI_STORE>(a, tmA, wq, st);
+        case EPI_ARGMAX: return a.amax ? launch_epi<EPI_ARGMAX>(a, tmA, wq, st) : cudaErrorInvalidValue;
         default: return cudaErrorInvalidValue;
     }
 }

@@ -67,8 +67,10 @@ struct GemmArgs {
     int k_splits = 1;
     int* err = nullptr;
 };
-// tmA: f16 activations [T][K], box 64 x 128; weight tiles are dequantized in the kernel
-cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, cudaStream_t st);
+// tmA: f16 activations [T][K], box 64 x 128; weight tiles are dequantized in
+// the kernel.  Q8_0 weights also take wq[4], the byte maps gemm_ws_launch
+// takes, with box rows 128 (SwiGLU: 64).
+cudaError_t gemm_tc_launch(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap* wq, cudaStream_t st);
 cudaError_t gemm_tc_prepare();
 // sum split-K partials in order and apply a.epi (QKV / RESID / STORE)
 cudaError_t splitk_epilogue_launch(const GemmArgs& a, cudaStream_t st);
