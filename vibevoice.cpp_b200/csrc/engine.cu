@@ -31,7 +31,7 @@ using namespace vvq2;
 namespace {
 
 constexpr int PART_SLOTS = 1024;   // (row, split) attention partial slots (>= GEMV_MAX_M x 64 splits)
-constexpr int PREFILL_ROWS_DEFAULT = 4096;   // token rows per tensor-core chunk (VVQ2_PREFILL_ROWS overrides)
+constexpr int PREFILL_ROWS_DEFAULT = 16384;  // token rows per tensor-core chunk (VVQ2_PREFILL_ROWS overrides)
 
 // cuTensorMapEncodeTiled from the driver, fetched through the runtime (no -lcuda)
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
