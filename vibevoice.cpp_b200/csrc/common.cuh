@@ -104,6 +104,12 @@ __device__ __forceinline__ float silu_ref(float x) {
     return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
 }
 
+// The same function with the fast exponential and divide intrinsics (a few
+// ulp of f32), for epilogues whose output is rounded to f16 at once (2^-11):
+// the tensor-core GEMMs' SwiGLU.  Large -x: the divisor is inf and the
+// result 0; large x: x.
+__device__ __forceinline__ float silu_f16out(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 // NEOX rotation of the pair (x0, x1) = (x[i], x[i + hd/2]) at position pos,
 // with ggml's CPU theta cache: theta_0 = pos, theta_{k+1} = theta_k * ts
 // (ggml_rope_cache_init), ts = powf(theta_base, -2/hd) computed on the host.

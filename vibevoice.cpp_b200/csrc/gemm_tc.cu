@@ -281,9 +281,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                             __half* dst = a.yh + (size_t)tr * a.yh_stride + i;
                             if (i + 1 < a.N)
                                 *reinterpret_cast<__half2*>(dst) =
-                                    __floats2half2_rn(__fmul_rn(silu_ref(g0), u0), __fmul_rn(silu_ref(g1), u1));
+                                    __floats2half2_rn(__fmul_rn(silu_f16out(g0), u0), __fmul_rn(silu_f16out(g1), u1));
                             else if (i < a.N)
-                                *dst = __float2half_rn(__fmul_rn(silu_ref(g0), u0));
+                                *dst = __float2half_rn(__fmul_rn(silu_f16out(g0), u0));
                         } else {
                             const int pj = (lane & ~7) | ((lane ^ rr) & 7);
                             float4 x = *reinterpret_cast<const float4*>(stg + rr * (BN * 4) + pj * 16);
@@ -365,9 +365,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                         for (int e = 0; e < 32; e += 2) {
                             if (i0 + e + 1 < a.N) {
                                 *reinterpret_cast<__half2*>(a.yh + (size_t)t * a.yh_stride + i0 + e) =
-                                    __floats2half2_rn(__fmul_rn(silu_ref(g[e]), u[e]), __fmul_rn(silu_ref(g[e + 1]), u[e + 1]));
+                                    __floats2half2_rn(__fmul_rn(silu_f16out(g[e]), u[e]), __fmul_rn(silu_f16out(g[e + 1]), u[e + 1]));
                             } else if (i0 + e < a.N) {
-                                a.yh[(size_t)t * a.yh_stride + i0 + e] = __float2half_rn(__fmul_rn(silu_ref(g[e]), u[e]));
+                                a.yh[(size_t)t * a.yh_stride + i0 + e] = __float2half_rn(__fmul_rn(silu_f16out(g[e]), u[e]));
                             }
                         }
                     }

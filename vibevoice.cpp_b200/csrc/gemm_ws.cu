@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             for (int j = 0; j < 32; ++j)
                                 if (j < ne)
                                     yh[(size_t)j * a.yh_stride] = __float2half_rn(
-                                        __fmul_rn(silu_ref(__uint_as_float(u0[j])), __uint_as_float(u1[j])));
+                                        __fmul_rn(silu_f16out(__uint_as_float(u0[j])), __uint_as_float(u1[j])));
                         }
                     } else {   // EPI_QKV
                         const int hd = a.hd, half = hd >> 1;
