@@ -143,40 +143,11 @@ __device__ __forceinline__ void produce_row(const DevW& W, int row, int k0, uint
     }
 }
 
-// Q8_0: one row's 64 stored bytes (q + 128, two blocks) and the two block
-// scales (f16 bits, first block in the low half) to the swizzled tile row p.
-// Exact f16 math: the byte in the mantissa of 1024, minus 1152, is q exactly;
-// one f16 multiply by the block scale gives RN(q * d), the exact f32 product
-// rounded to f16.
-__device__ __forceinline__ void q8_0_tile_row(const uint4 (&raw)[4], uint32_t dbits, uint8_t* bt, int p) {
-    const __half2 s0 = __halves2half2(__ushort_as_half((unsigned short)(dbits & 0xffff)),
-                                      __ushort_as_half((unsigned short)(dbits & 0xffff)));
-    const __half2 s1 = __halves2half2(__ushort_as_half((unsigned short)(dbits >> 16)),
-                                      __ushort_as_half((unsigned short)(dbits >> 16)));
-    const __half2 off = __float2half2_rn(-1152.0f), one = __float2half2_rn(1.0f);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const __half2 sc = j < 4 ? s0 : s1;
-        uint32_t o[4];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint32_t w = wsel(raw[j / 2], (j % 2) * 2 + h);
-            const uint32_t lo = __byte_perm(w, 0x64646464u, 0x5140);
-            const uint32_t hi = __byte_perm(w, 0x64646464u, 0x7362);
-            __half2 qlo = __hfma2(*reinterpret_cast<const __half2*>(&lo), one, off);
-            __half2 qhi = __hfma2(*reinterpret_cast<const __half2*>(&hi), one, off);
-            qlo = __hmul2(qlo, sc);
-            qhi = __hmul2(qhi, sc);
-            o[2 * h] = *reinterpret_cast<const uint32_t*>(&qlo);
-            o[2 * h + 1] = *reinterpret_cast<const uint32_t*>(&qhi);
-        }
-        store_chunk(bt, p, j, make_uint4(o[0], o[1], o[2], o[3]));
-    }
-}
-
 // Q8_0: 16 stored bytes (q + 128) of one block with its scale (f16 bits) to
 // the two swizzled 16-byte chunks j0, j0 + 1 of a tile row (rowp: the row's
-// 128 bytes, swz: its row index mod 8), the same exact f16 math.
+// 128 bytes, swz: its row index mod 8).  Exact f16 math: the byte in the
+// mantissa of 1024, minus 1152, is q exactly; one f16 multiply by the block
+// scale gives RN(q * d), the exact f32 product rounded to f16.
 __device__ __forceinline__ void q8_0_chunk_pair(const uint4& v, unsigned short dbits, uint8_t* rowp, int swz, int j0) {
     const __half2 sc = __halves2half2(__ushort_as_half(dbits), __ushort_as_half(dbits));
     const __half2 off = __float2half2_rn(-1152.0f), one = __float2half2_rn(1.0f);

@@ -20,14 +20,16 @@
 // Chunks with enough rows to fill the SMs with 256 x 256 tiles run the
 // persistent kernel of gemm_ws.cu instead; this one serves the few-row
 // GEMMs (batched decode of many streams, short prompt chunks, split-K).
-// Pipeline: 4 stages of {A0, A1, B} 16 KB tiles (BK = 64), mbarriers full/empty.
-// The Q8_0 weight producers fetch each row's raw blocks 4 k-blocks ahead of
-// their conversion.  Epilogues that write rows stage the accumulators
-// through the drained pipeline buffers so that a warp stores whole rows.  The
-// kernel is launched as a programmatic dependent: barrier setup, TMEM
-// allocation and the first weight fetches overlap the previous kernel; the
-// TMA warp waits (griddepcontrol.wait) before loading anything that kernel
-// wrote.  Every wait is bounded; a timeout sets args.err and unwinds without
+// Pipeline: stages of {A0, A1, B} 16 KB tiles (BK = 64), mbarriers
+// full/empty; 4 stages, or 3 for Q8_0, whose raw bytes (each k-block's
+// quants and its rows' block scales) arrive by TMA in an 8-deep ring that the
+// producers read from shared memory, 512 contiguous bytes per warp load
+// (other types: each producer thread decodes its row from global memory).
+// Epilogues that write rows stage the accumulators through the drained
+// pipeline buffers so that a warp stores whole rows.  The kernel is launched
+// as a programmatic dependent: barrier setup, TMEM allocation and the first
+// raw weight loads overlap the previous kernel; the TMA thread waits
+// (griddepcontrol.wait) before loading anything that kernel wrote.  Every wait is bounded; a timeout sets args.err and unwinds without
 // leaving TMEM allocated.
 #include <algorithm>
 
