@@ -34,11 +34,12 @@
 //    (exact dequantized int8 weights x f32 activations, packed FFMA2),
 //    reduces them with one transposing butterfly and applies the epilogue
 //    (bias, residual add, SwiGLU, running argmax).
-//  * attention: one item per (row, KV head, split of whole 64-key pages) on
-//    128-thread groups.  The first page of each group's item is requested by
-//    TMA as soon as the shared memory it lands in is free (past keys do not
-//    depend on this step), i.e. during the previous layer's down-projection
-//    hand-over.  The item applies RoPE to this step's raw q/k, patches the new
+//  * attention: one item per (row, KV head, split of whole 64-key pages) per
+//    CTA, run by all 512 threads (four quarters share the page's keys and
+//    the group's q heads).  The first page of a CTA's first item is
+//    requested by TMA as soon as the shared memory it lands in is free (past
+//    keys do not depend on this step), i.e. during the previous layer's
+//    down-projection hand-over.  The item applies RoPE to this step's raw q/k, patches the new
 //    key/value row into its tile, appends it to the paged cache and writes an
 //    (O, max, sum) partial; one CTA per (row, q head) merges the partials
 //    (log-sum-exp) into the attention output.
@@ -67,7 +68,6 @@ constexpr int MT = 512;                 // threads per CTA
 constexpr int NCW = 16;                 // warps (all compute and stream)
 constexpr int NCT = NCW * 32;
 constexpr int MAX_STAGES = 32;          // ring slots: NCW x D
-constexpr int ATT_THREADS = 128;
 constexpr int MAXG = 8;                 // q heads per KV head
 constexpr int PAGE = KV_PAGE;           // keys per page / tile
 constexpr int MAX_MERGE = MEGA_MAX_SPLITS;
