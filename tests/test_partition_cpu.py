@@ -1,10 +1,14 @@
 """Host side of the multi-GPU attention partition (config 5), on CPU with a
 world-size-2 gloo group: the ownership plan covers every head and key once,
 and per-rank partial attention over its (heads, sequence part) merged with
-the (O, LSE) rule after an all-gather equals full causal attention.  The
-partitioned GPU path itself is tested in test_gpu_partition.py."""
+the (O, LSE) rule after an all-gather equals full causal attention; the
+engine's own interleave helpers (compiled for the host) agree with that
+plan.  The partitioned GPU path itself is tested in test_gpu_partition.py."""
 import os
+import shutil
+import subprocess
 import sys
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -46,6 +50,35 @@ def test_plan_covers_each_head_and_key_once():
         assert feats == list(range(18944))
     with pytest.raises(ValueError):
         PT.ffn_range(0, 8, 4864 + 64)
+
+
+def test_engine_interleave_matches_plan(tmp_path):
+    """The engine's own interleave helpers (common.cuh, compiled for the host:
+    the functions its local_row() and the kernels call) against the plan
+    above: which part stores a position, its cache index in that part, and a
+    row's (pos, cidx, kvlen) as each part sees it."""
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(nvcc).exists():
+        pytest.skip("nvcc not available")
+    root = Path(__file__).resolve().parent.parent
+    exe, dump = tmp_path / "zz_host", tmp_path / "zz.bin"
+    r = subprocess.run([nvcc, "-std=c++17", "-O1", "-I", str(root / "vibevoice.cpp_b200" / "csrc"),
+                        str(root / "tests" / "zz_rows_host.cu"), "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+    n = 1300                                   # five 256-position periods and a ragged tail
+    assert subprocess.run([str(exe), str(n), str(dump)]).returncode == 0
+    got = np.fromfile(dump, np.int32).reshape(n, 9)
+    keys = [PT.keys_of_part(s, 2, n + 1) for s in (0, 1)]
+    for p in range(n):
+        part, c0, c1 = got[p, :3]
+        assert part == PT.part_of(p) and c0 == PT.part_count(0, p) and c1 == PT.part_count(1, p), p
+        for s in (0, 1):
+            lpos, lcidx, lkv = got[p, 3 + 3 * s:6 + 3 * s]
+            held = keys[s][keys[s] <= p]
+            # the part's last key at or before p; the row's own index if it stores p; keys below p + 1
+            assert lpos == len(held) - 1, (p, s)
+            assert lcidx == (len(held) - 1 if PT.part_of(p) == s else -1), (p, s)
+            assert lkv == len(held), (p, s)
 
 
 def _worker(rank, world, port, seq_parts, q_all, k_all, v_all, q_pos, out):
